@@ -1,0 +1,397 @@
+#!/usr/bin/env python3
+"""Batch-1 greedy decode throughput of the B200 engine (one JSON line).
+
+Workload (per GPU): the seeded Qwen2.5-0.5B-shape per-row int8 model, a
+128-token uniform-random prompt prefilled untimed, then K timed greedy decode
+steps (a "step" = one token through the whole model, LM head and argmax),
+FP32 KV cache, as the reference's `bench` command runs it
+(src/main.cpp:128-179 of mottopanikeiku/cpu-decode): one warm-up pass, then
+rewind to the context and time.
+
+* value: tokens/s with the model resident in HBM; steps chained on the device
+  (the argmax of step t is the token of step t+1, no host round trip), timed
+  with CUDA events on the launching stream.
+* e2e: the same greedy loop through the C ABI call a user makes (dcb_step)
+  with host buffers: the token goes in as a launch argument, the full logits
+  vector (vocab floats) and the argmax come back to host memory every step.
+* roofline: the step kernel's algorithmic bytes per token (the reference's own
+  byte model) over its average launch time, against the measured HBM peak.
+* cpu_baseline: the reference's own CPU engine (built from its sources into
+  oracle/_ref) timed on this host's cores on a bounded sample.
+
+Several GPUs (torchrun) run independent replicas, one sequence each, with no
+collective on the data path (weak scaling); the job time is the max over ranks.
+`--impl reference` times the reference CPU engine instead (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+CONTEXT = 128
+SEED = 0
+MODEL_CACHE = Path(os.environ.get("DCB_MODEL_CACHE", "/tmp/dcb_models"))
+METRIC = "batch-1 decode tokens/s at ctx 128/4096; achieved HBM GB/s vs B200 peak"
+
+
+def load_package():
+    import importlib.util
+    if "cpu_decode_b200" in sys.modules:
+        return sys.modules["cpu_decode_b200"]
+    pkg = ROOT / "cpu-decode_b200"
+    spec = importlib.util.spec_from_file_location("cpu_decode_b200", pkg / "__init__.py",
+                                                  submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["cpu_decode_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def model_bytes_per_token(d, pos: int, kv_bytes: int = 4) -> int:
+    """Algorithmic bytes of one token at cache position `pos` (the reference's
+    byte model, src/kernels.cpp:184-185 and src/model.cpp:311-316): all weights
+    and scales once, norms/biases, the embedding row, the new K/V row and the
+    K/V rows 0..pos once."""
+    H, I, L, V, kvd = d.hidden, d.intermediate, d.layers, d.vocab, d.kv_dim
+    weights = L * (H * H + 2 * kvd * H + H * H + 2 * I * H + H * I) + V * H
+    scales = 4 * (L * (H + 2 * kvd + H + 2 * I + H) + V)
+    norms = 4 * (L * (3 * H + 2 * kvd) + H)
+    embed = H + 4
+    kv = L * 2 * kvd * kv_bytes * (1 + (pos + 1))
+    return weights + scales + norms + embed + kv
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks sampled while the GPU is busy."""
+
+    def __init__(self, index: int):
+        self.path = Path(tempfile.mkstemp(suffix=".csv")[1])
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(", ") for r in self.path.read_text().splitlines() if r.strip()]
+        self.path.unlink(missing_ok=True)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(model_dir: Path, steps: int = 16) -> dict:
+    """The reference CPU engine on this host's cores, bounded sample."""
+    exe = ROOT / "oracle" / "_ref" / "cpu-decode"
+    threads = len(os.sched_getaffinity(0))
+    tokens = ",".join(str(t) for t in prompt_tokens())
+    if exe.exists():
+        cpuinfo = Path("/proc/cpuinfo").read_text()
+        kernel = "simd512x4" if "avx512bw" in cpuinfo else "simd256"
+        out = subprocess.run([str(exe), "bench", "--model", str(model_dir), "--tokens", tokens, "--context",
+                              str(CONTEXT), "--steps", str(steps), "--repeats", "1", "--threads", str(threads),
+                              "--kernel", kernel], capture_output=True, text=True, check=True)
+        res = json.loads(out.stdout)
+        tps = res["samples"][0]["tokens_per_second"]
+        return {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
+                "sample": f"reference cpu-decode bench --kernel {kernel}: ctx {CONTEXT}, {steps} greedy steps, 1 repeat"}
+    sys.path.insert(0, str(ROOT))
+    import oracle
+    orc = oracle.Oracle(model_dir, CONTEXT + steps + 1, threads=threads)
+    prompt = prompt_tokens()
+    for i, t in enumerate(prompt):
+        logits = orc.step(t, i + 1 == len(prompt))
+    nxt = oracle.argmax(logits)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        nxt = oracle.argmax(orc.step(nxt))
+    dt = time.perf_counter() - t0
+    return {"value": round(steps / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"C restatement of the reference step: ctx {CONTEXT}, {steps} greedy steps"}
+
+
+def prompt_tokens() -> list[int]:
+    dcb = load_package()
+    import cpu_decode_b200.synthetic as syn
+    return syn.random_tokens(CONTEXT, syn.QWEN05.vocab, seed=SEED + 11)
+
+
+def ensure_model() -> Path:
+    load_package()
+    import cpu_decode_b200.synthetic as syn
+    return syn.ensure_random_model(MODEL_CACHE / f"qwen05_seed{SEED}", syn.QWEN05, seed=SEED)
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    model = ensure_model()
+    steps = max(1, args.steps)
+    exe = ROOT / "oracle" / "_ref" / "cpu-decode"
+    if not exe.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "reference CPU build (oracle/_ref) is missing"}))
+        return
+    samples = []
+    for _ in range(max(1, args.warmup) + 1):
+        samples.append(cpu_baseline(model, steps=min(steps, 16)))
+    base = samples[-1]
+    v = base["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": min(steps, 16), "warmup": args.warmup, "ms_per_step": round(1000.0 / v, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, f32 math",
+            "data": "synthetic (seeded random-init weights and tokens)",
+            "config": {"workload": "qwen2.5-0.5b-shape int8, batch 1, ctx 128 prompt + greedy decode, FP32 KV",
+                       "context": CONTEXT},
+            "cpu_baseline": base,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-long", action="store_true", help="skip the ctx 4096 extra measurement")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dcb = load_package()
+    model = ensure_model() if rank == 0 else None
+    if dist:
+        dist.barrier()
+        model = ensure_model()
+    import cpu_decode_b200.synthetic as syn
+    d = syn.QWEN05
+    K, W = max(1, args.steps), max(3, args.warmup)
+    capacity = CONTEXT + K + W + 2
+    eng = dcb.Engine(model, capacity, device=local)
+    stream = torch.cuda.current_stream()
+    eng.set_stream(stream.cuda_stream)
+    prompt = prompt_tokens()
+
+    # Prefill (untimed), seed token from the last prompt position.
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for i, t in enumerate(prompt):
+        eng.step_async(t, head=(i + 1 == len(prompt)), argmax_dev=tok.data_ptr())
+    eng.synchronize()
+    seed = tok.clone()
+
+    def decode_window(n: int) -> None:
+        for _ in range(n):
+            eng.step_async(token_dev=tok.data_ptr(), head=True, argmax_dev=tok.data_ptr())
+
+    # Warm-up, then a ~1 s untimed burst for the clock sampler, then rewind.
+    clocks = ClockSampler(torch.cuda.current_device())
+    decode_window(W)
+    eng.synchronize()
+    burst_end = time.time() + 1.0
+    while time.time() < burst_end:
+        eng.rewind(CONTEXT)
+        tok.copy_(seed)
+        decode_window(K)
+        eng.synchronize()
+    eng.rewind(CONTEXT)
+    tok.copy_(seed)
+
+    launches0 = eng.launch_count
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    decode_window(K)
+    end.record(stream)
+    torch.cuda.synchronize()
+    eng.synchronize()
+    if dist:
+        dist.barrier()
+    clock_info = clocks.stop()
+    ms = start.elapsed_time(end)
+    gpu_launches = eng.launch_count - launches0
+    generated_last = int(tok.item())
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * K / (ms / 1000.0)
+    avg_bytes = sum(model_bytes_per_token(d, CONTEXT + i) for i in range(K)) / K
+    per_launch_s = ms / 1000.0 / K
+    peak, peak_kind = measured_peaks()
+    achieved = avg_bytes / per_launch_s / 1e9
+
+    # e2e through the public C ABI with host buffers (synchronous per step).
+    eng.rewind(CONTEXT)
+    nxt = int(seed.item())
+    import ctypes
+    pinned = torch.empty(d.vocab, dtype=torch.float32, pin_memory=True)  # the caller's logits buffer
+    host_ptr = pinned.data_ptr()
+    am = ctypes.c_int()
+    lib = dcb.lib()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        rc = lib.dcb_step(eng._h, nxt, 1, host_ptr, ctypes.addressof(am))
+        if rc:
+            raise RuntimeError(lib.dcb_last_error().decode())
+        nxt = am.value
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * K / e2e_s
+    assert nxt == generated_last, "host-driven and device-chained greedy streams diverged"
+
+    extra = {}
+    if not args.no_long and rank == 0:
+        extra["ctx4096"] = long_context(dcb, model, d, K, W, local)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 weights, f32 math",
+            "data": "synthetic (seeded random-init weights N(0,0.02) and uniform token ids)",
+            "config": {"workload": "qwen2.5-0.5b-shape int8 (24x896, 14/2 heads, FFN 4864, vocab 151936), "
+                                   "batch 1, 128-token prompt + greedy decode, FP32 KV",
+                       "context": CONTEXT, "global_batch": world, "parallelism": f"replicas{world}",
+                       "l2": "inputs larger than L2 (496 MB of weights per step)"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": d.vocab * 4 + 8},
+            "gpu_launches": int(gpu_launches),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": int(avg_bytes),
+                         "traffic": profiled_traffic("decode_step_kernel_ctx128.md"),
+                         "kernel": "decode_step_kernel"},
+            "clocks": clock_info,
+            "launch": eng.launch_info(),
+        }
+        line.update(extra)
+        if not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline(model)
+            except Exception as exc:  # reported, never fatal
+                line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+        print(json.dumps(line))
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def long_context(dcb, model, d, K, W, device) -> dict:
+    """Config 3 at ctx 4096: KV pre-filled with seeded N(0,1) rows, greedy steps."""
+    import torch
+    import cpu_decode_b200.synthetic as syn
+    ctx = 4096
+    out = {}
+    long_dir = MODEL_CACHE / "qwen05_seed0_long"
+    long_dir.mkdir(parents=True, exist_ok=True)
+    cfg = json.loads((model / "config.json").read_text())
+    cfg["max_position_embeddings"] = 40960
+    (long_dir / "config.json").write_text(json.dumps(cfg))
+    link = long_dir / "model.safetensors"
+    if not link.exists():
+        link.symlink_to((model / "model.safetensors").resolve())
+    rng = np.random.default_rng(4096)
+    kv = [(rng.standard_normal((ctx, d.kv_dim), dtype=np.float32), rng.standard_normal((ctx, d.kv_dim), dtype=np.float32))
+          for _ in range(d.layers)]
+    for kvt in ("f32", "f16"):
+        eng = dcb.Engine(long_dir, ctx + K + W + 2, kv_dtype=kvt, device=device)
+        stream = torch.cuda.current_stream()
+        eng.set_stream(stream.cuda_stream)
+        for l, (k, v) in enumerate(kv):
+            eng.kv_write(l, 0, k, v)
+        tok = torch.full((1,), 1234, dtype=torch.int32, device="cuda")
+        eng.set_position(ctx)
+        for _ in range(W):
+            eng.step_async(token_dev=tok.data_ptr(), head=True, argmax_dev=tok.data_ptr())
+        eng.synchronize()
+        eng.set_position(ctx)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record(stream)
+        for _ in range(K):
+            eng.step_async(token_dev=tok.data_ptr(), head=True, argmax_dev=tok.data_ptr())
+        e.record(stream)
+        torch.cuda.synchronize()
+        eng.synchronize()
+        ms = s.elapsed_time(e)
+        kvb = 4 if kvt == "f32" else 2
+        avg = sum(model_bytes_per_token(d, ctx + i, kvb) for i in range(K)) / K
+        peak, _ = measured_peaks()
+        gbs = avg / (ms / 1000.0 / K) / 1e9
+        out[kvt] = {"tokens_per_s": round(K / (ms / 1000.0), 2), "ms_per_step": round(ms / K, 5),
+                    "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "bytes_per_token": int(avg)}
+        eng.close()
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+"""Python access to the B200 decode engine (libdecode_b200.so) through its C ABI.
+
+The engine is the reference's ``decode::Engine`` (include/decode.hpp:41-58 of
+mottopanikeiku/cpu-decode) rebuilt on sm_100a: ``Engine(directory, capacity)``
+loads the per-row int8 safetensors model, ``step(token, head)`` runs one token
+and returns the logits, ``rewind``/``reset``/``position`` keep the reference's
+cache semantics. Isolated operators (int8 GEMV, split-KV attention, RMSNorm,
+RoPE, argmax) take device pointers, e.g. ``tensor.data_ptr()`` of CUDA tensors.
+
+There is no CPU path: importing works anywhere, but every call loads the CUDA
+library and fails loudly when it is missing or no GPU is present.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libdecode_b200.so"
+
+KV_F32, KV_F16 = 0, 1
+KV_DTYPES = {"f32": KV_F32, "f16": KV_F16}
+
+ERRORS = {1: ValueError, 2: ValueError, 3: RuntimeError, 4: RuntimeError, 5: RuntimeError, 6: TimeoutError,
+          7: NotImplementedError}
+
+# Every symbol include/decode_b200.h declares.
+EXPORTS = (
+    "dcb_last_error", "dcb_set_error", "dcb_create", "dcb_create_from_dir", "dcb_destroy", "dcb_step",
+    "dcb_step_async", "dcb_synchronize", "dcb_rewind", "dcb_reset", "dcb_position", "dcb_set_stream", "dcb_stream",
+    "dcb_logits_device", "dcb_kv_write", "dcb_kv_read", "dcb_set_position", "dcb_launch_info", "dcb_launch_count",
+    "dcb_gemv_i8", "dcb_attention", "dcb_rmsnorm", "dcb_rope", "dcb_argmax",
+)
+
+
+def build(force: bool = False) -> Path:
+    """Compile libdecode_b200.so in-tree for sm_100a (nvcc cross-compiles without a GPU)."""
+    if force or not LIB_PATH.exists():
+        subprocess.run(["make", "-s", "-C", str(HERE), "-j4"], check=True)
+    return LIB_PATH
+
+
+_LIB: C.CDLL | None = None
+
+
+def lib() -> C.CDLL:
+    """The loaded CUDA library. Raises when it has not been built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH.name} is not built; run `make -C {HERE}` (needs nvcc)")
+    L = C.CDLL(str(LIB_PATH))
+    vp, sz, i32 = C.c_void_p, C.c_size_t, C.c_int
+    L.dcb_last_error.restype = C.c_char_p
+    L.dcb_set_error.argtypes = [C.c_char_p]
+    L.dcb_create_from_dir.argtypes = [C.c_char_p, sz, i32, i32, i32, C.POINTER(vp)]
+    L.dcb_destroy.argtypes = [vp]
+    L.dcb_step.argtypes = [vp, i32, i32, vp, vp]
+    L.dcb_step_async.argtypes = [vp, i32, vp, i32, vp]
+    L.dcb_synchronize.argtypes = [vp]
+    L.dcb_rewind.argtypes = [vp, sz]
+    L.dcb_reset.argtypes = [vp]
+    L.dcb_position.argtypes = [vp]
+    L.dcb_position.restype = sz
+    L.dcb_set_stream.argtypes = [vp, vp]
+    L.dcb_stream.argtypes = [vp]
+    L.dcb_stream.restype = vp
+    L.dcb_logits_device.argtypes = [vp]
+    L.dcb_logits_device.restype = vp
+    L.dcb_kv_write.argtypes = [vp, i32, sz, sz, vp, vp]
+    L.dcb_kv_read.argtypes = [vp, i32, sz, sz, vp, vp]
+    L.dcb_set_position.argtypes = [vp, sz]
+    L.dcb_launch_info.argtypes = [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]
+    L.dcb_launch_count.argtypes = [vp]
+    L.dcb_launch_count.restype = C.c_uint64
+    L.dcb_gemv_i8.argtypes = [vp, vp, vp, vp, vp, i32, i32, vp]
+    L.dcb_attention.argtypes = [vp, vp, vp, i32, vp, i32, i32, i32, i32, C.c_float, vp]
+    L.dcb_rmsnorm.argtypes = [vp, vp, vp, i32, C.c_float, vp]
+    L.dcb_rope.argtypes = [vp, i32, i32, i32, C.c_float, i32, vp]
+    L.dcb_argmax.argtypes = [vp, i32, vp, vp]
+    _LIB = L
+    return L
+
+
+def _check(rc: int) -> None:
+    if rc:
+        msg = lib().dcb_last_error().decode()
+        raise ERRORS.get(rc, RuntimeError)(msg)
+
+
+class Engine:
+    """One model on one GPU with its own KV cache (the reference's Engine)."""
+
+    def __init__(self, directory, capacity: int, kv_dtype: str = "f32", cached_rope: bool = True, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().dcb_create_from_dir(str(directory).encode(), int(capacity), KV_DTYPES[kv_dtype],
+                                         int(bool(cached_rope)), int(device), C.byref(h)))
+        self._h = h
+        import json
+        cfg = json.loads((Path(directory) / "config.json").read_text())
+        self.vocab = int(cfg["vocab_size"])
+        self.layers = int(cfg["num_hidden_layers"])
+        self.kv_dim = int(cfg["num_key_value_heads"]) * (int(cfg["hidden_size"]) // int(cfg["num_attention_heads"]))
+        self.capacity = int(capacity)
+        self.logits = np.zeros(self.vocab, np.float32)
+        self._argmax = C.c_int(0)
+
+    # -- the reference API -------------------------------------------------------
+    def step(self, token: int, head: bool = True, logits: bool = True):
+        """Run one token. Returns (logits or None, argmax or None)."""
+        want = head and logits
+        _check(lib().dcb_step(self._h, int(token), int(bool(head)),
+                              self.logits.ctypes.data if want else None,
+                              C.addressof(self._argmax) if head else None))
+        return (self.logits if want else None), (int(self._argmax.value) if head else None)
+
+    def rewind(self, position: int) -> None:
+        _check(lib().dcb_rewind(self._h, int(position)))
+
+    def reset(self) -> None:
+        _check(lib().dcb_reset(self._h))
+
+    @property
+    def position(self) -> int:
+        return int(lib().dcb_position(self._h))
+
+    # -- device-resident stepping --------------------------------------------------
+    def step_async(self, token: int = 0, token_dev: int | None = None, head: bool = True,
+                   argmax_dev: int | None = None) -> None:
+        _check(lib().dcb_step_async(self._h, int(token), token_dev, int(bool(head)), argmax_dev))
+
+    def synchronize(self) -> None:
+        _check(lib().dcb_synchronize(self._h))
+
+    def set_stream(self, stream_handle: int | None) -> None:
+        _check(lib().dcb_set_stream(self._h, stream_handle))
+
+    @property
+    def stream(self) -> int:
+        return int(lib().dcb_stream(self._h) or 0)
+
+    @property
+    def logits_device(self) -> int:
+        return int(lib().dcb_logits_device(self._h))
+
+    def set_position(self, position: int) -> None:
+        _check(lib().dcb_set_position(self._h, int(position)))
+
+    def kv_write(self, layer: int, start: int, keys: np.ndarray, values: np.ndarray) -> None:
+        k = np.ascontiguousarray(keys, np.float32).reshape(-1, self.kv_dim)
+        v = np.ascontiguousarray(values, np.float32).reshape(-1, self.kv_dim)
+        assert k.shape == v.shape
+        _check(lib().dcb_kv_write(self._h, int(layer), int(start), k.shape[0], k.ctypes.data, v.ctypes.data))
+
+    def kv_read(self, layer: int, start: int, count: int):
+        k = np.zeros((count, self.kv_dim), np.float32)
+        v = np.zeros((count, self.kv_dim), np.float32)
+        _check(lib().dcb_kv_read(self._h, int(layer), int(start), int(count), k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def launch_info(self) -> dict:
+        b, t, s, m = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+        _check(lib().dcb_launch_info(self._h, C.byref(b), C.byref(t), C.byref(s), C.byref(m)))
+        return {"blocks": b.value, "threads": t.value, "smem_bytes": s.value, "sms": m.value}
+
+    @property
+    def launch_count(self) -> int:
+        return int(lib().dcb_launch_count(self._h))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().dcb_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---- isolated operators on device pointers ------------------------------------------
+def gemv_i8(w: int, scales: int, bias: int | None, x: int, y: int, rows: int, cols: int, stream: int | None = None):
+    _check(lib().dcb_gemv_i8(w, scales, bias, x, y, rows, cols, stream))
+
+
+def attention(q: int, keys: int, values: int, kv_dtype: str, out: int, length: int, heads: int, kv_heads: int,
+              dim: int, rope_theta: float = 0.0, stream: int | None = None):
+    _check(lib().dcb_attention(q, keys, values, KV_DTYPES[kv_dtype], out, length, heads, kv_heads, dim,
+                               float(rope_theta), stream))
+
+
+def rmsnorm(x: int, w: int, out: int, n: int, eps: float, stream: int | None = None):
+    _check(lib().dcb_rmsnorm(x, w, out, n, float(eps), stream))
+
+
+def rope(x: int, heads: int, dim: int, pos: int, theta: float, direct: bool, stream: int | None = None):
+    _check(lib().dcb_rope(x, heads, dim, pos, float(theta), int(bool(direct)), stream))
+
+
+def argmax(x: int, n: int, out: int, stream: int | None = None):
+    _check(lib().dcb_argmax(x, n, out, stream))

@@ -1,0 +1,152 @@
+/* decode_b200.h — C ABI of the B200 (sm_100a) int8 decode engine.
+ *
+ * Plain C types only; no exceptions cross this boundary. Every call returns 0
+ * (DCB_OK) or an error code; dcb_last_error() gives the message of the last
+ * failure on the calling thread. Messages of argument errors are the
+ * reference engine's own strings, so a C++ wrapper can rethrow them unchanged.
+ *
+ * Each entry point names the interface of mottopanikeiku/cpu-decode it
+ * replaces (file:line in that project).
+ */
+#ifndef DECODE_B200_H
+#define DECODE_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    DCB_OK = 0,
+    DCB_ERR_ARGUMENT = 1,   /* invalid argument; message says which */
+    DCB_ERR_TOKEN = 2,      /* "token ID outside vocabulary" */
+    DCB_ERR_CAPACITY = 3,   /* "context capacity exceeded" */
+    DCB_ERR_REWIND = 4,     /* "cannot rewind forward" */
+    DCB_ERR_CUDA = 5,       /* a CUDA runtime call failed */
+    DCB_ERR_DEVICE_WAIT = 6,/* a device-side wait ran out of time; state was reset */
+    DCB_ERR_UNSUPPORTED = 7
+};
+
+enum { DCB_KV_F32 = 0, DCB_KV_F16 = 1 };
+
+/* One decoder layer, host pointers, reference layout: row-major [rows][cols]
+ * int8 matrices with FP32 per-row scales, FP32 vectors
+ * (src/model.cpp:159-163, 196-215). */
+typedef struct {
+    const int8_t *q, *k, *v, *o, *gate, *up, *down;
+    const float *q_scales, *k_scales, *v_scales, *o_scales, *gate_scales, *up_scales, *down_scales;
+    const float *input_norm, *post_norm, *q_bias, *k_bias, *v_bias;
+} dcb_layer_desc;
+
+/* A tied-head Qwen2 model (src/model.cpp:134-158 Config, :192 embedding). The
+ * embedding matrix is also the LM head. */
+typedef struct {
+    int32_t hidden, intermediate, layers, heads, kv_heads, head_dim, vocab;
+    float epsilon, theta;
+    const int8_t* embed;
+    const float* embed_scales;
+    const float* final_norm;
+    const dcb_layer_desc* layer; /* [layers] */
+} dcb_model_desc;
+
+typedef struct dcb_engine dcb_engine;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* dcb_last_error(void);
+
+/* Replaces Engine::Impl::Impl (src/model.cpp:185-229): uploads the weights to
+ * the device once, in the engine's own layout, and allocates a device KV cache
+ * of `capacity` positions (kv_dtype DCB_KV_F32 or DCB_KV_F16). cached_rope
+ * selects the cached (model.cpp:269-274) or direct (kernels.cpp:138-149)
+ * angle formula. The host weights may be freed after the call returns. */
+int dcb_create(const dcb_model_desc* model, size_t capacity, int kv_dtype, int cached_rope,
+               int device, dcb_engine** out);
+void dcb_destroy(dcb_engine* e);
+
+/* Same, from a model directory in the reference's format (config.json +
+ * model.safetensors[.index.json]), validated like the reference's loader
+ * (src/model.cpp:63-158, 185-250) with its messages. `capacity` is checked
+ * against max_position_embeddings, as Engine::Engine does (src/model.cpp:187). */
+int dcb_create_from_dir(const char* directory, size_t capacity, int kv_dtype, int cached_rope, int device,
+                        dcb_engine** out);
+
+/* Set the message returned by dcb_last_error() on this thread. */
+void dcb_set_error(const char* message);
+
+/* Replaces Engine::step (src/model.cpp:258-329) plus the caller's argmax
+ * (src/main.cpp:35-37). Runs one token at the current position and advances
+ * it. With head != 0 the LM head runs: the logits are copied to host_logits
+ * (vocab floats) when it is not NULL, and the first index of the maximum to
+ * *argmax_out when it is not NULL. With head == 0 neither output is written.
+ * Synchronous: returns when the outputs are in host memory. */
+int dcb_step(dcb_engine* e, int token, int head, float* host_logits, int* argmax_out);
+
+/* Device-resident variant for callers that chain steps on the GPU: the token
+ * is read from device memory `token_dev` when it is not NULL (else `token` is
+ * used) and the argmax is written to device memory `argmax_dev` when it is not
+ * NULL; both may be the same address, so greedy decoding needs no host round
+ * trip. Asynchronous on the engine's stream; errors of the device side are
+ * reported by the next dcb_synchronize(). No counterpart in the reference. */
+int dcb_step_async(dcb_engine* e, int token, const int* token_dev, int head, int* argmax_dev);
+int dcb_synchronize(dcb_engine* e);
+
+/* Engine::rewind / reset / position (src/model.cpp:335-342). */
+int dcb_rewind(dcb_engine* e, size_t position);
+int dcb_reset(dcb_engine* e);
+size_t dcb_position(const dcb_engine* e);
+
+/* The stream the engine launches on (a cudaStream_t; NULL = its own stream). */
+int dcb_set_stream(dcb_engine* e, void* stream);
+void* dcb_stream(const dcb_engine* e);
+
+/* Device pointer of the last logits (vocab floats) and of the argmax int. */
+const float* dcb_logits_device(const dcb_engine* e);
+
+/* KV cache access, for a cache pre-filled from elsewhere (e.g. a long prompt
+ * computed by another engine). Rows [start, start+count) of `layer`, each
+ * kv_heads*head_dim FP32 values, host memory. Writing rows does not move the
+ * position; dcb_set_position() does (it may move forward, unlike rewind).
+ * No counterpart in the reference, whose KV cache is private. */
+int dcb_kv_write(dcb_engine* e, int layer, size_t start, size_t count, const float* keys, const float* values);
+int dcb_kv_read(const dcb_engine* e, int layer, size_t start, size_t count, float* keys, float* values);
+int dcb_set_position(dcb_engine* e, size_t position);
+
+/* Launch configuration actually used (for reports): grid blocks, threads per
+ * block, shared bytes per block, SM count. */
+int dcb_launch_info(const dcb_engine* e, int* blocks, int* threads, int* smem_bytes, int* sms);
+
+/* Number of device kernel launches issued by the engine since creation. */
+uint64_t dcb_launch_count(const dcb_engine* e);
+
+/* ---- isolated operators (device pointers, on `stream`) -------------------- */
+
+/* Replaces decode::matvec for int8 matrices (src/kernels.cpp:107-120):
+ * y[r] = scales[r] * sum_j float(w[r][j]) * x[j]  (+ bias[r] when bias != NULL).
+ * w is row-major [rows][cols]; cols % 4 == 0. All pointers are device memory. */
+int dcb_gemv_i8(const int8_t* w, const float* scales, const float* bias, const float* x, float* y,
+                int rows, int cols, void* stream);
+
+/* Replaces decode::attention (src/kernels.cpp:150-179) for one query at
+ * position length-1 with the split-half RoPE of that position applied to q
+ * first when rope_theta > 0 (cached angle formula, src/model.cpp:222-224,271).
+ * keys/values: [length][kv_heads*dim] rows of kv_dtype; q_in, out: heads*dim
+ * FP32. Split-KV flash decoding with a log-sum-exp combine. Device pointers. */
+int dcb_attention(const float* q_in, const void* keys, const void* values, int kv_dtype, float* out,
+                  int length, int heads, int kv_heads, int dim, float rope_theta, void* stream);
+
+/* Replaces decode::rmsnorm (src/kernels.cpp:132-137) on device memory. */
+int dcb_rmsnorm(const float* x, const float* weight, float* out, int n, float epsilon, void* stream);
+
+/* Replaces decode::rope (src/kernels.cpp:138-149, direct != 0) and the cached
+ * rotation (src/model.cpp:269-297, direct == 0) in place on device memory. */
+int dcb_rope(float* x, int heads, int dim, int position, float theta, int direct, void* stream);
+
+/* Index of the first maximum of x[0..n) written to *out (device pointers),
+ * std::max_element semantics (src/main.cpp:35-37). */
+int dcb_argmax(const float* x, int n, int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
