@@ -229,7 +229,9 @@ def main() -> None:
     K, W = max(1, args.steps), max(3, args.warmup)
     capacity = CONTEXT + K + W + 2
     eng = dcb.Engine(model, capacity, device=local)
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the engine launches on it and the events are recorded on it.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
     prompt = prompt_tokens()
 
@@ -365,6 +367,7 @@ def long_context(dcb, model, d, K, W, device) -> dict:
     for kvt in ("f32", "f16"):
         eng = dcb.Engine(long_dir, ctx + K + W + 2, kv_dtype=kvt, device=device)
         stream = torch.cuda.current_stream()
+        assert stream.cuda_stream, "the engine must launch on the stream the events are recorded on"
         eng.set_stream(stream.cuda_stream)
         for l, (k, v) in enumerate(kv):
             eng.kv_write(l, 0, k, v)

@@ -33,7 +33,7 @@ EXPORTS = (
     "dcb_last_error", "dcb_set_error", "dcb_create", "dcb_create_from_dir", "dcb_destroy", "dcb_step",
     "dcb_step_async", "dcb_synchronize", "dcb_rewind", "dcb_reset", "dcb_position", "dcb_set_stream", "dcb_stream",
     "dcb_logits_device", "dcb_kv_write", "dcb_kv_read", "dcb_set_position", "dcb_launch_info", "dcb_launch_count",
-    "dcb_gemv_i8", "dcb_attention", "dcb_rmsnorm", "dcb_rope", "dcb_argmax",
+    "dcb_gemv_i8", "dcb_attention", "dcb_rmsnorm", "dcb_rope", "dcb_argmax", "dcb_trace_enable", "dcb_trace_read",
 )
 
 
@@ -83,6 +83,8 @@ def lib() -> C.CDLL:
     L.dcb_rmsnorm.argtypes = [vp, vp, vp, i32, C.c_float, vp]
     L.dcb_rope.argtypes = [vp, i32, i32, i32, C.c_float, i32, vp]
     L.dcb_argmax.argtypes = [vp, i32, vp, vp]
+    L.dcb_trace_enable.argtypes = [vp, i32]
+    L.dcb_trace_read.argtypes = [vp, vp, vp, C.POINTER(i32)]
     _LIB = L
     return L
 
@@ -167,6 +169,31 @@ class Engine:
         b, t, s, m = C.c_int(), C.c_int(), C.c_int(), C.c_int()
         _check(lib().dcb_launch_info(self._h, C.byref(b), C.byref(t), C.byref(s), C.byref(m)))
         return {"blocks": b.value, "threads": t.value, "smem_bytes": s.value, "sms": m.value}
+
+    def trace(self, on: bool = True) -> None:
+        _check(lib().dcb_trace_enable(self._h, int(bool(on))))
+
+    def trace_read(self) -> dict:
+        """Per-phase timing of the last step, in microseconds from the kernel
+        start: for each phase, when the last block finished it (`done`), and over
+        the blocks that had work in it, the mean and max of ready->done."""
+        blocks = self.launch_info()["blocks"]
+        n = C.c_int()
+        ready = np.zeros(512 * blocks, np.uint64)
+        done = np.zeros(512 * blocks, np.uint64)
+        _check(lib().dcb_trace_read(self._h, ready.ctypes.data, done.ctypes.data, C.byref(n)))
+        k = n.value
+        ready = ready[:k * blocks].reshape(k, blocks).astype(np.int64)
+        done = done[:k * blocks].reshape(k, blocks).astype(np.int64)
+        t0 = done[0].min()
+        last_done = (done.max(axis=1) - t0) / 1000.0
+        work = np.where(ready > 0, done - ready, 0) / 1000.0
+        busy = (ready > 0).sum(axis=1)
+        mean_work = np.where(busy > 0, work.sum(axis=1) / np.maximum(busy, 1), 0.0)
+        first_ready = np.where(busy > 0, (np.where(ready > 0, ready, np.iinfo(np.int64).max).min(axis=1) - t0) / 1000.0, 0.0)
+        last_ready = np.where(busy > 0, (ready.max(axis=1) - t0) / 1000.0, 0.0)
+        return {"phases": k, "done_us": last_done, "mean_work_us": mean_work, "max_work_us": work.max(axis=1),
+                "busy_blocks": busy, "first_ready_us": first_ready, "last_ready_us": last_ready}
 
     @property
     def launch_count(self) -> int:

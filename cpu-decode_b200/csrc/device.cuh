@@ -76,20 +76,26 @@ __device__ __forceinline__ float i8_lane(uint32_t biased, int k) {
     return __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7440u + (uint32_t)k)) - 8388736.0f;
 }
 
-// acc += dot(4 int8 in w, x) with the int8 widened exactly to FP32.
-__device__ __forceinline__ float dot4(uint32_t w, float4 x, float acc) {
+// acc += dot(4 int8 in w, x) with the int8 widened exactly to FP32, as two
+// packed FP32 lanes (Blackwell f32x2 add/fma: half the FP32 instructions).
+__device__ __forceinline__ float2 dot4(uint32_t w, float4 x, float2 acc) {
     const uint32_t u = w ^ 0x80808080u;
-    acc = fmaf(i8_lane(u, 0), x.x, acc);
-    acc = fmaf(i8_lane(u, 1), x.y, acc);
-    acc = fmaf(i8_lane(u, 2), x.z, acc);
-    acc = fmaf(i8_lane(u, 3), x.w, acc);
+    const float2 bias = make_float2(-8388736.0f, -8388736.0f);
+    float2 lo = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u)),
+                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441u)));
+    float2 hi = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442u)),
+                            __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443u)));
+    lo = __fadd2_rn(lo, bias);
+    hi = __fadd2_rn(hi, bias);
+    acc = __ffma2_rn(lo, make_float2(x.x, x.y), acc);
+    acc = __ffma2_rn(hi, make_float2(x.z, x.w), acc);
     return acc;
 }
 
 // An activation vector staged in shared memory for 16-byte weight chunks:
 // chunk c (weights 16c..16c+15) multiplies xs4[k*nch + c] for k = 0..3, so a
 // warp reading consecutive chunks reads consecutive float4s (no bank conflicts).
-__device__ __forceinline__ float dot16(int4 w, const float4* xs4, int nch, int c, float acc) {
+__device__ __forceinline__ float2 dot16(int4 w, const float4* xs4, int nch, int c, float2 acc) {
     acc = dot4((uint32_t)w.x, xs4[c], acc);
     acc = dot4((uint32_t)w.y, xs4[nch + c], acc);
     acc = dot4((uint32_t)w.z, xs4[2 * nch + c], acc);
@@ -118,9 +124,9 @@ __device__ __forceinline__ void rows_dot_unrolled(const int8_t* const (&rows)[R]
         for (int r = 0; r < R; ++r)
             w[r][c] = (ch < nch && rows[r]) ? ld_stream(rows[r] + (size_t)ch * 16) : make_int4(0, 0, 0, 0);
     }
-    float acc[R];
+    float2 acc[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int r = 0; r < R; ++r) acc[r] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < MAXC; ++c) {
         const int ch = lane + 32 * c;
@@ -130,16 +136,16 @@ __device__ __forceinline__ void rows_dot_unrolled(const int8_t* const (&rows)[R]
         }
     }
 #pragma unroll
-    for (int r = 0; r < R; ++r) out[r] = warp_sum(acc[r]);
+    for (int r = 0; r < R; ++r) out[r] = warp_sum(acc[r].x + acc[r].y);
 }
 
 // Same for long rows: loop over groups of U chunks per lane.
 template <int R, int U>
 __device__ __forceinline__ void rows_dot_loop(const int8_t* const (&rows)[R], const float4* xs4, int nch, int lane,
                                               float (&out)[R]) {
-    float acc[R];
+    float2 acc[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
+    for (int r = 0; r < R; ++r) acc[r] = make_float2(0.f, 0.f);
     for (int base = 0; base < nch; base += 32 * U) {
         int4 w[R][U];
 #pragma unroll
@@ -159,7 +165,7 @@ __device__ __forceinline__ void rows_dot_loop(const int8_t* const (&rows)[R], co
         }
     }
 #pragma unroll
-    for (int r = 0; r < R; ++r) out[r] = warp_sum(acc[r]);
+    for (int r = 0; r < R; ++r) out[r] = warp_sum(acc[r].x + acc[r].y);
 }
 
 __device__ __forceinline__ float kv_load(const float* p) { return __ldcg(p); }

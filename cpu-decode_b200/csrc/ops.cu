@@ -71,12 +71,12 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_i8_narrow_kernel(const int8
     const int r = blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5);
     if (r >= rows) return;
     const uint32_t* row = reinterpret_cast<const uint32_t*>(w + (size_t)r * cols);
-    float acc = 0.f;
+    float2 acc2 = make_float2(0.f, 0.f);
     for (int c = lane; c < cols / 4; c += 32) {
         const float4 xv = make_float4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
-        acc = dot4(__ldg(row + c), xv, acc);
+        acc2 = dot4(__ldg(row + c), xv, acc2);
     }
-    acc = warp_sum(acc);
+    const float acc = warp_sum(acc2.x + acc2.y);
     if (lane == 0) y[r] = acc * scales[r] + (bias ? bias[r] : 0.f);
 }
 

@@ -1,0 +1,1198 @@
+// The decode step as one persistent cooperative kernel (one block per SM).
+//
+// One launch runs the reference's Engine::Impl::step (src/model.cpp:258-329)
+// for one token: embedding, then per layer
+//   QKV  : RMSNorm prologue, Q/K/V int8 GEMV + bias + split-half RoPE, K/V row
+//          written to the cache at `pos`
+//   ATTN : GQA attention over positions 0..pos (one block per query head and
+//          KV split, log-sum-exp combine across splits)
+//   O    : O GEMV + residual
+//   GU   : RMSNorm prologue, gate/up GEMV, SiLU(gate)*up
+//   DOWN : down GEMV + residual
+// then the final RMSNorm, the tied LM head and the argmax.
+//
+// Data movement, B200-first:
+//  * Weights never wait on activations. Each block owns fixed row ranges of
+//    every projection; its rows (int8 + FP32 scale + bias, packed per row) are
+//    brought into shared memory by TMA bulk copies (cp.async.bulk + mbarrier)
+//    one layer ahead, so a GEMV phase only waits for its input vector.
+//  * No grid barriers. Activations travel between blocks as 64-bit words
+//    {value, tag}: a producer stores each element once with its tag, consumers
+//    poll exactly the elements they need until the tag of this step and layer
+//    shows. One L2 round trip per dependency; a stale value is never used.
+//  * The LM head (136 MB at the Qwen shape) streams through a 3-stage shared
+//    memory ring, loaded with an evict-first L2 policy.
+// Every wait is bounded in time; on expiry the block records an error, drains
+// its own copies in flight and returns.
+#pragma once
+#include "device.cuh"
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace dcb {
+
+constexpr int NT = 512;
+constexpr int NW = NT / 32;
+constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;  // one second
+constexpr int ERR_WAIT = 1;
+constexpr int ERR_TOKEN = 2;
+constexpr int ATT_CHUNK = 64;  // KV positions per staged chunk
+constexpr int ATT_PER_WARP = ATT_CHUNK / NW;
+constexpr int HEAD_ROWS = 2 * NW;  // LM-head rows per ring stage: two per warp
+constexpr int HEAD_MAX_STAGES = 8;  // LM-head ring stages (the host picks how many fit)
+constexpr int HEAD_L2_AHEAD = 12;   // LM-head chunks kept in flight into L2 beyond the ring
+constexpr int HEAD_MAXC = 2;        // 16-byte chunks per lane of a hidden-size row (hidden <= 1024)
+constexpr int TRACE_MAX_PHASES = 512;
+constexpr int MAXD = 4;        // head_dim <= 128: lane owns dims lane + 32k
+constexpr int DOWN_MAX_ROWS = 8;  // down rows per block (H <= 8 * grid)
+
+// Per-layer weights, packed rows: [K int8 | FP32 scale | FP32 bias | 8 pad].
+struct LayerW {
+    const uint8_t* qkv;   // 2*qkv_pairs rows (RoPE pairs (j, j+d/2) adjacent), stride SH
+    const uint8_t* o;     // H rows, stride SH
+    const uint8_t* gu;    // 2I rows (gate_j, up_j adjacent), stride SH
+    const uint8_t* down;  // H rows, stride SI
+};
+
+struct Sync {
+    unsigned amax_done;
+    int error;
+};
+
+struct ArgBest {
+    float v;
+    int i;
+};
+
+struct Params {
+    int H, I, L, NH, NKV, D, V, Kh, Ki, SH, SI, qkv_pairs;
+    float eps;
+    int cached_rope;
+    int capacity;
+    const LayerW* layers;
+    const uint8_t* embed;   // V packed rows, stride SH (the tied LM head)
+    const float* norms;     // [L+1][2][Kh]: (input, post-attention) RMSNorm gains per layer, then (final, 0)
+    const float* rope_inv;  // [D/2] 1/theta^(2j/D)  (cached angle formula)
+    const float* rope_den;  // [D/2] theta^(2j/D)    (direct angle formula)
+    void* kcache;           // [L][NKV][capacity][D], head-major
+    void* vcache;
+    uint64_t* ll_xa;    // [H]   residual stream entering a layer (and the head)
+    uint64_t* ll_xb;    // [H]   residual stream after attention
+    uint64_t* ll_q;     // [H]   rotated queries
+    uint64_t* ll_kv;    // [2*NKV*D] the new K and V rows
+    uint64_t* ll_attn;  // [H]   attention output
+    uint64_t* ll_h;     // [I]   SiLU(gate)*up
+    float* part;          // [NH][nsplit][D+2] attention split partials
+    unsigned* head_done;  // [NH] split arrival counters
+    float* logits;        // [V]
+    ArgBest* amax;        // [grid]
+    Sync* sync;
+    int* result;
+    uint64_t* trace;  // [2][TRACE_MAX_PHASES][grid] ready/done ns, or null
+    // shared memory layout (bytes)
+    int off_gu, off_down, off_qkv, off_o, off_att, off_xs, off_xq, off_gpart, off_xr, off_misc, off_norm;
+    int xq_plane;      // bytes per fixed-point plane of a hidden-sized vector (>= Kh)
+    int down_x_off;    // DOWN input staging inside the attention buffers: floats at off_att,
+    int down_plane;    // planes at off_att + down_x_off, down_plane bytes each (>= Ki)
+    int gpart_floats;  // floats per block-GEMV partial buffer (NW * max rows of a phase)
+    int att_chunk_bytes;
+    int head_stages;  // LM-head ring stages over [off_gu, off_xs)
+    int trace_layer;  // layer whose phases get detailed marks when tracing
+};
+
+struct StepArgs {
+    int token;
+    const int* token_dev;
+    int pos;
+    int head;
+    int* argmax_dev;
+    int nsplit;
+    int split_len;
+    unsigned seq;
+};
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+__device__ __forceinline__ int part_lo(int b, int G, int n) { return (int)((long long)b * n / G); }
+
+// ---- mbarrier + bulk copy ------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* m, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(m)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* m) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(m)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint64_t* m, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* m, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(m)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(m))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* m,
+                                               uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(m)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// Shared memory read by threads (generic proxy) before the TMA (async proxy) rewrites it.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// One thread: fill a shared slot with `bytes` (16-byte aligned, multiple of 16).
+// `*fills` counts the fills issued on `m` (used to drain them on abort).
+__device__ __forceinline__ void fill_slot(void* dst, const void* src, uint32_t bytes, uint64_t* m, unsigned* fills,
+                                          uint64_t policy = 0) {
+    ++*fills;
+    mbar_expect(m, bytes);
+    constexpr uint32_t piece = 32768;
+    for (uint32_t o = 0; o < bytes; o += piece) {
+        const uint32_t n = bytes - o < piece ? bytes - o : piece;
+        if (policy)
+            bulk_load_hint(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, n, m, policy);
+        else
+            bulk_load(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, n, m);
+    }
+}
+
+// ---- tagged activation words -----------------------------------------------------
+__device__ __forceinline__ void ll_store(uint64_t* p, float v, uint32_t tag) {
+    const uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ll_load(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+struct BlockState {
+    int* abort;  // shared flag
+    Sync* sync;
+};
+
+__device__ __forceinline__ bool should_abort(const BlockState& st) {
+    return *reinterpret_cast<volatile int*>(st.abort) != 0;
+}
+__device__ __forceinline__ void raise_abort(const BlockState& st, int code) {
+    atomicCAS(&st.sync->error, 0, code);
+    *reinterpret_cast<volatile int*>(st.abort) = 1;
+}
+// Periodic check inside a wait loop: true when the wait must end.
+__device__ __forceinline__ bool wait_expired(const BlockState& st, uint64_t& t0) {
+    if (should_abort(st) || ld_volatile(&st.sync->error)) {
+        *reinterpret_cast<volatile int*>(st.abort) = 1;
+        return true;
+    }
+    const uint64_t now = globaltimer();
+    if (!t0) {
+        t0 = now;
+    } else if (now - t0 > WAIT_LIMIT_NS) {
+        raise_abort(st, ERR_WAIT);
+        return true;
+    }
+    return false;
+}
+
+// Wait (all threads) until mbarrier `m` completes phase `parity`. Bounded.
+// Ends with __syncthreads so that every thread takes the same decision.
+__device__ bool mbar_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
+    uint64_t t0 = 0;
+    unsigned spins = 0;
+    while (!mbar_test(m, parity))
+        if ((++spins & 63u) == 0 && wait_expired(st, t0)) break;
+    __syncthreads();
+    return !should_abort(st);
+}
+
+// ---- staged activation vectors and the block GEMV ----------------------------------
+// A GEMV input is staged once per phase as 24-bit fixed point: with
+// scale = max|v| / 8323072, q_j = rint(v_j / scale) = hi*2^16 + mid*2^8 + lo
+// with hi, mid, lo signed bytes, kept as three byte planes (16*nch bytes each),
+// so that 4 int8 weights times 4 activations are three exact dp4a operations
+// (6 issue cycles per 4 weights on sm_100 against about 17 for widening each
+// byte to FP32). The quantisation error is below 2^-23 * max|v| per element,
+// the order of the FP32 rounding in the reference's own sums.
+constexpr float FIX_MAX = 8323072.0f;  // 2^23 - 2^16: keeps hi within [-127, 127]
+
+// Element j arrived with value v: raw to xr (when set), v * gain[j] (the RMSNorm
+// gain folded in; v when gain is null) to xf.
+__device__ __forceinline__ void accept(int j, float v, float* xr, float* xf, const float* gain, float& ss,
+                                       float& mx) {
+    if (xr) xr[j] = v;
+    const float g = gain ? v * gain[j] : v;
+    xf[j] = g;
+    ss = fmaf(v, v, ss);
+    mx = fmaxf(mx, fabsf(g));
+}
+
+struct Staged {
+    float scale;  // value of one unit of q
+    float inv;    // RMSNorm factor 1/sqrt(mean(v^2) + eps) of the raw values (src/kernels.cpp:132-137)
+};
+
+// All elements accepted: reduce (sum v^2, max |v*gain|) and quantise xf into
+// the planes (padding n..16*nch as zeros). Two barriers.
+__device__ Staged finish_stage(int n, int nch, const float* xf, int8_t* xq, int plane, float ss, float mx, float* red,
+                               float eps) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(FULL, ss, o);
+        mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        red[threadIdx.x >> 5] = ss;
+        red[NW + (threadIdx.x >> 5)] = mx;
+    }
+    __syncthreads();
+    float t = 0.f, m = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; w += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(red + w);
+        const float4 b = *reinterpret_cast<const float4*>(red + NW + w);
+        t += (a.x + a.y) + (a.z + a.w);
+        m = fmaxf(fmaxf(m, fmaxf(b.x, b.y)), fmaxf(b.z, b.w));
+    }
+    Staged out;
+    out.inv = __frsqrt_rn(t / (float)n + eps);
+    const float rs = m > 0.f ? FIX_MAX * __frcp_rn(m) : 0.f;
+    out.scale = m > 0.f ? __frcp_rn(rs) : 1.0f;
+    for (int quad = threadIdx.x; quad < nch * 4; quad += NT) {
+        uint32_t ph = 0, pm = 0, pl = 0;
+        const float4 v4 = 4 * quad + 3 < n ? *reinterpret_cast<const float4*>(xf + 4 * quad)
+                                           : make_float4(4 * quad < n ? xf[4 * quad] : 0.f,
+                                                         4 * quad + 1 < n ? xf[4 * quad + 1] : 0.f,
+                                                         4 * quad + 2 < n ? xf[4 * quad + 2] : 0.f, 0.f);
+        const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int q = __float2int_rn(vv[e] * rs);
+            const int lo = (int)(int8_t)(q & 0xff);
+            const int q1 = (q - lo) >> 8;
+            const int md = (int)(int8_t)(q1 & 0xff);
+            const int hi = (q1 - md) >> 8;
+            ph |= (uint32_t)(hi & 0xff) << (8 * e);
+            pm |= (uint32_t)(md & 0xff) << (8 * e);
+            pl |= (uint32_t)(lo & 0xff) << (8 * e);
+        }
+        reinterpret_cast<uint32_t*>(xq)[quad] = ph;
+        reinterpret_cast<uint32_t*>(xq + plane)[quad] = pm;
+        reinterpret_cast<uint32_t*>(xq + 2 * plane)[quad] = pl;
+    }
+    __syncthreads();
+    return out;
+}
+
+// One warp waits for phase `parity` of `m` (no block barrier). Bounded.
+__device__ bool mbar_wait_warp(uint64_t* m, uint32_t parity, const BlockState& st) {
+    uint64_t t0 = 0;
+    unsigned spins = 0;
+    bool done = false;
+    while (!(done = mbar_test(m, parity)))
+        if ((++spins & 63u) == 0 && wait_expired(st, t0)) break;
+    return __all_sync(FULL, done) != 0;
+}
+// A single thread waits for phase `parity` of `m`. Bounded.
+__device__ bool mbar_wait_one(uint64_t* m, uint32_t parity, const BlockState& st) {
+    uint64_t t0 = 0;
+    unsigned spins = 0;
+    while (!mbar_test(m, parity))
+        if ((++spins & 63u) == 0 && wait_expired(st, t0)) return false;
+    return true;
+}
+
+// Block-cooperative: wait until the n tagged words at src carry `tag`, accept
+// them and stage the vector. Words are polled in groups of W per thread, all
+// loads of a group in flight together. Returns false when the step must abort.
+template <int W>
+__device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr, float* xf, int8_t* xq, int plane,
+                             int nch, const float* gain, float* red, float eps, Staged& out, const BlockState& st) {
+    uint64_t t0 = 0;
+    unsigned rounds = 0;
+    float ss = 0.f, mx = 0.f;
+    for (int base = 0; base < n; base += W * NT) {
+        uint64_t w[W];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const int j = base + threadIdx.x + k * NT;
+            if (j < n) {
+                w[k] = ll_load(src + j);
+                pending |= 1u << k;
+            }
+        }
+        while (true) {
+#pragma unroll
+            for (int k = 0; k < W; ++k) {
+                if ((pending >> k) & 1u) {
+                    if ((uint32_t)(w[k] >> 32) == tag) {
+                        accept(base + threadIdx.x + k * NT, __uint_as_float((uint32_t)w[k]), xr, xf, gain, ss, mx);
+                        pending &= ~(1u << k);
+                    }
+                }
+            }
+            if (!pending) break;
+            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+#pragma unroll
+            for (int k = 0; k < W; ++k)
+                if ((pending >> k) & 1u) w[k] = ll_load(src + base + threadIdx.x + k * NT);
+        }
+        if (should_abort(st)) break;
+    }
+    out = finish_stage(n, nch, xf, xq, plane, ss, mx, red, eps);
+    return !should_abort(st);
+}
+
+// 16 int8 weights times 16 staged activations, exact in three int32 planes.
+__device__ __forceinline__ void dp4a16(const int4& w, const int4& h, const int4& m, const int4& l, int& ah, int& am,
+                                       int& al) {
+    ah = __dp4a(w.x, h.x, ah);
+    am = __dp4a(w.x, m.x, am);
+    al = __dp4a(w.x, l.x, al);
+    ah = __dp4a(w.y, h.y, ah);
+    am = __dp4a(w.y, m.y, am);
+    al = __dp4a(w.y, l.y, al);
+    ah = __dp4a(w.z, h.z, ah);
+    am = __dp4a(w.z, m.z, am);
+    al = __dp4a(w.z, l.z, al);
+    ah = __dp4a(w.w, h.w, ah);
+    am = __dp4a(w.w, m.w, am);
+    al = __dp4a(w.w, l.w, al);
+}
+// sum_j w_j q_j from the three plane sums (each exact; one rounding per step).
+__device__ __forceinline__ float planes_to_float(int ah, int am, int al) {
+    return fmaf(65536.0f, (float)ah, fmaf(256.0f, (float)am, (float)al));
+}
+__device__ __forceinline__ void load_planes(const int8_t* xq, int plane, int c, int4& h, int4& m, int4& l) {
+    h = reinterpret_cast<const int4*>(xq)[c];
+    m = reinterpret_cast<const int4*>(xq + plane)[c];
+    l = reinterpret_cast<const int4*>(xq + 2 * plane)[c];
+}
+
+// Partial dot products sum_j w_rj q_j of R packed rows in shared memory (stride
+// S bytes, nch chunks of 16 int8 each) with the staged vector. Warp w covers
+// chunks [w*nch/NW, (w+1)*nch/NW); in a warp, LPR consecutive lanes share a row
+// slot and split its chunks, and each lane keeps up to P rows (slot,
+// slot + 32/LPR, ...) in flight with independent accumulators, reusing each
+// activation chunk for all of them. No per-row warp reduction: partial[w*R + r]
+// is written and the caller sums over w after the closing barrier (and scales
+// by Staged::scale). Rows are 912 or 4880 bytes apart, so the lanes' 16-byte
+// reads of different rows fall in distinct banks.
+template <int LPR, int P>
+__device__ void block_gemv(const uint8_t* rows, int S, int R, int nch, const int8_t* xq, int plane, float* partial) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = warp * nch / NW, c1 = (warp + 1) * nch / NW;
+    const int sub = lane % LPR, slot = lane / LPR;
+    constexpr int RPP = 32 / LPR;
+    for (int r0 = 0; r0 < R; r0 += RPP * P) {
+        int ah[P], am[P], al[P];
+#pragma unroll
+        for (int p = 0; p < P; ++p) ah[p] = am[p] = al[p] = 0;
+        for (int c = c0 + sub; c < c1; c += LPR) {
+            int4 h, m, l;
+            load_planes(xq, plane, c, h, m, l);
+#pragma unroll
+            for (int p = 0; p < P; ++p) {
+                const int r = r0 + p * RPP + slot;
+                if (r < R)
+                    dp4a16(*reinterpret_cast<const int4*>(rows + (size_t)r * S + (size_t)c * 16), h, m, l, ah[p], am[p],
+                           al[p]);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            const int r = r0 + p * RPP + slot;
+            float t = planes_to_float(ah[p], am[p], al[p]);
+#pragma unroll
+            for (int o = LPR / 2; o > 0; o >>= 1) t += __shfl_xor_sync(FULL, t, o);
+            if (sub == 0 && r < R) partial[warp * R + r] = t;
+        }
+    }
+    __syncthreads();
+}
+
+// Sum of row r's partials over the warps.
+__device__ __forceinline__ float gemv_row(const float* partial, int R, int r) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) s += partial[w * R + r];
+    return s;
+}
+
+__device__ __forceinline__ float row_scale(const uint8_t* row, int K) {
+    return *reinterpret_cast<const float*>(row + K);
+}
+__device__ __forceinline__ float row_bias(const uint8_t* row, int K) {
+    return *reinterpret_cast<const float*>(row + K + 4);
+}
+
+__device__ __forceinline__ void trace_mark(const Params& P, int which, int phase) {
+    if (P.trace && threadIdx.x == 0)
+        P.trace[((size_t)which * TRACE_MAX_PHASES + phase) * gridDim.x + blockIdx.x] = globaltimer();
+}
+// SM clock counter next to the kernel start (which = 0) and end (1) marks:
+// rows 500 + which of the done record, so a trace also yields the SM clock rate.
+__device__ __forceinline__ void trace_clock(const Params& P, int which) {
+    if (P.trace && threadIdx.x == 0)
+        P.trace[((size_t)TRACE_MAX_PHASES + 500 + which) * gridDim.x + blockIdx.x] = clock64();
+}
+// Detailed marks inside phase k (0..4, or 5 for the LM head) of the traced
+// layer: slot TRACE_DETAIL + 8k + m of the ready record.
+constexpr int TRACE_DETAIL = 400;
+__device__ __forceinline__ void trace_detail(const Params& P, int layer, int k, int m) {
+    if (P.trace && layer == P.trace_layer && threadIdx.x == 0)
+        P.trace[((size_t)TRACE_DETAIL + 8 * k + m) * gridDim.x + blockIdx.x] = globaltimer();
+}
+
+__device__ __forceinline__ float kv_to_float(float v) { return v; }
+__device__ __forceinline__ float kv_to_float(__half v) { return __half2float(v); }
+__device__ __forceinline__ float round_to(float v, float) { return v; }
+__device__ __forceinline__ float round_to(float v, __half) { return __half2float(__float2half_rn(v)); }
+
+__device__ __forceinline__ void load4(const float* p, float (&out)[4]) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    out[0] = v.x;
+    out[1] = v.y;
+    out[2] = v.z;
+    out[3] = v.w;
+}
+__device__ __forceinline__ void load4(const __half* p, float (&out)[4]) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    out[0] = a.x;
+    out[1] = a.y;
+    out[2] = b.x;
+    out[3] = b.y;
+}
+
+// ---- attention unit: query head h over positions [t0, t1) --------------------------
+struct AttnPlan {
+    int h, g, t0, t1, nchunks;
+    bool bulk;  // rows are multiples of 16 bytes: TMA bulk copies, else plain loads
+};
+
+template <typename KV>
+__device__ __forceinline__ const KV* kv_rows(const Params& P, const void* base, int l, int g, int t) {
+    return static_cast<const KV*>(base) + (((size_t)l * P.NKV + g) * P.capacity + t) * P.D;
+}
+
+// Thread 0: copy the cached rows (positions below pos) of chunk c into buffer c%2.
+template <typename KV>
+__device__ void att_issue(const Params& P, const StepArgs& A, const AttnPlan& ap, int l, int c, uint8_t* att,
+                          uint64_t* mb_att, unsigned* fills) {
+    const int c0 = ap.t0 + c * ATT_CHUNK;
+    const int cend = min(min(ap.t1, c0 + ATT_CHUNK), A.pos);
+    if (cend <= c0 || !ap.bulk) return;
+    const uint32_t rows = (uint32_t)(cend - c0), rb = (uint32_t)(P.D * sizeof(KV));
+    KV* kdst = reinterpret_cast<KV*>(att + (size_t)(c & 1) * P.att_chunk_bytes);
+    KV* vdst = kdst + (size_t)ATT_CHUNK * P.D;
+    ++fills[c & 1];
+    mbar_expect(mb_att + (c & 1), 2 * rows * rb);
+    bulk_load(kdst, kv_rows<KV>(P, P.kcache, l, ap.g, c0), rows * rb, mb_att + (c & 1));
+    bulk_load(vdst, kv_rows<KV>(P, P.vcache, l, ap.g, c0), rows * rb, mb_att + (c & 1));
+}
+
+template <typename KV>
+__device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPlan& ap, int l, uint32_t tag,
+                                uint8_t* att, uint64_t* mb_att, unsigned (&att_fills)[2], unsigned* issued,
+                                float* misc, const BlockState& st) {
+    const int D = P.D, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int kvd = P.NKV * D;
+    float* sq = misc;                      // [D]
+    float* sk_new = misc + 128;            // [2][D] new K and V rows of group g
+    float* wpart = misc + 384;             // [NW][D+2]
+    __shared__ int s_last;
+    const bool has_new = ap.t0 <= A.pos && A.pos < ap.t1;
+    trace_detail(P, l, 1, 0);
+    {
+        // One round trip for the query and, where needed, the new K/V row:
+        // thread t < D polls q[t], D <= t < 3D the new K then V rows.
+        const int t = threadIdx.x, nwords = has_new ? 3 * D : D;
+        if (t < nwords) {
+            const uint64_t* src = t < D ? P.ll_q + (size_t)ap.h * D + t
+                                        : P.ll_kv + (t < 2 * D ? 0 : kvd) + (size_t)ap.g * D + (t % D);
+            float* dst = t < D ? sq + t : sk_new + (t - D);
+            uint64_t t0 = 0;
+            unsigned rounds = 0;
+            uint64_t w = ll_load(src);
+            while ((uint32_t)(w >> 32) != tag) {
+                if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+                w = ll_load(src);
+            }
+            *dst = __uint_as_float((uint32_t)w);
+        }
+        __syncthreads();
+        if (should_abort(st)) return false;
+    }
+    trace_detail(P, l, 1, 1);
+    const float scale = 1.0f / sqrtf((float)D);
+    // Scores: the 8 lanes of group `grp` take position warp*4+grp of a chunk;
+    // lane part p owns dims 32k + 4p + e (e < 4), read as one 16-byte vector.
+    const int grp = lane >> 3, part = lane & 7;
+    float qv[MAXD][4];
+#pragma unroll
+    for (int k = 0; k < MAXD; ++k)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int j = 32 * k + 4 * part + e;
+            qv[k][e] = j < D ? sq[j] : 0.f;
+        }
+    float m_run = -INFINITY, l_run = 0.f, o[MAXD];
+#pragma unroll
+    for (int k = 0; k < MAXD; ++k) o[k] = 0.f;
+
+    for (int c = 0; c < ap.nchunks; ++c) {
+        const int c0 = ap.t0 + c * ATT_CHUNK;
+        const int n = min(ATT_CHUNK, ap.t1 - c0);
+        const int ncache = max(0, min(n, A.pos - c0));
+        KV* kb = reinterpret_cast<KV*>(att + (size_t)(c & 1) * P.att_chunk_bytes);
+        KV* vb = kb + (size_t)ATT_CHUNK * D;
+        if (ap.bulk) {
+            if (ncache > 0) {
+                if (!mbar_wait(mb_att + (c & 1), att_fills[c & 1] & 1u, st)) return false;
+                ++att_fills[c & 1];
+                trace_detail(P, l, 1, c == 0 ? 2 : 4);
+            }
+        } else {
+            for (int e = threadIdx.x; e < ncache * D; e += NT) {
+                const int t = e / D, j = e % D;
+                kb[(size_t)t * D + j] = *(kv_rows<KV>(P, P.kcache, l, ap.g, c0 + t) + j);
+                vb[(size_t)t * D + j] = *(kv_rows<KV>(P, P.vcache, l, ap.g, c0 + t) + j);
+            }
+        }
+        if (has_new && A.pos >= c0 && A.pos < c0 + n) {
+            const int t = A.pos - c0;
+            for (int j = threadIdx.x; j < D; j += NT) {
+                kv_store(kb + (size_t)t * D + j, sk_new[j]);
+                kv_store(vb + (size_t)t * D + j, sk_new[D + j]);
+            }
+        }
+        __syncthreads();
+        const int t = warp * ATT_PER_WARP + grp;
+        float sc = 0.f;
+        if (t < n) {
+            const KV* kr = kb + (size_t)t * D;
+#pragma unroll
+            for (int k = 0; k < MAXD; ++k) {
+                const int j0 = 32 * k + 4 * part;
+                if (j0 + 3 < D && (D & 3) == 0) {
+                    float kk[4];
+                    load4(kr + j0, kk);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sc = fmaf(qv[k][e], kk[e], sc);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (j0 + e < D) sc = fmaf(qv[k][e], kv_to_float(kr[j0 + e]), sc);
+                }
+            }
+        }
+        sc += __shfl_xor_sync(FULL, sc, 4);
+        sc += __shfl_xor_sync(FULL, sc, 2);
+        sc += __shfl_xor_sync(FULL, sc, 1);
+        sc = t < n ? sc * scale : -INFINITY;
+        float cmax = fmaxf(sc, __shfl_xor_sync(FULL, sc, 8));
+        cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, 16));
+        if (cmax > -INFINITY) {
+            const float m_new = fmaxf(m_run, cmax);
+            const float alpha = expf(m_run - m_new);
+            const float p = t < n ? expf(sc - m_new) : 0.f;
+            float psum = p + __shfl_xor_sync(FULL, p, 8);
+            psum += __shfl_xor_sync(FULL, psum, 16);
+            l_run = l_run * alpha + psum;
+#pragma unroll
+            for (int k = 0; k < MAXD; ++k) o[k] *= alpha;
+#pragma unroll
+            for (int i = 0; i < ATT_PER_WARP; ++i) {
+                const float pi = __shfl_sync(FULL, p, 8 * i);
+                const int ti = warp * ATT_PER_WARP + i;
+                if (ti < n) {
+#pragma unroll
+                    for (int k = 0; k < MAXD; ++k)
+                        if (lane + 32 * k < D) o[k] = fmaf(pi, kv_to_float(vb[(size_t)ti * D + lane + 32 * k]), o[k]);
+                }
+            }
+            m_run = m_new;
+        }
+        __syncthreads();  // buffer c&1 consumed
+        trace_detail(P, l, 1, c == 0 ? 3 : 5);
+        if (threadIdx.x == 0 && c + 2 < ap.nchunks) {
+            fence_proxy_async();
+            att_issue<KV>(P, A, ap, l, c + 2, att, mb_att, issued);
+        }
+    }
+    // Merge the warps' softmax states.
+    if (lane == 0) {
+        wpart[warp * (D + 2)] = m_run;
+        wpart[warp * (D + 2) + 1] = l_run;
+    }
+#pragma unroll
+    for (int k = 0; k < MAXD; ++k)
+        if (lane + 32 * k < D) wpart[warp * (D + 2) + 2 + lane + 32 * k] = o[k];
+    __syncthreads();
+    // Thread j < D merges dimension j over the warps (all threads compute M, L).
+    if (threadIdx.x < D) {
+        const int j = threadIdx.x;
+        float mw[NW];
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            mw[w] = wpart[w * (D + 2)];
+            M = fmaxf(M, mw[w]);
+        }
+        float Lsum = 0.f, acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float f = mw[w] == -INFINITY ? 0.f : expf(mw[w] - M);
+            Lsum = fmaf(f, wpart[w * (D + 2) + 1], Lsum);
+            acc = fmaf(f, wpart[w * (D + 2) + 2 + j], acc);
+        }
+        if (A.nsplit == 1) {
+            ll_store(P.ll_attn + (size_t)ap.h * D + j, acc / Lsum, tag);
+        } else {
+            float* pp = P.part + ((size_t)ap.h * A.nsplit + blockIdx.x % A.nsplit) * (D + 2);
+            if (j == 0) {
+                pp[0] = M;
+                pp[1] = Lsum;
+            }
+            pp[2 + j] = acc;
+        }
+    }
+    trace_detail(P, l, 1, 6);
+    if (A.nsplit == 1) return true;
+    // The last split of head h to finish merges all of them.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(P.head_done + ap.h, 1u);
+        s_last = prev == (unsigned)A.nsplit - 1;
+        if (s_last) __threadfence();
+    }
+    __syncthreads();
+    if (s_last && warp == 0) {
+        const float* base = P.part + (size_t)ap.h * A.nsplit * (D + 2);
+        float M = -INFINITY;
+        for (int i = lane; i < A.nsplit; i += 32) M = fmaxf(M, __ldcg(base + (size_t)i * (D + 2)));
+        M = warp_max(M);
+        float Lsum = 0.f;
+        for (int i = lane; i < A.nsplit; i += 32)
+            Lsum += expf(__ldcg(base + (size_t)i * (D + 2)) - M) * __ldcg(base + (size_t)i * (D + 2) + 1);
+        Lsum = warp_sum(Lsum);
+        const float inv = 1.0f / Lsum;
+        for (int j = lane; j < D; j += 32) {
+            float acc = 0.f;
+            for (int i = 0; i < A.nsplit; ++i) {
+                const float* pp = base + (size_t)i * (D + 2);
+                acc = fmaf(expf(__ldcg(pp) - M), __ldcg(pp + 2 + j), acc);
+            }
+            ll_store(P.ll_attn + (size_t)ap.h * D + j, acc * inv, tag);
+        }
+        if (lane == 0) P.head_done[ap.h] = 0;
+    }
+    return true;
+}
+
+template <typename KV>
+__global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, const StepArgs A) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint8_t* s_gu = sm + P.off_gu;
+    uint8_t* s_down = sm + P.off_down;
+    uint8_t* s_qkv = sm + P.off_qkv;
+    uint8_t* s_o = sm + P.off_o;
+    uint8_t* s_att = sm + P.off_att;
+    float* xf = reinterpret_cast<float*>(sm + P.off_xs);       // staged values before quantisation
+    int8_t* xq = reinterpret_cast<int8_t*>(sm + P.off_xq);     // fixed-point planes of the staged vector
+    const int QP = P.xq_plane;
+    // DOWN's input (intermediate-sized) is staged in the attention buffers, which
+    // hold no copies between the end of this layer's attention and the next
+    // layer's prefetch (issued after a block barrier and a proxy fence).
+    float* xf_i = reinterpret_cast<float*>(sm + P.off_att);
+    int8_t* xq_i = reinterpret_cast<int8_t*>(sm + P.off_att + P.down_x_off);
+    float* gpart = reinterpret_cast<float*>(sm + P.off_gpart);  // block-GEMV partial sums, two buffers
+    float* xr = reinterpret_cast<float*>(sm + P.off_xr);
+    float* misc = reinterpret_cast<float*>(sm + P.off_misc);
+    constexpr int NMB = 4 + HEAD_MAX_STAGES + 2 + 2 + HEAD_MAX_STAGES;
+    __shared__ __align__(8) uint64_t mb[NMB];
+    uint64_t* mb_gu = mb + 0;
+    uint64_t* mb_down = mb + 1;
+    uint64_t* mb_qkv = mb + 2;
+    uint64_t* mb_o = mb + 3;
+    uint64_t* mb_head = mb + 4;
+    uint64_t* mb_att = mb + 4 + HEAD_MAX_STAGES;
+    uint64_t* mb_norm = mb + 4 + HEAD_MAX_STAGES + 2;
+    uint64_t* mb_head_empty = mb + 4 + HEAD_MAX_STAGES + 4;  // NW arrivals each
+    float* s_norms = reinterpret_cast<float*>(sm + P.off_norm);  // [2 buffers][2][Kh]
+    __shared__ float s_cos[64], s_sin[64];
+    __shared__ float red[2 * NW + 8];
+    __shared__ int s_abort;
+    __shared__ unsigned s_fills[NMB];  // fills issued per mbarrier (thread 0)
+
+    const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int H = P.H, I = P.I, D = P.D, half = D / 2, kvd = P.NKV * D;
+    const int nch_h = P.Kh / 16, nch_i = P.Ki / 16;
+    const BlockState st{&s_abort, P.sync};
+
+    // This block's rows in every phase.
+    const int qa = part_lo(b, G, P.qkv_pairs), qn = part_lo(b + 1, G, P.qkv_pairs) - qa;
+    const int oa = part_lo(b, G, H), on = part_lo(b + 1, G, H) - oa;
+    const int ga = part_lo(b, G, I), gn = part_lo(b + 1, G, I) - ga;
+    const int da = part_lo(b, G, H), dn = part_lo(b + 1, G, H) - da;
+    const int ha = part_lo(b, G, P.V), hn = part_lo(b + 1, G, P.V) - ha;
+    const int head_chunks = A.head ? (hn + HEAD_ROWS - 1) / HEAD_ROWS : 0;
+    const uint32_t head_stage_bytes = (uint32_t)HEAD_ROWS * P.SH;
+
+    // This block's attention unit (at most one).
+    AttnPlan ap{};
+    const bool has_att = b < P.NH * A.nsplit;
+    if (has_att) {
+        ap.h = b / A.nsplit;
+        ap.g = ap.h / (P.NH / P.NKV);
+        ap.t0 = (b % A.nsplit) * A.split_len;
+        ap.t1 = min(A.pos + 1, ap.t0 + A.split_len);
+        ap.nchunks = (ap.t1 - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK;
+        ap.bulk = ((size_t)D * sizeof(KV)) % 16 == 0;
+    }
+    unsigned att_fills[2] = {0u, 0u};
+    uint64_t head_policy = 0;
+    int head_issued = 0;
+
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < NMB; ++i) {
+            mbar_init(mb + i, i >= 4 + HEAD_MAX_STAGES + 4 ? NW : 1);
+            s_fills[i] = 0;
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        head_policy = evict_first_policy();
+        const LayerW& W = P.layers[0];
+        if (qn) fill_slot(s_qkv, W.qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH, mb_qkv, s_fills + 2);
+        if (on) fill_slot(s_o, W.o + (size_t)oa * P.SH, (uint32_t)on * P.SH, mb_o, s_fills + 3);
+        if (gn) fill_slot(s_gu, W.gu + (size_t)ga * 2 * P.SH, (uint32_t)gn * 2 * P.SH, mb_gu, s_fills + 0);
+        if (dn) fill_slot(s_down, W.down + (size_t)da * P.SI, (uint32_t)dn * P.SI, mb_down, s_fills + 1);
+        // RMSNorm gains of layers 0 and 1 (entry L holds the final norm).
+        for (int e = 0; e < 2 && e <= P.L; ++e)
+            fill_slot(s_norms + (size_t)e * 2 * P.Kh, P.norms + (size_t)e * 2 * P.Kh, (uint32_t)(2 * P.Kh * 4),
+                      mb_norm + e, s_fills + NMB - 2 + e);
+    }
+    // RoPE cos/sin of this position, once per step (src/model.cpp:269-274).
+    if (tid < half) {
+        const float angle = P.cached_rope ? __fmul_rn((float)A.pos, P.rope_inv[tid]) : __fdiv_rn((float)A.pos, P.rope_den[tid]);
+        sincosf(angle, &s_sin[tid], &s_cos[tid]);
+    }
+    __syncthreads();
+    trace_mark(P, 0, 0);
+    trace_mark(P, 1, 0);
+    trace_clock(P, 0);
+
+    // Thread 0: LM-head chunk c into ring stage c % head_stages.
+    const int NS = P.head_stages;
+    auto prefetch_head = [&](int c) {  // thread 0: LM-head chunk c into L2 only
+        if (c >= head_chunks) return;
+        const int r0 = ha + c * HEAD_ROWS, rows = min(HEAD_ROWS, ha + hn - r0);
+        prefetch_l2(P.embed + (size_t)r0 * P.SH, (uint32_t)rows * P.SH);
+    };
+    auto fill_head = [&](int c) {
+        const int r0 = ha + c * HEAD_ROWS, rows = min(HEAD_ROWS, ha + hn - r0);
+        fill_slot(sm + P.off_gu + (size_t)(c % NS) * head_stage_bytes, P.embed + (size_t)r0 * P.SH,
+                  (uint32_t)rows * P.SH, mb_head + c % NS, s_fills + 4 + c % NS, head_policy);
+    };
+
+    int token = A.token_dev ? __ldcg(A.token_dev) : A.token;
+    if ((unsigned)token >= (unsigned)P.V) {  // a device-supplied token out of range
+        if (tid == 0) atomicCAS(&P.sync->error, 0, ERR_TOKEN);
+        token = 0;
+    }
+    const uint32_t seq_tag = A.seq << 8;  // tag of layer l's outputs: seq_tag | (l + 1)
+    bool ok = true;
+    KV* const kc = static_cast<KV*>(P.kcache);
+    KV* const vc = static_cast<KV*>(P.vcache);
+
+    for (int l = 0; l < P.L; ++l) {
+        const LayerW& W = P.layers[l];
+        const uint32_t tag = seq_tag | (uint32_t)(l + 1);
+        const int ph = 5 * l;
+
+        // RMSNorm gains of layer l+1 into the buffer layer l-1 used.
+        if (tid == 0 && l >= 1 && l + 1 <= P.L) {
+            const int e = l + 1;
+            fence_proxy_async();
+            fill_slot(s_norms + (size_t)(e & 1) * 2 * P.Kh, P.norms + (size_t)e * 2 * P.Kh, (uint32_t)(2 * P.Kh * 4),
+                      mb_norm + (e & 1), s_fills + NMB - 2 + (e & 1));
+        }
+        const float* in_norm = s_norms + (size_t)(l & 1) * 2 * P.Kh;
+        const float* post_norm = in_norm + P.Kh;
+        const uint32_t norm_parity = (uint32_t)(l >> 1) & 1u;
+
+        // HBM has slack during the last layer: start the LM-head rows into L2.
+        if (tid == 0 && A.head && l == P.L - 1)
+            for (int c = NS; c < NS + HEAD_L2_AHEAD; ++c) prefetch_head(c);
+
+        // The cached KV rows do not depend on this step: start their copies now.
+        if (has_att && tid == 0) {
+            fence_proxy_async();  // the previous layer read and wrote these buffers
+            for (int c = 0; c < min(2, ap.nchunks); ++c)
+                att_issue<KV>(P, A, ap, l, c, s_att, mb_att, s_fills + 4 + HEAD_MAX_STAGES);
+        }
+
+        // ---- QKV (src/model.cpp:276-302); x entering layer l carries `tag`.
+        trace_detail(P, l, 0, 0);
+        if (qn || on) {
+            // x with the input RMSNorm gain folded in; 1/rms scales the results.
+            if (qn && !mbar_wait(mb_norm + (l & 1), norm_parity, st)) { ok = false; break; }
+            Staged sx;
+            if (l == 0) {
+                const uint8_t* er = P.embed + (size_t)token * P.SH;
+                const float es = row_scale(er, P.Kh);
+                float ss = 0.f, mx = 0.f;
+                for (int j = tid; j < H; j += NT) accept(j, (float)(int8_t)er[j] * es, xr, xf, in_norm, ss, mx);
+                sx = finish_stage(H, nch_h, xf, xq, QP, ss, mx, red, P.eps);
+            } else if (!gather_stage<2>(P.ll_xa, H, tag, xr, xf, xq, QP, nch_h, in_norm, red, P.eps, sx, st)) {
+                ok = false;
+                break;
+            }
+            const float inv = sx.inv * sx.scale;
+            trace_detail(P, l, 0, 1);
+            if (qn) {
+                trace_detail(P, l, 0, 2);
+                if (!mbar_wait(mb_qkv, (uint32_t)l & 1u, st)) { ok = false; break; }
+                trace_mark(P, 0, ph + 1);
+                trace_detail(P, l, 0, 3);
+                const int qpairs = P.NH * half, kpairs = P.NKV * half;
+                block_gemv<4, 1>(s_qkv, P.SH, 2 * qn, nch_h, xq, QP, gpart);
+                // One thread per RoPE pair (rows j, j + d/2 of a head).
+                if (tid < qn) {
+                    const int w = tid, u = qa + w;
+                    const uint8_t* r0 = s_qkv + (size_t)w * 2 * P.SH;
+                    float y0 = gemv_row(gpart, 2 * qn, 2 * w) * inv * row_scale(r0, P.Kh) + row_bias(r0, P.Kh);
+                    float y1 = gemv_row(gpart, 2 * qn, 2 * w + 1) * inv * row_scale(r0 + P.SH, P.Kh) +
+                               row_bias(r0 + P.SH, P.Kh);
+                    const int kind = u < qpairs ? 0 : (u < qpairs + kpairs ? 1 : 2);
+                    const int pu = kind == 0 ? u : (kind == 1 ? u - qpairs : u - qpairs - kpairs);
+                    const int hd = pu / half, j = pu % half;
+                    if (kind < 2) {
+                        const float sn = s_sin[j], cs = s_cos[j];
+                        const float a = y0, bb = y1;
+                        y0 = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(bb, sn));
+                        y1 = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
+                    }
+                    if (kind == 0) {
+                        ll_store(P.ll_q + hd * D + j, y0, tag);
+                        ll_store(P.ll_q + hd * D + j + half, y1, tag);
+                    } else {
+                        KV* cache = (kind == 1 ? kc : vc) + (((size_t)l * P.NKV + hd) * P.capacity + A.pos) * D;
+                        kv_store(cache + j, y0);
+                        kv_store(cache + j + half, y1);
+                        uint64_t* nw = P.ll_kv + (kind == 1 ? 0 : kvd) + hd * D;
+                        ll_store(nw + j, round_to(y0, KV()), tag);
+                        ll_store(nw + j + half, round_to(y1, KV()), tag);
+                    }
+                }
+                trace_detail(P, l, 0, 4);
+                __syncthreads();
+                trace_detail(P, l, 0, 5);
+                if (tid == 0 && l + 1 < P.L) {
+                    fence_proxy_async();
+                    fill_slot(s_qkv, P.layers[l + 1].qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH, mb_qkv,
+                              s_fills + 2);
+                }
+                trace_detail(P, l, 0, 6);
+            }
+        }
+        trace_mark(P, 1, ph + 1);
+
+        // ---- ATTN over positions 0..pos (src/kernels.cpp:150-179)
+        if (has_att) {
+            trace_mark(P, 0, ph + 2);
+            if (!attention_block<KV>(P, A, ap, l, tag, s_att, mb_att, att_fills, s_fills + 4 + HEAD_MAX_STAGES, misc,
+                                     st)) {
+                ok = false;
+                break;
+            }
+        }
+        trace_mark(P, 1, ph + 2);
+
+        // ---- O projection + residual (src/model.cpp:304-305)
+        if (on) {
+            trace_detail(P, l, 2, 0);
+            Staged sa;
+            if (!gather_stage<2>(P.ll_attn, H, tag, nullptr, xf, xq, QP, nch_h, nullptr, red, P.eps, sa, st)) {
+                ok = false;
+                break;
+            }
+            trace_detail(P, l, 2, 1);
+            if (!mbar_wait(mb_o, (uint32_t)l & 1u, st)) { ok = false; break; }
+            trace_mark(P, 0, ph + 3);
+            trace_detail(P, l, 2, 2);
+            block_gemv<4, 1>(s_o, P.SH, on, nch_h, xq, QP, gpart);
+            if (tid < on) {
+                const int r = oa + tid;
+                ll_store(P.ll_xb + r,
+                         xr[r] + gemv_row(gpart, on, tid) * sa.scale * row_scale(s_o + (size_t)tid * P.SH, P.Kh), tag);
+            }
+            trace_detail(P, l, 2, 3);
+            __syncthreads();
+            trace_detail(P, l, 2, 4);
+            if (tid == 0 && l + 1 < P.L) {
+                fence_proxy_async();
+                fill_slot(s_o, P.layers[l + 1].o + (size_t)oa * P.SH, (uint32_t)on * P.SH, mb_o, s_fills + 3);
+            }
+            trace_detail(P, l, 2, 5);
+        }
+        trace_mark(P, 1, ph + 3);
+
+        // ---- gate/up + SiLU (src/model.cpp:306-308)
+        if (gn || dn) {
+            trace_detail(P, l, 3, 0);
+            if (gn && !mbar_wait(mb_norm + (l & 1), norm_parity, st)) { ok = false; break; }
+            Staged sb;
+            if (!gather_stage<2>(P.ll_xb, H, tag, xr, xf, xq, QP, nch_h, post_norm, red, P.eps, sb, st)) {
+                ok = false;
+                break;
+            }
+            const float inv = sb.inv * sb.scale;
+            trace_detail(P, l, 3, 1);
+            if (gn) {
+                trace_detail(P, l, 3, 2);
+                if (!mbar_wait(mb_gu, (uint32_t)l & 1u, st)) { ok = false; break; }
+                trace_mark(P, 0, ph + 4);
+                trace_detail(P, l, 3, 3);
+                block_gemv<2, 5>(s_gu, P.SH, 2 * gn, nch_h, xq, QP, gpart);
+                if (tid < gn) {
+                    const uint8_t* r0 = s_gu + (size_t)tid * 2 * P.SH;
+                    const float g = gemv_row(gpart, 2 * gn, 2 * tid) * inv * row_scale(r0, P.Kh);
+                    const float u = gemv_row(gpart, 2 * gn, 2 * tid + 1) * inv * row_scale(r0 + P.SH, P.Kh);
+                    ll_store(P.ll_h + ga + tid, (g / (1.0f + expf(-g))) * u, tag);
+                }
+                trace_detail(P, l, 3, 4);
+                __syncthreads();
+                trace_detail(P, l, 3, 5);
+                if (tid == 0) {
+                    fence_proxy_async();
+                    if (l + 1 < P.L) {
+                        fill_slot(s_gu, P.layers[l + 1].gu + (size_t)ga * 2 * P.SH, (uint32_t)gn * 2 * P.SH, mb_gu,
+                                  s_fills + 0);
+                    } else {
+                        // Last layer: LM-head stages clear of the down slot can start now.
+                        while (head_issued < min(NS, head_chunks) &&
+                               (size_t)(head_issued + 1) * head_stage_bytes <= (size_t)(P.off_down - P.off_gu))
+                            fill_head(head_issued++);
+                    }
+                }
+                trace_detail(P, l, 3, 6);
+            }
+        }
+        trace_mark(P, 1, ph + 4);
+
+        // ---- down + residual (src/model.cpp:309-310); x entering layer l+1 carries tag + 1.
+        if (dn) {
+            trace_detail(P, l, 4, 0);
+            Staged sh;
+            if (!gather_stage<10>(P.ll_h, I, tag, nullptr, xf_i, xq_i, P.down_plane, nch_i, nullptr, red, P.eps, sh,
+                                  st)) {
+                ok = false;
+                break;
+            }
+            trace_detail(P, l, 4, 1);
+            if (!mbar_wait(mb_down, (uint32_t)l & 1u, st)) { ok = false; break; }
+            trace_mark(P, 0, ph + 5);
+            trace_detail(P, l, 4, 2);
+            block_gemv<4, 1>(s_down, P.SI, dn, nch_i, xq_i, P.down_plane, gpart);
+            trace_detail(P, l, 4, 3);
+            if (tid < dn) {
+                const int r = da + tid;
+                ll_store(P.ll_xa + r,
+                         xr[r] + gemv_row(gpart, dn, tid) * sh.scale * row_scale(s_down + (size_t)tid * P.SI, P.Ki),
+                         tag + 1);
+            }
+            __syncthreads();
+            trace_detail(P, l, 4, 4);
+            if (tid == 0) {
+                fence_proxy_async();
+                if (l + 1 < P.L)
+                    fill_slot(s_down, P.layers[l + 1].down + (size_t)da * P.SI, (uint32_t)dn * P.SI, mb_down,
+                              s_fills + 1);
+                else
+                    while (head_issued < min(NS, head_chunks)) fill_head(head_issued++);
+            }
+            trace_detail(P, l, 4, 5);
+        }
+        trace_mark(P, 1, ph + 5);
+    }
+
+    if (ok && A.head) {
+        // ---- final RMSNorm + tied LM head + argmax (src/model.cpp:318-326, src/main.cpp:35-37)
+        float best_v = -INFINITY;
+        int best_i = 0x7fffffff;
+        if (hn) {
+            if (tid == 0)
+                while (head_issued < min(NS, head_chunks)) fill_head(head_issued++);
+            Staged sf;
+            if (!mbar_wait(mb_norm + (P.L & 1), (uint32_t)(P.L >> 1) & 1u, st)) ok = false;
+            if (ok && !gather_stage<2>(P.ll_xa, H, seq_tag | (uint32_t)(P.L + 1), nullptr, xf, xq, QP, nch_h,
+                                       s_norms + (size_t)(P.L & 1) * 2 * P.Kh, red, P.eps, sf, st))
+                ok = false;
+            const float inv = sf.inv * sf.scale;
+            if (ok) {
+                // The lane's activation chunks (lane + 32k) stay in registers.
+                int4 xv[HEAD_MAXC][3];
+#pragma unroll
+                for (int k = 0; k < HEAD_MAXC; ++k) {
+                    const int ch = lane + 32 * k;
+                    if (ch < nch_h) {
+                        load_planes(xq, QP, ch, xv[k][0], xv[k][1], xv[k][2]);
+                    } else {
+                        xv[k][0] = xv[k][1] = xv[k][2] = make_int4(0, 0, 0, 0);
+                    }
+                }
+                trace_mark(P, 0, 5 * P.L + 1);
+                // Each warp takes rows 2w, 2w+1 of every stage and waits on the
+                // stage by itself; lane 0 arrives on the stage's "empty" barrier and
+                // thread 0 refills a stage once all warps released it.
+                for (int c = 0; c < head_chunks; ++c) {
+                    const int sidx = c % NS;
+                    if (!mbar_wait_warp(mb_head + sidx, (uint32_t)(c / NS) & 1u, st)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t* stage = sm + P.off_gu + (size_t)sidx * head_stage_bytes;
+                    const int r0 = ha + c * HEAD_ROWS, rows = min(HEAD_ROWS, ha + hn - r0);
+                    const int w0 = 2 * warp;
+                    float d0 = 0.f, d1 = 0.f, sc0 = 0.f, sc1 = 0.f;
+                    if (w0 < rows) {
+                        const uint8_t* ra = stage + (size_t)w0 * P.SH;
+                        const uint8_t* rb = stage + (size_t)min(w0 + 1, rows - 1) * P.SH;
+                        int ah0 = 0, am0 = 0, al0 = 0, ah1 = 0, am1 = 0, al1 = 0;
+#pragma unroll
+                        for (int k = 0; k < HEAD_MAXC; ++k) {
+                            const int ch = lane + 32 * k;
+                            if (ch < nch_h) {
+                                dp4a16(*reinterpret_cast<const int4*>(ra + (size_t)ch * 16), xv[k][0], xv[k][1], xv[k][2],
+                                       ah0, am0, al0);
+                                dp4a16(*reinterpret_cast<const int4*>(rb + (size_t)ch * 16), xv[k][0], xv[k][1], xv[k][2],
+                                       ah1, am1, al1);
+                            }
+                        }
+                        sc0 = row_scale(ra, P.Kh);
+                        sc1 = row_scale(rb, P.Kh);
+                        d0 = planes_to_float(ah0, am0, al0);
+                        d1 = planes_to_float(ah1, am1, al1);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(mb_head_empty + sidx);
+                    d0 = warp_sum(d0);
+                    d1 = warp_sum(d1);
+                    if (w0 < rows) {
+#pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            if (w0 + k < rows) {
+                                const int r = r0 + w0 + k;
+                                const float v = (k ? d1 * sc1 : d0 * sc0) * inv;
+                                if (lane == k) P.logits[r] = v;
+                                if (better(v, r, best_v, best_i)) {
+                                    best_v = v;
+                                    best_i = r;
+                                }
+                            }
+                        }
+                    }
+                    if (tid == 0) {
+                        prefetch_head(c + NS + HEAD_L2_AHEAD);
+                        if (c + NS < head_chunks) {
+                            // All warps released the stage (phase c / NS of its empty barrier).
+                            // On expiry the abort flag is raised and every warp leaves at its next wait.
+                            if (mbar_wait_one(mb_head_empty + sidx, (uint32_t)(c / NS) & 1u, st)) {
+                                fence_proxy_async();
+                                fill_head(c + NS);
+                                ++head_issued;
+                            }
+                        }
+                    }
+                }
+                __syncthreads();
+                if (should_abort(st)) ok = false;
+            }
+        }
+        if (ok) {
+            // Each warp's best is uniform across its lanes; merge the warps.
+            if (lane == 0) {
+                red[warp] = best_v;
+                reinterpret_cast<int*>(red)[NW + warp] = best_i;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                for (int w = 0; w < NW; ++w) {
+                    const float v = red[w];
+                    const int i = reinterpret_cast<const int*>(red)[NW + w];
+                    if (better(v, i, best_v, best_i)) {
+                        best_v = v;
+                        best_i = i;
+                    }
+                }
+                P.amax[b] = {best_v, best_i};
+                __threadfence();
+                const unsigned prev = atomicAdd(&P.sync->amax_done, 1u);
+                if (prev == (unsigned)G - 1) {
+                    __threadfence();
+                    ArgBest r = {-INFINITY, 0x7fffffff};
+                    for (int c = 0; c < G; ++c) {
+                        ArgBest t;
+                        t.v = __ldcg(&P.amax[c].v);
+                        t.i = __ldcg(&P.amax[c].i);
+                        if (better(t.v, t.i, r.v, r.i)) r = t;
+                    }
+                    if (r.i == 0x7fffffff) r.i = 0;
+                    P.result[0] = r.i;
+                    if (A.argmax_dev) *A.argmax_dev = r.i;
+                    P.sync->amax_done = 0;
+                }
+            }
+        }
+        trace_mark(P, 1, 5 * P.L + 1);
+    }
+    if (ok && tid == 0) {
+        // Warm L2 with this block's first-layer rows for the next token.
+        const LayerW& W0 = P.layers[0];
+        if (qn) prefetch_l2(W0.qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH);
+        if (on) prefetch_l2(W0.o + (size_t)oa * P.SH, (uint32_t)on * P.SH);
+    }
+
+    // On abort, wait (bounded) for this block's copies in flight before the
+    // shared memory they target is released.
+    __syncthreads();
+    if (!ok && tid == 0) {
+        const uint64_t t0 = globaltimer();
+        for (int i = 0; i < NMB; ++i) {
+            // Fill number k completes phase k of its mbarrier (parity k & 1).
+            if (!s_fills[i]) continue;
+            const uint32_t parity = (s_fills[i] - 1) & 1u;
+            while (!mbar_test(mb + i, parity) && globaltimer() - t0 < WAIT_LIMIT_NS) {
+            }
+        }
+    }
+    trace_mark(P, 0, 5 * P.L + 2);
+    trace_mark(P, 1, 5 * P.L + 2);
+    trace_clock(P, 1);
+}
+
+}  // namespace dcb

@@ -119,6 +119,18 @@ int dcb_launch_info(const dcb_engine* e, int* blocks, int* threads, int* smem_by
 /* Number of device kernel launches issued by the engine since creation. */
 uint64_t dcb_launch_count(const dcb_engine* e);
 
+/* Phase tracing (diagnostics; no counterpart in the reference, whose Profile
+ * times operations on the host). When enabled, every step records per block b
+ * and phase k (k = 0 kernel start; 5*l+1..5*l+5 the QKV, ATTN, O, GU, DOWN
+ * phases of layer l; 5*L+1 the LM head; 5*L+2 the kernel end) the globaltimer
+ * ns at which the block's inputs were ready (ready[k*blocks + b]; 0 when the
+ * block had no work in that phase) and at which it finished it (done[...]).
+ * Both records hold 512 phase rows of `blocks` entries; rows 400+8k+m of
+ * `ready` hold detailed marks m inside phase k (0..4) of one traced layer.
+ * dcb_trace_read clears the record after reading it. */
+int dcb_trace_enable(dcb_engine* e, int on);
+int dcb_trace_read(dcb_engine* e, uint64_t* ready, uint64_t* done, int* phases);
+
 /* ---- isolated operators (device pointers, on `stream`) -------------------- */
 
 /* Replaces decode::matvec for int8 matrices (src/kernels.cpp:107-120):
