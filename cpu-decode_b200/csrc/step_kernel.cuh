@@ -744,7 +744,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     uint64_t* mb_head_empty = mb + 4 + HEAD_MAX_STAGES + 4;  // NW arrivals each
     float* s_norms = reinterpret_cast<float*>(sm + P.off_norm);  // [2 buffers][2][Kh]
     __shared__ float s_cos[64], s_sin[64];
-    __shared__ float red[2 * NW + 8];
+    __shared__ __align__(16) float red[2 * NW + 8];  // read as float4 in finish_stage
     __shared__ int s_abort;
     __shared__ unsigned s_fills[NMB];  // fills issued per mbarrier (thread 0)
 
