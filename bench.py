@@ -204,9 +204,14 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the ctx 4096 extra measurement")
+    ap.add_argument("--ncu-case", action="store_true",
+                    help="the profiling case: KV rows 0..127 written from the host, then 5 decode launches")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.ncu_case:
+        ncu_case()
         return
 
     import torch
@@ -345,6 +350,33 @@ def main() -> None:
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def ncu_case() -> None:
+    """Five decode launches at context 128 with few launches before them (the
+    KV rows come from the host, no prefill): launches 4 and 5 are the ones a
+    profiler captures (`-k regex:decode_step -s 3 -c 2`)."""
+    import torch
+    dcb = load_package()
+    import cpu_decode_b200.synthetic as syn
+    model = ensure_model()
+    d = syn.QWEN05
+    eng = dcb.Engine(model, CONTEXT + 8)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    eng.set_stream(stream.cuda_stream)
+    rng = np.random.default_rng(128)
+    for l in range(d.layers):
+        eng.kv_write(l, 0, rng.standard_normal((CONTEXT, d.kv_dim), dtype=np.float32),
+                     rng.standard_normal((CONTEXT, d.kv_dim), dtype=np.float32))
+    eng.set_position(CONTEXT)
+    tok = torch.full((1,), prompt_tokens()[-1], dtype=torch.int32, device="cuda")
+    for _ in range(5):
+        eng.step_async(token_dev=tok.data_ptr(), head=True, argmax_dev=tok.data_ptr())
+    eng.synchronize()
+    print(json.dumps({"ncu_case": "decode_step_kernel ctx 128", "launches": eng.launch_count,
+                      "last_token": int(tok.item())}))
+    eng.close()
 
 
 def long_context(dcb, model, d, K, W, device) -> dict:
