@@ -33,7 +33,8 @@ EXPORTS = (
     "dcb_last_error", "dcb_set_error", "dcb_create", "dcb_create_from_dir", "dcb_destroy", "dcb_step",
     "dcb_step_async", "dcb_synchronize", "dcb_rewind", "dcb_reset", "dcb_position", "dcb_set_stream", "dcb_stream",
     "dcb_logits_device", "dcb_kv_write", "dcb_kv_read", "dcb_set_position", "dcb_launch_info", "dcb_launch_count",
-    "dcb_gemv_i8", "dcb_attention", "dcb_rmsnorm", "dcb_rope", "dcb_argmax", "dcb_trace_enable", "dcb_trace_read",
+    "dcb_gemv_i8", "dcb_attention", "dcb_attention_noalloc", "dcb_rmsnorm", "dcb_rope", "dcb_argmax",
+    "dcb_trace_enable", "dcb_trace_read",
 )
 
 
@@ -80,6 +81,7 @@ def lib() -> C.CDLL:
     L.dcb_launch_count.restype = C.c_uint64
     L.dcb_gemv_i8.argtypes = [vp, vp, vp, vp, vp, i32, i32, vp]
     L.dcb_attention.argtypes = [vp, vp, vp, i32, vp, i32, i32, i32, i32, C.c_float, vp]
+    L.dcb_attention_noalloc.argtypes = [vp, vp, vp, i32, vp, i32, i32, i32, i32, C.c_float, vp]
     L.dcb_rmsnorm.argtypes = [vp, vp, vp, i32, C.c_float, vp]
     L.dcb_rope.argtypes = [vp, i32, i32, i32, C.c_float, i32, vp]
     L.dcb_argmax.argtypes = [vp, i32, vp, vp]

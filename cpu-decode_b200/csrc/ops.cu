@@ -278,3 +278,136 @@ int dcb_argmax(const float* x, int n, int* out, void* stream) {
 }
 
 }  // extern "C"
+
+// ---- attention with its scratch in a static device array --------------------------
+// dcb_attention_noalloc is dcb_attention with the cudaMallocAsync scratch
+// replaced by one fixed array per device, for callers that must not allocate
+// device memory per call. Layout: [0, 1 KiB) RoPE inverse frequencies (256
+// floats), [1 KiB, 2 KiB) per-group arrival counters (up to 256 unsigned), then
+// the split partials (heads x splits x (dim + 2) floats).
+#include <mutex>
+
+namespace {
+constexpr size_t NOALLOC_BYTES = DCB_ATTENTION_NOALLOC_SCRATCH_BYTES;
+constexpr size_t NOALLOC_CNT_OFF = 1024, NOALLOC_PART_OFF = 2048;
+constexpr int NOALLOC_MAX_KV_HEADS = 256;
+constexpr int NOALLOC_MAX_DEVICES = 64;
+
+__device__ __align__(256) unsigned char g_attention_scratch[NOALLOC_BYTES];
+
+struct NoallocDevice {
+    std::once_flag once;
+    cudaError_t status = cudaSuccess;
+    const char* what = "";
+    char* scratch = nullptr;
+    int sms = 0;
+    int max_dynamic[2] = {0, 0};  // dynamic shared memory cap of attention_kernel<float>, <__half>
+};
+NoallocDevice g_noalloc[NOALLOC_MAX_DEVICES];
+
+template <typename KV>
+cudaError_t raise_smem_cap(int optin, int& cap) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, attention_kernel<KV>);
+    if (e != cudaSuccess) return e;
+    cap = optin - (int)fa.sharedSizeBytes;
+    return cudaFuncSetAttribute(attention_kernel<KV>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+}
+
+// Once per device, with that device current: the scratch's device address and
+// the kernel attributes (the dynamic shared memory cap raised to what the
+// device allows next to the kernel's static shared memory, so later calls set
+// nothing).
+void noalloc_setup(NoallocDevice& d, int dev) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
+    if (e != cudaSuccess) {
+        d.status = e;
+        d.what = "attention scratch address";
+        return;
+    }
+    d.scratch = static_cast<char*>(p);
+    int optin = 0;
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) {
+        d.status = e;
+        d.what = "device attributes";
+        return;
+    }
+    if ((e = raise_smem_cap<float>(optin, d.max_dynamic[0])) != cudaSuccess ||
+        (e = raise_smem_cap<__half>(optin, d.max_dynamic[1])) != cudaSuccess) {
+        d.status = e;
+        d.what = "attention kernel attributes";
+    }
+}
+}  // namespace
+
+extern "C" int dcb_attention_noalloc(const float* q_in, const void* keys, const void* values, int kv_dtype,
+                                     float* out, int length, int heads, int kv_heads, int dim, float rope_theta,
+                                     void* stream) {
+    if (!q_in || !keys || !values || !out || length <= 0 || kv_heads <= 0 || heads % kv_heads || dim <= 0 ||
+        dim % 2 || dim > 128)
+        return fail(DCB_ERR_ARGUMENT, "invalid attention dimensions");
+    if (kv_dtype != DCB_KV_F32 && kv_dtype != DCB_KV_F16) return fail(DCB_ERR_ARGUMENT, "invalid KV dtype");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "current device");
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES)
+        return fail(DCB_ERR_UNSUPPORTED, "dcb_attention_noalloc supports device ordinals below 64");
+    NoallocDevice& d = g_noalloc[dev];
+    std::call_once(d.once, noalloc_setup, std::ref(d), dev);
+    if (d.status != cudaSuccess) return cuda_fail(d.status, d.what);
+
+    // The split of dcb_attention, so both produce the same partials.
+    const int chunks = (length + KV_CHUNK - 1) / KV_CHUNK;
+    const int want = std::max(1, 2 * d.sms / kv_heads);
+    const int n = std::min(chunks, want);
+    const int split_len = ((chunks + n - 1) / n) * KV_CHUNK;
+    const int nsplit = (length + split_len - 1) / split_len;
+    const int gq = heads / kv_heads;
+    const size_t part_bytes = (size_t)heads * nsplit * (dim + 2) * sizeof(float);
+    if (kv_heads > NOALLOC_MAX_KV_HEADS || NOALLOC_PART_OFF + part_bytes > NOALLOC_BYTES)
+        return fail(DCB_ERR_ARGUMENT,
+                    "dcb_attention_noalloc: needs " + std::to_string(NOALLOC_PART_OFF + part_bytes) +
+                        " bytes of scratch (" + std::to_string(kv_heads) + " KV heads, " + std::to_string(heads) +
+                        " heads x " + std::to_string(nsplit) + " splits x " + std::to_string(dim + 2) +
+                        " floats); the static scratch holds " + std::to_string(NOALLOC_BYTES) +
+                        " bytes and at most 256 KV heads");
+    const size_t smem = attention_smem_floats(dim, gq) * sizeof(float);
+    if (smem > (size_t)d.max_dynamic[kv_dtype == DCB_KV_F16 ? 1 : 0])
+        return fail(DCB_ERR_UNSUPPORTED, "attention needs more shared memory than a block has");
+
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* inv = reinterpret_cast<float*>(d.scratch);
+    unsigned* cnt = reinterpret_cast<unsigned*>(d.scratch + NOALLOC_CNT_OFF);
+    float* part = reinterpret_cast<float*>(d.scratch + NOALLOC_PART_OFF);
+    // The arrival counters must be zero when the kernel starts.
+    if ((e = cudaMemsetAsync(cnt, 0, (size_t)kv_heads * sizeof(unsigned), st)) != cudaSuccess)
+        return cuda_fail(e, "attention counters");
+    AttnIO io;
+    io.q = q_in;
+    io.rope_inv = nullptr;
+    io.rope_pos = length - 1;
+    if (rope_theta > 0) {
+        rope_inv_kernel<<<1, 64, 0, st>>>(inv, dim, rope_theta);
+        io.rope_inv = inv;
+    }
+    io.keys = keys;
+    io.values = values;
+    io.out = out;
+    io.part = part;
+    io.group_done = cnt;
+    io.heads = heads;
+    io.kv_heads = kv_heads;
+    io.d = dim;
+    io.length = length;
+    io.nsplit = nsplit;
+    io.split_len = split_len;
+    const int threads = std::min(512, std::max(128, ((gq + 3) / 4) * 128));
+    if (kv_dtype == DCB_KV_F16)
+        attention_kernel<__half><<<kv_heads * nsplit, threads, smem, st>>>(io);
+    else
+        attention_kernel<float><<<kv_heads * nsplit, threads, smem, st>>>(io);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail(e, "attention launch");
+}
