@@ -320,7 +320,13 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     if (int rc = e->alloc(&P.sync, 1)) return bail(rc);
     if (int rc = e->alloc(&P.result, 4)) return bail(rc);
 
-    // ---- shared memory plan (bytes): weight slots, attention chunks, vectors
+    // ---- shared memory plan (bytes): weight slots, attention chunk ring, vectors
+    e->kernel = kv_dtype == DCB_KV_F16 ? (void*)decode_step_kernel<__half> : (void*)decode_step_kernel<float>;
+    int max_optin = 0;
+    DCB_CUDA(cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    cudaFuncAttributes fattr;
+    DCB_CUDA(cudaFuncGetAttributes(&fattr, e->kernel));
+    const size_t budget = (size_t)max_optin - fattr.sharedSizeBytes;  // dynamic shared memory available
     const size_t gu_slot = (size_t)ceil_div(I, G) * 2 * P.SH;
     const size_t down_slot = (size_t)ceil_div(H, G) * P.SI;
     const size_t qkv_slot = (size_t)ceil_div(P.qkv_pairs, G) * 2 * P.SH;
@@ -336,36 +342,44 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     off = round_up(off + o_slot, 128);
     off = std::max(off, round_up((size_t)3 * HEAD_ROWS * P.SH, 128));  // at least three LM-head stages
     P.off_att = (int)off;
-    P.att_chunk_bytes = (int)(2 * (size_t)ATT_CHUNK * D * e->kv_elem());
-    P.down_x_off = (int)round_up((size_t)P.Ki * sizeof(float), 128);
-    P.down_plane = (int)round_up((size_t)P.Ki, 128);
-    off = round_up(off + std::max(2 * (size_t)P.att_chunk_bytes, (size_t)P.down_x_off + 3 * (size_t)P.down_plane), 128);
-    P.off_xs = (int)off;
-    // The LM-head ring overlays the weight slots and the attention buffers.
-    P.head_stages = (int)std::min<size_t>(HEAD_MAX_STAGES, (size_t)(P.off_xs - P.off_gu) / ((size_t)HEAD_ROWS * P.SH));
-    P.trace_layer = std::min(5, e->L - 1);
-    if (const char* v = std::getenv("DCB_SPLIT_MIN")) e->split_min = std::max(ATT_CHUNK, std::atoi(v) / ATT_CHUNK * ATT_CHUNK);
-    off = round_up(off + (size_t)P.Kh * sizeof(float), 128);
-    P.off_xq = (int)off;
+    // Vectors after the attention ring: staged floats, fixed-point planes,
+    // GEMV partials (two buffers), raw residual, attention scratch.
     P.xq_plane = (int)round_up((size_t)P.Kh, 128);
-    off = round_up(off + 3 * (size_t)P.xq_plane, 128);
-    P.off_gpart = (int)off;
     {
         const int max_rows = std::max({2 * ceil_div(P.qkv_pairs, G), ceil_div(H, G), 2 * ceil_div(I, G), HEAD_ROWS});
         P.gpart_floats = NW * max_rows;
     }
-    off = round_up(off + 2 * (size_t)P.gpart_floats * sizeof(float), 128);
+    const size_t xs_bytes = round_up((size_t)P.Kh * sizeof(float), 128);
+    const size_t xq_bytes = round_up(3 * (size_t)P.xq_plane, 128);
+    const size_t gpart_bytes = round_up(2 * (size_t)P.gpart_floats * sizeof(float), 128);
+    const size_t xr_bytes = round_up((size_t)P.Kh * sizeof(float), 128);
+    const size_t misc_bytes = round_up((size_t)(384 + NW * (D + 2)) * sizeof(float), 128);
+    const size_t tail = xs_bytes + xq_bytes + gpart_bytes + xr_bytes + misc_bytes;
+    // The attention ring takes what is left (2..ATT_MAX_BUFS chunks); DOWN's
+    // intermediate-sized input staging overlays it, so it is at least that big.
+    P.att_chunk_bytes = (int)(2 * (size_t)ATT_CHUNK * D * e->kv_elem());
+    P.down_x_off = (int)round_up((size_t)P.Ki * sizeof(float), 128);
+    P.down_plane = (int)round_up((size_t)P.Ki, 128);
+    const size_t down_stage = round_up((size_t)P.down_x_off + 3 * (size_t)P.down_plane, 128);
+    const size_t room = budget > off + tail ? budget - off - tail : 0;
+    P.att_bufs = (int)std::min<size_t>(ATT_MAX_BUFS, std::max<size_t>(2, room / P.att_chunk_bytes));
+    off = round_up(off + std::max((size_t)P.att_bufs * P.att_chunk_bytes, down_stage), 128);
+    P.off_xs = (int)off;
+    // The LM-head ring overlays the weight slots and the attention ring.
+    P.head_stages = (int)std::min<size_t>(HEAD_MAX_STAGES, (size_t)(P.off_xs - P.off_gu) / ((size_t)HEAD_ROWS * P.SH));
+    P.trace_layer = std::min(5, e->L - 1);
+    if (const char* v = std::getenv("DCB_SPLIT_MIN")) e->split_min = std::max(ATT_CHUNK, std::atoi(v) / ATT_CHUNK * ATT_CHUNK);
+    off += xs_bytes;
+    P.off_xq = (int)off;
+    off += xq_bytes;
+    P.off_gpart = (int)off;
+    off += gpart_bytes;
     P.off_xr = (int)off;
-    off = round_up(off + (size_t)P.Kh * sizeof(float), 128);
+    off += xr_bytes;
     P.off_misc = (int)off;
-    off = round_up(off + (size_t)(384 + NW * (D + 2)) * sizeof(float), 128);
-    P.off_norm = (int)off;
-    off = round_up(off + (size_t)4 * P.Kh * sizeof(float), 128);
+    off += misc_bytes;
     e->smem = (int)off;
-    e->kernel = kv_dtype == DCB_KV_F16 ? (void*)decode_step_kernel<__half> : (void*)decode_step_kernel<float>;
-    int max_optin = 0;
-    DCB_CUDA(cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
-    if (e->smem > max_optin) return bail(fail(DCB_ERR_UNSUPPORTED, "model too large for shared memory staging"));
+    if ((size_t)e->smem > budget) return bail(fail(DCB_ERR_UNSUPPORTED, "model too large for shared memory staging"));
     if (cudaFuncSetAttribute(e->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem) != cudaSuccess)
         return bail(fail(DCB_ERR_UNSUPPORTED, "cannot reserve shared memory for the step kernel"));
     int per_sm = 0;

@@ -39,6 +39,7 @@ constexpr int ERR_WAIT = 1;
 constexpr int ERR_TOKEN = 2;
 constexpr int ATT_CHUNK = 64;  // KV positions per staged chunk
 constexpr int ATT_PER_WARP = ATT_CHUNK / NW;
+constexpr int ATT_MAX_BUFS = 6;  // staged chunk ring (the host picks how many fit)
 constexpr int HEAD_ROWS = 2 * NW;  // LM-head rows per ring stage: two per warp
 constexpr int HEAD_MAX_STAGES = 8;  // LM-head ring stages (the host picks how many fit)
 constexpr int HEAD_L2_AHEAD = 12;   // LM-head chunks kept in flight into L2 beyond the ring
@@ -91,12 +92,13 @@ struct Params {
     int* result;
     uint64_t* trace;  // [2][TRACE_MAX_PHASES][grid] ready/done ns, or null
     // shared memory layout (bytes)
-    int off_gu, off_down, off_qkv, off_o, off_att, off_xs, off_xq, off_gpart, off_xr, off_misc, off_norm;
+    int off_gu, off_down, off_qkv, off_o, off_att, off_xs, off_xq, off_gpart, off_xr, off_misc;
     int xq_plane;      // bytes per fixed-point plane of a hidden-sized vector (>= Kh)
     int down_x_off;    // DOWN input staging inside the attention buffers: floats at off_att,
     int down_plane;    // planes at off_att + down_x_off, down_plane bytes each (>= Ki)
     int gpart_floats;  // floats per block-GEMV partial buffer (NW * max rows of a phase)
     int att_chunk_bytes;
+    int att_bufs;     // chunk buffers in the attention ring (2..ATT_MAX_BUFS)
     int head_stages;  // LM-head ring stages over [off_gu, off_xs)
     int trace_layer;  // layer whose phases get detailed marks when tracing
 };
@@ -235,12 +237,11 @@ __device__ bool mbar_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
 // the order of the FP32 rounding in the reference's own sums.
 constexpr float FIX_MAX = 8323072.0f;  // 2^23 - 2^16: keeps hi within [-127, 127]
 
-// Element j arrived with value v: raw to xr (when set), v * gain[j] (the RMSNorm
-// gain folded in; v when gain is null) to xf.
-__device__ __forceinline__ void accept(int j, float v, float* xr, float* xf, const float* gain, float& ss,
-                                       float& mx) {
+// Element j arrived with value v: raw to xr (when set), v * gain (the RMSNorm
+// gain of element j folded in; 1 where there is none) to xf.
+__device__ __forceinline__ void accept(int j, float v, float* xr, float* xf, float gain, float& ss, float& mx) {
     if (xr) xr[j] = v;
-    const float g = gain ? v * gain[j] : v;
+    const float g = v * gain;
     xf[j] = g;
     ss = fmaf(v, v, ss);
     mx = fmaxf(mx, fabsf(g));
@@ -323,8 +324,10 @@ __device__ bool mbar_wait_one(uint64_t* m, uint32_t parity, const BlockState& st
 
 // Block-cooperative: wait until the n tagged words at src carry `tag`, accept
 // them and stage the vector. Words are polled in groups of W per thread, all
-// loads of a group in flight together. Returns false when the step must abort.
-template <int W>
+// loads of a group in flight together; with GAIN, the RMSNorm gains of the
+// same elements (global memory, gain[j]) are loaded alongside the first poll.
+// Returns false when the step must abort.
+template <int W, bool GAIN>
 __device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr, float* xf, int8_t* xq, int plane,
                              int nch, const float* gain, float* red, float eps, Staged& out, const BlockState& st) {
     uint64_t t0 = 0;
@@ -332,12 +335,15 @@ __device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr
     float ss = 0.f, mx = 0.f;
     for (int base = 0; base < n; base += W * NT) {
         uint64_t w[W];
+        float g[W];
         unsigned pending = 0;
 #pragma unroll
         for (int k = 0; k < W; ++k) {
             const int j = base + threadIdx.x + k * NT;
+            g[k] = 1.f;
             if (j < n) {
                 w[k] = ll_load(src + j);
+                if (GAIN) g[k] = __ldg(gain + j);
                 pending |= 1u << k;
             }
         }
@@ -346,7 +352,7 @@ __device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr
             for (int k = 0; k < W; ++k) {
                 if ((pending >> k) & 1u) {
                     if ((uint32_t)(w[k] >> 32) == tag) {
-                        accept(base + threadIdx.x + k * NT, __uint_as_float((uint32_t)w[k]), xr, xf, gain, ss, mx);
+                        accept(base + threadIdx.x + k * NT, __uint_as_float((uint32_t)w[k]), xr, xf, g[k], ss, mx);
                         pending &= ~(1u << k);
                     }
                 }
@@ -487,9 +493,14 @@ __device__ __forceinline__ void load4(const __half* p, float (&out)[4]) {
 }
 
 // ---- attention unit: query head h over positions [t0, t1) --------------------------
+// The cached rows of the block's range come in 64-position chunks through a
+// ring of att_bufs buffers ([K rows | V rows] each), the first att_bufs issued
+// when the layer starts. The new row (position pos) is not copied: it arrives
+// as tagged words and is read from shared memory where t == pos.
 struct AttnPlan {
     int h, g, t0, t1, nchunks;
-    bool bulk;  // rows are multiples of 16 bytes: TMA bulk copies, else plain loads
+    int nissued;  // chunks holding cached rows (start below pos): the ones copied
+    bool bulk;    // rows are multiples of 16 bytes: bulk copies, else plain loads
 };
 
 template <typename KV>
@@ -497,31 +508,44 @@ __device__ __forceinline__ const KV* kv_rows(const Params& P, const void* base, 
     return static_cast<const KV*>(base) + (((size_t)l * P.NKV + g) * P.capacity + t) * P.D;
 }
 
-// Thread 0: copy the cached rows (positions below pos) of chunk c into buffer c%2.
+// Thread 0: copy the cached rows (positions below pos) of chunk c into buffer c % att_bufs.
 template <typename KV>
 __device__ void att_issue(const Params& P, const StepArgs& A, const AttnPlan& ap, int l, int c, uint8_t* att,
                           uint64_t* mb_att, unsigned* fills) {
     const int c0 = ap.t0 + c * ATT_CHUNK;
     const int cend = min(min(ap.t1, c0 + ATT_CHUNK), A.pos);
     if (cend <= c0 || !ap.bulk) return;
+    const int buf = c % P.att_bufs;
     const uint32_t rows = (uint32_t)(cend - c0), rb = (uint32_t)(P.D * sizeof(KV));
-    KV* kdst = reinterpret_cast<KV*>(att + (size_t)(c & 1) * P.att_chunk_bytes);
+    KV* kdst = reinterpret_cast<KV*>(att + (size_t)buf * P.att_chunk_bytes);
     KV* vdst = kdst + (size_t)ATT_CHUNK * P.D;
-    ++fills[c & 1];
-    mbar_expect(mb_att + (c & 1), 2 * rows * rb);
-    bulk_load(kdst, kv_rows<KV>(P, P.kcache, l, ap.g, c0), rows * rb, mb_att + (c & 1));
-    bulk_load(vdst, kv_rows<KV>(P, P.vcache, l, ap.g, c0), rows * rb, mb_att + (c & 1));
+    ++fills[buf];
+    mbar_expect(mb_att + buf, 2 * rows * rb);
+    bulk_load(kdst, kv_rows<KV>(P, P.kcache, l, ap.g, c0), rows * rb, mb_att + buf);
+    bulk_load(vdst, kv_rows<KV>(P, P.vcache, l, ap.g, c0), rows * rb, mb_att + buf);
 }
 
-template <typename KV>
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Softmax in base 2: scores are scaled by log2(e)/sqrt(D) and exponentiated
+// with ex2, so that exp(s - m) = 2^((s - m) * log2(e)).
+constexpr float LOG2E = 1.4426950408889634f;
+
+// DT: head_dim known at compile time (64), or 0 for any even head_dim <= 128.
+template <typename KV, int DT>
 __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPlan& ap, int l, uint32_t tag,
-                                uint8_t* att, uint64_t* mb_att, unsigned (&att_fills)[2], unsigned* issued,
-                                float* misc, const BlockState& st) {
-    const int D = P.D, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int kvd = P.NKV * D;
+                                uint8_t* att, uint64_t* mb_att, unsigned* issued, float* misc,
+                                const BlockState& st) {
+    constexpr int MD = DT ? (DT + 31) / 32 : MAXD;  // 32-dim groups a lane covers
+    const int D = DT ? DT : P.D, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int kvd = P.NKV * D, NB = P.att_bufs;
     float* sq = misc;                      // [D]
-    float* sk_new = misc + 128;            // [2][D] new K and V rows of group g
-    float* wpart = misc + 384;             // [NW][D+2]
+    float* s_new = misc + 128;             // [2][D] new K and V rows of group g (rounded to KV)
+    float* wpart = misc + 384;             // [NW][D+2]: m, l, o of each warp
     __shared__ int s_last;
     const bool has_new = ap.t0 <= A.pos && A.pos < ap.t1;
     trace_detail(P, l, 1, 0);
@@ -532,7 +556,6 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
         if (t < nwords) {
             const uint64_t* src = t < D ? P.ll_q + (size_t)ap.h * D + t
                                         : P.ll_kv + (t < 2 * D ? 0 : kvd) + (size_t)ap.g * D + (t % D);
-            float* dst = t < D ? sq + t : sk_new + (t - D);
             uint64_t t0 = 0;
             unsigned rounds = 0;
             uint64_t w = ll_load(src);
@@ -540,148 +563,160 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
                 if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
                 w = ll_load(src);
             }
-            *dst = __uint_as_float((uint32_t)w);
+            const float v = __uint_as_float((uint32_t)w);
+            if (t < D) sq[t] = v;
+            else s_new[t - D] = round_to(v, KV());
         }
         __syncthreads();
         if (should_abort(st)) return false;
     }
     trace_detail(P, l, 1, 1);
-    const float scale = 1.0f / sqrtf((float)D);
+    const float qscale = LOG2E / sqrtf((float)D);
     // Scores: the 8 lanes of group `grp` take position warp*4+grp of a chunk;
-    // lane part p owns dims 32k + 4p + e (e < 4), read as one 16-byte vector.
+    // lane part p owns dims 32k + 4p + e (e < 4), read as one vector.
     const int grp = lane >> 3, part = lane & 7;
-    float qv[MAXD][4];
+    float qv[MD][4];
 #pragma unroll
-    for (int k = 0; k < MAXD; ++k)
+    for (int k = 0; k < MD; ++k)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int j = 32 * k + 4 * part + e;
-            qv[k][e] = j < D ? sq[j] : 0.f;
+            qv[k][e] = j < D ? sq[j] * qscale : 0.f;
         }
-    float m_run = -INFINITY, l_run = 0.f, o[MAXD];
+    float m_run = -INFINITY, l_run = 0.f, o[MD];
 #pragma unroll
-    for (int k = 0; k < MAXD; ++k) o[k] = 0.f;
+    for (int k = 0; k < MD; ++k) o[k] = 0.f;
 
+    // Fill number of buffer b before this layer: every layer issues the same chunks.
+    const int nissued = ap.nissued;
     for (int c = 0; c < ap.nchunks; ++c) {
         const int c0 = ap.t0 + c * ATT_CHUNK;
         const int n = min(ATT_CHUNK, ap.t1 - c0);
         const int ncache = max(0, min(n, A.pos - c0));
-        KV* kb = reinterpret_cast<KV*>(att + (size_t)(c & 1) * P.att_chunk_bytes);
-        KV* vb = kb + (size_t)ATT_CHUNK * D;
-        if (ap.bulk) {
-            if (ncache > 0) {
-                if (!mbar_wait(mb_att + (c & 1), att_fills[c & 1] & 1u, st)) return false;
-                ++att_fills[c & 1];
-                trace_detail(P, l, 1, c == 0 ? 2 : 4);
+        const int buf = c % NB;
+        const KV* kb = reinterpret_cast<const KV*>(att + (size_t)buf * P.att_chunk_bytes);
+        const KV* vb = kb + (size_t)ATT_CHUNK * D;
+        if (ncache > 0) {
+            if (ap.bulk) {
+                const int per_layer = (nissued - buf + NB - 1) / NB;  // fills of this buffer per layer
+                const uint32_t parity = (uint32_t)(l * per_layer + c / NB) & 1u;
+                if (!mbar_wait(mb_att + buf, parity, st)) return false;
+            } else {
+                KV* kw = const_cast<KV*>(kb);
+                KV* vw = const_cast<KV*>(vb);
+                for (int e = threadIdx.x; e < ncache * D; e += NT) {
+                    const int t = e / D, j = e % D;
+                    kw[(size_t)t * D + j] = *(kv_rows<KV>(P, P.kcache, l, ap.g, c0 + t) + j);
+                    vw[(size_t)t * D + j] = *(kv_rows<KV>(P, P.vcache, l, ap.g, c0 + t) + j);
+                }
+                __syncthreads();
             }
-        } else {
-            for (int e = threadIdx.x; e < ncache * D; e += NT) {
-                const int t = e / D, j = e % D;
-                kb[(size_t)t * D + j] = *(kv_rows<KV>(P, P.kcache, l, ap.g, c0 + t) + j);
-                vb[(size_t)t * D + j] = *(kv_rows<KV>(P, P.vcache, l, ap.g, c0 + t) + j);
-            }
+            trace_detail(P, l, 1, c == 0 ? 2 : 4);
         }
-        if (has_new && A.pos >= c0 && A.pos < c0 + n) {
-            const int t = A.pos - c0;
-            for (int j = threadIdx.x; j < D; j += NT) {
-                kv_store(kb + (size_t)t * D + j, sk_new[j]);
-                kv_store(vb + (size_t)t * D + j, sk_new[D + j]);
-            }
-        }
-        __syncthreads();
         const int t = warp * ATT_PER_WARP + grp;
         float sc = 0.f;
         if (t < n) {
-            const KV* kr = kb + (size_t)t * D;
+            const bool is_new = c0 + t == A.pos;
 #pragma unroll
-            for (int k = 0; k < MAXD; ++k) {
+            for (int k = 0; k < MD; ++k) {
                 const int j0 = 32 * k + 4 * part;
+                float kk[4];
                 if (j0 + 3 < D && (D & 3) == 0) {
-                    float kk[4];
-                    load4(kr + j0, kk);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) sc = fmaf(qv[k][e], kk[e], sc);
+                    if (is_new) load4(s_new + j0, kk);
+                    else load4(kb + (size_t)t * D + j0, kk);
                 } else {
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
-                        if (j0 + e < D) sc = fmaf(qv[k][e], kv_to_float(kr[j0 + e]), sc);
+                        kk[e] = j0 + e < D ? (is_new ? s_new[j0 + e] : kv_to_float(kb[(size_t)t * D + j0 + e])) : 0.f;
                 }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) sc = fmaf(qv[k][e], kk[e], sc);
             }
         }
         sc += __shfl_xor_sync(FULL, sc, 4);
         sc += __shfl_xor_sync(FULL, sc, 2);
         sc += __shfl_xor_sync(FULL, sc, 1);
-        sc = t < n ? sc * scale : -INFINITY;
+        sc = t < n ? sc : -INFINITY;
         float cmax = fmaxf(sc, __shfl_xor_sync(FULL, sc, 8));
         cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, 16));
         if (cmax > -INFINITY) {
             const float m_new = fmaxf(m_run, cmax);
-            const float alpha = expf(m_run - m_new);
-            const float p = t < n ? expf(sc - m_new) : 0.f;
+            const float alpha = ex2_approx(m_run - m_new);
+            const float p = ex2_approx(sc - m_new);
             float psum = p + __shfl_xor_sync(FULL, p, 8);
             psum += __shfl_xor_sync(FULL, psum, 16);
-            l_run = l_run * alpha + psum;
+            l_run = fmaf(l_run, alpha, psum);
 #pragma unroll
-            for (int k = 0; k < MAXD; ++k) o[k] *= alpha;
+            for (int k = 0; k < MD; ++k) o[k] *= alpha;
 #pragma unroll
             for (int i = 0; i < ATT_PER_WARP; ++i) {
                 const float pi = __shfl_sync(FULL, p, 8 * i);
                 const int ti = warp * ATT_PER_WARP + i;
                 if (ti < n) {
+                    if (c0 + ti == A.pos) {
 #pragma unroll
-                    for (int k = 0; k < MAXD; ++k)
-                        if (lane + 32 * k < D) o[k] = fmaf(pi, kv_to_float(vb[(size_t)ti * D + lane + 32 * k]), o[k]);
+                        for (int k = 0; k < MD; ++k)
+                            if (lane + 32 * k < D) o[k] = fmaf(pi, s_new[D + lane + 32 * k], o[k]);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < MD; ++k)
+                            if (lane + 32 * k < D) o[k] = fmaf(pi, kv_to_float(vb[(size_t)ti * D + lane + 32 * k]), o[k]);
+                    }
                 }
             }
             m_run = m_new;
         }
-        __syncthreads();  // buffer c&1 consumed
         trace_detail(P, l, 1, c == 0 ? 3 : 5);
-        if (threadIdx.x == 0 && c + 2 < ap.nchunks) {
-            fence_proxy_async();
-            att_issue<KV>(P, A, ap, l, c + 2, att, mb_att, issued);
+        if (c + NB < ap.nchunks || !ap.bulk) {
+            __syncthreads();  // buffer `buf` consumed by every warp
+            if (threadIdx.x == 0 && c + NB < ap.nchunks) {
+                fence_proxy_async();
+                att_issue<KV>(P, A, ap, l, c + NB, att, mb_att, issued);
+            }
         }
     }
-    // Merge the warps' softmax states.
+    // Merge the warps' softmax states: warp w's (m, l, o) to shared memory;
+    // lanes of warps 0..ceil(D/32)-1 then weight warp w by 2^(m_w - M).
     if (lane == 0) {
         wpart[warp * (D + 2)] = m_run;
         wpart[warp * (D + 2) + 1] = l_run;
     }
 #pragma unroll
-    for (int k = 0; k < MAXD; ++k)
+    for (int k = 0; k < MD; ++k)
         if (lane + 32 * k < D) wpart[warp * (D + 2) + 2 + lane + 32 * k] = o[k];
     __syncthreads();
-    // Thread j < D merges dimension j over the warps (all threads compute M, L).
-    if (threadIdx.x < D) {
+    if (threadIdx.x < ((D + 31) & ~31)) {
         const int j = threadIdx.x;
-        float mw[NW];
-        float M = -INFINITY;
+        const float mw = lane < NW ? wpart[lane * (D + 2)] : -INFINITY;
+        float M = mw;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, off));
+        const float f = (lane < NW && mw > -INFINITY) ? ex2_approx(mw - M) : 0.f;
+        float Lsum = lane < NW ? f * wpart[lane * (D + 2) + 1] : 0.f;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) Lsum += __shfl_xor_sync(FULL, Lsum, off);
+        float acc = 0.f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
-            mw[w] = wpart[w * (D + 2)];
-            M = fmaxf(M, mw[w]);
+            const float fw = __shfl_sync(FULL, f, w);
+            if (j < D) acc = fmaf(fw, wpart[w * (D + 2) + 2 + j], acc);
         }
-        float Lsum = 0.f, acc = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            const float f = mw[w] == -INFINITY ? 0.f : expf(mw[w] - M);
-            Lsum = fmaf(f, wpart[w * (D + 2) + 1], Lsum);
-            acc = fmaf(f, wpart[w * (D + 2) + 2 + j], acc);
-        }
-        if (A.nsplit == 1) {
-            ll_store(P.ll_attn + (size_t)ap.h * D + j, acc / Lsum, tag);
-        } else {
-            float* pp = P.part + ((size_t)ap.h * A.nsplit + blockIdx.x % A.nsplit) * (D + 2);
-            if (j == 0) {
-                pp[0] = M;
-                pp[1] = Lsum;
+        if (j < D) {
+            if (A.nsplit == 1) {
+                ll_store(P.ll_attn + (size_t)ap.h * D + j, acc / Lsum, tag);
+            } else {
+                float* pp = P.part + ((size_t)ap.h * A.nsplit + blockIdx.x % A.nsplit) * (D + 2);
+                if (j == 0) {
+                    pp[0] = M;
+                    pp[1] = Lsum;
+                }
+                pp[2 + j] = acc;
             }
-            pp[2 + j] = acc;
         }
     }
     trace_detail(P, l, 1, 6);
     if (A.nsplit == 1) return true;
-    // The last split of head h to finish merges all of them.
+    // The last split of head h to finish merges all of them (m in base 2).
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -697,14 +732,14 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
         M = warp_max(M);
         float Lsum = 0.f;
         for (int i = lane; i < A.nsplit; i += 32)
-            Lsum += expf(__ldcg(base + (size_t)i * (D + 2)) - M) * __ldcg(base + (size_t)i * (D + 2) + 1);
+            Lsum += ex2_approx(__ldcg(base + (size_t)i * (D + 2)) - M) * __ldcg(base + (size_t)i * (D + 2) + 1);
         Lsum = warp_sum(Lsum);
         const float inv = 1.0f / Lsum;
         for (int j = lane; j < D; j += 32) {
             float acc = 0.f;
             for (int i = 0; i < A.nsplit; ++i) {
                 const float* pp = base + (size_t)i * (D + 2);
-                acc = fmaf(expf(__ldcg(pp) - M), __ldcg(pp + 2 + j), acc);
+                acc = fmaf(ex2_approx(__ldcg(pp) - M), __ldcg(pp + 2 + j), acc);
             }
             ll_store(P.ll_attn + (size_t)ap.h * D + j, acc * inv, tag);
         }
@@ -732,17 +767,18 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     float* gpart = reinterpret_cast<float*>(sm + P.off_gpart);  // block-GEMV partial sums, two buffers
     float* xr = reinterpret_cast<float*>(sm + P.off_xr);
     float* misc = reinterpret_cast<float*>(sm + P.off_misc);
-    constexpr int NMB = 4 + HEAD_MAX_STAGES + 2 + 2 + HEAD_MAX_STAGES;
+    // mbarriers: four weight slots, the LM-head ring, the attention ring (one
+    // arrival + bytes each), then the LM-head "stage empty" barriers (NW arrivals).
+    constexpr int MB_HEAD = 4, MB_ATT = MB_HEAD + HEAD_MAX_STAGES, MB_EMPTY = MB_ATT + ATT_MAX_BUFS;
+    constexpr int NMB = MB_EMPTY + HEAD_MAX_STAGES;
     __shared__ __align__(8) uint64_t mb[NMB];
     uint64_t* mb_gu = mb + 0;
     uint64_t* mb_down = mb + 1;
     uint64_t* mb_qkv = mb + 2;
     uint64_t* mb_o = mb + 3;
-    uint64_t* mb_head = mb + 4;
-    uint64_t* mb_att = mb + 4 + HEAD_MAX_STAGES;
-    uint64_t* mb_norm = mb + 4 + HEAD_MAX_STAGES + 2;
-    uint64_t* mb_head_empty = mb + 4 + HEAD_MAX_STAGES + 4;  // NW arrivals each
-    float* s_norms = reinterpret_cast<float*>(sm + P.off_norm);  // [2 buffers][2][Kh]
+    uint64_t* mb_head = mb + MB_HEAD;
+    uint64_t* mb_att = mb + MB_ATT;
+    uint64_t* mb_head_empty = mb + MB_EMPTY;
     __shared__ float s_cos[64], s_sin[64];
     __shared__ __align__(16) float red[2 * NW + 8];  // read as float4 in finish_stage
     __shared__ int s_abort;
@@ -771,16 +807,16 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         ap.t0 = (b % A.nsplit) * A.split_len;
         ap.t1 = min(A.pos + 1, ap.t0 + A.split_len);
         ap.nchunks = (ap.t1 - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK;
+        ap.nissued = min(ap.nchunks, max(0, (A.pos - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK));
         ap.bulk = ((size_t)D * sizeof(KV)) % 16 == 0;
     }
-    unsigned att_fills[2] = {0u, 0u};
     uint64_t head_policy = 0;
     int head_issued = 0;
 
     if (tid == 0) {
         s_abort = 0;
         for (int i = 0; i < NMB; ++i) {
-            mbar_init(mb + i, i >= 4 + HEAD_MAX_STAGES + 4 ? NW : 1);
+            mbar_init(mb + i, i >= MB_EMPTY ? NW : 1);
             s_fills[i] = 0;
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -790,10 +826,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         if (on) fill_slot(s_o, W.o + (size_t)oa * P.SH, (uint32_t)on * P.SH, mb_o, s_fills + 3);
         if (gn) fill_slot(s_gu, W.gu + (size_t)ga * 2 * P.SH, (uint32_t)gn * 2 * P.SH, mb_gu, s_fills + 0);
         if (dn) fill_slot(s_down, W.down + (size_t)da * P.SI, (uint32_t)dn * P.SI, mb_down, s_fills + 1);
-        // RMSNorm gains of layers 0 and 1 (entry L holds the final norm).
-        for (int e = 0; e < 2 && e <= P.L; ++e)
-            fill_slot(s_norms + (size_t)e * 2 * P.Kh, P.norms + (size_t)e * 2 * P.Kh, (uint32_t)(2 * P.Kh * 4),
-                      mb_norm + e, s_fills + NMB - 2 + e);
     }
     // RoPE cos/sin of this position, once per step (src/model.cpp:269-274).
     if (tid < half) {
@@ -815,7 +847,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     auto fill_head = [&](int c) {
         const int r0 = ha + c * HEAD_ROWS, rows = min(HEAD_ROWS, ha + hn - r0);
         fill_slot(sm + P.off_gu + (size_t)(c % NS) * head_stage_bytes, P.embed + (size_t)r0 * P.SH,
-                  (uint32_t)rows * P.SH, mb_head + c % NS, s_fills + 4 + c % NS, head_policy);
+                  (uint32_t)rows * P.SH, mb_head + c % NS, s_fills + MB_HEAD + c % NS, head_policy);
     };
 
     int token = A.token_dev ? __ldcg(A.token_dev) : A.token;
@@ -833,16 +865,9 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         const uint32_t tag = seq_tag | (uint32_t)(l + 1);
         const int ph = 5 * l;
 
-        // RMSNorm gains of layer l+1 into the buffer layer l-1 used.
-        if (tid == 0 && l >= 1 && l + 1 <= P.L) {
-            const int e = l + 1;
-            fence_proxy_async();
-            fill_slot(s_norms + (size_t)(e & 1) * 2 * P.Kh, P.norms + (size_t)e * 2 * P.Kh, (uint32_t)(2 * P.Kh * 4),
-                      mb_norm + (e & 1), s_fills + NMB - 2 + (e & 1));
-        }
-        const float* in_norm = s_norms + (size_t)(l & 1) * 2 * P.Kh;
+        // RMSNorm gains of layer l (global memory; read while the words are polled).
+        const float* in_norm = P.norms + (size_t)l * 2 * P.Kh;
         const float* post_norm = in_norm + P.Kh;
-        const uint32_t norm_parity = (uint32_t)(l >> 1) & 1u;
 
         // HBM has slack during the last layer: start the LM-head rows into L2.
         if (tid == 0 && A.head && l == P.L - 1)
@@ -851,23 +876,23 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // The cached KV rows do not depend on this step: start their copies now.
         if (has_att && tid == 0) {
             fence_proxy_async();  // the previous layer read and wrote these buffers
-            for (int c = 0; c < min(2, ap.nchunks); ++c)
-                att_issue<KV>(P, A, ap, l, c, s_att, mb_att, s_fills + 4 + HEAD_MAX_STAGES);
+            for (int c = 0; c < min(P.att_bufs, ap.nchunks); ++c)
+                att_issue<KV>(P, A, ap, l, c, s_att, mb_att, s_fills + MB_ATT);
         }
 
         // ---- QKV (src/model.cpp:276-302); x entering layer l carries `tag`.
         trace_detail(P, l, 0, 0);
         if (qn || on) {
             // x with the input RMSNorm gain folded in; 1/rms scales the results.
-            if (qn && !mbar_wait(mb_norm + (l & 1), norm_parity, st)) { ok = false; break; }
             Staged sx;
             if (l == 0) {
                 const uint8_t* er = P.embed + (size_t)token * P.SH;
                 const float es = row_scale(er, P.Kh);
                 float ss = 0.f, mx = 0.f;
-                for (int j = tid; j < H; j += NT) accept(j, (float)(int8_t)er[j] * es, xr, xf, in_norm, ss, mx);
+                for (int j = tid; j < H; j += NT)
+                    accept(j, (float)(int8_t)er[j] * es, xr, xf, __ldg(in_norm + j), ss, mx);
                 sx = finish_stage(H, nch_h, xf, xq, QP, ss, mx, red, P.eps);
-            } else if (!gather_stage<2>(P.ll_xa, H, tag, xr, xf, xq, QP, nch_h, in_norm, red, P.eps, sx, st)) {
+            } else if (!gather_stage<2, true>(P.ll_xa, H, tag, xr, xf, xq, QP, nch_h, in_norm, red, P.eps, sx, st)) {
                 ok = false;
                 break;
             }
@@ -924,8 +949,10 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // ---- ATTN over positions 0..pos (src/kernels.cpp:150-179)
         if (has_att) {
             trace_mark(P, 0, ph + 2);
-            if (!attention_block<KV>(P, A, ap, l, tag, s_att, mb_att, att_fills, s_fills + 4 + HEAD_MAX_STAGES, misc,
-                                     st)) {
+            const bool att_ok =
+                D == 64 ? attention_block<KV, 64>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, st)
+                        : attention_block<KV, 0>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, st);
+            if (!att_ok) {
                 ok = false;
                 break;
             }
@@ -936,7 +963,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         if (on) {
             trace_detail(P, l, 2, 0);
             Staged sa;
-            if (!gather_stage<2>(P.ll_attn, H, tag, nullptr, xf, xq, QP, nch_h, nullptr, red, P.eps, sa, st)) {
+            if (!gather_stage<2, false>(P.ll_attn, H, tag, nullptr, xf, xq, QP, nch_h, nullptr, red, P.eps, sa, st)) {
                 ok = false;
                 break;
             }
@@ -964,9 +991,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // ---- gate/up + SiLU (src/model.cpp:306-308)
         if (gn || dn) {
             trace_detail(P, l, 3, 0);
-            if (gn && !mbar_wait(mb_norm + (l & 1), norm_parity, st)) { ok = false; break; }
             Staged sb;
-            if (!gather_stage<2>(P.ll_xb, H, tag, xr, xf, xq, QP, nch_h, post_norm, red, P.eps, sb, st)) {
+            if (!gather_stage<2, true>(P.ll_xb, H, tag, xr, xf, xq, QP, nch_h, post_norm, red, P.eps, sb, st)) {
                 ok = false;
                 break;
             }
@@ -1008,8 +1034,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         if (dn) {
             trace_detail(P, l, 4, 0);
             Staged sh;
-            if (!gather_stage<10>(P.ll_h, I, tag, nullptr, xf_i, xq_i, P.down_plane, nch_i, nullptr, red, P.eps, sh,
-                                  st)) {
+            if (!gather_stage<10, false>(P.ll_h, I, tag, nullptr, xf_i, xq_i, P.down_plane, nch_i, nullptr, red, P.eps,
+                                         sh, st)) {
                 ok = false;
                 break;
             }
@@ -1048,9 +1074,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
             if (tid == 0)
                 while (head_issued < min(NS, head_chunks)) fill_head(head_issued++);
             Staged sf;
-            if (!mbar_wait(mb_norm + (P.L & 1), (uint32_t)(P.L >> 1) & 1u, st)) ok = false;
-            if (ok && !gather_stage<2>(P.ll_xa, H, seq_tag | (uint32_t)(P.L + 1), nullptr, xf, xq, QP, nch_h,
-                                       s_norms + (size_t)(P.L & 1) * 2 * P.Kh, red, P.eps, sf, st))
+            if (!gather_stage<2, true>(P.ll_xa, H, seq_tag | (uint32_t)(P.L + 1), nullptr, xf, xq, QP, nch_h,
+                                       P.norms + (size_t)P.L * 2 * P.Kh, red, P.eps, sf, st))
                 ok = false;
             const float inv = sf.inv * sf.scale;
             if (ok) {
