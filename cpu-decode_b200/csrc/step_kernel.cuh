@@ -904,7 +904,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                 trace_mark(P, 0, ph + 1);
                 trace_detail(P, l, 0, 3);
                 const int qpairs = P.NH * half, kpairs = P.NKV * half;
-                block_gemv<4, 1>(s_qkv, P.SH, 2 * qn, nch_h, xq, QP, gpart);
+                block_gemv<8, 2>(s_qkv, P.SH, 2 * qn, nch_h, xq, QP, gpart);
                 // One thread per RoPE pair (rows j, j + d/2 of a head).
                 if (tid < qn) {
                     const int w = tid, u = qa + w;
@@ -971,7 +971,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
             if (!mbar_wait(mb_o, (uint32_t)l & 1u, st)) { ok = false; break; }
             trace_mark(P, 0, ph + 3);
             trace_detail(P, l, 2, 2);
-            block_gemv<4, 1>(s_o, P.SH, on, nch_h, xq, QP, gpart);
+            block_gemv<8, 2>(s_o, P.SH, on, nch_h, xq, QP, gpart);
             if (tid < on) {
                 const int r = oa + tid;
                 ll_store(P.ll_xb + r,
@@ -1003,7 +1003,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                 if (!mbar_wait(mb_gu, (uint32_t)l & 1u, st)) { ok = false; break; }
                 trace_mark(P, 0, ph + 4);
                 trace_detail(P, l, 3, 3);
-                block_gemv<2, 5>(s_gu, P.SH, 2 * gn, nch_h, xq, QP, gpart);
+                block_gemv<1, 3>(s_gu, P.SH, 2 * gn, nch_h, xq, QP, gpart);
                 if (tid < gn) {
                     const uint8_t* r0 = s_gu + (size_t)tid * 2 * P.SH;
                     const float g = gemv_row(gpart, 2 * gn, 2 * tid) * inv * row_scale(r0, P.Kh);
@@ -1043,7 +1043,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
             if (!mbar_wait(mb_down, (uint32_t)l & 1u, st)) { ok = false; break; }
             trace_mark(P, 0, ph + 5);
             trace_detail(P, l, 4, 2);
-            block_gemv<4, 1>(s_down, P.SI, dn, nch_i, xq_i, P.down_plane, gpart);
+            block_gemv<8, 2>(s_down, P.SI, dn, nch_i, xq_i, P.down_plane, gpart);
             trace_detail(P, l, 4, 3);
             if (tid < dn) {
                 const int r = da + tid;
