@@ -317,6 +317,8 @@ def main() -> None:
     extra = {}
     if not args.no_long and rank == 0:
         extra["ctx4096"] = long_context(dcb, model, d, K, W, local)
+        extra["gemv_sweep"] = gemv_sweep(dcb)
+        extra["attention_sweep"] = attention_sweep(dcb)
 
     if rank == 0:
         line = {
@@ -377,6 +379,85 @@ def ncu_case() -> None:
     print(json.dumps({"ncu_case": "decode_step_kernel ctx 128", "launches": eng.launch_count,
                       "last_token": int(tok.item())}))
     eng.close()
+
+
+GEMV_SHAPES = [("qkv", 1152, 896, True), ("o", 896, 896, False), ("gate_up", 9728, 896, False),
+               ("down", 896, 4864, False), ("lm_head", 151936, 896, False)]
+ROTATE_BYTES = 300 << 20  # buffer copies cycled per shape: more than L2 (126 MB), so each call reads HBM
+
+
+def _timed_calls(fn, n_calls: int, warmup: int = 3) -> float:
+    """Mean device time (ms) of one fn(i) call, CUDA events on the current stream."""
+    import torch
+    for i in range(warmup):
+        fn(i)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for i in range(n_calls):
+        fn(warmup + i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / n_calls
+
+
+def gemv_sweep(dcb) -> dict:
+    """The isolated per-row int8 GEMV at the five projection shapes (int8
+    uniform [-127, 127], scales uniform [1e-4, 1e-3], x N(0,1)): algorithmic
+    bytes = rows*cols + 4*rows (scales) + 4*cols (x) + 4*rows (y) [+ 4*rows bias]."""
+    import torch
+    peak, _ = measured_peaks()
+    g = torch.Generator(device="cuda").manual_seed(1)
+    out = {}
+    for name, rows, cols, bias in GEMV_SHAPES:
+        copies = max(2, -(-ROTATE_BYTES // (rows * cols)))
+        w = [torch.randint(-127, 128, (rows, cols), dtype=torch.int8, device="cuda", generator=g) for _ in range(copies)]
+        sc = torch.rand(rows, device="cuda", generator=g) * 9e-4 + 1e-4
+        b = torch.randn(rows, device="cuda", generator=g) if bias else None
+        x = torch.randn(cols, device="cuda", generator=g)
+        y = torch.empty(rows, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def call(i):
+            dcb.gemv_i8(w[i % copies].data_ptr(), sc.data_ptr(), b.data_ptr() if bias else None, x.data_ptr(),
+                        y.data_ptr(), rows, cols, stream)
+        ms = _timed_calls(call, max(20, 2 * copies))
+        nbytes = rows * cols + 4 * rows + 4 * cols + 4 * rows + (4 * rows if bias else 0)
+        gbs = nbytes / (ms / 1000.0) / 1e9
+        out[name] = {"rows": rows, "cols": cols, "us_per_call": round(ms * 1000.0, 2), "bytes": nbytes,
+                     "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        del w
+    return out
+
+
+def attention_sweep(dcb) -> dict:
+    """Isolated GQA decode attention: 14 query heads over 2 KV heads, head_dim
+    64, one query at position L-1 with RoPE theta 1e6, q/K/V N(0,1). KV bytes =
+    L*2*2*64*{4,2}, each KV head read once for its 7 query heads."""
+    import torch
+    peak, _ = measured_peaks()
+    heads, kvh, dim = 14, 2, 64
+    g = torch.Generator(device="cuda").manual_seed(2)
+    out = {}
+    for kv, dt, es in (("f32", torch.float32, 4), ("f16", torch.float16, 2)):
+        for length in (128, 1024, 4096, 32768):
+            nbytes = length * 2 * kvh * dim * es
+            copies = max(2, -(-ROTATE_BYTES // nbytes))
+            k = [torch.randn(length, kvh * dim, device="cuda", generator=g).to(dt) for _ in range(copies)]
+            v = [torch.randn(length, kvh * dim, device="cuda", generator=g).to(dt) for _ in range(copies)]
+            q = torch.randn(heads * dim, device="cuda", generator=g)
+            o = torch.empty(heads * dim, device="cuda")
+            stream = torch.cuda.current_stream().cuda_stream
+
+            def call(i):
+                dcb.attention(q.data_ptr(), k[i % copies].data_ptr(), v[i % copies].data_ptr(), kv, o.data_ptr(),
+                              length, heads, kvh, dim, 1e6, stream)
+            ms = _timed_calls(call, max(20, 2 * copies))
+            gbs = nbytes / (ms / 1000.0) / 1e9
+            out[f"{kv}_{length}"] = {"us_per_call": round(ms * 1000.0, 2), "kv_bytes": nbytes,
+                                     "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+            del k, v
+    return out
 
 
 def long_context(dcb, model, d, K, W, device) -> dict:

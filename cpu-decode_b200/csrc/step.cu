@@ -135,7 +135,9 @@ int validate(const dcb_model_desc* m) {
 // each split covers at least split_min positions (a multiple of 64).
 void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len) {
     const int chunks = ceil_div(length, ATT_CHUNK);
-    const int n = std::max(1, std::min(ceil_div(length, e->split_min), e->grid / e->NH));
+    // Split 0 gathers the other splits' (D+2)-float partials into the chunk buffers.
+    const int table_max = 1 + e->P.att_bufs * e->P.att_chunk_bytes / (int)((e->D + 2) * sizeof(float));
+    const int n = std::max(1, std::min({ceil_div(length, e->split_min), e->grid / e->NH, table_max}));
     *split_len = ceil_div(chunks, n) * ATT_CHUNK;
     *nsplit = ceil_div(length, *split_len);
 }
@@ -159,7 +161,6 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
 int device_error(dcb_engine* e, int err) {
     if (!err) return 0;
     DCB_CUDA(cudaMemset(e->P.sync, 0, sizeof(Sync)));
-    DCB_CUDA(cudaMemset(e->P.head_done, 0, sizeof(unsigned) * e->NH));
     if (err == ERR_TOKEN) return fail(DCB_ERR_TOKEN, "token ID outside vocabulary");
     return fail(DCB_ERR_DEVICE_WAIT, "a device-side wait ran out of time; the step was abandoned");
 }
@@ -313,8 +314,7 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     if (int rc = e->alloc(&P.ll_kv, 2 * e->NKV * D)) return bail(rc);
     if (int rc = e->alloc(&P.ll_attn, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_h, I)) return bail(rc);
-    if (int rc = e->alloc(&P.part, (size_t)e->NH * (G + 1) * (D + 2))) return bail(rc);
-    if (int rc = e->alloc(&P.head_done, e->NH)) return bail(rc);
+    if (int rc = e->alloc(&P.ll_part, (size_t)e->NH * (G + 1) * (D + 2))) return bail(rc);
     if (int rc = e->alloc(&P.logits, e->V)) return bail(rc);
     if (int rc = e->alloc(&P.amax, G)) return bail(rc);
     if (int rc = e->alloc(&P.sync, 1)) return bail(rc);

@@ -84,8 +84,7 @@ struct Params {
     uint64_t* ll_kv;    // [2*NKV*D] the new K and V rows
     uint64_t* ll_attn;  // [H]   attention output
     uint64_t* ll_h;     // [I]   SiLU(gate)*up
-    float* part;          // [NH][nsplit][D+2] attention split partials
-    unsigned* head_done;  // [NH] split arrival counters
+    uint64_t* ll_part;    // [NH][nsplit][D+2] tagged attention split partials (m, l, o)
     float* logits;        // [V]
     ArgBest* amax;        // [grid]
     Sync* sync;
@@ -130,8 +129,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* m) {
 __device__ __forceinline__ void mbar_expect(uint64_t* m, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
 }
+// Phase `parity` of m complete? test_wait answers at once (a completed phase
+// costs about a shared-memory load); try_wait may first suspend the thread
+// for a while, which suits a phase that is still running.
 __device__ __forceinline__ bool mbar_test(uint64_t* m, uint32_t parity) {
     uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(m)), "r"(parity)
+        : "memory");
+    if (ok) return true;
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
         : "=r"(ok)
@@ -405,7 +413,7 @@ __device__ __forceinline__ void load_planes(const int8_t* xq, int plane, int c, 
 // by Staged::scale). Rows are 912 or 4880 bytes apart, so the lanes' 16-byte
 // reads of different rows fall in distinct banks.
 template <int LPR, int P>
-__device__ void block_gemv(const uint8_t* rows, int S, int R, int nch, const int8_t* xq, int plane, float* partial) {
+__device__ __noinline__ void block_gemv(const uint8_t* rows, int S, int R, int nch, const int8_t* xq, int plane, float* partial) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c0 = warp * nch / NW, c1 = (warp + 1) * nch / NW;
     const int sub = lane % LPR, slot = lane / LPR;
@@ -546,7 +554,6 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
     float* sq = misc;                      // [D]
     float* s_new = misc + 128;             // [2][D] new K and V rows of group g (rounded to KV)
     float* wpart = misc + 384;             // [NW][D+2]: m, l, o of each warp
-    __shared__ int s_last;
     const bool has_new = ap.t0 <= A.pos && A.pos < ap.t1;
     trace_detail(P, l, 1, 0);
     {
@@ -685,6 +692,8 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
     for (int k = 0; k < MD; ++k)
         if (lane + 32 * k < D) wpart[warp * (D + 2) + 2 + lane + 32 * k] = o[k];
     __syncthreads();
+    const int split = blockIdx.x % A.nsplit;
+    float own_m = 0.f, own_l = 0.f, own_acc = 0.f;  // split 0 of several: its own partial (threads j < D)
     if (threadIdx.x < ((D + 31) & ~31)) {
         const int j = threadIdx.x;
         const float mw = lane < NW ? wpart[lane * (D + 2)] : -INFINITY;
@@ -704,46 +713,74 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
         if (j < D) {
             if (A.nsplit == 1) {
                 ll_store(P.ll_attn + (size_t)ap.h * D + j, acc / Lsum, tag);
+            } else if (split == 0) {
+                own_m = M;
+                own_l = Lsum;
+                own_acc = acc;
             } else {
-                float* pp = P.part + ((size_t)ap.h * A.nsplit + blockIdx.x % A.nsplit) * (D + 2);
+                // (m, l, unnormalised o) of this split as tagged words for split 0.
+                uint64_t* pw = P.ll_part + ((size_t)ap.h * A.nsplit + split) * (D + 2);
+                ll_store(pw + 2 + j, acc, tag);
                 if (j == 0) {
-                    pp[0] = M;
-                    pp[1] = Lsum;
+                    ll_store(pw, M, tag);
+                    ll_store(pw + 1, Lsum, tag);
                 }
-                pp[2 + j] = acc;
             }
         }
     }
     trace_detail(P, l, 1, 6);
-    if (A.nsplit == 1) return true;
-    // The last split of head h to finish merges all of them (m in base 2).
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(P.head_done + ap.h, 1u);
-        s_last = prev == (unsigned)A.nsplit - 1;
-        if (s_last) __threadfence();
-    }
-    __syncthreads();
-    if (s_last && warp == 0) {
-        const float* base = P.part + (size_t)ap.h * A.nsplit * (D + 2);
-        float M = -INFINITY;
-        for (int i = lane; i < A.nsplit; i += 32) M = fmaxf(M, __ldcg(base + (size_t)i * (D + 2)));
-        M = warp_max(M);
-        float Lsum = 0.f;
-        for (int i = lane; i < A.nsplit; i += 32)
-            Lsum += ex2_approx(__ldcg(base + (size_t)i * (D + 2)) - M) * __ldcg(base + (size_t)i * (D + 2) + 1);
-        Lsum = warp_sum(Lsum);
-        const float inv = 1.0f / Lsum;
-        for (int j = lane; j < D; j += 32) {
-            float acc = 0.f;
-            for (int i = 0; i < A.nsplit; ++i) {
-                const float* pp = base + (size_t)i * (D + 2);
-                acc = fmaf(ex2_approx(__ldcg(pp) - M), __ldcg(pp + 2 + j), acc);
+    if (A.nsplit == 1 || split != 0) return true;
+    // Split 0 merges the others (m in base 2): thread t polls words t, t + NT,
+    // ... of their (nsplit-1)*(D+2)-word table, all loads in flight, into the
+    // chunk buffers (consumed by now); then thread j < D combines dimension j
+    // in split order.
+    {
+        const int nwords = (A.nsplit - 1) * (D + 2);
+        const uint64_t* src = P.ll_part + ((size_t)ap.h * A.nsplit + 1) * (D + 2);
+        float* table = reinterpret_cast<float*>(att);
+        constexpr int WT = 4;
+        for (int base = 0; base < nwords; base += WT * NT) {
+            uint64_t w[WT];
+            unsigned pending = 0;
+#pragma unroll
+            for (int k = 0; k < WT; ++k) {
+                const int i = base + threadIdx.x + k * NT;
+                if (i < nwords) {
+                    w[k] = ll_load(src + i);
+                    pending |= 1u << k;
+                }
             }
-            ll_store(P.ll_attn + (size_t)ap.h * D + j, acc * inv, tag);
+            uint64_t t0 = 0;
+            unsigned rounds = 0;
+            while (true) {
+#pragma unroll
+                for (int k = 0; k < WT; ++k)
+                    if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
+                        table[base + threadIdx.x + k * NT] = __uint_as_float((uint32_t)w[k]);
+                        pending &= ~(1u << k);
+                    }
+                if (!pending) break;
+                if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+#pragma unroll
+                for (int k = 0; k < WT; ++k)
+                    if ((pending >> k) & 1u) w[k] = ll_load(src + base + threadIdx.x + k * NT);
+            }
         }
-        if (lane == 0) P.head_done[ap.h] = 0;
+        __syncthreads();
+        if (should_abort(st)) return false;
+        if ((int)threadIdx.x < D) {
+            const int j = threadIdx.x;
+            float Mx = own_m;
+            for (int i = 0; i + 1 < A.nsplit; ++i) Mx = fmaxf(Mx, table[i * (D + 2)]);
+            const float f0 = ex2_approx(own_m - Mx);
+            float num = f0 * own_acc, den = f0 * own_l;
+            for (int i = 0; i + 1 < A.nsplit; ++i) {
+                const float f = ex2_approx(table[i * (D + 2)] - Mx);
+                num = fmaf(f, table[i * (D + 2) + 2 + j], num);
+                den = fmaf(f, table[i * (D + 2) + 1], den);
+            }
+            ll_store(P.ll_attn + (size_t)ap.h * D + j, num / den, tag);
+        }
     }
     return true;
 }
