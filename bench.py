@@ -386,8 +386,10 @@ GEMV_SHAPES = [("qkv", 1152, 896, True), ("o", 896, 896, False), ("gate_up", 972
 ROTATE_BYTES = 300 << 20  # buffer copies cycled per shape: more than L2 (126 MB), so each call reads HBM
 
 
-def _timed_calls(fn, n_calls: int, warmup: int = 3) -> float:
-    """Mean device time (ms) of one fn(i) call, CUDA events on the current stream."""
+def _timed_calls(fn, n_calls: int, warmup: int = 3) -> tuple[float, float]:
+    """Mean device time (ms) of one fn(i) call, CUDA events on the current
+    stream: issued one by one, and replayed as a CUDA graph of n_calls
+    back-to-back calls (no host launch cost)."""
     import torch
     for i in range(warmup):
         fn(i)
@@ -398,7 +400,20 @@ def _timed_calls(fn, n_calls: int, warmup: int = 3) -> float:
         fn(warmup + i)
     e.record()
     torch.cuda.synchronize()
-    return s.elapsed_time(e) / n_calls
+    eager = s.elapsed_time(e) / n_calls
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.current_stream()):
+        for i in range(n_calls):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    s.record()
+    graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    graphed = s.elapsed_time(e) / n_calls
+    del graph
+    return eager, graphed
 
 
 def gemv_sweep(dcb) -> dict:
@@ -421,10 +436,11 @@ def gemv_sweep(dcb) -> dict:
         def call(i):
             dcb.gemv_i8(w[i % copies].data_ptr(), sc.data_ptr(), b.data_ptr() if bias else None, x.data_ptr(),
                         y.data_ptr(), rows, cols, stream)
-        ms = _timed_calls(call, max(20, 2 * copies))
+        ms, ms_graph = _timed_calls(call, max(20, 2 * copies))
         nbytes = rows * cols + 4 * rows + 4 * cols + 4 * rows + (4 * rows if bias else 0)
-        gbs = nbytes / (ms / 1000.0) / 1e9
-        out[name] = {"rows": rows, "cols": cols, "us_per_call": round(ms * 1000.0, 2), "bytes": nbytes,
+        gbs = nbytes / (ms_graph / 1000.0) / 1e9
+        out[name] = {"rows": rows, "cols": cols, "us_per_call": round(ms_graph * 1000.0, 2),
+                     "us_per_call_eager": round(ms * 1000.0, 2), "bytes": nbytes,
                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
         del w
     return out
@@ -452,9 +468,10 @@ def attention_sweep(dcb) -> dict:
             def call(i):
                 dcb.attention(q.data_ptr(), k[i % copies].data_ptr(), v[i % copies].data_ptr(), kv, o.data_ptr(),
                               length, heads, kvh, dim, 1e6, stream)
-            ms = _timed_calls(call, max(20, 2 * copies))
-            gbs = nbytes / (ms / 1000.0) / 1e9
-            out[f"{kv}_{length}"] = {"us_per_call": round(ms * 1000.0, 2), "kv_bytes": nbytes,
+            ms, ms_graph = _timed_calls(call, max(20, 2 * copies))
+            gbs = nbytes / (ms_graph / 1000.0) / 1e9
+            out[f"{kv}_{length}"] = {"us_per_call": round(ms_graph * 1000.0, 2),
+                                     "us_per_call_eager": round(ms * 1000.0, 2), "kv_bytes": nbytes,
                                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
             del k, v
     return out

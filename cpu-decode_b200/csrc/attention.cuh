@@ -1,177 +1,337 @@
-// Split-KV GQA decode attention for one query position, executed by one
-// thread block per (KV head, KV split). Follows the reference's softmax
-// attention (src/kernels.cpp:150-179): scores q.k * (1/sqrt(d)), max-subtracted
-// exp, normalised, times V. Each split keeps a running (max, sum, unnormalised
-// output) over 64-position chunks staged in shared memory; splits are merged
-// with a log-sum-exp combine by the last block of the KV group to finish.
+// Split-KV GQA decode attention for one query position (the isolated
+// operator): one thread block per (KV head, KV split) takes all query heads
+// of its group over the split's positions, so each staged K/V byte serves every
+// head of the group. Follows the reference's softmax attention
+// (src/kernels.cpp:150-179): scores q.k / sqrt(d), max-subtracted exp,
+// normalised, times V; here in base 2 (scores scaled by log2(e)/sqrt(d), ex2).
+// K/V arrive in 64-position chunks, double-buffered with 16-byte cp.async.
+// With several splits, attention_combine_kernel merges the per-split
+// (max, sum, unnormalised output) in split order.
 #pragma once
 #include "device.cuh"
 
 namespace dcb {
 
-constexpr int KV_CHUNK = 64;
-
-// Shared-memory floats needed by attention_unit for head_dim d and g query
-// heads per KV head.
-__host__ __device__ constexpr int attention_smem_floats(int d, int g) {
-    return 2 * KV_CHUNK * (d + 1) + g * d + 4;
-}
+constexpr int AT_NT = 512;       // threads per block
+constexpr int AT_NW = AT_NT / 32;
+constexpr int AT_T = 64;         // positions per staged chunk (4 per warp, 8 lanes each)
+constexpr int AT_GH = 8;         // query heads per pass over the split
+constexpr int AT_MAXD = 4;       // head_dim <= 128: lane owns dims lane + 32k
 
 struct AttnIO {
-    const float* q;        // [heads*d] query, already rotated unless rope_inv != nullptr
-    const float* rope_inv; // optional: rotate q by pos*rope_inv[j] while staging
-    int rope_pos;
-    const void* keys;      // [length][kv_heads*d] (this layer)
+    const float* q;       // [heads*d] query
+    const void* keys;     // [length][kv_heads*d] rows of KV
     const void* values;
-    float* out;            // [heads*d]
-    float* part;           // [heads][nsplit][d+2] partials when nsplit > 1
-    unsigned* group_done;  // [kv_heads] arrival counters (zero between uses)
+    float* out;           // [heads*d]
+    float* part;          // [heads][nsplit][d+2] (max, sum, output) per split when nsplit > 1
+    float rope_theta;     // > 0: rotate q (split halves) by position length-1 while staging
     int heads, kv_heads, d, length, nsplit, split_len;
 };
 
-// One (KV head g, split s) unit. Block-uniform control flow; uses all warps.
-template <typename KV>
-__device__ void attention_unit(const AttnIO& io, int g, int s, float* sm) {
-    const int d = io.d, gq = io.heads / io.kv_heads, kvd = io.kv_heads * d;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int ld = d + 1;  // padded row: lane-per-position reads hit distinct banks
-    float* sK = sm;
-    float* sV = sK + KV_CHUNK * ld;
-    float* sQ = sV + KV_CHUNK * ld;
-    __shared__ int s_last;
-    const KV* kb = static_cast<const KV*>(io.keys);
-    const KV* vb = static_cast<const KV*>(io.values);
-    const int t0 = s * io.split_len;
-    const int t1 = min(io.length, t0 + io.split_len);
-    const float scale = 1.0f / sqrtf((float)d);
+// Dynamic shared memory of attention_split_kernel for head_dim d, KV element
+// size es and gq query heads per KV head.
+__host__ __device__ constexpr size_t attention_smem_bytes(int d, int es, int gq) {
+    return 2 * 2 * (size_t)AT_T * d * es                       // two chunk buffers of K and V rows
+           + (size_t)gq * d * sizeof(float)                    // scaled queries
+           + (size_t)AT_NW * AT_GH * (d + 2) * sizeof(float);  // warp partials of a head pass
+}
 
-    __syncthreads();  // the previous unit of this block is done with shared memory
-    // Stage the group's queries (rotating them when asked).
-    for (int e = threadIdx.x; e < gq * d; e += blockDim.x) {
-        const int hl = e / d, j = e % d, h = g * gq + hl;
-        float v = __ldcg(io.q + h * d + j);
-        if (io.rope_inv) {
-            const int half = d / 2, jj = j < half ? j : j - half;
-            const float a = __ldcg(io.q + h * d + jj), b = __ldcg(io.q + h * d + jj + half);
-            const float angle = __fmul_rn((float)io.rope_pos, io.rope_inv[jj]);
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ float at_ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ void at_load4(const float* p, float (&o)[4]) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    o[0] = v.x, o[1] = v.y, o[2] = v.z, o[3] = v.w;
+}
+__device__ __forceinline__ void at_load4(const __half* p, float (&o)[4]) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    o[0] = a.x, o[1] = a.y, o[2] = b.x, o[3] = b.y;
+}
+__device__ __forceinline__ float at_float(float v) { return v; }
+__device__ __forceinline__ float at_float(__half v) { return __half2float(v); }
+
+// DT: head_dim known at compile time (64), or 0 for any even head_dim <= 128.
+template <typename KV, int DT>
+__global__ void __launch_bounds__(AT_NT) attention_split_kernel(AttnIO io) {
+    extern __shared__ __align__(16) unsigned char at_sm[];
+    constexpr int MD = DT ? (DT + 31) / 32 : AT_MAXD;
+    const int D = DT ? DT : io.d;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = blockIdx.x / io.nsplit, s = blockIdx.x % io.nsplit;
+    const int gq = io.heads / io.kv_heads, kvd = io.kv_heads * D;
+    const int t0 = s * io.split_len, t1 = min(io.length, t0 + io.split_len);
+    const int nchunks = (t1 - t0 + AT_T - 1) / AT_T;
+    const size_t buf_elems = 2 * (size_t)AT_T * D;  // K rows then V rows
+    KV* bufs = reinterpret_cast<KV*>(at_sm);
+    float* sq = reinterpret_cast<float*>(at_sm + 2 * buf_elems * sizeof(KV));
+    float* wpart = sq + gq * D;  // [AT_NW][AT_GH][D+2]
+    const KV* kg = static_cast<const KV*>(io.keys) + (size_t)g * D;
+    const KV* vg = static_cast<const KV*>(io.values) + (size_t)g * D;
+    // 16-byte copies need 16-byte rows and bases; otherwise plain loads.
+    const bool async16 = (D * sizeof(KV)) % 16 == 0 && (kvd * sizeof(KV)) % 16 == 0 &&
+                         (reinterpret_cast<uintptr_t>(kg) & 15) == 0 && (reinterpret_cast<uintptr_t>(vg) & 15) == 0;
+
+    auto issue = [&](int c) {
+        const int c0 = t0 + c * AT_T, n = min(AT_T, t1 - c0);
+        KV* kb = bufs + (size_t)(c & 1) * buf_elems;
+        KV* vb = kb + (size_t)AT_T * D;
+        if (async16) {
+            constexpr int EP = 16 / sizeof(KV);  // elements per 16-byte piece
+            const int pieces = D / EP;
+            for (int e = threadIdx.x; e < n * pieces; e += AT_NT) {
+                const int t = e / pieces, pc = e - t * pieces;
+                const size_t src = (size_t)(c0 + t) * kvd + (size_t)pc * EP;
+                cp_async16(kb + (size_t)t * D + pc * EP, kg + src);
+                cp_async16(vb + (size_t)t * D + pc * EP, vg + src);
+            }
+        } else {
+            for (int e = threadIdx.x; e < n * D; e += AT_NT) {
+                const int t = e / D, j = e - t * D;
+                kb[(size_t)t * D + j] = kg[(size_t)(c0 + t) * kvd + j];
+                vb[(size_t)t * D + j] = vg[(size_t)(c0 + t) * kvd + j];
+            }
+        }
+        cp_async_commit();
+    };
+
+    // Queries of the group, rotated at position length-1 when asked (cached
+    // angle formula of src/model.cpp:222-224,271), scaled by log2(e)/sqrt(D).
+    const float qscale = 1.4426950408889634f / sqrtf((float)D);
+    for (int e = threadIdx.x; e < gq * D; e += AT_NT) {
+        const int hl = e / D, j = e - hl * D;
+        const float* qh = io.q + (size_t)(g * gq + hl) * D;
+        float v = qh[j];
+        if (io.rope_theta > 0.f) {
+            const int half = D / 2, jj = j < half ? j : j - half;
+            const float inv = 1.0f / powf(io.rope_theta, (float)(2 * jj) / (float)D);
+            const float angle = __fmul_rn((float)(io.length - 1), inv);
             float sn, cs;
             sincosf(angle, &sn, &cs);
-            v = j < half ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn))
-                         : __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+            const float a = qh[jj], b = qh[jj + half];
+            v = j < half ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
         }
-        sQ[hl * d + j] = v;
+        sq[e] = v * qscale;
     }
 
-    // Per warp: one query head at a time (gq <= nwarps in practice; loop otherwise).
-    constexpr int MAXD = 4;  // d <= 128: dims lane + 32*k
-    for (int hb = 0; hb < gq; hb += nwarps) {
-        const int hl = hb + warp;
-        const bool active = hl < gq;
-        float m_run = -INFINITY, l_run = 0.f;
-        float o[MAXD];
+    const int grp = lane >> 3, part = lane & 7;
+    for (int hb = 0; hb < gq; hb += AT_GH) {
+        const int nh = min(AT_GH, gq - hb);
+        float m_run[AT_GH], l_run[AT_GH], o[AT_GH][MD];
 #pragma unroll
-        for (int k = 0; k < MAXD; ++k) o[k] = 0.f;
-        for (int c0 = t0; c0 < t1; c0 += KV_CHUNK) {
-            const int n = min(KV_CHUNK, t1 - c0);
-            __syncthreads();  // previous chunk fully consumed (and sQ written)
-            for (int e = threadIdx.x; e < n * d; e += blockDim.x) {
-                const int t = e / d, j = e % d;
-                const size_t off = (size_t)(c0 + t) * kvd + (size_t)g * d + j;
-                sK[t * ld + j] = kv_load(kb + off);
-                sV[t * ld + j] = kv_load(vb + off);
+        for (int hh = 0; hh < AT_GH; ++hh) {
+            m_run[hh] = -INFINITY;
+            l_run[hh] = 0.f;
+#pragma unroll
+            for (int k = 0; k < MD; ++k) o[hh][k] = 0.f;
+        }
+        __syncthreads();  // queries staged; the previous pass is done with the buffers
+        issue(0);
+        for (int c = 0; c < nchunks; ++c) {
+            if (c + 1 < nchunks) {
+                issue(c + 1);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
             }
             __syncthreads();
-            if (active) {
-                const float* qh = sQ + hl * d;
-                float sc[2];
+            const int c0 = t0 + c * AT_T, n = min(AT_T, t1 - c0);
+            const KV* kb = bufs + (size_t)(c & 1) * buf_elems;
+            const KV* vb = kb + (size_t)AT_T * D;
+            const int t = warp * 4 + grp;
+            // This lane's K dims of position t: 32k + 4*part + e.
+            float kk[MD][4];
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int t = lane + 32 * i;
-                    float dot = 0.f;
-                    if (t < n) {
-                        const float* kr = sK + t * ld;
-                        for (int j = 0; j < d; ++j) dot = fmaf(qh[j], kr[j], dot);
-                        sc[i] = dot * scale;
-                    } else {
-                        sc[i] = -INFINITY;
+            for (int k = 0; k < MD; ++k) {
+                const int j0 = 32 * k + 4 * part;
+                if (t < n && j0 + 3 < D && (D & 3) == 0) {
+                    at_load4(kb + (size_t)t * D + j0, kk[k]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) kk[k][e] = (t < n && j0 + e < D) ? at_float(kb[(size_t)t * D + j0 + e]) : 0.f;
+                }
+            }
+            float p[AT_GH];
+#pragma unroll
+            for (int hh = 0; hh < AT_GH; ++hh) {
+                p[hh] = 0.f;
+                if (hh < nh) {
+                    const float* qh = sq + (size_t)(hb + hh) * D;
+                    float sc = 0.f;
+#pragma unroll
+                    for (int k = 0; k < MD; ++k) {
+                        const int j0 = 32 * k + 4 * part;
+                        if (j0 + 3 < D && (D & 3) == 0) {
+                            float qv[4];
+                            at_load4(qh + j0, qv);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) sc = fmaf(qv[e], kk[k][e], sc);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                if (j0 + e < D) sc = fmaf(qh[j0 + e], kk[k][e], sc);
+                        }
+                    }
+                    sc += __shfl_xor_sync(FULL, sc, 4);
+                    sc += __shfl_xor_sync(FULL, sc, 2);
+                    sc += __shfl_xor_sync(FULL, sc, 1);
+                    sc = t < n ? sc : -INFINITY;
+                    float cmax = fmaxf(sc, __shfl_xor_sync(FULL, sc, 8));
+                    cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, 16));
+                    if (cmax > -INFINITY) {
+                        const float m_new = fmaxf(m_run[hh], cmax);
+                        const float alpha = at_ex2(m_run[hh] - m_new);
+                        p[hh] = at_ex2(sc - m_new);
+                        float psum = p[hh] + __shfl_xor_sync(FULL, p[hh], 8);
+                        psum += __shfl_xor_sync(FULL, psum, 16);
+                        l_run[hh] = fmaf(l_run[hh], alpha, psum);
+#pragma unroll
+                        for (int k = 0; k < MD; ++k) o[hh][k] *= alpha;
+                        m_run[hh] = m_new;
                     }
                 }
-                const float m_new = fmaxf(m_run, warp_max(fmaxf(sc[0], sc[1])));
-                const float alpha = expf(m_run - m_new);
-                float p[2];
+            }
+            // V rows of this warp's 4 positions, each read once for all heads.
 #pragma unroll
-                for (int i = 0; i < 2; ++i) p[i] = (lane + 32 * i < n) ? expf(sc[i] - m_new) : 0.f;
-                l_run = l_run * alpha + warp_sum(p[0] + p[1]);
+            for (int i = 0; i < 4; ++i) {
+                const int ti = warp * 4 + i;
+                if (ti < n) {
+                    float vr[MD];
 #pragma unroll
-                for (int k = 0; k < MAXD; ++k) o[k] *= alpha;
-                for (int t = 0; t < n; ++t) {
-                    const float pt = __shfl_sync(FULL, p[t >> 5], t & 31);
-                    const float* vr = sV + t * ld;
+                    for (int k = 0; k < MD; ++k)
+                        vr[k] = lane + 32 * k < D ? at_float(vb[(size_t)ti * D + lane + 32 * k]) : 0.f;
 #pragma unroll
-                    for (int k = 0; k < MAXD; ++k) {
-                        const int j = lane + 32 * k;
-                        if (j < d) o[k] = fmaf(pt, vr[j], o[k]);
+                    for (int hh = 0; hh < AT_GH; ++hh) {
+                        const float pi = __shfl_sync(FULL, p[hh], 8 * i);
+                        if (hh < nh) {
+#pragma unroll
+                            for (int k = 0; k < MD; ++k) o[hh][k] = fmaf(pi, vr[k], o[hh][k]);
+                        }
                     }
                 }
-                m_run = m_new;
+            }
+            __syncthreads();  // buffer c & 1 consumed before chunk c + 2 is issued into it
+        }
+        // Merge the warps: warp w's (m, l, o) per head to shared memory, then
+        // thread (hh, j) weights warp w by 2^(m_w - M).
+#pragma unroll
+        for (int hh = 0; hh < AT_GH; ++hh) {
+            if (hh < nh) {
+                float* wp = wpart + ((size_t)warp * AT_GH + hh) * (D + 2);
+                if (lane == 0) {
+                    wp[0] = m_run[hh];
+                    wp[1] = l_run[hh];
+                }
+#pragma unroll
+                for (int k = 0; k < MD; ++k)
+                    if (lane + 32 * k < D) wp[2 + lane + 32 * k] = o[hh][k];
             }
         }
-        if (active) {
-            const int h = g * gq + hl;
+        __syncthreads();
+        for (int e = threadIdx.x; e < nh * D; e += AT_NT) {
+            const int hh = e / D, j = e - hh * D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < AT_NW; ++w) M = fmaxf(M, wpart[((size_t)w * AT_GH + hh) * (D + 2)]);
+            float L = 0.f, acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < AT_NW; ++w) {
+                const float* wp = wpart + ((size_t)w * AT_GH + hh) * (D + 2);
+                const float f = wp[0] > -INFINITY ? at_ex2(wp[0] - M) : 0.f;
+                L = fmaf(f, wp[1], L);
+                acc = fmaf(f, wp[2 + j], acc);
+            }
+            const int h = g * gq + hb + hh;
             if (io.nsplit == 1) {
-                const float inv = 1.0f / l_run;
-#pragma unroll
-                for (int k = 0; k < MAXD; ++k) {
-                    const int j = lane + 32 * k;
-                    if (j < d) io.out[h * d + j] = o[k] * inv;
-                }
+                io.out[(size_t)h * D + j] = acc / L;
             } else {
-                float* pp = io.part + ((size_t)h * io.nsplit + s) * (d + 2);
-                if (lane == 0) { pp[0] = m_run; pp[1] = l_run; }
-#pragma unroll
-                for (int k = 0; k < MAXD; ++k) {
-                    const int j = lane + 32 * k;
-                    if (j < d) pp[2 + j] = o[k];
+                float* pp = io.part + ((size_t)h * io.nsplit + s) * (D + 2);
+                if (j == 0) {
+                    pp[0] = M;
+                    pp[1] = L;
                 }
+                pp[2 + j] = acc;
             }
         }
     }
-    if (io.nsplit == 1) return;
+}
 
-    // Last block of this KV group to finish merges all splits of its heads.
+// Merge the splits of head blockIdx.x: out[j] = sum_s 2^(m_s - M) o_s[j] /
+// sum_s 2^(m_s - M) l_s. Every load a thread needs is issued before the
+// reductions: thread i < nsplit takes split i's (m, l); thread (q, j) of group
+// q (groups of d threads) takes o_s[j] of splits q, q + ngroups, ... (up to
+// AT_CU of them in registers; more splits loop).
+constexpr int AT_CU = 24;
+__global__ void __launch_bounds__(AT_NT) attention_combine_kernel(AttnIO io) {
+    __shared__ float s_w[1024];  // 2^(m_s - M) per split (nsplit <= 1024)
+    __shared__ float s_red[AT_NT];
+    const int h = blockIdx.x, D = io.d, ns = io.nsplit;
+    const float* base = io.part + (size_t)h * ns * (D + 2);
+    const int ngroups = AT_NT / D;
+    const int j = threadIdx.x % D, q = threadIdx.x / D;
+    float ov[AT_CU];
+#pragma unroll
+    for (int u = 0; u < AT_CU; ++u) {
+        const int i = q + u * ngroups;
+        ov[u] = (q < ngroups && i < ns) ? base[(size_t)i * (D + 2) + 2 + j] : 0.f;
+    }
+    float mi = -INFINITY, li = 0.f;
+    if ((int)threadIdx.x < ns) {
+        mi = base[(size_t)threadIdx.x * (D + 2)];
+        li = base[(size_t)threadIdx.x * (D + 2) + 1];
+    }
+    float m = mi;
+    for (int i = threadIdx.x + AT_NT; i < ns; i += AT_NT) m = fmaxf(m, base[(size_t)i * (D + 2)]);
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(io.group_done + g, 1u);
-        s_last = (prev == (unsigned)io.nsplit - 1);
-        if (s_last) __threadfence();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < AT_NW; ++w) M = fmaxf(M, s_red[w]);
+    float lsum = 0.f;
+    for (int i = threadIdx.x; i < ns; i += AT_NT) {
+        const bool own = i == (int)threadIdx.x;
+        const float f = at_ex2((own ? mi : base[(size_t)i * (D + 2)]) - M);
+        s_w[i] = f;
+        lsum = fmaf(f, own ? li : base[(size_t)i * (D + 2) + 1], lsum);
+    }
+    lsum = warp_sum(lsum);
+    __syncthreads();  // s_red's maxima read by every thread before it is reused
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = lsum;
+    __syncthreads();
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < AT_NW; ++w) L += s_red[w];
+    float acc = 0.f;
+    if (q < ngroups) {
+#pragma unroll
+        for (int u = 0; u < AT_CU; ++u) {
+            const int i = q + u * ngroups;
+            if (i < ns) acc = fmaf(s_w[i], ov[u], acc);
+        }
+        for (int i = q + AT_CU * ngroups; i < ns; i += ngroups) acc = fmaf(s_w[i], base[(size_t)i * (D + 2) + 2 + j], acc);
     }
     __syncthreads();
-    if (!s_last) return;
-    for (int hl = warp; hl < gq; hl += nwarps) {
-        const int h = g * gq + hl;
-        const float* base = io.part + (size_t)h * io.nsplit * (d + 2);
-        float m = -INFINITY;
-        for (int i = lane; i < io.nsplit; i += 32) m = fmaxf(m, __ldcg(base + (size_t)i * (d + 2)));
-        m = warp_max(m);
-        float lsum = 0.f;
-        for (int i = lane; i < io.nsplit; i += 32) {
-            const float* pp = base + (size_t)i * (d + 2);
-            lsum += expf(__ldcg(pp) - m) * __ldcg(pp + 1);
-        }
-        lsum = warp_sum(lsum);
-        const float inv = 1.0f / lsum;
-        for (int j = lane; j < d; j += 32) {
-            float acc = 0.f;
-            for (int i = 0; i < io.nsplit; ++i) {
-                const float* pp = base + (size_t)i * (d + 2);
-                acc = fmaf(expf(__ldcg(pp) - m), __ldcg(pp + 2 + j), acc);
-            }
-            io.out[h * d + j] = acc * inv;
-        }
-    }
+    s_red[threadIdx.x] = acc;
     __syncthreads();
-    if (threadIdx.x == 0) io.group_done[g] = 0;  // ready for the next use
+    if ((int)threadIdx.x < D) {
+        float t = 0.f;
+        for (int k = 0; k < ngroups; ++k) t += s_red[k * D + threadIdx.x];
+        io.out[(size_t)h * D + threadIdx.x] = t / L;
+    }
 }
 
 }  // namespace dcb

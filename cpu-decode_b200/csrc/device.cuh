@@ -92,80 +92,54 @@ __device__ __forceinline__ float2 dot4(uint32_t w, float4 x, float2 acc) {
     return acc;
 }
 
-// An activation vector staged in shared memory for 16-byte weight chunks:
-// chunk c (weights 16c..16c+15) multiplies xs4[k*nch + c] for k = 0..3, so a
-// warp reading consecutive chunks reads consecutive float4s (no bank conflicts).
-__device__ __forceinline__ float2 dot16(int4 w, const float4* xs4, int nch, int c, float2 acc) {
-    acc = dot4((uint32_t)w.x, xs4[c], acc);
-    acc = dot4((uint32_t)w.y, xs4[nch + c], acc);
-    acc = dot4((uint32_t)w.z, xs4[2 * nch + c], acc);
-    acc = dot4((uint32_t)w.w, xs4[3 * nch + c], acc);
-    return acc;
+// ---- 24-bit fixed point for exact dp4a dot products --------------------------------
+// A vector v is staged with scale s = max|v| / FIX_MAX as q_j = rint(v_j / s) =
+// hi*2^16 + mid*2^8 + lo (hi, mid, lo signed bytes) in three byte planes, so
+// 4 int8 weights times 4 staged values are three exact dp4a. The error is
+// below 2^-23 * max|v| per element.
+constexpr float FIX_MAX = 8323072.0f;  // 2^23 - 2^16: keeps hi within [-127, 127]
+
+// Four values times rs (= FIX_MAX / max|v|) into the packed hi, mid, lo bytes.
+__device__ __forceinline__ void fix_pack4(float4 v4, float rs, uint32_t& ph, uint32_t& pm, uint32_t& pl) {
+    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+    ph = pm = pl = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int q = __float2int_rn(vv[e] * rs);
+        const int lo = (int)(int8_t)(q & 0xff);
+        const int q1 = (q - lo) >> 8;
+        const int md = (int)(int8_t)(q1 & 0xff);
+        const int hi = (q1 - md) >> 8;
+        ph |= (uint32_t)(hi & 0xff) << (8 * e);
+        pm |= (uint32_t)(md & 0xff) << (8 * e);
+        pl |= (uint32_t)(lo & 0xff) << (8 * e);
+    }
 }
 
-// Index of element j of the logical vector inside the chunk-interleaved layout.
-__device__ __forceinline__ int xs_index(int j, int nch) {
-    const int c = j >> 4, r = j & 15;
-    return ((r >> 2) * nch + c) * 4 + (r & 3);
+// 16 int8 weights times 16 staged activations, exact in three int32 planes.
+__device__ __forceinline__ void dp4a16(const int4& w, const int4& h, const int4& m, const int4& l, int& ah, int& am,
+                                       int& al) {
+    ah = __dp4a(w.x, h.x, ah);
+    am = __dp4a(w.x, m.x, am);
+    al = __dp4a(w.x, l.x, al);
+    ah = __dp4a(w.y, h.y, ah);
+    am = __dp4a(w.y, m.y, am);
+    al = __dp4a(w.y, l.y, al);
+    ah = __dp4a(w.z, h.z, ah);
+    am = __dp4a(w.z, m.z, am);
+    al = __dp4a(w.z, l.z, al);
+    ah = __dp4a(w.w, h.w, ah);
+    am = __dp4a(w.w, m.w, am);
+    al = __dp4a(w.w, l.w, al);
 }
-
-// R rows of `nch` 16-byte chunks each, dotted with the staged vector; the
-// result of row r is returned (warp-reduced) in out[r] on every lane. Rows
-// whose pointer is null contribute 0. MAXC = chunks per lane, fully unrolled
-// so all of a lane's loads are in flight together.
-template <int R, int MAXC>
-__device__ __forceinline__ void rows_dot_unrolled(const int8_t* const (&rows)[R], const float4* xs4, int nch,
-                                                  int lane, float (&out)[R]) {
-    int4 w[R][MAXC];
-#pragma unroll
-    for (int c = 0; c < MAXC; ++c) {
-        const int ch = lane + 32 * c;
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-            w[r][c] = (ch < nch && rows[r]) ? ld_stream(rows[r] + (size_t)ch * 16) : make_int4(0, 0, 0, 0);
-    }
-    float2 acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int c = 0; c < MAXC; ++c) {
-        const int ch = lane + 32 * c;
-        if (ch < nch) {
-#pragma unroll
-            for (int r = 0; r < R; ++r) acc[r] = dot16(w[r][c], xs4, nch, ch, acc[r]);
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) out[r] = warp_sum(acc[r].x + acc[r].y);
+// sum_j w_j q_j from the three plane sums (each exact; one rounding per step).
+__device__ __forceinline__ float planes_to_float(int ah, int am, int al) {
+    return fmaf(65536.0f, (float)ah, fmaf(256.0f, (float)am, (float)al));
 }
-
-// Same for long rows: loop over groups of U chunks per lane.
-template <int R, int U>
-__device__ __forceinline__ void rows_dot_loop(const int8_t* const (&rows)[R], const float4* xs4, int nch, int lane,
-                                              float (&out)[R]) {
-    float2 acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = make_float2(0.f, 0.f);
-    for (int base = 0; base < nch; base += 32 * U) {
-        int4 w[R][U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int ch = base + lane + 32 * u;
-#pragma unroll
-            for (int r = 0; r < R; ++r)
-                w[r][u] = (ch < nch && rows[r]) ? ld_stream(rows[r] + (size_t)ch * 16) : make_int4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int ch = base + lane + 32 * u;
-            if (ch < nch) {
-#pragma unroll
-                for (int r = 0; r < R; ++r) acc[r] = dot16(w[r][u], xs4, nch, ch, acc[r]);
-            }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) out[r] = warp_sum(acc[r].x + acc[r].y);
+__device__ __forceinline__ void load_planes(const int8_t* xq, int plane, int c, int4& h, int4& m, int4& l) {
+    h = reinterpret_cast<const int4*>(xq)[c];
+    m = reinterpret_cast<const int4*>(xq + plane)[c];
+    l = reinterpret_cast<const int4*>(xq + 2 * plane)[c];
 }
 
 __device__ __forceinline__ float kv_load(const float* p) { return __ldcg(p); }

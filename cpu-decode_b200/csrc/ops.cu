@@ -8,6 +8,7 @@
 
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <string>
 
@@ -29,35 +30,77 @@ int cuda_fail(cudaError_t e, const char* what) {
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 
-// y[r] = scale[r] * dot(w[r], x) (+ bias[r]); R rows per warp, rows 16-byte aligned.
-template <int R, int MAXC>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_i8_kernel(const int8_t* __restrict__ w,
-                                                               const float* __restrict__ scales,
-                                                               const float* __restrict__ bias,
-                                                               const float* __restrict__ x, float* __restrict__ y,
-                                                               int rows, int cols) {
-    extern __shared__ __align__(16) float4 xs4[];
-    const int nch = cols / 16;
-    float* xs = reinterpret_cast<float*>(xs4);
-    for (int j = threadIdx.x; j < cols; j += blockDim.x) xs[xs_index(j, nch)] = x[j];
+constexpr int GEMV_NT = 512, GEMV_NW = GEMV_NT / 32;
+
+// y[r] = scale[r] * dot(w[r], x) (+ bias[r]) for rows of a multiple of 16
+// int8 (16-byte aligned). Persistent: every block stages x once as three
+// fixed-point byte planes (scale max|x| / FIX_MAX), then its warps take row
+// groups of R in turn, each lane streaming 16-byte chunks lane, lane + 32, ...
+// with U chunks of all R rows in flight, three exact dp4a per 4 weights.
+template <int R, int U>
+__global__ void __launch_bounds__(GEMV_NT) gemv_dp4a_kernel(const int8_t* __restrict__ w,
+                                                          const float* __restrict__ scales,
+                                                          const float* __restrict__ bias,
+                                                          const float* __restrict__ x, float* __restrict__ y,
+                                                          int rows, int cols) {
+    extern __shared__ __align__(16) int8_t xq[];  // planes hi | mid | lo, cols bytes each
+    __shared__ float red[GEMV_NW];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float mx = 0.f;
+    for (int j = tid; j < cols; j += GEMV_NT) mx = fmaxf(mx, fabsf(__ldg(x + j)));
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int r0 = (blockIdx.x * GEMV_WARPS + warp) * R;
-    if (r0 >= rows) return;
-    const int8_t* rp[R];
+    float M = 0.f;
 #pragma unroll
-    for (int r = 0; r < R; ++r) rp[r] = r0 + r < rows ? w + (size_t)(r0 + r) * cols : nullptr;
-    float dot[R];
-    if (MAXC > 0) rows_dot_unrolled<R, (MAXC > 0 ? MAXC : 1)>(rp, xs4, nch, lane, dot);
-    else rows_dot_loop<R, 2>(rp, xs4, nch, lane, dot);
-    if (lane < R && r0 + lane < rows) {
-        float v = 0.f;
+    for (int k = 0; k < GEMV_NW; ++k) M = fmaxf(M, red[k]);
+    const float rs = M > 0.f ? FIX_MAX * __frcp_rn(M) : 0.f;
+    const float xs = M > 0.f ? __frcp_rn(rs) : 1.f;
+    for (int quad = tid; quad < cols / 4; quad += GEMV_NT) {
+        const float4 v = make_float4(__ldg(x + 4 * quad), __ldg(x + 4 * quad + 1), __ldg(x + 4 * quad + 2),
+                                     __ldg(x + 4 * quad + 3));
+        uint32_t ph, pm, pl;
+        fix_pack4(v, rs, ph, pm, pl);
+        reinterpret_cast<uint32_t*>(xq)[quad] = ph;
+        reinterpret_cast<uint32_t*>(xq + cols)[quad] = pm;
+        reinterpret_cast<uint32_t*>(xq + 2 * cols)[quad] = pl;
+    }
+    __syncthreads();
+    const int nch = cols / 16;
+    const int stride = gridDim.x * GEMV_NW * R;
+    for (int r0 = (blockIdx.x * GEMV_NW + warp) * R; r0 < rows; r0 += stride) {
+        int ah[R], am[R], al[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r)
-            if (r == lane) v = dot[r];
-        v *= scales[r0 + lane];
-        if (bias) v += bias[r0 + lane];
-        y[r0 + lane] = v;
+        for (int r = 0; r < R; ++r) ah[r] = am[r] = al[r] = 0;
+        for (int c0 = lane; c0 < nch; c0 += 32 * U) {
+            int4 wv[U][R];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int c = c0 + 32 * u;
+                    wv[u][r] = (c < nch && r0 + r < rows) ? ld_stream(w + (size_t)(r0 + r) * cols + (size_t)c * 16)
+                                                          : make_int4(0, 0, 0, 0);
+                }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < nch) {
+                    int4 h, m, l;
+                    load_planes(xq, cols, c, h, m, l);
+#pragma unroll
+                    for (int r = 0; r < R; ++r) dp4a16(wv[u][r], h, m, l, ah[r], am[r], al[r]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float t = warp_sum(planes_to_float(ah[r], am[r], al[r]));
+            if (lane == 0 && r0 + r < rows) {
+                const float v = t * xs * scales[r0 + r];
+                y[r0 + r] = bias ? v + bias[r0 + r] : v;
+            }
+        }
     }
 }
 
@@ -78,18 +121,6 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_i8_narrow_kernel(const int8
     }
     const float acc = warp_sum(acc2.x + acc2.y);
     if (lane == 0) y[r] = acc * scales[r] + (bias ? bias[r] : 0.f);
-}
-
-template <typename KV>
-__global__ void __launch_bounds__(512) attention_kernel(AttnIO io) {
-    extern __shared__ __align__(16) float att_sm[];
-    const int u = blockIdx.x;
-    attention_unit<KV>(io, u / io.nsplit, u % io.nsplit, att_sm);
-}
-
-__global__ void rope_inv_kernel(float* inv, int dim, float theta) {
-    const int j = threadIdx.x;
-    if (j < dim / 2) inv[j] = 1.0f / powf(theta, (float)(2 * j) / (float)dim);
 }
 
 __global__ void rmsnorm_kernel(const float* x, const float* w, float* out, int n, float eps) {
@@ -150,24 +181,79 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* x, int n, int
     }
 }
 
-template <int R>
+// Multiprocessor count of each device, looked up once.
+std::atomic<int> g_sm_count[64];
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    int n = g_sm_count[dev].load(std::memory_order_relaxed);
+    if (!n) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_sm_count[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
+template <int R, int U>
 int launch_gemv(const int8_t* w, const float* s, const float* b, const float* x, float* y, int rows, int cols,
                 cudaStream_t st) {
-    const int blocks = (rows + GEMV_WARPS * R - 1) / (GEMV_WARPS * R);
-    const size_t smem = (size_t)cols * sizeof(float);
-    const int nch = cols / 16;
-    const void* k;
-    if (nch <= 32) k = (const void*)gemv_i8_kernel<R, 1>;
-    else if (nch <= 64) k = (const void*)gemv_i8_kernel<R, 2>;
-    else if (nch <= 128) k = (const void*)gemv_i8_kernel<R, 4>;
-    else k = (const void*)gemv_i8_kernel<R, 0>;
+    const int groups = (rows + R - 1) / R;
+    const int blocks = std::max(1, std::min(2 * sm_count(), (groups + GEMV_NW - 1) / GEMV_NW));
+    const size_t smem = 3 * (size_t)cols;
+    const void* k = (const void*)gemv_dp4a_kernel<R, U>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return cuda_fail(e, "gemv shared memory");
     }
     void* args[] = {(void*)&w, (void*)&s, (void*)&b, (void*)&x, (void*)&y, (void*)&rows, (void*)&cols};
-    cudaError_t e = cudaLaunchKernel(k, dim3(blocks), dim3(GEMV_THREADS), args, smem, st);
+    cudaError_t e = cudaLaunchKernel(k, dim3(blocks), dim3(GEMV_NT), args, smem, st);
     return e == cudaSuccess ? 0 : cuda_fail(e, "gemv launch");
+}
+
+// Split plan of the isolated attention: about two blocks per SM across the KV
+// heads, whole 64-position chunks per split.
+void attention_plan(int length, int kv_heads, int sms, int* nsplit, int* split_len) {
+    const int chunks = (length + AT_T - 1) / AT_T;
+    const int want = std::max(1, 2 * sms / kv_heads);
+    const int n = std::min(chunks, want);
+    *split_len = ((chunks + n - 1) / n) * AT_T;
+    *nsplit = (length + *split_len - 1) / *split_len;
+}
+
+template <typename KV, int DT>
+cudaError_t launch_split(const AttnIO& io, size_t smem, cudaStream_t st) {
+    const void* k = (const void*)attention_split_kernel<KV, DT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    AttnIO a = io;
+    void* args[] = {(void*)&a};
+    return cudaLaunchKernel(k, dim3(io.kv_heads * io.nsplit), dim3(AT_NT), args, smem, st);
+}
+
+// The split kernel, then (several splits) the combine kernel, on stream st.
+int launch_attention(const AttnIO& io, int kv_dtype, cudaStream_t st) {
+    const int es = kv_dtype == DCB_KV_F16 ? 2 : 4;
+    const size_t smem = attention_smem_bytes(io.d, es, io.heads / io.kv_heads);
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (smem + 1024 > (size_t)optin)
+        return fail(DCB_ERR_UNSUPPORTED, "attention needs more shared memory than a block has");
+    cudaError_t e;
+    if (kv_dtype == DCB_KV_F16)
+        e = io.d == 64 ? launch_split<__half, 64>(io, smem, st) : launch_split<__half, 0>(io, smem, st);
+    else
+        e = io.d == 64 ? launch_split<float, 64>(io, smem, st) : launch_split<float, 0>(io, smem, st);
+    if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+    if (io.nsplit > 1) {
+        AttnIO a = io;
+        void* args[] = {(void*)&a};
+        e = cudaLaunchKernel((const void*)attention_combine_kernel, dim3(io.heads), dim3(AT_NT), args, 0, st);
+        if (e != cudaSuccess) return cuda_fail(e, "attention combine launch");
+    }
+    return 0;
 }
 
 }  // namespace
@@ -187,12 +273,11 @@ int dcb_gemv_i8(const int8_t* w, const float* scales, const float* bias, const f
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? 0 : cuda_fail(e, "gemv launch");
     }
-    // Four rows per warp once there are enough rows to fill the GPU twice over.
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (rows >= 2 * sms * GEMV_WARPS * 4) return launch_gemv<4>(w, scales, bias, x, y, rows, cols, st);
-    return launch_gemv<1>(w, scales, bias, x, y, rows, cols, st);
+    // Rows per warp: as many (up to 4) as every warp of two blocks per SM gets.
+    const int warps = 2 * sm_count() * GEMV_NW;
+    if (rows >= 4 * warps) return launch_gemv<4, 2>(w, scales, bias, x, y, rows, cols, st);
+    if (rows >= 2 * warps) return launch_gemv<2, 2>(w, scales, bias, x, y, rows, cols, st);
+    return launch_gemv<1, 4>(w, scales, bias, x, y, rows, cols, st);
 }
 
 int dcb_attention(const float* q_in, const void* keys, const void* values, int kv_dtype, float* out, int length,
@@ -202,57 +287,29 @@ int dcb_attention(const float* q_in, const void* keys, const void* values, int k
         return fail(DCB_ERR_ARGUMENT, "invalid attention dimensions");
     if (kv_dtype != DCB_KV_F32 && kv_dtype != DCB_KV_F16) return fail(DCB_ERR_ARGUMENT, "invalid KV dtype");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int chunks = (length + KV_CHUNK - 1) / KV_CHUNK;
-    const int want = std::max(1, 2 * sms / kv_heads);
-    const int n = std::min(chunks, want);
-    const int split_len = ((chunks + n - 1) / n) * KV_CHUNK;
-    const int nsplit = (length + split_len - 1) / split_len;
-    const int gq = heads / kv_heads;
-    // Scratch: rope table, partials, per-group counters (stream-ordered).
-    const size_t inv_bytes = 256 * sizeof(float);
-    const size_t part_bytes = (size_t)heads * nsplit * (dim + 2) * sizeof(float);
-    const size_t cnt_bytes = (size_t)kv_heads * sizeof(unsigned);
-    char* scratch = nullptr;
-    cudaError_t e = cudaMallocAsync((void**)&scratch, inv_bytes + part_bytes + cnt_bytes, st);
-    if (e != cudaSuccess) return cuda_fail(e, "attention scratch");
-    float* inv = reinterpret_cast<float*>(scratch);
-    float* part = reinterpret_cast<float*>(scratch + inv_bytes);
-    unsigned* cnt = reinterpret_cast<unsigned*>(scratch + inv_bytes + part_bytes);
-    cudaMemsetAsync(cnt, 0, cnt_bytes, st);
     AttnIO io;
     io.q = q_in;
-    io.rope_inv = nullptr;
-    io.rope_pos = length - 1;
-    if (rope_theta > 0) {
-        rope_inv_kernel<<<1, 64, 0, st>>>(inv, dim, rope_theta);
-        io.rope_inv = inv;
-    }
     io.keys = keys;
     io.values = values;
     io.out = out;
-    io.part = part;
-    io.group_done = cnt;
+    io.part = nullptr;
+    io.rope_theta = rope_theta;
     io.heads = heads;
     io.kv_heads = kv_heads;
     io.d = dim;
     io.length = length;
-    io.nsplit = nsplit;
-    io.split_len = split_len;
-    const size_t smem = attention_smem_floats(dim, gq) * sizeof(float);
-    const int threads = std::min(512, std::max(128, ((gq + 3) / 4) * 128));
-    if (kv_dtype == DCB_KV_F16) {
-        cudaFuncSetAttribute(attention_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attention_kernel<__half><<<kv_heads * nsplit, threads, smem, st>>>(io);
-    } else {
-        cudaFuncSetAttribute(attention_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attention_kernel<float><<<kv_heads * nsplit, threads, smem, st>>>(io);
+    attention_plan(length, kv_heads, sm_count(), &io.nsplit, &io.split_len);
+    // Scratch: the split partials (stream-ordered).
+    float* part = nullptr;
+    if (io.nsplit > 1) {
+        const size_t part_bytes = (size_t)heads * io.nsplit * (dim + 2) * sizeof(float);
+        cudaError_t e = cudaMallocAsync((void**)&part, part_bytes, st);
+        if (e != cudaSuccess) return cuda_fail(e, "attention scratch");
+        io.part = part;
     }
-    e = cudaGetLastError();
-    cudaFreeAsync(scratch, st);
-    return e == cudaSuccess ? 0 : cuda_fail(e, "attention launch");
+    const int rc = launch_attention(io, kv_dtype, st);
+    if (part) cudaFreeAsync(part, st);
+    return rc;
 }
 
 int dcb_rmsnorm(const float* x, const float* w, float* out, int n, float eps, void* stream) {
@@ -282,15 +339,13 @@ int dcb_argmax(const float* x, int n, int* out, void* stream) {
 // ---- attention with its scratch in a static device array --------------------------
 // dcb_attention_noalloc is dcb_attention with the cudaMallocAsync scratch
 // replaced by one fixed array per device, for callers that must not allocate
-// device memory per call. Layout: [0, 1 KiB) RoPE inverse frequencies (256
-// floats), [1 KiB, 2 KiB) per-group arrival counters (up to 256 unsigned), then
-// the split partials (heads x splits x (dim + 2) floats).
+// device memory per call. The array holds the split partials (heads x splits
+// x (dim + 2) floats); a call writes every word it reads, so nothing in it has
+// to start at zero.
 #include <mutex>
 
 namespace {
 constexpr size_t NOALLOC_BYTES = DCB_ATTENTION_NOALLOC_SCRATCH_BYTES;
-constexpr size_t NOALLOC_CNT_OFF = 1024, NOALLOC_PART_OFF = 2048;
-constexpr int NOALLOC_MAX_KV_HEADS = 256;
 constexpr int NOALLOC_MAX_DEVICES = 64;
 
 __device__ __align__(256) unsigned char g_attention_scratch[NOALLOC_BYTES];
@@ -301,23 +356,22 @@ struct NoallocDevice {
     const char* what = "";
     char* scratch = nullptr;
     int sms = 0;
-    int max_dynamic[2] = {0, 0};  // dynamic shared memory cap of attention_kernel<float>, <__half>
 };
 NoallocDevice g_noalloc[NOALLOC_MAX_DEVICES];
 
-template <typename KV>
-cudaError_t raise_smem_cap(int optin, int& cap) {
+template <typename KV, int DT>
+cudaError_t raise_smem_cap(int optin) {
     cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, attention_kernel<KV>);
+    cudaError_t e = cudaFuncGetAttributes(&fa, attention_split_kernel<KV, DT>);
     if (e != cudaSuccess) return e;
-    cap = optin - (int)fa.sharedSizeBytes;
-    return cudaFuncSetAttribute(attention_kernel<KV>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+    return cudaFuncSetAttribute(attention_split_kernel<KV, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                optin - (int)fa.sharedSizeBytes);
 }
 
 // Once per device, with that device current: the scratch's device address and
 // the kernel attributes (the dynamic shared memory cap raised to what the
-// device allows next to the kernel's static shared memory, so later calls set
-// nothing).
+// device allows next to the kernels' static shared memory, so that later
+// calls leave the attributes as they are).
 void noalloc_setup(NoallocDevice& d, int dev) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
@@ -334,8 +388,8 @@ void noalloc_setup(NoallocDevice& d, int dev) {
         d.what = "device attributes";
         return;
     }
-    if ((e = raise_smem_cap<float>(optin, d.max_dynamic[0])) != cudaSuccess ||
-        (e = raise_smem_cap<__half>(optin, d.max_dynamic[1])) != cudaSuccess) {
+    if ((e = raise_smem_cap<float, 64>(optin)) != cudaSuccess || (e = raise_smem_cap<float, 0>(optin)) != cudaSuccess ||
+        (e = raise_smem_cap<__half, 64>(optin)) != cudaSuccess || (e = raise_smem_cap<__half, 0>(optin)) != cudaSuccess) {
         d.status = e;
         d.what = "attention kernel attributes";
     }
@@ -358,56 +412,25 @@ extern "C" int dcb_attention_noalloc(const float* q_in, const void* keys, const 
     std::call_once(d.once, noalloc_setup, std::ref(d), dev);
     if (d.status != cudaSuccess) return cuda_fail(d.status, d.what);
 
-    // The split of dcb_attention, so both produce the same partials.
-    const int chunks = (length + KV_CHUNK - 1) / KV_CHUNK;
-    const int want = std::max(1, 2 * d.sms / kv_heads);
-    const int n = std::min(chunks, want);
-    const int split_len = ((chunks + n - 1) / n) * KV_CHUNK;
-    const int nsplit = (length + split_len - 1) / split_len;
-    const int gq = heads / kv_heads;
-    const size_t part_bytes = (size_t)heads * nsplit * (dim + 2) * sizeof(float);
-    if (kv_heads > NOALLOC_MAX_KV_HEADS || NOALLOC_PART_OFF + part_bytes > NOALLOC_BYTES)
-        return fail(DCB_ERR_ARGUMENT,
-                    "dcb_attention_noalloc: needs " + std::to_string(NOALLOC_PART_OFF + part_bytes) +
-                        " bytes of scratch (" + std::to_string(kv_heads) + " KV heads, " + std::to_string(heads) +
-                        " heads x " + std::to_string(nsplit) + " splits x " + std::to_string(dim + 2) +
-                        " floats); the static scratch holds " + std::to_string(NOALLOC_BYTES) +
-                        " bytes and at most 256 KV heads");
-    const size_t smem = attention_smem_floats(dim, gq) * sizeof(float);
-    if (smem > (size_t)d.max_dynamic[kv_dtype == DCB_KV_F16 ? 1 : 0])
-        return fail(DCB_ERR_UNSUPPORTED, "attention needs more shared memory than a block has");
-
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    float* inv = reinterpret_cast<float*>(d.scratch);
-    unsigned* cnt = reinterpret_cast<unsigned*>(d.scratch + NOALLOC_CNT_OFF);
-    float* part = reinterpret_cast<float*>(d.scratch + NOALLOC_PART_OFF);
-    // The arrival counters must be zero when the kernel starts.
-    if ((e = cudaMemsetAsync(cnt, 0, (size_t)kv_heads * sizeof(unsigned), st)) != cudaSuccess)
-        return cuda_fail(e, "attention counters");
     AttnIO io;
     io.q = q_in;
-    io.rope_inv = nullptr;
-    io.rope_pos = length - 1;
-    if (rope_theta > 0) {
-        rope_inv_kernel<<<1, 64, 0, st>>>(inv, dim, rope_theta);
-        io.rope_inv = inv;
-    }
     io.keys = keys;
     io.values = values;
     io.out = out;
-    io.part = part;
-    io.group_done = cnt;
+    io.part = reinterpret_cast<float*>(d.scratch);
+    io.rope_theta = rope_theta;
     io.heads = heads;
     io.kv_heads = kv_heads;
     io.d = dim;
     io.length = length;
-    io.nsplit = nsplit;
-    io.split_len = split_len;
-    const int threads = std::min(512, std::max(128, ((gq + 3) / 4) * 128));
-    if (kv_dtype == DCB_KV_F16)
-        attention_kernel<__half><<<kv_heads * nsplit, threads, smem, st>>>(io);
-    else
-        attention_kernel<float><<<kv_heads * nsplit, threads, smem, st>>>(io);
-    e = cudaGetLastError();
-    return e == cudaSuccess ? 0 : cuda_fail(e, "attention launch");
+    // The split of dcb_attention, so both produce the same partials.
+    attention_plan(length, kv_heads, d.sms, &io.nsplit, &io.split_len);
+    const size_t part_bytes = io.nsplit > 1 ? (size_t)heads * io.nsplit * (dim + 2) * sizeof(float) : 0;
+    if (part_bytes > NOALLOC_BYTES)
+        return fail(DCB_ERR_ARGUMENT,
+                    "dcb_attention_noalloc: needs " + std::to_string(part_bytes) + " bytes of scratch (" +
+                        std::to_string(heads) + " heads x " + std::to_string(io.nsplit) + " splits x " +
+                        std::to_string(dim + 2) + " floats); the static scratch holds " +
+                        std::to_string(NOALLOC_BYTES) + " bytes");
+    return launch_attention(io, kv_dtype, static_cast<cudaStream_t>(stream));
 }

@@ -243,7 +243,6 @@ __device__ bool mbar_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
 // (6 issue cycles per 4 weights on sm_100 against about 17 for widening each
 // byte to FP32). The quantisation error is below 2^-23 * max|v| per element,
 // the order of the FP32 rounding in the reference's own sums.
-constexpr float FIX_MAX = 8323072.0f;  // 2^23 - 2^16: keeps hi within [-127, 127]
 
 // Element j arrived with value v: raw to xr (when set), v * gain (the RMSNorm
 // gain of element j folded in; 1 where there is none) to xf.
@@ -292,18 +291,7 @@ __device__ Staged finish_stage(int n, int nch, const float* xf, int8_t* xq, int 
                                            : make_float4(4 * quad < n ? xf[4 * quad] : 0.f,
                                                          4 * quad + 1 < n ? xf[4 * quad + 1] : 0.f,
                                                          4 * quad + 2 < n ? xf[4 * quad + 2] : 0.f, 0.f);
-        const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int q = __float2int_rn(vv[e] * rs);
-            const int lo = (int)(int8_t)(q & 0xff);
-            const int q1 = (q - lo) >> 8;
-            const int md = (int)(int8_t)(q1 & 0xff);
-            const int hi = (q1 - md) >> 8;
-            ph |= (uint32_t)(hi & 0xff) << (8 * e);
-            pm |= (uint32_t)(md & 0xff) << (8 * e);
-            pl |= (uint32_t)(lo & 0xff) << (8 * e);
-        }
+        fix_pack4(v4, rs, ph, pm, pl);
         reinterpret_cast<uint32_t*>(xq)[quad] = ph;
         reinterpret_cast<uint32_t*>(xq + plane)[quad] = pm;
         reinterpret_cast<uint32_t*>(xq + 2 * plane)[quad] = pl;
@@ -375,32 +363,6 @@ __device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr
     }
     out = finish_stage(n, nch, xf, xq, plane, ss, mx, red, eps);
     return !should_abort(st);
-}
-
-// 16 int8 weights times 16 staged activations, exact in three int32 planes.
-__device__ __forceinline__ void dp4a16(const int4& w, const int4& h, const int4& m, const int4& l, int& ah, int& am,
-                                       int& al) {
-    ah = __dp4a(w.x, h.x, ah);
-    am = __dp4a(w.x, m.x, am);
-    al = __dp4a(w.x, l.x, al);
-    ah = __dp4a(w.y, h.y, ah);
-    am = __dp4a(w.y, m.y, am);
-    al = __dp4a(w.y, l.y, al);
-    ah = __dp4a(w.z, h.z, ah);
-    am = __dp4a(w.z, m.z, am);
-    al = __dp4a(w.z, l.z, al);
-    ah = __dp4a(w.w, h.w, ah);
-    am = __dp4a(w.w, m.w, am);
-    al = __dp4a(w.w, l.w, al);
-}
-// sum_j w_j q_j from the three plane sums (each exact; one rounding per step).
-__device__ __forceinline__ float planes_to_float(int ah, int am, int al) {
-    return fmaf(65536.0f, (float)ah, fmaf(256.0f, (float)am, (float)al));
-}
-__device__ __forceinline__ void load_planes(const int8_t* xq, int plane, int c, int4& h, int4& m, int4& l) {
-    h = reinterpret_cast<const int4*>(xq)[c];
-    m = reinterpret_cast<const int4*>(xq + plane)[c];
-    l = reinterpret_cast<const int4*>(xq + 2 * plane)[c];
 }
 
 // Partial dot products sum_j w_rj q_j of R packed rows in shared memory (stride

@@ -150,19 +150,18 @@ int dcb_attention(const float* q_in, const void* keys, const void* values, int k
 /* No counterpart in the reference: its attention (src/kernels.cpp:150-179)
  * works in host memory and needs no scratch. dcb_attention_noalloc is
  * dcb_attention with the same arguments, results and errors, but its scratch
- * (RoPE table, split partials, arrival counters) lives in one fixed array of
+ * (the per-split partial results) lives in one fixed array of
  * DCB_ATTENTION_NOALLOC_SCRATCH_BYTES compiled into this library, one per
  * device, instead of a cudaMallocAsync per call. It is for callers that must
  * not allocate device memory once serving starts: a server that reserved all
  * of HBM up front for weights and KV cache (a per-call allocation can fail
  * there), or a decode loop that keeps the allocator off its latency-critical
  * path (a stream-ordered allocation may grow its pool through the driver).
- * Limits: kv_heads <= 256 and heads * splits * (dim + 2) * 4 <=
- * DCB_ATTENTION_NOALLOC_SCRATCH_BYTES - 2048, with splits chosen as
- * dcb_attention chooses them (about two blocks per SM across the KV heads,
- * 64-position chunks); larger calls return DCB_ERR_ARGUMENT and a message
- * giving the bytes needed. The per-group arrival counters must be zero when
- * the kernel starts: each call clears them with cudaMemsetAsync on `stream`.
+ * Limit: heads * splits * (dim + 2) * 4 <= DCB_ATTENTION_NOALLOC_SCRATCH_BYTES,
+ * with splits chosen as dcb_attention chooses them (about two blocks per SM
+ * across the KV heads, 64-position chunks); larger calls return
+ * DCB_ERR_ARGUMENT and a message giving the bytes needed. Nothing in the
+ * scratch has to start at zero: a call writes every word before it reads it.
  * The scratch is shared: calls on the same device that overlap in time
  * (streams without ordering between them, or concurrent host threads) race on
  * it; issue them on one stream or order them with events. The first call on
