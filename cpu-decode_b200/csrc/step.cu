@@ -340,13 +340,12 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     off = round_up(off + qkv_slot, 128);
     P.off_o = (int)off;
     off = round_up(off + o_slot, 128);
-    off = std::max(off, round_up((size_t)3 * HEAD_ROWS * P.SH, 128));  // at least three LM-head stages
     P.off_att = (int)off;
     // Vectors after the attention ring: staged floats, fixed-point planes,
     // GEMV partials (two buffers), raw residual, attention scratch.
     P.xq_plane = (int)round_up((size_t)P.Kh, 128);
     {
-        const int max_rows = std::max({2 * ceil_div(P.qkv_pairs, G), ceil_div(H, G), 2 * ceil_div(I, G), HEAD_ROWS});
+        const int max_rows = std::max({2 * ceil_div(P.qkv_pairs, G), ceil_div(H, G), 2 * ceil_div(I, G)});
         P.gpart_floats = NW * max_rows;
     }
     const size_t xs_bytes = round_up((size_t)P.Kh * sizeof(float), 128);
@@ -365,8 +364,6 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     P.att_bufs = (int)std::min<size_t>(ATT_MAX_BUFS, std::max<size_t>(2, room / P.att_chunk_bytes));
     off = round_up(off + std::max((size_t)P.att_bufs * P.att_chunk_bytes, down_stage), 128);
     P.off_xs = (int)off;
-    // The LM-head ring overlays the weight slots and the attention ring.
-    P.head_stages = (int)std::min<size_t>(HEAD_MAX_STAGES, (size_t)(P.off_xs - P.off_gu) / ((size_t)HEAD_ROWS * P.SH));
     P.trace_layer = std::min(5, e->L - 1);
     if (const char* v = std::getenv("DCB_SPLIT_MIN")) e->split_min = std::max(ATT_CHUNK, std::atoi(v) / ATT_CHUNK * ATT_CHUNK);
     off += xs_bytes;

@@ -5,7 +5,7 @@
 //   QKV  : RMSNorm prologue, Q/K/V int8 GEMV + bias + split-half RoPE, K/V row
 //          written to the cache at `pos`
 //   ATTN : GQA attention over positions 0..pos (one block per query head and
-//          KV split, log-sum-exp combine across splits)
+//          KV split; split 0 merges the splits' (max, sum, output))
 //   O    : O GEMV + residual
 //   GU   : RMSNorm prologue, gate/up GEMV, SiLU(gate)*up
 //   DOWN : down GEMV + residual
@@ -20,8 +20,9 @@
 //    {value, tag}: a producer stores each element once with its tag, consumers
 //    poll exactly the elements they need until the tag of this step and layer
 //    shows. One L2 round trip per dependency; a stale value is never used.
-//  * The LM head (136 MB at the Qwen shape) streams through a 3-stage shared
-//    memory ring, loaded with an evict-first L2 policy.
+//  * The LM head (136 MB at the Qwen shape) streams straight from HBM: every
+//    warp keeps the 16-byte chunks of its next row group in flight while it
+//    reduces the current one.
 // Every wait is bounded in time; on expiry the block records an error, drains
 // its own copies in flight and returns.
 #pragma once
@@ -40,9 +41,8 @@ constexpr int ERR_TOKEN = 2;
 constexpr int ATT_CHUNK = 64;  // KV positions per staged chunk
 constexpr int ATT_PER_WARP = ATT_CHUNK / NW;
 constexpr int ATT_MAX_BUFS = 6;  // staged chunk ring (the host picks how many fit)
-constexpr int HEAD_ROWS = 2 * NW;  // LM-head rows per ring stage: two per warp
-constexpr int HEAD_MAX_STAGES = 8;  // LM-head ring stages (the host picks how many fit)
-constexpr int HEAD_L2_AHEAD = 12;   // LM-head chunks kept in flight into L2 beyond the ring
+constexpr int HEAD_R = 4;           // LM-head rows a warp reduces per group (the next group in flight)
+constexpr int HEAD_L2_ROWS = 256;   // LM-head rows per block prefetched into L2 during the last layer
 constexpr int HEAD_MAXC = 2;        // 16-byte chunks per lane of a hidden-size row (hidden <= 1024)
 constexpr int TRACE_MAX_PHASES = 512;
 constexpr int MAXD = 4;        // head_dim <= 128: lane owns dims lane + 32k
@@ -98,7 +98,6 @@ struct Params {
     int gpart_floats;  // floats per block-GEMV partial buffer (NW * max rows of a phase)
     int att_chunk_bytes;
     int att_bufs;     // chunk buffers in the attention ring (2..ATT_MAX_BUFS)
-    int head_stages;  // LM-head ring stages over [off_gu, off_xs)
     int trace_layer;  // layer whose phases get detailed marks when tracing
 };
 
@@ -153,35 +152,17 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  "l"(src), "r"(bytes), "r"(smem_u32(m))
                  : "memory");
 }
-__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* m,
-                                               uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(m)), "l"(policy)
-        : "memory");
-}
-__device__ __forceinline__ uint64_t evict_first_policy() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-// Shared memory read by threads (generic proxy) before the TMA (async proxy) rewrites it.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // One thread: fill a shared slot with `bytes` (16-byte aligned, multiple of 16).
 // `*fills` counts the fills issued on `m` (used to drain them on abort).
-__device__ __forceinline__ void fill_slot(void* dst, const void* src, uint32_t bytes, uint64_t* m, unsigned* fills,
-                                          uint64_t policy = 0) {
+__device__ __forceinline__ void fill_slot(void* dst, const void* src, uint32_t bytes, uint64_t* m, unsigned* fills) {
     ++*fills;
     mbar_expect(m, bytes);
     constexpr uint32_t piece = 32768;
     for (uint32_t o = 0; o < bytes; o += piece) {
         const uint32_t n = bytes - o < piece ? bytes - o : piece;
-        if (policy)
-            bulk_load_hint(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, n, m, policy);
-        else
-            bulk_load(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, n, m);
+        bulk_load(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, n, m);
     }
 }
 
@@ -766,18 +747,15 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     float* gpart = reinterpret_cast<float*>(sm + P.off_gpart);  // block-GEMV partial sums, two buffers
     float* xr = reinterpret_cast<float*>(sm + P.off_xr);
     float* misc = reinterpret_cast<float*>(sm + P.off_misc);
-    // mbarriers: four weight slots, the LM-head ring, the attention ring (one
-    // arrival + bytes each), then the LM-head "stage empty" barriers (NW arrivals).
-    constexpr int MB_HEAD = 4, MB_ATT = MB_HEAD + HEAD_MAX_STAGES, MB_EMPTY = MB_ATT + ATT_MAX_BUFS;
-    constexpr int NMB = MB_EMPTY + HEAD_MAX_STAGES;
+    // mbarriers: four weight slots, then the attention chunk ring (one arrival + bytes each).
+    constexpr int MB_ATT = 4;
+    constexpr int NMB = MB_ATT + ATT_MAX_BUFS;
     __shared__ __align__(8) uint64_t mb[NMB];
     uint64_t* mb_gu = mb + 0;
     uint64_t* mb_down = mb + 1;
     uint64_t* mb_qkv = mb + 2;
     uint64_t* mb_o = mb + 3;
-    uint64_t* mb_head = mb + MB_HEAD;
     uint64_t* mb_att = mb + MB_ATT;
-    uint64_t* mb_head_empty = mb + MB_EMPTY;
     __shared__ float s_cos[64], s_sin[64];
     __shared__ __align__(16) float red[2 * NW + 8];  // read as float4 in finish_stage
     __shared__ int s_abort;
@@ -794,8 +772,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     const int ga = part_lo(b, G, I), gn = part_lo(b + 1, G, I) - ga;
     const int da = part_lo(b, G, H), dn = part_lo(b + 1, G, H) - da;
     const int ha = part_lo(b, G, P.V), hn = part_lo(b + 1, G, P.V) - ha;
-    const int head_chunks = A.head ? (hn + HEAD_ROWS - 1) / HEAD_ROWS : 0;
-    const uint32_t head_stage_bytes = (uint32_t)HEAD_ROWS * P.SH;
 
     // This block's attention unit (at most one).
     AttnPlan ap{};
@@ -809,17 +785,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         ap.nissued = min(ap.nchunks, max(0, (A.pos - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK));
         ap.bulk = ((size_t)D * sizeof(KV)) % 16 == 0;
     }
-    uint64_t head_policy = 0;
-    int head_issued = 0;
 
     if (tid == 0) {
         s_abort = 0;
         for (int i = 0; i < NMB; ++i) {
-            mbar_init(mb + i, i >= MB_EMPTY ? NW : 1);
+            mbar_init(mb + i, 1);
             s_fills[i] = 0;
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        head_policy = evict_first_policy();
         const LayerW& W = P.layers[0];
         if (qn) fill_slot(s_qkv, W.qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH, mb_qkv, s_fills + 2);
         if (on) fill_slot(s_o, W.o + (size_t)oa * P.SH, (uint32_t)on * P.SH, mb_o, s_fills + 3);
@@ -835,19 +808,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     trace_mark(P, 0, 0);
     trace_mark(P, 1, 0);
     trace_clock(P, 0);
-
-    // Thread 0: LM-head chunk c into ring stage c % head_stages.
-    const int NS = P.head_stages;
-    auto prefetch_head = [&](int c) {  // thread 0: LM-head chunk c into L2 only
-        if (c >= head_chunks) return;
-        const int r0 = ha + c * HEAD_ROWS, rows = min(HEAD_ROWS, ha + hn - r0);
-        prefetch_l2(P.embed + (size_t)r0 * P.SH, (uint32_t)rows * P.SH);
-    };
-    auto fill_head = [&](int c) {
-        const int r0 = ha + c * HEAD_ROWS, rows = min(HEAD_ROWS, ha + hn - r0);
-        fill_slot(sm + P.off_gu + (size_t)(c % NS) * head_stage_bytes, P.embed + (size_t)r0 * P.SH,
-                  (uint32_t)rows * P.SH, mb_head + c % NS, s_fills + MB_HEAD + c % NS, head_policy);
-    };
 
     int token = A.token_dev ? __ldcg(A.token_dev) : A.token;
     if ((unsigned)token >= (unsigned)P.V) {  // a device-supplied token out of range
@@ -868,9 +828,9 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         const float* in_norm = P.norms + (size_t)l * 2 * P.Kh;
         const float* post_norm = in_norm + P.Kh;
 
-        // HBM has slack during the last layer: start the LM-head rows into L2.
-        if (tid == 0 && A.head && l == P.L - 1)
-            for (int c = NS; c < NS + HEAD_L2_AHEAD; ++c) prefetch_head(c);
+        // HBM has slack during the last layer: start this block's first LM-head rows into L2.
+        if (tid == 0 && A.head && l == P.L - 1 && hn)
+            prefetch_slice(P.embed + (size_t)ha * P.SH, (size_t)min(hn, HEAD_L2_ROWS) * P.SH, 0, 1);
 
         // The cached KV rows do not depend on this step: start their copies now.
         if (has_att && tid == 0) {
@@ -1014,15 +974,9 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                 trace_detail(P, l, 3, 5);
                 if (tid == 0) {
                     fence_proxy_async();
-                    if (l + 1 < P.L) {
+                    if (l + 1 < P.L)
                         fill_slot(s_gu, P.layers[l + 1].gu + (size_t)ga * 2 * P.SH, (uint32_t)gn * 2 * P.SH, mb_gu,
                                   s_fills + 0);
-                    } else {
-                        // Last layer: LM-head stages clear of the down slot can start now.
-                        while (head_issued < min(NS, head_chunks) &&
-                               (size_t)(head_issued + 1) * head_stage_bytes <= (size_t)(P.off_down - P.off_gu))
-                            fill_head(head_issued++);
-                    }
                 }
                 trace_detail(P, l, 3, 6);
             }
@@ -1057,8 +1011,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                 if (l + 1 < P.L)
                     fill_slot(s_down, P.layers[l + 1].down + (size_t)da * P.SI, (uint32_t)dn * P.SI, mb_down,
                               s_fills + 1);
-                else
-                    while (head_issued < min(NS, head_chunks)) fill_head(head_issued++);
             }
             trace_detail(P, l, 4, 5);
         }
@@ -1070,8 +1022,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         float best_v = -INFINITY;
         int best_i = 0x7fffffff;
         if (hn) {
-            if (tid == 0)
-                while (head_issued < min(NS, head_chunks)) fill_head(head_issued++);
             Staged sf;
             if (!gather_stage<2, true>(P.ll_xa, H, seq_tag | (uint32_t)(P.L + 1), nullptr, xf, xq, QP, nch_h,
                                        P.norms + (size_t)P.L * 2 * P.Kh, red, P.eps, sf, st))
@@ -1090,67 +1040,50 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                     }
                 }
                 trace_mark(P, 0, 5 * P.L + 1);
-                // Each warp takes rows 2w, 2w+1 of every stage and waits on the
-                // stage by itself; lane 0 arrives on the stage's "empty" barrier and
-                // thread 0 refills a stage once all warps released it.
-                for (int c = 0; c < head_chunks; ++c) {
-                    const int sidx = c % NS;
-                    if (!mbar_wait_warp(mb_head + sidx, (uint32_t)(c / NS) & 1u, st)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint8_t* stage = sm + P.off_gu + (size_t)sidx * head_stage_bytes;
-                    const int r0 = ha + c * HEAD_ROWS, rows = min(HEAD_ROWS, ha + hn - r0);
-                    const int w0 = 2 * warp;
-                    float d0 = 0.f, d1 = 0.f, sc0 = 0.f, sc1 = 0.f;
-                    if (w0 < rows) {
-                        const uint8_t* ra = stage + (size_t)w0 * P.SH;
-                        const uint8_t* rb = stage + (size_t)min(w0 + 1, rows - 1) * P.SH;
-                        int ah0 = 0, am0 = 0, al0 = 0, ah1 = 0, am1 = 0, al1 = 0;
+                // Each warp streams row groups of HEAD_R (groups warp, warp + NW,
+                // ...) straight from HBM, with the next group's 16-byte chunks and
+                // row scales in flight while the current group is reduced.
+                const int ngroups = (hn + HEAD_R - 1) / HEAD_R;
+                int4 wc[HEAD_R][HEAD_MAXC], wn[HEAD_R][HEAD_MAXC];
+                float sc[HEAD_R], sn[HEAD_R];
+                auto load_group = [&](int gi, int4 (&wv)[HEAD_R][HEAD_MAXC], float (&sv)[HEAD_R]) {
+#pragma unroll
+                    for (int rr = 0; rr < HEAD_R; ++rr) {
+                        const int r = ha + gi * HEAD_R + rr;
+                        const bool valid = r < ha + hn;
+                        const uint8_t* row = P.embed + (size_t)(valid ? r : ha) * P.SH;
 #pragma unroll
                         for (int k = 0; k < HEAD_MAXC; ++k) {
                             const int ch = lane + 32 * k;
-                            if (ch < nch_h) {
-                                dp4a16(*reinterpret_cast<const int4*>(ra + (size_t)ch * 16), xv[k][0], xv[k][1], xv[k][2],
-                                       ah0, am0, al0);
-                                dp4a16(*reinterpret_cast<const int4*>(rb + (size_t)ch * 16), xv[k][0], xv[k][1], xv[k][2],
-                                       ah1, am1, al1);
-                            }
+                            wv[rr][k] = (valid && ch < nch_h) ? ld_stream(row + (size_t)ch * 16) : make_int4(0, 0, 0, 0);
                         }
-                        sc0 = row_scale(ra, P.Kh);
-                        sc1 = row_scale(rb, P.Kh);
-                        d0 = planes_to_float(ah0, am0, al0);
-                        d1 = planes_to_float(ah1, am1, al1);
+                        sv[rr] = valid ? __ldg(reinterpret_cast<const float*>(row + P.Kh)) : 0.f;
                     }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(mb_head_empty + sidx);
-                    d0 = warp_sum(d0);
-                    d1 = warp_sum(d1);
-                    if (w0 < rows) {
+                };
+                if (warp < ngroups) load_group(warp, wc, sc);
+                for (int gi = warp; gi < ngroups; gi += NW) {
+                    if (gi + NW < ngroups) load_group(gi + NW, wn, sn);
 #pragma unroll
-                        for (int k = 0; k < 2; ++k) {
-                            if (w0 + k < rows) {
-                                const int r = r0 + w0 + k;
-                                const float v = (k ? d1 * sc1 : d0 * sc0) * inv;
-                                if (lane == k) P.logits[r] = v;
-                                if (better(v, r, best_v, best_i)) {
-                                    best_v = v;
-                                    best_i = r;
-                                }
+                    for (int rr = 0; rr < HEAD_R; ++rr) {
+                        int ah = 0, am = 0, al = 0;
+#pragma unroll
+                        for (int k = 0; k < HEAD_MAXC; ++k) dp4a16(wc[rr][k], xv[k][0], xv[k][1], xv[k][2], ah, am, al);
+                        const float d = warp_sum(planes_to_float(ah, am, al));
+                        const int r = ha + gi * HEAD_R + rr;
+                        if (r < ha + hn) {
+                            const float v = d * sc[rr] * inv;
+                            if (lane == rr) P.logits[r] = v;
+                            if (better(v, r, best_v, best_i)) {
+                                best_v = v;
+                                best_i = r;
                             }
                         }
                     }
-                    if (tid == 0) {
-                        prefetch_head(c + NS + HEAD_L2_AHEAD);
-                        if (c + NS < head_chunks) {
-                            // All warps released the stage (phase c / NS of its empty barrier).
-                            // On expiry the abort flag is raised and every warp leaves at its next wait.
-                            if (mbar_wait_one(mb_head_empty + sidx, (uint32_t)(c / NS) & 1u, st)) {
-                                fence_proxy_async();
-                                fill_head(c + NS);
-                                ++head_issued;
-                            }
-                        }
+#pragma unroll
+                    for (int rr = 0; rr < HEAD_R; ++rr) {
+                        sc[rr] = sn[rr];
+#pragma unroll
+                        for (int k = 0; k < HEAD_MAXC; ++k) wc[rr][k] = wn[rr][k];
                     }
                 }
                 __syncthreads();
