@@ -53,7 +53,7 @@ struct dcb_engine {
     int* h_result = nullptr;  // pinned [2]: argmax, error
     uint64_t* trace = nullptr;
     uint64_t launches = 0;
-    int split_min = 512;  // positions per attention split, at least
+    int split_min = 64;   // positions per attention split, at least (one chunk)
 
     ~dcb_engine() {
         cudaSetDevice(device);
