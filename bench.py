@@ -316,7 +316,8 @@ def main() -> None:
 
     extra = {}
     if not args.no_long and rank == 0:
-        extra["ctx4096"] = long_context(dcb, model, d, K, W, local)
+        extra["ctx4096"] = long_context(dcb, model, d, K, W, local, 4096)
+        extra["ctx32768"] = long_context(dcb, model, d, min(K, 32), W, local, 32768)
         extra["gemv_sweep"] = gemv_sweep(dcb)
         extra["attention_sweep"] = attention_sweep(dcb)
 
@@ -477,11 +478,12 @@ def attention_sweep(dcb) -> dict:
     return out
 
 
-def long_context(dcb, model, d, K, W, device) -> dict:
-    """Config 3 at ctx 4096: KV pre-filled with seeded N(0,1) rows, greedy steps."""
+def long_context(dcb, model, d, K, W, device, ctx: int = 4096) -> dict:
+    """The full model at a long context: KV rows 0..ctx-1 pre-filled with
+    seeded N(0,1) values (as if already rotated), then greedy steps, F16 and
+    FP32 KV."""
     import torch
     import cpu_decode_b200.synthetic as syn
-    ctx = 4096
     out = {}
     long_dir = MODEL_CACHE / "qwen05_seed0_long"
     long_dir.mkdir(parents=True, exist_ok=True)
@@ -491,7 +493,7 @@ def long_context(dcb, model, d, K, W, device) -> dict:
     link = long_dir / "model.safetensors"
     if not link.exists():
         link.symlink_to((model / "model.safetensors").resolve())
-    rng = np.random.default_rng(4096)
+    rng = np.random.default_rng(ctx)
     kv = [(rng.standard_normal((ctx, d.kv_dim), dtype=np.float32), rng.standard_normal((ctx, d.kv_dim), dtype=np.float32))
           for _ in range(d.layers)]
     for kvt in ("f32", "f16"):
