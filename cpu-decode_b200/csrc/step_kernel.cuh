@@ -205,13 +205,17 @@ __device__ __forceinline__ bool wait_expired(const BlockState& st, uint64_t& t0)
     return false;
 }
 
-// Wait (all threads) until mbarrier `m` completes phase `parity`. Bounded.
-// Ends with __syncthreads so that every thread takes the same decision.
+// Block-wide wait until mbarrier `m` completes phase `parity`. Bounded.
+// Thread 0 alone tests the barrier (512 threads testing one shared word
+// serialise on it); the closing __syncthreads orders the completed copies
+// before every thread's reads and lets all threads take the same decision.
 __device__ bool mbar_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
-    uint64_t t0 = 0;
-    unsigned spins = 0;
-    while (!mbar_test(m, parity))
-        if ((++spins & 63u) == 0 && wait_expired(st, t0)) break;
+    if (threadIdx.x == 0) {
+        uint64_t t0 = 0;
+        unsigned spins = 0;
+        while (!mbar_test(m, parity))
+            if ((++spins & 63u) == 0 && wait_expired(st, t0)) break;
+    }
     __syncthreads();
     return !should_abort(st);
 }
@@ -279,24 +283,6 @@ __device__ Staged finish_stage(int n, int nch, const float* xf, int8_t* xq, int 
     }
     __syncthreads();
     return out;
-}
-
-// One warp waits for phase `parity` of `m` (no block barrier). Bounded.
-__device__ bool mbar_wait_warp(uint64_t* m, uint32_t parity, const BlockState& st) {
-    uint64_t t0 = 0;
-    unsigned spins = 0;
-    bool done = false;
-    while (!(done = mbar_test(m, parity)))
-        if ((++spins & 63u) == 0 && wait_expired(st, t0)) break;
-    return __all_sync(FULL, done) != 0;
-}
-// A single thread waits for phase `parity` of `m`. Bounded.
-__device__ bool mbar_wait_one(uint64_t* m, uint32_t parity, const BlockState& st) {
-    uint64_t t0 = 0;
-    unsigned spins = 0;
-    while (!mbar_test(m, parity))
-        if ((++spins & 63u) == 0 && wait_expired(st, t0)) return false;
-    return true;
 }
 
 // Block-cooperative: wait until the n tagged words at src carry `tag`, accept
