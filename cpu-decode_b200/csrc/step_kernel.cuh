@@ -332,6 +332,124 @@ __device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr
     return !should_abort(st);
 }
 
+// ---- per-warp staging of a GEMV input ---------------------------------------------
+// Warp w owns K-chunks [w*nch/NW, (w+1)*nch/NW) of the input (16 elements
+// each), the same chunks block_gemv gives it. warp_stage waits for exactly
+// those elements (tagged words, or int8 row values times row_sc when `row` is
+// set), keeps the raw values in xr (when set), folds in the RMSNorm gain and
+// quantises them into the planes with the warp's own scale max|v|/FIX_MAX
+// (returned in wscale). Its share of sum v^2 goes to ss_out[warp] (when set).
+// No block barrier: every warp starts its share of the GEMV as soon as its own
+// inputs are in. Returns false when the wait ran out (the abort flag is set).
+template <int W, bool GAIN>
+__device__ bool warp_stage(const uint64_t* src, const uint8_t* row, float row_sc, int n, uint32_t tag, float* xr,
+                           float* xf, int8_t* xq, int plane, int nch, const float* gain, float* ss_out, float& wscale,
+                           const BlockState& st) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = warp * nch / NW, c1 = (warp + 1) * nch / NW;
+    const int e0 = 16 * c0, e1 = min(16 * c1, n);
+    bool okw = true;
+    float ss = 0.f, mx = 0.f;
+    uint64_t t0 = 0;
+    unsigned rounds = 0;
+    for (int base = e0; base < e1; base += 32 * W) {
+        float v[W], g[W];
+        uint64_t w[W];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const int j = base + lane + 32 * k;
+            v[k] = 0.f;
+            g[k] = 1.f;
+            if (j < e1) {
+                if (GAIN) g[k] = __ldg(gain + j);
+                if (row) {
+                    v[k] = (float)(int8_t)row[j] * row_sc;
+                } else {
+                    w[k] = ll_load(src + j);
+                    pending |= 1u << k;
+                }
+            }
+        }
+        while (pending) {
+#pragma unroll
+            for (int k = 0; k < W; ++k)
+                if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
+                    v[k] = __uint_as_float((uint32_t)w[k]);
+                    pending &= ~(1u << k);
+                }
+            if (!pending) break;
+            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) {
+                okw = false;
+                break;
+            }
+#pragma unroll
+            for (int k = 0; k < W; ++k)
+                if ((pending >> k) & 1u) w[k] = ll_load(src + base + lane + 32 * k);
+        }
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const int j = base + lane + 32 * k;
+            if (j < e1) {
+                if (xr) xr[j] = v[k];
+                const float gv = v[k] * g[k];
+                xf[j] = gv;
+                ss = fmaf(v[k], v[k], ss);
+                mx = fmaxf(mx, fabsf(gv));
+            }
+        }
+        if (!okw) break;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(FULL, ss, o);
+        mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    }
+    if (ss_out && lane == 0) ss_out[warp] = ss;
+    const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
+    wscale = mx > 0.f ? __frcp_rn(rs) : 1.0f;
+    __syncwarp();
+    for (int quad = 4 * c0 + lane; quad < 4 * c1; quad += 32) {
+        const int j = 4 * quad;
+        const float4 v4 = j + 3 < n ? *reinterpret_cast<const float4*>(xf + j)
+                                    : make_float4(j < n ? xf[j] : 0.f, j + 1 < n ? xf[j + 1] : 0.f,
+                                                  j + 2 < n ? xf[j + 2] : 0.f, 0.f);
+        uint32_t ph, pm, pl;
+        fix_pack4(v4, rs, ph, pm, pl);
+        reinterpret_cast<uint32_t*>(xq)[quad] = ph;
+        reinterpret_cast<uint32_t*>(xq + plane)[quad] = pm;
+        reinterpret_cast<uint32_t*>(xq + 2 * plane)[quad] = pl;
+    }
+    __syncwarp();
+    return okw;
+}
+
+// One warp waits for phase `parity` of mbarrier m: lane 0 tests, then the
+// warp synchronises (ordering the completed copies before every lane's reads).
+// Bounded; false when the wait ran out (the abort flag is set).
+__device__ bool warp_slot_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
+    bool okw = true;
+    if ((threadIdx.x & 31) == 0) {
+        uint64_t t0 = 0;
+        unsigned spins = 0;
+        while (!mbar_test(m, parity))
+            if ((++spins & 63u) == 0 && wait_expired(st, t0)) {
+                okw = false;
+                break;
+            }
+    }
+    __syncwarp();
+    return __shfl_sync(FULL, okw, 0);
+}
+
+// 1/sqrt(mean(v^2) + eps) from the warps' shares of sum v^2 (src/kernels.cpp:132-137).
+__device__ __forceinline__ float rms_inv(const float* ss, int n, float eps) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) t += ss[w];
+    return __frsqrt_rn(t / (float)n + eps);
+}
+
 // Partial dot products sum_j w_rj q_j of R packed rows in shared memory (stride
 // S bytes, nch chunks of 16 int8 each) with the staged vector. Warp w covers
 // chunks [w*nch/NW, (w+1)*nch/NW); in a warp, LPR consecutive lanes share a row
@@ -342,12 +460,13 @@ __device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr
 // by Staged::scale). Rows are 912 or 4880 bytes apart, so the lanes' 16-byte
 // reads of different rows fall in distinct banks.
 template <int LPR, int P>
-__device__ __noinline__ void block_gemv(const uint8_t* rows, int S, int R, int nch, const int8_t* xq, int plane, float* partial) {
+__device__ __noinline__ void block_gemv(const uint8_t* rows, int S, int R, int nch, const int8_t* xq, int plane,
+                                        float* partial, float wscale = 1.0f, bool run = true) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c0 = warp * nch / NW, c1 = (warp + 1) * nch / NW;
     const int sub = lane % LPR, slot = lane / LPR;
     constexpr int RPP = 32 / LPR;
-    for (int r0 = 0; r0 < R; r0 += RPP * P) {
+    for (int r0 = 0; run && r0 < R; r0 += RPP * P) {
         int ah[P], am[P], al[P];
 #pragma unroll
         for (int p = 0; p < P; ++p) ah[p] = am[p] = al[p] = 0;
@@ -368,7 +487,7 @@ __device__ __noinline__ void block_gemv(const uint8_t* rows, int S, int R, int n
             float t = planes_to_float(ah[p], am[p], al[p]);
 #pragma unroll
             for (int o = LPR / 2; o > 0; o >>= 1) t += __shfl_xor_sync(FULL, t, o);
-            if (sub == 0 && r < R) partial[warp * R + r] = t;
+            if (sub == 0 && r < R) partial[warp * R + r] = t * wscale;
         }
     }
     __syncthreads();
@@ -744,6 +863,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     uint64_t* mb_att = mb + MB_ATT;
     __shared__ float s_cos[64], s_sin[64];
     __shared__ __align__(16) float red[2 * NW + 8];  // read as float4 in finish_stage
+    __shared__ float s_ss[NW];  // the warps' shares of sum x^2 for the RMSNorm of a phase
     __shared__ int s_abort;
     __shared__ unsigned s_fills[NMB];  // fills issued per mbarrier (thread 0)
 
@@ -826,32 +946,29 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         }
 
         // ---- QKV (src/model.cpp:276-302); x entering layer l carries `tag`.
+        // Each warp stages its own chunks of x (RMSNorm gain folded in) and
+        // starts its share of the GEMV; 1/rms scales the row totals.
         trace_detail(P, l, 0, 0);
         if (qn || on) {
-            // x with the input RMSNorm gain folded in; 1/rms scales the results.
-            Staged sx;
-            if (l == 0) {
-                const uint8_t* er = P.embed + (size_t)token * P.SH;
-                const float es = row_scale(er, P.Kh);
-                float ss = 0.f, mx = 0.f;
-                for (int j = tid; j < H; j += NT)
-                    accept(j, (float)(int8_t)er[j] * es, xr, xf, __ldg(in_norm + j), ss, mx);
-                sx = finish_stage(H, nch_h, xf, xq, QP, ss, mx, red, P.eps);
-            } else if (!gather_stage<2, true>(P.ll_xa, H, tag, xr, xf, xq, QP, nch_h, in_norm, red, P.eps, sx, st)) {
-                ok = false;
-                break;
-            }
-            const float inv = sx.inv * sx.scale;
+            float wsc;
+            const uint8_t* er = l == 0 ? P.embed + (size_t)token * P.SH : nullptr;
+            const bool okw = warp_stage<2, true>(P.ll_xa, er, er ? row_scale(er, P.Kh) : 0.f, H, tag, xr, xf, xq, QP,
+                                                 nch_h, in_norm, s_ss, wsc, st);
             trace_detail(P, l, 0, 1);
             if (qn) {
                 trace_detail(P, l, 0, 2);
-                if (!mbar_wait(mb_qkv, (uint32_t)l & 1u, st)) { ok = false; break; }
+                const bool okg = okw && warp_slot_wait(mb_qkv, (uint32_t)l & 1u, st);
                 trace_mark(P, 0, ph + 1);
                 trace_detail(P, l, 0, 3);
                 const int qpairs = P.NH * half, kpairs = P.NKV * half;
-                block_gemv<8, 2>(s_qkv, P.SH, 2 * qn, nch_h, xq, QP, gpart);
+                block_gemv<8, 2>(s_qkv, P.SH, 2 * qn, nch_h, xq, QP, gpart, wsc, okg);
+                if (should_abort(st)) {
+                    ok = false;
+                    break;
+                }
                 // One thread per RoPE pair (rows j, j + d/2 of a head).
                 if (tid < qn) {
+                    const float inv = rms_inv(s_ss, H, P.eps);
                     const int w = tid, u = qa + w;
                     const uint8_t* r0 = s_qkv + (size_t)w * 2 * P.SH;
                     float y0 = gemv_row(gpart, 2 * qn, 2 * w) * inv * row_scale(r0, P.Kh) + row_bias(r0, P.Kh);
@@ -907,20 +1024,21 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // ---- O projection + residual (src/model.cpp:304-305)
         if (on) {
             trace_detail(P, l, 2, 0);
-            Staged sa;
-            if (!gather_stage<2, false>(P.ll_attn, H, tag, nullptr, xf, xq, QP, nch_h, nullptr, red, P.eps, sa, st)) {
+            float wsc;
+            const bool okw = warp_stage<2, false>(P.ll_attn, nullptr, 0.f, H, tag, nullptr, xf, xq, QP, nch_h, nullptr,
+                                                  nullptr, wsc, st);
+            trace_detail(P, l, 2, 1);
+            const bool okg = okw && warp_slot_wait(mb_o, (uint32_t)l & 1u, st);
+            trace_mark(P, 0, ph + 3);
+            trace_detail(P, l, 2, 2);
+            block_gemv<8, 2>(s_o, P.SH, on, nch_h, xq, QP, gpart, wsc, okg);
+            if (should_abort(st)) {
                 ok = false;
                 break;
             }
-            trace_detail(P, l, 2, 1);
-            if (!mbar_wait(mb_o, (uint32_t)l & 1u, st)) { ok = false; break; }
-            trace_mark(P, 0, ph + 3);
-            trace_detail(P, l, 2, 2);
-            block_gemv<8, 2>(s_o, P.SH, on, nch_h, xq, QP, gpart);
             if (tid < on) {
                 const int r = oa + tid;
-                ll_store(P.ll_xb + r,
-                         xr[r] + gemv_row(gpart, on, tid) * sa.scale * row_scale(s_o + (size_t)tid * P.SH, P.Kh), tag);
+                ll_store(P.ll_xb + r, xr[r] + gemv_row(gpart, on, tid) * row_scale(s_o + (size_t)tid * P.SH, P.Kh), tag);
             }
             trace_detail(P, l, 2, 3);
             __syncthreads();
@@ -936,20 +1054,22 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // ---- gate/up + SiLU (src/model.cpp:306-308)
         if (gn || dn) {
             trace_detail(P, l, 3, 0);
-            Staged sb;
-            if (!gather_stage<2, true>(P.ll_xb, H, tag, xr, xf, xq, QP, nch_h, post_norm, red, P.eps, sb, st)) {
-                ok = false;
-                break;
-            }
-            const float inv = sb.inv * sb.scale;
+            float wsc;
+            const bool okw = warp_stage<2, true>(P.ll_xb, nullptr, 0.f, H, tag, xr, xf, xq, QP, nch_h, post_norm, s_ss,
+                                                 wsc, st);
             trace_detail(P, l, 3, 1);
             if (gn) {
                 trace_detail(P, l, 3, 2);
-                if (!mbar_wait(mb_gu, (uint32_t)l & 1u, st)) { ok = false; break; }
+                const bool okg = okw && warp_slot_wait(mb_gu, (uint32_t)l & 1u, st);
                 trace_mark(P, 0, ph + 4);
                 trace_detail(P, l, 3, 3);
-                block_gemv<1, 3>(s_gu, P.SH, 2 * gn, nch_h, xq, QP, gpart);
+                block_gemv<1, 3>(s_gu, P.SH, 2 * gn, nch_h, xq, QP, gpart, wsc, okg);
+                if (should_abort(st)) {
+                    ok = false;
+                    break;
+                }
                 if (tid < gn) {
+                    const float inv = rms_inv(s_ss, H, P.eps);
                     const uint8_t* r0 = s_gu + (size_t)tid * 2 * P.SH;
                     const float g = gemv_row(gpart, 2 * gn, 2 * tid) * inv * row_scale(r0, P.Kh);
                     const float u = gemv_row(gpart, 2 * gn, 2 * tid + 1) * inv * row_scale(r0 + P.SH, P.Kh);
@@ -972,22 +1092,22 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // ---- down + residual (src/model.cpp:309-310); x entering layer l+1 carries tag + 1.
         if (dn) {
             trace_detail(P, l, 4, 0);
-            Staged sh;
-            if (!gather_stage<10, false>(P.ll_h, I, tag, nullptr, xf_i, xq_i, P.down_plane, nch_i, nullptr, red, P.eps,
-                                         sh, st)) {
+            float wsc;
+            const bool okw = warp_stage<10, false>(P.ll_h, nullptr, 0.f, I, tag, nullptr, xf_i, xq_i, P.down_plane,
+                                                   nch_i, nullptr, nullptr, wsc, st);
+            trace_detail(P, l, 4, 1);
+            const bool okg = okw && warp_slot_wait(mb_down, (uint32_t)l & 1u, st);
+            trace_mark(P, 0, ph + 5);
+            trace_detail(P, l, 4, 2);
+            block_gemv<8, 2>(s_down, P.SI, dn, nch_i, xq_i, P.down_plane, gpart, wsc, okg);
+            if (should_abort(st)) {
                 ok = false;
                 break;
             }
-            trace_detail(P, l, 4, 1);
-            if (!mbar_wait(mb_down, (uint32_t)l & 1u, st)) { ok = false; break; }
-            trace_mark(P, 0, ph + 5);
-            trace_detail(P, l, 4, 2);
-            block_gemv<8, 2>(s_down, P.SI, dn, nch_i, xq_i, P.down_plane, gpart);
             trace_detail(P, l, 4, 3);
             if (tid < dn) {
                 const int r = da + tid;
-                ll_store(P.ll_xa + r,
-                         xr[r] + gemv_row(gpart, dn, tid) * sh.scale * row_scale(s_down + (size_t)tid * P.SI, P.Ki),
+                ll_store(P.ll_xa + r, xr[r] + gemv_row(gpart, dn, tid) * row_scale(s_down + (size_t)tid * P.SI, P.Ki),
                          tag + 1);
             }
             __syncthreads();
