@@ -50,7 +50,7 @@ struct dcb_engine {
     std::vector<void*> allocations;
     int grid = 0, smem = 0, sms = 0;
     void* kernel = nullptr;
-    int* h_result = nullptr;  // pinned [2]: argmax, error
+    int* h_result = nullptr;  // pinned [2]: error, argmax (copied together from Sync)
     uint64_t* trace = nullptr;
     uint64_t launches = 0;
     int split_min = 64;   // positions per attention split, at least (one chunk)
@@ -142,8 +142,9 @@ void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len) 
     *nsplit = ceil_div(length, *split_len);
 }
 
-int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax_dev) {
+int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax_dev, float* host_logits = nullptr) {
     StepArgs A{};
+    A.host_logits = host_logits;
     A.token = token;
     A.token_dev = token_dev;
     A.pos = (int)e->pos;
@@ -318,7 +319,6 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     if (int rc = e->alloc(&P.logits, e->V)) return bail(rc);
     if (int rc = e->alloc(&P.amax, G)) return bail(rc);
     if (int rc = e->alloc(&P.sync, 1)) return bail(rc);
-    if (int rc = e->alloc(&P.result, 4)) return bail(rc);
 
     // ---- shared memory plan (bytes): weight slots, attention chunk ring, vectors
     e->kernel = kv_dtype == DCB_KV_F16 ? (void*)decode_step_kernel<__half> : (void*)decode_step_kernel<float>;
@@ -400,15 +400,26 @@ int dcb_step(dcb_engine* e, int token, int head, float* host_logits, int* argmax
     if (token < 0 || token >= e->V) return fail(DCB_ERR_TOKEN, "token ID outside vocabulary");
     if (e->pos >= e->capacity) return fail(DCB_ERR_CAPACITY, "context capacity exceeded");
     DCB_CUDA(cudaSetDevice(e->device));
-    if (int rc = launch(e, token, nullptr, head, nullptr)) return rc;
-    if (head && host_logits)
+    // Pinned (registered or cudaHostAlloc'd) logits buffers are written by the
+    // LM head itself over PCIe; any other buffer gets a copy after the kernel.
+    float* mapped = nullptr;
+    if (head && host_logits) {
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, host_logits) == cudaSuccess && at.type == cudaMemoryTypeHost &&
+            at.devicePointer)
+            mapped = static_cast<float*>(at.devicePointer);
+        else
+            cudaGetLastError();  // a pageable pointer is not an error here
+    }
+    if (int rc = launch(e, token, nullptr, head, nullptr, mapped)) return rc;
+    if (head && host_logits && !mapped)
         DCB_CUDA(cudaMemcpyAsync(host_logits, e->P.logits, (size_t)e->V * sizeof(float), cudaMemcpyDeviceToHost,
                                  e->stream));
-    DCB_CUDA(cudaMemcpyAsync(e->h_result, e->P.result, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
-    DCB_CUDA(cudaMemcpyAsync(e->h_result + 1, &e->P.sync->error, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    // error and argmax in one copy (adjacent in Sync)
+    DCB_CUDA(cudaMemcpyAsync(e->h_result, &e->P.sync->error, 2 * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     DCB_CUDA(cudaStreamSynchronize(e->stream));
-    if (int rc = device_error(e, e->h_result[1])) return rc;
-    if (head && argmax_out) *argmax_out = e->h_result[0];
+    if (int rc = device_error(e, e->h_result[0])) return rc;
+    if (head && argmax_out) *argmax_out = e->h_result[1];
     ++e->pos;
     return 0;
 }

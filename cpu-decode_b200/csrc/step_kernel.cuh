@@ -58,7 +58,8 @@ struct LayerW {
 
 struct Sync {
     unsigned amax_done;
-    int error;
+    int error;   // first error of the step (ERR_*), 0 if none
+    int result;  // argmax of the logits; follows `error` so one 8-byte copy reads both
 };
 
 struct ArgBest {
@@ -88,7 +89,6 @@ struct Params {
     float* logits;        // [V]
     ArgBest* amax;        // [grid]
     Sync* sync;
-    int* result;
     uint64_t* trace;  // [2][TRACE_MAX_PHASES][grid] ready/done ns, or null
     // shared memory layout (bytes)
     int off_gu, off_down, off_qkv, off_o, off_att, off_xs, off_xq, off_gpart, off_xr, off_misc;
@@ -110,6 +110,7 @@ struct StepArgs {
     int nsplit;
     int split_len;
     unsigned seq;
+    float* host_logits;  // mapped pinned host memory the LM head also writes, or null
 };
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
@@ -1169,6 +1170,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                 if (warp < ngroups) load_group(warp, wc, sc);
                 for (int gi = warp; gi < ngroups; gi += NW) {
                     if (gi + NW < ngroups) load_group(gi + NW, wn, sn);
+                    float vmine = 0.f;  // lane rr keeps row rr's logit: one store per group
 #pragma unroll
                     for (int rr = 0; rr < HEAD_R; ++rr) {
                         int ah = 0, am = 0, al = 0;
@@ -1178,11 +1180,18 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                         const int r = ha + gi * HEAD_R + rr;
                         if (r < ha + hn) {
                             const float v = d * sc[rr] * inv;
-                            if (lane == rr) P.logits[r] = v;
+                            if (lane == rr) vmine = v;
                             if (better(v, r, best_v, best_i)) {
                                 best_v = v;
                                 best_i = r;
                             }
+                        }
+                    }
+                    {
+                        const int r = ha + gi * HEAD_R + lane;
+                        if (lane < HEAD_R && r < ha + hn) {
+                            P.logits[r] = vmine;
+                            if (A.host_logits) A.host_logits[r] = vmine;
                         }
                     }
 #pragma unroll
@@ -1225,7 +1234,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                         if (better(t.v, t.i, r.v, r.i)) r = t;
                     }
                     if (r.i == 0x7fffffff) r.i = 0;
-                    P.result[0] = r.i;
+                    P.sync->result = r.i;
                     if (A.argmax_dev) *A.argmax_dev = r.i;
                     P.sync->amax_done = 0;
                 }
