@@ -315,6 +315,10 @@ def main() -> None:
     assert nxt == generated_last, "host-driven and device-chained greedy streams diverged"
 
     extra = {}
+    if dist and not args.no_long:
+        split = kv_split_context(dcb, model, d, min(K, 32), W, local, dist, 32768)
+        if rank == 0:
+            extra["ctx32768_kv_split"] = split
     if not args.no_long and rank == 0:
         extra["ctx4096"] = long_context(dcb, model, d, K, W, local, 4096)
         extra["ctx32768"] = long_context(dcb, model, d, min(K, 32), W, local, 32768)
@@ -478,13 +482,8 @@ def attention_sweep(dcb) -> dict:
     return out
 
 
-def long_context(dcb, model, d, K, W, device, ctx: int = 4096) -> dict:
-    """The full model at a long context: KV rows 0..ctx-1 pre-filled with
-    seeded N(0,1) values (as if already rotated), then greedy steps, F16 and
-    FP32 KV."""
-    import torch
-    import cpu_decode_b200.synthetic as syn
-    out = {}
+def _long_model_dir(model: Path) -> Path:
+    """The same model with max_position_embeddings raised for long contexts."""
     long_dir = MODEL_CACHE / "qwen05_seed0_long"
     long_dir.mkdir(parents=True, exist_ok=True)
     cfg = json.loads((model / "config.json").read_text())
@@ -493,6 +492,76 @@ def long_context(dcb, model, d, K, W, device, ctx: int = 4096) -> dict:
     link = long_dir / "model.safetensors"
     if not link.exists():
         link.symlink_to((model / "model.safetensors").resolve())
+    return long_dir
+
+
+def kv_split_context(dcb, model, d, K, W, device, dist, ctx: int) -> dict:
+    """One stream at `ctx` pre-filled positions with its KV cache split over
+    all ranks (one GPU each): each rank keeps a contiguous range, the last one
+    also the new tokens; every rank runs the whole step and the ranks merge the
+    per-head attention partials over NVLink each layer. Same seeded K/V rows as
+    the one-GPU measurement. Device-chained greedy steps, time = max over
+    ranks (strong scaling: the total work is fixed)."""
+    import torch
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if rank == 0:
+        _long_model_dir(model)
+    dist.barrier()
+    long_dir = MODEL_CACHE / "qwen05_seed0_long"
+    out = {}
+    for kvt in ("f32",):
+        begin, end = dcb.kv_shard_ranges(ctx, world)[rank]
+        cap = (end if end is not None else ctx + K + W + 2) - begin
+        eng = dcb.Engine(long_dir, cap, kv_dtype=kvt, device=device)
+        stream = torch.cuda.current_stream()
+        eng.set_stream(stream.cuda_stream)
+        peers = dcb.split_kv(eng, begin, end)
+        rng = np.random.default_rng(ctx)
+        top = ctx if end is None else end
+        for l in range(d.layers):  # the same rows as the one-GPU run draws, this rank's slice
+            k = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+            v = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+            eng.kv_write(l, begin, k[begin:top], v[begin:top])
+        tok = torch.full((1,), 1234, dtype=torch.int32, device="cuda")
+        eng.set_position(ctx)
+        for _ in range(W):
+            eng.step_async(token_dev=tok.data_ptr(), head=True, argmax_dev=tok.data_ptr())
+        eng.synchronize()
+        eng.set_position(ctx)
+        tok.fill_(1234)
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record(stream)
+        for _ in range(K):
+            eng.step_async(token_dev=tok.data_ptr(), head=True, argmax_dev=tok.data_ptr())
+        e.record(stream)
+        torch.cuda.synchronize()
+        eng.synchronize()
+        ms = torch.tensor([s.elapsed_time(e)], device="cuda")
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        last = torch.tensor([int(tok.item())], device="cuda", dtype=torch.int64)
+        lmax, lmin = last.clone(), last.clone()
+        dist.all_reduce(lmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lmin, op=dist.ReduceOp.MIN)
+        dist.barrier()
+        eng.close()
+        for p in peers:
+            dcb.ipc_close(p)
+        t = float(ms.item())
+        out[kvt] = {"gpus": world, "tokens_per_s": round(K / (t / 1000.0), 2), "ms_per_step": round(t / K, 5),
+                    "ranks_agree": bool(lmax.item() == lmin.item())}
+    return out
+
+
+def long_context(dcb, model, d, K, W, device, ctx: int = 4096) -> dict:
+    """The full model at a long context: KV rows 0..ctx-1 pre-filled with
+    seeded N(0,1) values (as if already rotated), then greedy steps, F16 and
+    FP32 KV."""
+    import torch
+    import cpu_decode_b200.synthetic as syn
+    out = {}
+    long_dir = _long_model_dir(model)
     rng = np.random.default_rng(ctx)
     kv = [(rng.standard_normal((ctx, d.kv_dim), dtype=np.float32), rng.standard_normal((ctx, d.kv_dim), dtype=np.float32))
           for _ in range(d.layers)]

@@ -34,7 +34,8 @@ EXPORTS = (
     "dcb_step_async", "dcb_synchronize", "dcb_rewind", "dcb_reset", "dcb_position", "dcb_set_stream", "dcb_stream",
     "dcb_logits_device", "dcb_kv_write", "dcb_kv_read", "dcb_set_position", "dcb_launch_info", "dcb_launch_count",
     "dcb_gemv_i8", "dcb_attention", "dcb_attention_noalloc", "dcb_rmsnorm", "dcb_rope", "dcb_argmax",
-    "dcb_trace_enable", "dcb_trace_read",
+    "dcb_trace_enable", "dcb_trace_read", "dcb_exchange_buffer", "dcb_ipc_handle", "dcb_ipc_open", "dcb_ipc_close",
+    "dcb_set_kv_shard",
 )
 
 
@@ -87,6 +88,11 @@ def lib() -> C.CDLL:
     L.dcb_argmax.argtypes = [vp, i32, vp, vp]
     L.dcb_trace_enable.argtypes = [vp, i32]
     L.dcb_trace_read.argtypes = [vp, vp, vp, C.POINTER(i32)]
+    L.dcb_exchange_buffer.argtypes = [vp, C.POINTER(vp), C.POINTER(sz)]
+    L.dcb_ipc_handle.argtypes = [vp, vp]
+    L.dcb_ipc_open.argtypes = [vp, C.POINTER(vp)]
+    L.dcb_ipc_close.argtypes = [vp]
+    L.dcb_set_kv_shard.argtypes = [vp, i32, i32, sz, sz, vp]
     _LIB = L
     return L
 
@@ -201,6 +207,20 @@ class Engine:
     def launch_count(self) -> int:
         return int(lib().dcb_launch_count(self._h))
 
+    def exchange_buffer(self) -> int:
+        """Device pointer of the buffer peers write this engine's share of a
+        KV-split attention into."""
+        ptr, size = C.c_void_p(), C.c_size_t()
+        _check(lib().dcb_exchange_buffer(self._h, C.byref(ptr), C.byref(size)))
+        return int(ptr.value)
+
+    def set_kv_shard(self, rank: int, world: int, begin: int, end: int | None, peers: list[int]) -> None:
+        """Keep KV positions [begin, end) (end None: open) as rank `rank` of
+        `world` engines; peers[q] is rank q's exchange buffer opened here."""
+        arr = (C.c_void_p * max(1, world))(*[C.c_void_p(int(p) or None) for p in peers])
+        _check(lib().dcb_set_kv_shard(self._h, int(rank), int(world), int(begin),
+                                      SIZE_MAX if end is None else int(end), arr))
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib().dcb_destroy(self._h)
@@ -211,6 +231,55 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+# ---- one stream over several GPUs (KV sequence split) -------------------------------
+SIZE_MAX = (1 << 64) - 1
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_handle(device_ptr: int) -> bytes:
+    buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib().dcb_ipc_handle(device_ptr, buf))
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = C.c_void_p()
+    buf = C.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES)
+    _check(lib().dcb_ipc_open(buf, C.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close(device_ptr: int) -> None:
+    _check(lib().dcb_ipc_close(device_ptr))
+
+
+def kv_shard_ranges(total: int, world: int) -> list[tuple[int, int | None]]:
+    """Contiguous KV ranges of `total` cached positions over `world` engines;
+    the last range is open (it also keeps the positions generated later)."""
+    bounds = [total * r // world for r in range(world + 1)]
+    return [(bounds[r], bounds[r + 1] if r + 1 < world else None) for r in range(world)]
+
+
+def exchange_handles(handle: bytes, group=None) -> list[bytes]:
+    """All ranks' IPC handles, indexed by rank (torch.distributed plumbing)."""
+    import torch.distributed as dist
+    out: list = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(handle), group=group)
+    return [bytes(h) for h in out]
+
+
+def split_kv(engine: "Engine", begin: int, end: int | None, group=None) -> list[int]:
+    """Join the engines of all ranks of `group` into one KV-split stream: this
+    rank keeps [begin, end). Returns the peer buffers opened here (close them
+    with ipc_close after the engines are done)."""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    handles = exchange_handles(ipc_handle(engine.exchange_buffer()), group)
+    peers = [0 if q == rank else ipc_open(h) for q, h in enumerate(handles)]
+    engine.set_kv_shard(rank, world, begin, end, peers)
+    return [p for p in peers if p]
 
 
 # ---- isolated operators on device pointers ------------------------------------------

@@ -46,6 +46,12 @@ struct dcb_engine {
     int H, I, L, NH, NKV, D, V;
     int kv_dtype = DCB_KV_F32;
     size_t capacity = 0, pos = 0;
+    // KV sequence split: this engine keeps positions [kv_base, kv_end) (local
+    // rows from 0); one engine alone keeps [0, unbounded).
+    size_t kv_base = 0, kv_end = SIZE_MAX;
+    bool owns(size_t p) const { return p >= kv_base && p < kv_end; }
+    // Positions this engine attends over at position p (its range up to p).
+    size_t attended(size_t p) const { return p < kv_base ? 0 : std::min(kv_end, p + 1) - kv_base; }
     unsigned seq = 0;
     std::vector<void*> allocations;
     int grid = 0, smem = 0, sms = 0;
@@ -150,7 +156,7 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
     A.pos = (int)e->pos;
     A.head = head;
     A.argmax_dev = argmax_dev;
-    choose_split(e, (int)e->pos + 1, &A.nsplit, &A.split_len);
+    choose_split(e, (int)e->attended(e->pos), &A.nsplit, &A.split_len);
     if (++e->seq >= (1u << 24)) e->seq = 1;  // tags are seq << 8 | layer
     A.seq = e->seq;
     void* args[] = {(void*)&e->P, (void*)&A};
@@ -230,6 +236,10 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     P.eps = m->epsilon;
     P.cached_rope = cached_rope ? 1 : 0;
     P.capacity = (int)capacity;
+    P.kv_base = 0;
+    P.kv_end = 0x7fffffff;
+    P.world = 1;
+    P.rank = 0;
 
     // ---- weights in packed-row layout
     std::vector<LayerW> lw(e->L);
@@ -316,6 +326,16 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     if (int rc = e->alloc(&P.ll_attn, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_h, I)) return bail(rc);
     if (int rc = e->alloc(&P.ll_part, (size_t)e->NH * (G + 1) * (D + 2))) return bail(rc);
+    // KV-split exchange: [2 slots][NH][MAX_WORLD][D+2] tagged words, and the
+    // ranks' buffers (this engine's own until dcb_set_kv_shard).
+    if (int rc = e->alloc(&P.exch, (size_t)2 * e->NH * MAX_WORLD * (D + 2))) return bail(rc);
+    {
+        uint64_t** peers = nullptr;
+        if (int rc = e->alloc(&peers, MAX_WORLD)) return bail(rc);
+        uint64_t* own[MAX_WORLD] = {P.exch};
+        DCB_CUDA(cudaMemcpy(peers, own, sizeof(own), cudaMemcpyHostToDevice));
+        P.peers = peers;
+    }
     if (int rc = e->alloc(&P.logits, e->V)) return bail(rc);
     if (int rc = e->alloc(&P.amax, G)) return bail(rc);
     if (int rc = e->alloc(&P.sync, 1)) return bail(rc);
@@ -395,10 +415,19 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
 
 void dcb_destroy(dcb_engine* e) { delete e; }
 
+// The step at e->pos must have a row for its K/V if this engine keeps that
+// position, and at least one position to attend over.
+int check_position(const dcb_engine* e) {
+    if (e->owns(e->pos) && e->pos - e->kv_base >= e->capacity)
+        return fail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    if (e->pos < e->kv_base) return fail(DCB_ERR_ARGUMENT, "position before this engine's KV range");
+    return 0;
+}
+
 int dcb_step(dcb_engine* e, int token, int head, float* host_logits, int* argmax_out) {
     if (!e) return fail(DCB_ERR_ARGUMENT, "null engine");
     if (token < 0 || token >= e->V) return fail(DCB_ERR_TOKEN, "token ID outside vocabulary");
-    if (e->pos >= e->capacity) return fail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    if (int rc = check_position(e)) return rc;
     DCB_CUDA(cudaSetDevice(e->device));
     // Pinned (registered or cudaHostAlloc'd) logits buffers are written by the
     // LM head itself over PCIe; any other buffer gets a copy after the kernel.
@@ -427,7 +456,7 @@ int dcb_step(dcb_engine* e, int token, int head, float* host_logits, int* argmax
 int dcb_step_async(dcb_engine* e, int token, const int* token_dev, int head, int* argmax_dev) {
     if (!e) return fail(DCB_ERR_ARGUMENT, "null engine");
     if (!token_dev && (token < 0 || token >= e->V)) return fail(DCB_ERR_TOKEN, "token ID outside vocabulary");
-    if (e->pos >= e->capacity) return fail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    if (int rc = check_position(e)) return rc;
     DCB_CUDA(cudaSetDevice(e->device));
     if (int rc = launch(e, token, token_dev, head, argmax_dev)) return rc;
     ++e->pos;
@@ -456,7 +485,8 @@ size_t dcb_position(const dcb_engine* e) { return e ? e->pos : 0; }
 
 int dcb_set_position(dcb_engine* e, size_t position) {
     if (!e) return fail(DCB_ERR_ARGUMENT, "null engine");
-    if (position > e->capacity) return fail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    if (position > e->kv_base && std::min(position, e->kv_end) - e->kv_base > e->capacity)
+        return fail(DCB_ERR_CAPACITY, "context capacity exceeded");
     e->pos = position;
     return 0;
 }
@@ -482,8 +512,10 @@ const float* dcb_logits_device(const dcb_engine* e) { return e ? e->P.logits : n
 // cache is head-major, so each head is one strided 2-D copy.
 int dcb_kv_write(dcb_engine* e, int layer, size_t start, size_t count, const float* keys, const float* values) {
     if (!e || !keys || !values) return fail(DCB_ERR_ARGUMENT, "null argument");
-    if (layer < 0 || layer >= e->L || start + count > e->capacity)
+    if (layer < 0 || layer >= e->L || start < e->kv_base || start + count > e->kv_end ||
+        start - e->kv_base + count > e->capacity)
         return fail(DCB_ERR_ARGUMENT, "KV rows out of range");
+    start -= e->kv_base;  // local rows
     if (!count) return 0;
     DCB_CUDA(cudaSetDevice(e->device));
     DCB_CUDA(cudaStreamSynchronize(e->stream));
@@ -509,8 +541,10 @@ int dcb_kv_write(dcb_engine* e, int layer, size_t start, size_t count, const flo
 
 int dcb_kv_read(const dcb_engine* e, int layer, size_t start, size_t count, float* keys, float* values) {
     if (!e || !keys || !values) return fail(DCB_ERR_ARGUMENT, "null argument");
-    if (layer < 0 || layer >= e->L || start + count > e->capacity)
+    if (layer < 0 || layer >= e->L || start < e->kv_base || start + count > e->kv_end ||
+        start - e->kv_base + count > e->capacity)
         return fail(DCB_ERR_ARGUMENT, "KV rows out of range");
+    start -= e->kv_base;  // local rows
     if (!count) return 0;
     DCB_CUDA(cudaSetDevice(e->device));
     DCB_CUDA(cudaStreamSynchronize(e->stream));
@@ -531,6 +565,62 @@ int dcb_kv_read(const dcb_engine* e, int layer, size_t start, size_t count, floa
             for (size_t i = 0; i < h.size(); ++i) dst[i] = __half2float(h[i]);
         }
     }
+    return 0;
+}
+
+int dcb_exchange_buffer(dcb_engine* e, void** exchange, size_t* bytes) {
+    if (!e || !exchange) return fail(DCB_ERR_ARGUMENT, "null argument");
+    *exchange = e->P.exch;
+    if (bytes) *bytes = (size_t)2 * e->NH * MAX_WORLD * (e->D + 2) * sizeof(uint64_t);
+    return 0;
+}
+
+int dcb_ipc_handle(const void* device_ptr, void* handle) {
+    if (!device_ptr || !handle) return fail(DCB_ERR_ARGUMENT, "null argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= DCB_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    DCB_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(device_ptr)));
+    std::memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+int dcb_ipc_open(const void* handle, void** device_ptr) {
+    if (!handle || !device_ptr) return fail(DCB_ERR_ARGUMENT, "null argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    DCB_CUDA(cudaIpcOpenMemHandle(device_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return 0;
+}
+
+int dcb_ipc_close(void* device_ptr) {
+    if (!device_ptr) return fail(DCB_ERR_ARGUMENT, "null argument");
+    DCB_CUDA(cudaIpcCloseMemHandle(device_ptr));
+    return 0;
+}
+
+int dcb_set_kv_shard(dcb_engine* e, int rank, int world, size_t kv_begin, size_t kv_end, void* const* peer_exchange) {
+    if (!e) return fail(DCB_ERR_ARGUMENT, "null engine");
+    if (world < 1 || world > MAX_WORLD || rank < 0 || rank >= world)
+        return fail(DCB_ERR_ARGUMENT, "invalid rank or world size (at most 8 GPUs)");
+    if (kv_begin >= kv_end || kv_begin > 0x7ffffffe || (kv_end != SIZE_MAX && kv_end > 0x7fffffff))
+        return fail(DCB_ERR_ARGUMENT, "invalid KV range");
+    if (kv_end != SIZE_MAX && kv_end - kv_begin > e->capacity)
+        return fail(DCB_ERR_CAPACITY, "KV range larger than the context capacity");
+    if (world > 1 && !peer_exchange) return fail(DCB_ERR_ARGUMENT, "null peer exchange buffers");
+    uint64_t* ptrs[MAX_WORLD] = {};
+    for (int q = 0; q < world; ++q) {
+        ptrs[q] = world == 1 || q == rank ? e->P.exch : static_cast<uint64_t*>(peer_exchange[q]);
+        if (!ptrs[q]) return fail(DCB_ERR_ARGUMENT, "null peer exchange buffer");
+    }
+    DCB_CUDA(cudaSetDevice(e->device));
+    DCB_CUDA(cudaStreamSynchronize(e->stream));
+    DCB_CUDA(cudaMemcpy(const_cast<uint64_t**>(e->P.peers), ptrs, sizeof(ptrs), cudaMemcpyHostToDevice));
+    e->kv_base = kv_begin;
+    e->kv_end = kv_end;
+    e->P.kv_base = (int)kv_begin;
+    e->P.kv_end = kv_end == SIZE_MAX ? 0x7fffffff : (int)kv_end;
+    e->P.world = world;
+    e->P.rank = rank;
     return 0;
 }
 

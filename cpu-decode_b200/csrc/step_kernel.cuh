@@ -41,6 +41,7 @@ constexpr int ERR_TOKEN = 2;
 constexpr int ATT_CHUNK = 64;  // KV positions per staged chunk
 constexpr int ATT_PER_WARP = ATT_CHUNK / NW;
 constexpr int ATT_MAX_BUFS = 6;  // staged chunk ring (the host picks how many fit)
+constexpr int MAX_WORLD = 8;     // GPUs that split one stream's KV sequence
 constexpr int HEAD_R = 4;           // LM-head rows a warp reduces per group (the next group in flight)
 constexpr int HEAD_L2_ROWS = 256;   // LM-head rows per block prefetched into L2 during the last layer
 constexpr int HEAD_MAXC = 2;        // 16-byte chunks per lane of a hidden-size row (hidden <= 1024)
@@ -72,6 +73,13 @@ struct Params {
     float eps;
     int cached_rope;
     int capacity;
+    // KV-sequence split over GPUs: this engine keeps positions [kv_base, kv_end)
+    // (local cache row t - kv_base) and attends over them; rank `rank` of
+    // `world` engines exchanges per-head partials through exch (its own
+    // buffer, [2][NH][world][D+2] tagged words) and peers[q] (rank q's buffer).
+    int kv_base, kv_end, world, rank;
+    uint64_t* exch;
+    uint64_t* const* peers;
     const LayerW* layers;
     const uint8_t* embed;   // V packed rows, stride SH (the tied LM head)
     const float* norms;     // [L+1][2][Kh]: (input, post-attention) RMSNorm gains per layer, then (final, 0)
@@ -175,6 +183,17 @@ __device__ __forceinline__ void ll_store(uint64_t* p, float v, uint32_t tag) {
 __device__ __forceinline__ uint64_t ll_load(const uint64_t* p) {
     uint64_t w;
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Tagged words another GPU reads or writes (NVLink peer memory): system scope.
+__device__ __forceinline__ void ll_store_sys(uint64_t* p, float v, uint32_t tag) {
+    const uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ll_load_sys(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
 
@@ -562,7 +581,7 @@ struct AttnPlan {
 
 template <typename KV>
 __device__ __forceinline__ const KV* kv_rows(const Params& P, const void* base, int l, int g, int t) {
-    return static_cast<const KV*>(base) + (((size_t)l * P.NKV + g) * P.capacity + t) * P.D;
+    return static_cast<const KV*>(base) + (((size_t)l * P.NKV + g) * P.capacity + (t - P.kv_base)) * P.D;
 }
 
 // Thread 0: copy the cached rows (positions below pos) of chunk c into buffer c % att_bufs.
@@ -760,7 +779,7 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
             if (j < D) acc = fmaf(fw, wpart[w * (D + 2) + 2 + j], acc);
         }
         if (j < D) {
-            if (A.nsplit == 1) {
+            if (A.nsplit == 1 && P.world == 1) {
                 ll_store(P.ll_attn + (size_t)ap.h * D + j, acc / Lsum, tag);
             } else if (split == 0) {
                 own_m = M;
@@ -778,7 +797,8 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
         }
     }
     trace_detail(P, l, 1, 6);
-    if (A.nsplit == 1 || split != 0) return true;
+    if (split != 0 || (A.nsplit == 1 && P.world == 1)) return true;
+    if (A.nsplit > 1) {
     // Split 0 merges the others (m in base 2): thread t polls words t, t + NT,
     // ... of their (nsplit-1)*(D+2)-word table, all loads in flight, into the
     // chunk buffers (consumed by now); then thread j < D combines dimension j
@@ -827,6 +847,80 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
                 const float f = ex2_approx(table[i * (D + 2)] - Mx);
                 num = fmaf(f, table[i * (D + 2) + 2 + j], num);
                 den = fmaf(f, table[i * (D + 2) + 1], den);
+            }
+            if (P.world == 1) {
+                ll_store(P.ll_attn + (size_t)ap.h * D + j, num / den, tag);
+            } else {
+                own_m = Mx;
+                own_l = den;
+                own_acc = num;
+            }
+        }
+    }
+    }
+    if (P.world == 1) return true;
+    // KV sequence split over GPUs: this GPU's (m, l, o) of head h goes to every
+    // rank's exchange buffer (system-scope tagged words over NVLink); then all
+    // ranks' partials are polled from the local buffer and merged in rank order,
+    // so every GPU ends with the same attention output. Slots alternate with the
+    // global layer count: a rank one layer ahead writes the other slot.
+    {
+        __syncthreads();  // the split tables above are consumed
+        float* own = reinterpret_cast<float*>(att);  // [D+2]: m, l, o
+        float* tab = own + (D + 2);                   // [world][D+2]
+        if ((int)threadIdx.x < D) {
+            own[2 + threadIdx.x] = own_acc;
+            if (threadIdx.x == 0) {
+                own[0] = own_m;
+                own[1] = own_l;
+            }
+        }
+        __syncthreads();
+        const int slot = (int)((A.seq * (unsigned)P.L + (unsigned)l) & 1u);
+        const int nw = P.world * (D + 2);
+        for (int i = threadIdx.x; i < nw; i += NT) {
+            const int q = i / (D + 2), k = i - q * (D + 2);
+            ll_store_sys(P.peers[q] + (((size_t)slot * P.NH + ap.h) * P.world + P.rank) * (D + 2) + k, own[k], tag);
+        }
+        const uint64_t* src = P.exch + ((size_t)slot * P.NH + ap.h) * P.world * (D + 2);
+        constexpr int WT = 4;  // world * (D+2) <= 8 * 130 < 4 * NT
+        uint64_t w[WT];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < WT; ++k) {
+            const int i = threadIdx.x + k * NT;
+            if (i < nw) {
+                w[k] = ll_load_sys(src + i);
+                pending |= 1u << k;
+            }
+        }
+        uint64_t t0 = 0;
+        unsigned rounds = 0;
+        while (pending) {
+#pragma unroll
+            for (int k = 0; k < WT; ++k)
+                if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
+                    tab[threadIdx.x + k * NT] = __uint_as_float((uint32_t)w[k]);
+                    pending &= ~(1u << k);
+                }
+            if (!pending) break;
+            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+#pragma unroll
+            for (int k = 0; k < WT; ++k)
+                if ((pending >> k) & 1u) w[k] = ll_load_sys(src + threadIdx.x + k * NT);
+        }
+        __syncthreads();
+        if (should_abort(st)) return false;
+        if ((int)threadIdx.x < D) {
+            const int j = threadIdx.x;
+            float Mx = -INFINITY;
+            for (int q = 0; q < P.world; ++q) Mx = fmaxf(Mx, tab[q * (D + 2)]);
+            float num = 0.f, den = 0.f;
+            for (int q = 0; q < P.world; ++q) {
+                const float mq = tab[q * (D + 2)];
+                const float f = mq > -INFINITY ? ex2_approx(mq - Mx) : 0.f;
+                num = fmaf(f, tab[q * (D + 2) + 2 + j], num);
+                den = fmaf(f, tab[q * (D + 2) + 1], den);
             }
             ll_store(P.ll_attn + (size_t)ap.h * D + j, num / den, tag);
         }
@@ -886,8 +980,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     if (has_att) {
         ap.h = b / A.nsplit;
         ap.g = ap.h / (P.NH / P.NKV);
-        ap.t0 = (b % A.nsplit) * A.split_len;
-        ap.t1 = min(A.pos + 1, ap.t0 + A.split_len);
+        ap.t0 = P.kv_base + (b % A.nsplit) * A.split_len;
+        ap.t1 = min(min(A.pos + 1, P.kv_end), ap.t0 + A.split_len);
         ap.nchunks = (ap.t1 - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK;
         ap.nissued = min(ap.nchunks, max(0, (A.pos - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK));
         ap.bulk = ((size_t)D * sizeof(KV)) % 16 == 0;
@@ -988,9 +1082,12 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                         ll_store(P.ll_q + hd * D + j, y0, tag);
                         ll_store(P.ll_q + hd * D + j + half, y1, tag);
                     } else {
-                        KV* cache = (kind == 1 ? kc : vc) + (((size_t)l * P.NKV + hd) * P.capacity + A.pos) * D;
-                        kv_store(cache + j, y0);
-                        kv_store(cache + j + half, y1);
+                        if (A.pos >= P.kv_base && A.pos < P.kv_end) {  // this engine keeps position pos
+                            KV* cache = (kind == 1 ? kc : vc) +
+                                        (((size_t)l * P.NKV + hd) * P.capacity + (A.pos - P.kv_base)) * D;
+                            kv_store(cache + j, y0);
+                            kv_store(cache + j + half, y1);
+                        }
                         uint64_t* nw = P.ll_kv + (kind == 1 ? 0 : kvd) + hd * D;
                         ll_store(nw + j, round_to(y0, KV()), tag);
                         ll_store(nw + j + half, round_to(y1, KV()), tag);

@@ -131,6 +131,41 @@ uint64_t dcb_launch_count(const dcb_engine* e);
 int dcb_trace_enable(dcb_engine* e, int on);
 int dcb_trace_read(dcb_engine* e, uint64_t* ready, uint64_t* done, int* phases);
 
+/* ---- one decode stream over several GPUs (KV sequence split) -------------- */
+
+/* No counterpart in the reference (it runs one sequence on one CPU): for very
+ * long contexts the KV cache of one stream can be split over up to 8 GPUs of a
+ * node, one engine (and one process) per GPU, all on the same model. Every
+ * engine runs the whole step; each attends only over the KV positions it
+ * keeps, and per layer the engines exchange each head's partial softmax state
+ * (max, sum, output) through NVLink peer memory and merge them in rank order,
+ * so all of them produce the same logits and tokens. Steps must be issued on
+ * all engines alike (same tokens, same order).
+ *
+ * Setup: each engine exports its exchange buffer (dcb_exchange_buffer,
+ * dcb_ipc_handle); the handles are shared between the processes (any
+ * transport); each process opens its peers' handles (dcb_ipc_open) and calls
+ * dcb_set_kv_shard with the opened pointers, indexed by rank. */
+enum { DCB_IPC_HANDLE_BYTES = 64 };
+
+/* The engine's exchange buffer (device memory) and its size in bytes. */
+int dcb_exchange_buffer(dcb_engine* e, void** exchange, size_t* bytes);
+
+/* cudaIpcGetMemHandle / cudaIpcOpenMemHandle / cudaIpcCloseMemHandle on a
+ * device pointer; handle points to DCB_IPC_HANDLE_BYTES bytes. */
+int dcb_ipc_handle(const void* device_ptr, void* handle);
+int dcb_ipc_open(const void* handle, void** device_ptr);
+int dcb_ipc_close(void* device_ptr);
+
+/* Make e rank `rank` of `world` engines sharing one stream: it keeps the KV
+ * rows of absolute positions [kv_begin, kv_end) (kv_end = SIZE_MAX: open, for
+ * the last rank, which then keeps the new tokens' rows too), as local rows
+ * 0.., and exchanges partials through peer_exchange[q] (rank q's exchange
+ * buffer as opened in this process; entry `rank` is ignored). dcb_kv_write,
+ * dcb_kv_read and dcb_set_position then take absolute positions. */
+int dcb_set_kv_shard(dcb_engine* e, int rank, int world, size_t kv_begin, size_t kv_end,
+                     void* const* peer_exchange);
+
 /* ---- isolated operators (device pointers, on `stream`) -------------------- */
 
 /* Replaces decode::matvec for int8 matrices (src/kernels.cpp:107-120):
