@@ -420,6 +420,11 @@ __device__ bool warp_stage(const uint64_t* src, const uint8_t* row, float row_sc
         }
         if (!okw) break;
     }
+    // Lanes with nothing left to wait for leave the loop with okw true while
+    // others time out; the callers' warp-wide steps (warp_slot_wait, the GEMV's
+    // shuffles) need one decision per warp, or half a warp waits forever in a
+    // __syncwarp that the other half never reaches.
+    okw = __all_sync(FULL, okw);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         ss += __shfl_xor_sync(FULL, ss, o);
