@@ -35,7 +35,9 @@ EXPORTS = (
     "dcb_logits_device", "dcb_kv_write", "dcb_kv_read", "dcb_set_position", "dcb_launch_info", "dcb_launch_count",
     "dcb_gemv_i8", "dcb_attention", "dcb_attention_noalloc", "dcb_rmsnorm", "dcb_rope", "dcb_argmax",
     "dcb_trace_enable", "dcb_trace_read", "dcb_exchange_buffer", "dcb_ipc_handle", "dcb_ipc_open", "dcb_ipc_close",
-    "dcb_set_kv_shard",
+    "dcb_set_kv_shard", "dcb_batch_create", "dcb_batch_destroy", "dcb_batch_info", "dcb_batch_set_position",
+    "dcb_batch_position", "dcb_batch_kv_write", "dcb_batch_kv_read", "dcb_batch_step", "dcb_batch_step_greedy",
+    "dcb_batch_read", "dcb_batch_stream", "dcb_batch_kernels_per_step",
 )
 
 
@@ -93,6 +95,21 @@ def lib() -> C.CDLL:
     L.dcb_ipc_open.argtypes = [vp, C.POINTER(vp)]
     L.dcb_ipc_close.argtypes = [vp]
     L.dcb_set_kv_shard.argtypes = [vp, i32, i32, sz, sz, vp]
+    L.dcb_batch_create.argtypes = [vp, i32, sz, i32, C.POINTER(vp)]
+    L.dcb_batch_destroy.argtypes = [vp]
+    L.dcb_batch_info.argtypes = [vp, C.POINTER(i32), C.POINTER(sz), C.POINTER(i32)]
+    L.dcb_batch_set_position.argtypes = [vp, i32, sz]
+    L.dcb_batch_position.argtypes = [vp, i32]
+    L.dcb_batch_position.restype = sz
+    L.dcb_batch_kv_write.argtypes = [vp, i32, i32, sz, sz, vp, vp]
+    L.dcb_batch_kv_read.argtypes = [vp, i32, i32, sz, sz, vp, vp]
+    L.dcb_batch_step.argtypes = [vp, i32, vp, vp, vp]
+    L.dcb_batch_step_greedy.argtypes = [vp, i32, i32]
+    L.dcb_batch_read.argtypes = [vp, i32, vp, vp]
+    L.dcb_batch_stream.argtypes = [vp]
+    L.dcb_batch_stream.restype = vp
+    L.dcb_batch_kernels_per_step.argtypes = [vp, i32]
+    L.dcb_batch_kernels_per_step.restype = C.c_uint64
     _LIB = L
     return L
 
@@ -224,6 +241,87 @@ class Engine:
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib().dcb_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """Up to 64 independent sequences stepping together on one GPU, sharing
+    `model`'s weights; sequence s has its own KV cache and position. The
+    reference has no batch API: per sequence this is Engine.step."""
+
+    def __init__(self, model: Engine, max_seqs: int, capacity: int, kv_dtype: str = "f32"):
+        self.model = model  # the weights stay alive with the batch
+        h = C.c_void_p()
+        _check(lib().dcb_batch_create(model._h, int(max_seqs), int(capacity), KV_DTYPES[kv_dtype], C.byref(h)))
+        self._h = h
+        slots, cap, split = C.c_int(), C.c_size_t(), C.c_int()
+        _check(lib().dcb_batch_info(h, C.byref(slots), C.byref(cap), C.byref(split)))
+        self.slots, self.capacity, self.split_len = slots.value, cap.value, split.value
+        self.vocab, self.layers, self.kv_dim = model.vocab, model.layers, model.kv_dim
+        self._argmax = np.zeros(self.slots, np.int32)
+
+    def set_position(self, seq: int, position: int) -> None:
+        _check(lib().dcb_batch_set_position(self._h, int(seq), int(position)))
+
+    def position(self, seq: int) -> int:
+        return int(lib().dcb_batch_position(self._h, int(seq)))
+
+    def kv_write(self, seq: int, layer: int, start: int, keys, values, count: int | None = None) -> None:
+        """Rows [start, start+count) of `layer`: numpy float32 [count][kv_dim],
+        or device pointers (ints) with `count` given."""
+        if isinstance(keys, int):
+            _check(lib().dcb_batch_kv_write(self._h, int(seq), int(layer), int(start), int(count), keys, values))
+            return
+        k = np.ascontiguousarray(keys, np.float32)
+        v = np.ascontiguousarray(values, np.float32)
+        _check(lib().dcb_batch_kv_write(self._h, int(seq), int(layer), int(start), k.shape[0],
+                                        k.ctypes.data, v.ctypes.data))
+
+    def kv_read(self, seq: int, layer: int, start: int, count: int):
+        k = np.zeros((count, self.kv_dim), np.float32)
+        v = np.zeros((count, self.kv_dim), np.float32)
+        _check(lib().dcb_batch_kv_read(self._h, int(seq), int(layer), int(start), int(count),
+                                       k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def step(self, tokens=None, n: int | None = None, logits: bool = True):
+        """One step of sequences 0..n-1 (n = len(tokens)); tokens None: each
+        sequence's previous argmax. Returns (logits [n][vocab] or None, argmax [n])."""
+        if tokens is not None:
+            t = np.ascontiguousarray(tokens, np.int32)
+            n = t.shape[0]
+        if n is None:
+            raise ValueError("n is needed without tokens")
+        out = np.zeros((n, self.vocab), np.float32) if logits else None
+        _check(lib().dcb_batch_step(self._h, int(n), t.ctypes.data if tokens is not None else None,
+                                    out.ctypes.data if logits else None, self._argmax.ctypes.data))
+        return out, self._argmax[:n].copy()
+
+    def step_greedy(self, n: int, steps: int) -> None:
+        _check(lib().dcb_batch_step_greedy(self._h, int(n), int(steps)))
+
+    def read(self, n: int, logits: bool = False):
+        toks = np.zeros(n, np.int32)
+        out = np.zeros((n, self.vocab), np.float32) if logits else None
+        _check(lib().dcb_batch_read(self._h, int(n), toks.ctypes.data, out.ctypes.data if logits else None))
+        return toks, out
+
+    @property
+    def stream(self) -> int:
+        return int(lib().dcb_batch_stream(self._h) or 0)
+
+    def kernels_per_step(self, n: int) -> int:
+        return int(lib().dcb_batch_kernels_per_step(self._h, int(n)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().dcb_batch_destroy(self._h)
             self._h = None
 
     def __del__(self):

@@ -64,25 +64,25 @@ __device__ __forceinline__ void at_load4(const __half* p, float (&o)[4]) {
 __device__ __forceinline__ float at_float(float v) { return v; }
 __device__ __forceinline__ float at_float(__half v) { return __half2float(v); }
 
-// DT: head_dim known at compile time (64), or 0 for any even head_dim <= 128.
-template <typename KV, int DT>
-__global__ void __launch_bounds__(AT_NT) attention_split_kernel(AttnIO io) {
-    extern __shared__ __align__(16) unsigned char at_sm[];
+// The pass over one split shared by the isolated operator and the batched
+// engine: K/V rows t0..t1-1 of one KV head (row t at kg + t*rs and vg + t*rs),
+// all gq query heads of its group, the queries already scaled by
+// log2(e)/sqrt(d) in shared memory after the two chunk buffers.
+// emit(head in group, j, M, L, acc) receives the split's max, sum and
+// unnormalised output of dimension j.
+template <typename KV, int DT, typename Emit>
+__device__ __forceinline__ void attention_split_body(unsigned char* at_sm, const KV* kg, const KV* vg, int d, int rs,
+                                                     int t0, int t1, int gq, Emit emit) {
     constexpr int MD = DT ? (DT + 31) / 32 : AT_MAXD;
-    const int D = DT ? DT : io.d;
+    const int D = DT ? DT : d;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = blockIdx.x / io.nsplit, s = blockIdx.x % io.nsplit;
-    const int gq = io.heads / io.kv_heads, kvd = io.kv_heads * D;
-    const int t0 = s * io.split_len, t1 = min(io.length, t0 + io.split_len);
     const int nchunks = (t1 - t0 + AT_T - 1) / AT_T;
     const size_t buf_elems = 2 * (size_t)AT_T * D;  // K rows then V rows
     KV* bufs = reinterpret_cast<KV*>(at_sm);
     float* sq = reinterpret_cast<float*>(at_sm + 2 * buf_elems * sizeof(KV));
     float* wpart = sq + gq * D;  // [AT_NW][AT_GH][D+2]
-    const KV* kg = static_cast<const KV*>(io.keys) + (size_t)g * D;
-    const KV* vg = static_cast<const KV*>(io.values) + (size_t)g * D;
     // 16-byte copies need 16-byte rows and bases; otherwise plain loads.
-    const bool async16 = (D * sizeof(KV)) % 16 == 0 && (kvd * sizeof(KV)) % 16 == 0 &&
+    const bool async16 = (D * sizeof(KV)) % 16 == 0 && (rs * sizeof(KV)) % 16 == 0 &&
                          (reinterpret_cast<uintptr_t>(kg) & 15) == 0 && (reinterpret_cast<uintptr_t>(vg) & 15) == 0;
 
     auto issue = [&](int c) {
@@ -94,38 +94,19 @@ __global__ void __launch_bounds__(AT_NT) attention_split_kernel(AttnIO io) {
             const int pieces = D / EP;
             for (int e = threadIdx.x; e < n * pieces; e += AT_NT) {
                 const int t = e / pieces, pc = e - t * pieces;
-                const size_t src = (size_t)(c0 + t) * kvd + (size_t)pc * EP;
+                const size_t src = (size_t)(c0 + t) * rs + (size_t)pc * EP;
                 cp_async16(kb + (size_t)t * D + pc * EP, kg + src);
                 cp_async16(vb + (size_t)t * D + pc * EP, vg + src);
             }
         } else {
             for (int e = threadIdx.x; e < n * D; e += AT_NT) {
                 const int t = e / D, j = e - t * D;
-                kb[(size_t)t * D + j] = kg[(size_t)(c0 + t) * kvd + j];
-                vb[(size_t)t * D + j] = vg[(size_t)(c0 + t) * kvd + j];
+                kb[(size_t)t * D + j] = kg[(size_t)(c0 + t) * rs + j];
+                vb[(size_t)t * D + j] = vg[(size_t)(c0 + t) * rs + j];
             }
         }
         cp_async_commit();
     };
-
-    // Queries of the group, rotated at position length-1 when asked (cached
-    // angle formula of src/model.cpp:222-224,271), scaled by log2(e)/sqrt(D).
-    const float qscale = 1.4426950408889634f / sqrtf((float)D);
-    for (int e = threadIdx.x; e < gq * D; e += AT_NT) {
-        const int hl = e / D, j = e - hl * D;
-        const float* qh = io.q + (size_t)(g * gq + hl) * D;
-        float v = qh[j];
-        if (io.rope_theta > 0.f) {
-            const int half = D / 2, jj = j < half ? j : j - half;
-            const float inv = 1.0f / powf(io.rope_theta, (float)(2 * jj) / (float)D);
-            const float angle = __fmul_rn((float)(io.length - 1), inv);
-            float sn, cs;
-            sincosf(angle, &sn, &cs);
-            const float a = qh[jj], b = qh[jj + half];
-            v = j < half ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
-        }
-        sq[e] = v * qscale;
-    }
 
     const int grp = lane >> 3, part = lane & 7;
     for (int hb = 0; hb < gq; hb += AT_GH) {
@@ -254,19 +235,54 @@ __global__ void __launch_bounds__(AT_NT) attention_split_kernel(AttnIO io) {
                 L = fmaf(f, wp[1], L);
                 acc = fmaf(f, wp[2 + j], acc);
             }
-            const int h = g * gq + hb + hh;
-            if (io.nsplit == 1) {
-                io.out[(size_t)h * D + j] = acc / L;
-            } else {
-                float* pp = io.part + ((size_t)h * io.nsplit + s) * (D + 2);
-                if (j == 0) {
-                    pp[0] = M;
-                    pp[1] = L;
-                }
-                pp[2 + j] = acc;
-            }
+            emit(hb + hh, j, M, L, acc);
         }
     }
+}
+
+// DT: head_dim known at compile time (64), or 0 for any even head_dim <= 128.
+template <typename KV, int DT>
+__global__ void __launch_bounds__(AT_NT) attention_split_kernel(AttnIO io) {
+    extern __shared__ __align__(16) unsigned char at_sm[];
+    const int D = DT ? DT : io.d;
+    const int g = blockIdx.x / io.nsplit, s = blockIdx.x % io.nsplit;
+    const int gq = io.heads / io.kv_heads, kvd = io.kv_heads * D;
+    const int t0 = s * io.split_len, t1 = min(io.length, t0 + io.split_len);
+    float* sq = reinterpret_cast<float*>(at_sm + 2 * 2 * (size_t)AT_T * D * sizeof(KV));
+    const KV* kg = static_cast<const KV*>(io.keys) + (size_t)g * D;
+    const KV* vg = static_cast<const KV*>(io.values) + (size_t)g * D;
+
+    // Queries of the group, rotated at position length-1 when asked (cached
+    // angle formula of src/model.cpp:222-224,271), scaled by log2(e)/sqrt(D).
+    const float qscale = 1.4426950408889634f / sqrtf((float)D);
+    for (int e = threadIdx.x; e < gq * D; e += AT_NT) {
+        const int hl = e / D, j = e - hl * D;
+        const float* qh = io.q + (size_t)(g * gq + hl) * D;
+        float v = qh[j];
+        if (io.rope_theta > 0.f) {
+            const int half = D / 2, jj = j < half ? j : j - half;
+            const float inv = 1.0f / powf(io.rope_theta, (float)(2 * jj) / (float)D);
+            const float angle = __fmul_rn((float)(io.length - 1), inv);
+            float sn, cs;
+            sincosf(angle, &sn, &cs);
+            const float a = qh[jj], b = qh[jj + half];
+            v = j < half ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+        }
+        sq[e] = v * qscale;
+    }
+    attention_split_body<KV, DT>(at_sm, kg, vg, D, kvd, t0, t1, gq, [&](int hl, int j, float M, float L, float acc) {
+        const int h = g * gq + hl;
+        if (io.nsplit == 1) {
+            io.out[(size_t)h * D + j] = acc / L;
+        } else {
+            float* pp = io.part + ((size_t)h * io.nsplit + s) * (D + 2);
+            if (j == 0) {
+                pp[0] = M;
+                pp[1] = L;
+            }
+            pp[2 + j] = acc;
+        }
+    });
 }
 
 // Merge the splits of head blockIdx.x: out[j] = sum_s 2^(m_s - M) o_s[j] /
@@ -275,7 +291,7 @@ __global__ void __launch_bounds__(AT_NT) attention_split_kernel(AttnIO io) {
 // q (groups of d threads) takes o_s[j] of splits q, q + ngroups, ... (up to
 // AT_CU of them in registers; more splits loop).
 constexpr int AT_CU = 24;
-__global__ void __launch_bounds__(AT_NT) attention_combine_kernel(AttnIO io) {
+static __global__ void __launch_bounds__(AT_NT) attention_combine_kernel(AttnIO io) {
     __shared__ float s_w[1024];  // 2^(m_s - M) per split (nsplit <= 1024)
     __shared__ float s_red[AT_NT];
     const int h = blockIdx.x, D = io.d, ns = io.nsplit;

@@ -1,0 +1,650 @@
+// Batched decode engine behind the dcb_batch_* C ABI: up to 64 independent
+// sequences on one GPU, sharing the weights a dcb_engine uploaded, each with
+// its own KV cache and position. One step is one CUDA graph of
+//   stage(embed, input norm)
+//   per layer: QKV GEMM (+bias, RoPE, KV write) -> split-KV attention ->
+//              combine + stage -> O GEMM (+residual) -> stage(post norm) ->
+//              gate/up GEMM (SiLU*up) -> stage -> down GEMM (+residual) ->
+//              stage(next norm)
+//   LM-head GEMM (+argmax per tile) -> argmax (next tokens, positions + 1)
+// with every projection on tcgen05 (batch_kernels.cuh). Positions and tokens
+// live on the device, so graph replays chain greedy steps without the host.
+#include "batch_kernels.cuh"
+#include "decode_b200.h"
+#include "model_view.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using namespace dcb;
+using namespace dcb::batch;
+
+namespace {
+int bfail(int code, const std::string& msg) {
+    set_last_error(msg);
+    return code;
+}
+#define BT_CUDA(call)                                                                                          \
+    do {                                                                                                       \
+        cudaError_t e_ = (call);                                                                               \
+        if (e_ != cudaSuccess) return bfail(DCB_ERR_CUDA, std::string(#call ": ") + cudaGetErrorString(e_));   \
+    } while (0)
+
+size_t rup(size_t v, size_t m) { return (v + m - 1) / m * m; }
+int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Tensor map over int8 rows: `inner` bytes of each row (the rest of its
+// `stride` is not read), `rows` rows; boxes of GK bytes x box_rows rows with
+// the 128-byte swizzle; out-of-range bytes read as zero.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t stride, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return bfail(DCB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride & 15) || box_rows < 1 || box_rows > 256)
+        return bfail(DCB_ERR_ARGUMENT, "tensor map: misaligned base or stride");
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {(cuuint32_t)GK, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return bfail(DCB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return 0;
+}
+
+// FP32 rows -> the cache's element type, on the device.
+template <typename KV>
+__global__ void to_kv_kernel(const float* src, KV* dst, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        kv_store(dst + i, src[i]);
+}
+}  // namespace
+
+struct dcb_batch {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    ModelView M;
+    int slots = 0, kv_dtype = DCB_KV_F32;
+    size_t capacity = 0;
+    int split_len = 256, max_splits = 0;
+    std::vector<void*> allocations;
+    float *x = nullptr, *h = nullptr, *q = nullptr, *xsc = nullptr, *xinv = nullptr, *part = nullptr,
+          *logits = nullptr;
+    int8_t *ph = nullptr, *pi = nullptr;
+    ArgBest* amax = nullptr;
+    int *tokens = nullptr, *pos = nullptr, *argmax = nullptr, *err = nullptr;
+    void *kc = nullptr, *vc = nullptr;
+    float* stage_f = nullptr;  // FP32 rows waiting for conversion to F16 (kv_write from device memory)
+    size_t stage_f_elems = 0;
+    int* h_io = nullptr;  // pinned: [slots] tokens in, then [slots] argmax + error word out
+    std::vector<CUtensorMap> map_qkv, map_o, map_gu, map_down;
+    CUtensorMap map_head{}, map_ph{}, map_pi{};
+    std::vector<size_t> pos_host;
+    cudaGraphExec_t exec = nullptr;
+    int graph_n = -1;
+    bool graph_logits = false;
+    uint64_t steps = 0;
+
+    ~dcb_batch() {
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        if (exec) cudaGraphExecDestroy(exec);
+        for (void* p : allocations) cudaFree(p);
+        if (h_io) cudaFreeHost(h_io);
+        if (stream) cudaStreamDestroy(stream);
+    }
+    template <class T>
+    int alloc(T** out, size_t count) {
+        void* p = nullptr;
+        const size_t bytes = rup(std::max<size_t>(count * sizeof(T), 16), 256);
+        cudaError_t e = cudaMalloc(&p, bytes);
+        if (e != cudaSuccess) return bfail(DCB_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+        allocations.push_back(p);
+        e = cudaMemset(p, 0, bytes);
+        if (e != cudaSuccess) return bfail(DCB_ERR_CUDA, std::string("cudaMemset: ") + cudaGetErrorString(e));
+        *out = static_cast<T*>(p);
+        return 0;
+    }
+    size_t kv_elem() const { return kv_dtype == DCB_KV_F16 ? 2 : 4; }
+    // Element offset of (sequence, layer, kv head, position) in the caches.
+    size_t kv_offset(int s, int l, int g, size_t t) const {
+        return ((((size_t)s * M.P.L + l) * M.P.NKV + g) * capacity + t) * M.P.D;
+    }
+};
+
+namespace {
+
+template <int EPI, typename KV>
+int launch_gemm(dcb_batch* b, const CUtensorMap& ma, const CUtensorMap& mb, int rows, int K, const GemmArgs& a0) {
+    GemmArgs a = a0;
+    a.M = rows;
+    a.nk = cdiv(K, GK);
+    const int smem = gemm_smem_bytes(b->slots);
+    gemm_i8_kernel<EPI, KV><<<cdiv(rows, GM), GT, smem, b->stream>>>(ma, mb, a);
+    BT_CUDA(cudaGetLastError());
+    return 0;
+}
+
+template <int EPI, typename KV>
+int allow_smem(int bytes) {
+    BT_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<EPI, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return 0;
+}
+
+template <typename KV>
+int enqueue_step(dcb_batch* b, int n, bool want_logits) {
+    const Params& P = b->M.P;
+    const int H = P.H, I = P.I, D = P.D;
+    const int st_smem_h = P.Kh * (int)sizeof(float), st_smem_i = P.Ki * (int)sizeof(float);
+
+    StageArgs sa{};
+    sa.slots = b->slots;
+    sa.nseq = n;
+    sa.eps = P.eps;
+    sa.err = b->err;
+    sa.vocab = P.V;
+
+    GemmArgs g{};
+    g.nseq = n;
+    g.slots = b->slots;
+    g.xsc = b->xsc;
+    g.NH = P.NH;
+    g.NKV = P.NKV;
+    g.D = D;
+    g.L = P.L;
+    g.capacity = (int)b->capacity;
+    g.cached_rope = P.cached_rope;
+    g.rope_inv = P.rope_inv;
+    g.rope_den = P.rope_den;
+    g.pos = b->pos;
+    g.kcache = b->kc;
+    g.vcache = b->vc;
+    g.amax = b->amax;
+    g.err = b->err;
+
+    // Layer 0 input: the tokens' embedding rows, RMSNorm-staged.
+    {
+        StageArgs s = sa;
+        s.n = H;
+        s.kp = P.Kh;
+        s.lds = P.Kh;
+        s.embed = P.embed;
+        s.SE = P.SH;
+        s.eoff = P.Kh;
+        s.tokens = b->tokens;
+        s.x_out = b->x;
+        s.gain = P.norms;
+        s.planes = b->ph;
+        s.xsc = b->xsc;
+        s.xinv = b->xinv;
+        stage_kernel<<<n, ST_NT, st_smem_h, b->stream>>>(s);
+        BT_CUDA(cudaGetLastError());
+    }
+    AttnArgs aa{};
+    aa.q = b->q;
+    aa.kcache = b->kc;
+    aa.vcache = b->vc;
+    aa.part = b->part;
+    aa.pos = b->pos;
+    aa.NH = P.NH;
+    aa.NKV = P.NKV;
+    aa.D = D;
+    aa.L = P.L;
+    aa.capacity = (int)b->capacity;
+    aa.split_len = b->split_len;
+    aa.max_splits = b->max_splits;
+    const size_t at_smem = attention_smem_bytes(D, (int)sizeof(KV), P.NH / P.NKV);
+    CombineArgs ca{};
+    ca.part = b->part;
+    ca.pos = b->pos;
+    ca.NH = P.NH;
+    ca.D = D;
+    ca.split_len = b->split_len;
+    ca.max_splits = b->max_splits;
+    ca.slots = b->slots;
+    ca.kp = P.Kh;
+    ca.planes = b->ph;
+    ca.xsc = b->xsc;
+    const int cb_smem = (P.NH * D + P.NH * b->max_splits) * (int)sizeof(float);
+
+    for (int l = 0; l < P.L; ++l) {
+        const float* in_norm = P.norms + (size_t)l * 2 * P.Kh;
+        const float* post_norm = in_norm + P.Kh;
+        const LayerW& W = b->M.layers[l];
+        // QKV + bias + RoPE; K/V rows of the new tokens into the caches.
+        {
+            GemmArgs a = g;
+            a.wscale = reinterpret_cast<const float*>(W.qkv + P.Kh);
+            a.wstride = P.SH / 4;
+            a.bias = a.wscale + 1;
+            a.bstride = P.SH / 4;
+            a.xinv = b->xinv;
+            a.out = b->q;
+            a.ldo = P.NH * D;
+            a.layer = l;
+            if (int rc = launch_gemm<EPI_QKV, KV>(b, b->map_qkv[l], b->map_ph, 2 * P.qkv_pairs, P.Kh, a)) return rc;
+        }
+        aa.layer = l;
+        if (D == 64)
+            attention_kernel<KV, 64><<<dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream>>>(aa);
+        else
+            attention_kernel<KV, 0><<<dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream>>>(aa);
+        BT_CUDA(cudaGetLastError());
+        combine_stage_kernel<<<n, ST_NT, cb_smem, b->stream>>>(ca);
+        BT_CUDA(cudaGetLastError());
+        // O + residual.
+        {
+            GemmArgs a = g;
+            a.wscale = reinterpret_cast<const float*>(W.o + P.Kh);
+            a.wstride = P.SH / 4;
+            a.out = b->x;
+            a.ldo = P.Kh;
+            if (int rc = launch_gemm<EPI_RESID, KV>(b, b->map_o[l], b->map_ph, H, P.Kh, a)) return rc;
+        }
+        {
+            StageArgs s = sa;
+            s.n = H;
+            s.kp = P.Kh;
+            s.src = b->x;
+            s.lds = P.Kh;
+            s.gain = post_norm;
+            s.planes = b->ph;
+            s.xsc = b->xsc;
+            s.xinv = b->xinv;
+            stage_kernel<<<n, ST_NT, st_smem_h, b->stream>>>(s);
+            BT_CUDA(cudaGetLastError());
+        }
+        // gate/up + SiLU.
+        {
+            GemmArgs a = g;
+            a.wscale = reinterpret_cast<const float*>(W.gu + P.Kh);
+            a.wstride = P.SH / 4;
+            a.xinv = b->xinv;
+            a.out = b->h;
+            a.ldo = P.Ki;
+            if (int rc = launch_gemm<EPI_GU, KV>(b, b->map_gu[l], b->map_ph, 2 * I, P.Kh, a)) return rc;
+        }
+        {
+            StageArgs s = sa;
+            s.n = I;
+            s.kp = P.Ki;
+            s.src = b->h;
+            s.lds = P.Ki;
+            s.planes = b->pi;
+            s.xsc = b->xsc;
+            stage_kernel<<<n, ST_NT, st_smem_i, b->stream>>>(s);
+            BT_CUDA(cudaGetLastError());
+        }
+        // down + residual.
+        {
+            GemmArgs a = g;
+            a.wscale = reinterpret_cast<const float*>(W.down + P.Ki);
+            a.wstride = P.SI / 4;
+            a.out = b->x;
+            a.ldo = P.Kh;
+            if (int rc = launch_gemm<EPI_RESID, KV>(b, b->map_down[l], b->map_pi, H, P.Ki, a)) return rc;
+        }
+        // Next layer's input norm, or the final norm before the head.
+        {
+            StageArgs s = sa;
+            s.n = H;
+            s.kp = P.Kh;
+            s.src = b->x;
+            s.lds = P.Kh;
+            s.gain = l + 1 < P.L ? P.norms + (size_t)(l + 1) * 2 * P.Kh : P.norms + (size_t)P.L * 2 * P.Kh;
+            s.planes = b->ph;
+            s.xsc = b->xsc;
+            s.xinv = b->xinv;
+            stage_kernel<<<n, ST_NT, st_smem_h, b->stream>>>(s);
+            BT_CUDA(cudaGetLastError());
+        }
+    }
+    // Tied LM head + per-tile argmax, then the argmax per sequence.
+    {
+        GemmArgs a = g;
+        a.wscale = reinterpret_cast<const float*>(P.embed + P.Kh);
+        a.wstride = P.SH / 4;
+        a.xinv = b->xinv;
+        a.out = want_logits ? b->logits : nullptr;
+        a.ldo = P.V;
+        if (int rc = launch_gemm<EPI_HEAD, KV>(b, b->map_head, b->map_ph, P.V, P.Kh, a)) return rc;
+    }
+    ArgmaxArgs ga{};
+    ga.amax = b->amax;
+    ga.tiles = cdiv(P.V, GM);
+    ga.slots = b->slots;
+    ga.nseq = n;
+    ga.argmax = b->argmax;
+    ga.tokens = b->tokens;
+    ga.pos = b->pos;
+    argmax_kernel<<<n, ARG_NT, 0, b->stream>>>(ga);
+    BT_CUDA(cudaGetLastError());
+    return 0;
+}
+
+int build_graph(dcb_batch* b, int n, bool want_logits) {
+    if (b->exec && b->graph_n == n && b->graph_logits == want_logits) return 0;
+    if (b->exec) {
+        cudaGraphExecDestroy(b->exec);
+        b->exec = nullptr;
+    }
+    BT_CUDA(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = b->kv_dtype == DCB_KV_F16 ? enqueue_step<__half>(b, n, want_logits)
+                                             : enqueue_step<float>(b, n, want_logits);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(b->stream, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (ce != cudaSuccess) return bfail(DCB_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    const cudaError_t ie = cudaGraphInstantiate(&b->exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return bfail(DCB_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+    b->graph_n = n;
+    b->graph_logits = want_logits;
+    return 0;
+}
+
+int check_seq(const dcb_batch* b, int s) {
+    if (s < 0 || s >= b->slots) return bfail(DCB_ERR_ARGUMENT, "sequence index out of range");
+    return 0;
+}
+
+// After a step: read the error word; on error reset it and report.
+int device_status(dcb_batch* b, int err) {
+    if (!err) return 0;
+    BT_CUDA(cudaMemsetAsync(b->err, 0, sizeof(int), b->stream));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    if (err == ERR_TOKEN) return bfail(DCB_ERR_TOKEN, "token ID outside vocabulary");
+    return bfail(DCB_ERR_DEVICE_WAIT, "a device-side wait ran out of time; the step was abandoned");
+}
+
+}  // namespace
+
+extern "C" {
+
+int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int kv_dtype, dcb_batch** out) {
+    if (!model || !out) return bfail(DCB_ERR_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (max_seqs < 1 || max_seqs > MAX_SLOTS) return bfail(DCB_ERR_ARGUMENT, "max_seqs must be 1..64");
+    if (capacity < 1 || capacity > (size_t)1 << 24) return bfail(DCB_ERR_ARGUMENT, "invalid context capacity");
+    if (kv_dtype != DCB_KV_F32 && kv_dtype != DCB_KV_F16) return bfail(DCB_ERR_ARGUMENT, "invalid KV dtype");
+    dcb_batch* b = new dcb_batch();
+    auto bail = [&](int rc) {
+        delete b;
+        return rc;
+    };
+    if (int rc = model_view(model, &b->M)) return bail(rc);
+    const Params& P = b->M.P;
+    b->device = b->M.device;
+    BT_CUDA(cudaSetDevice(b->device));
+    int major = 0, minor = 0;
+    BT_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, b->device));
+    BT_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, b->device));
+    if (major != 10 || minor != 0) return bail(bfail(DCB_ERR_UNSUPPORTED, "the batched engine needs an sm_100 GPU"));
+    if (P.D % 2 || P.D > 128 || P.NH % P.NKV) return bail(bfail(DCB_ERR_UNSUPPORTED, "unsupported head shape"));
+    b->slots = (int)rup((size_t)max_seqs, 16);
+    b->capacity = capacity;
+    b->kv_dtype = kv_dtype;
+    b->max_splits = cdiv((int)capacity, b->split_len);
+    const int S = b->slots;
+    if (int rc = b->alloc(&b->x, (size_t)S * P.Kh)) return bail(rc);
+    if (int rc = b->alloc(&b->h, (size_t)S * P.Ki)) return bail(rc);
+    if (int rc = b->alloc(&b->q, (size_t)S * P.NH * P.D)) return bail(rc);
+    if (int rc = b->alloc(&b->xsc, S)) return bail(rc);
+    if (int rc = b->alloc(&b->xinv, S)) return bail(rc);
+    if (int rc = b->alloc(&b->part, (size_t)S * P.NH * b->max_splits * (P.D + 2))) return bail(rc);
+    if (int rc = b->alloc(&b->logits, (size_t)S * P.V)) return bail(rc);
+    if (int rc = b->alloc(&b->ph, (size_t)3 * S * P.Kh)) return bail(rc);
+    if (int rc = b->alloc(&b->pi, (size_t)3 * S * P.Ki)) return bail(rc);
+    if (int rc = b->alloc(&b->amax, (size_t)cdiv(P.V, GM) * S)) return bail(rc);
+    if (int rc = b->alloc(&b->tokens, S)) return bail(rc);
+    if (int rc = b->alloc(&b->pos, S)) return bail(rc);
+    if (int rc = b->alloc(&b->argmax, S + 1)) return bail(rc);
+    b->err = b->argmax + S;  // read with the argmax in one copy
+    {
+        unsigned char *kc, *vc;
+        const size_t n = (size_t)S * P.L * P.NKV * capacity * P.D * b->kv_elem();
+        if (int rc = b->alloc(&kc, n)) return bail(rc);
+        if (int rc = b->alloc(&vc, n)) return bail(rc);
+        b->kc = kc;
+        b->vc = vc;
+    }
+    b->pos_host.assign(S, 0);
+    // Tensor maps: weights in their packed rows (int8 part only), and the planes.
+    b->map_qkv.resize(P.L);
+    b->map_o.resize(P.L);
+    b->map_gu.resize(P.L);
+    b->map_down.resize(P.L);
+    for (int l = 0; l < P.L; ++l) {
+        const LayerW& W = b->M.layers[l];
+        if (int rc = make_map(&b->map_qkv[l], W.qkv, P.Kh, 2 * (uint64_t)P.qkv_pairs, P.SH, GM)) return bail(rc);
+        if (int rc = make_map(&b->map_o[l], W.o, P.Kh, P.H, P.SH, GM)) return bail(rc);
+        if (int rc = make_map(&b->map_gu[l], W.gu, P.Kh, 2 * (uint64_t)P.I, P.SH, GM)) return bail(rc);
+        if (int rc = make_map(&b->map_down[l], W.down, P.Ki, P.H, P.SI, GM)) return bail(rc);
+    }
+    if (int rc = make_map(&b->map_head, P.embed, P.Kh, P.V, P.SH, GM)) return bail(rc);
+    if (int rc = make_map(&b->map_ph, b->ph, P.Kh, 3 * (uint64_t)S, P.Kh, 3 * S)) return bail(rc);
+    if (int rc = make_map(&b->map_pi, b->pi, P.Ki, 3 * (uint64_t)S, P.Ki, 3 * S)) return bail(rc);
+    const int smem = gemm_smem_bytes(S);
+    if (int rc = allow_smem<EPI_QKV, float>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_QKV, __half>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_RESID, float>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_RESID, __half>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_GU, float>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_GU, __half>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_HEAD, float>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_HEAD, __half>(smem)) return bail(rc);
+    {
+        const int at = (int)attention_smem_bytes(P.D, (int)b->kv_elem(), P.NH / P.NKV);
+        auto set = [&](const void* f) {
+            return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, at);
+        };
+        if (kv_dtype == DCB_KV_F16) {
+            BT_CUDA(set((const void*)attention_kernel<__half, 64>));
+            BT_CUDA(set((const void*)attention_kernel<__half, 0>));
+        } else {
+            BT_CUDA(set((const void*)attention_kernel<float, 64>));
+            BT_CUDA(set((const void*)attention_kernel<float, 0>));
+        }
+    }
+    if (cudaMallocHost(&b->h_io, (size_t)2 * (S + 1) * sizeof(int)) != cudaSuccess)
+        return bail(bfail(DCB_ERR_CUDA, "cudaMallocHost failed"));
+    BT_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    BT_CUDA(cudaDeviceSynchronize());
+    *out = b;
+    return 0;
+}
+
+void dcb_batch_destroy(dcb_batch* b) { delete b; }
+
+int dcb_batch_info(const dcb_batch* b, int* slots, size_t* capacity, int* split_len) {
+    if (!b) return bfail(DCB_ERR_ARGUMENT, "null batch");
+    if (slots) *slots = b->slots;
+    if (capacity) *capacity = b->capacity;
+    if (split_len) *split_len = b->split_len;
+    return 0;
+}
+
+int dcb_batch_set_position(dcb_batch* b, int seq, size_t position) {
+    if (!b) return bfail(DCB_ERR_ARGUMENT, "null batch");
+    if (int rc = check_seq(b, seq)) return rc;
+    if (position >= b->capacity) return bfail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    BT_CUDA(cudaSetDevice(b->device));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    const int p = (int)position;
+    BT_CUDA(cudaMemcpyAsync(b->pos + seq, &p, sizeof(int), cudaMemcpyHostToDevice, b->stream));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    b->pos_host[seq] = position;
+    return 0;
+}
+
+size_t dcb_batch_position(const dcb_batch* b, int seq) {
+    if (!b || seq < 0 || seq >= b->slots) return 0;
+    return b->pos_host[seq];
+}
+
+int dcb_batch_kv_write(dcb_batch* b, int seq, int layer, size_t start, size_t count, const float* keys,
+                       const float* values) {
+    if (!b || !keys || !values) return bfail(DCB_ERR_ARGUMENT, "null argument");
+    if (int rc = check_seq(b, seq)) return rc;
+    const Params& P = b->M.P;
+    if (layer < 0 || layer >= P.L || start + count > b->capacity) return bfail(DCB_ERR_ARGUMENT, "KV rows out of range");
+    if (!count) return 0;
+    BT_CUDA(cudaSetDevice(b->device));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    const size_t kvd = (size_t)P.NKV * P.D, es = b->kv_elem();
+    for (int which = 0; which < 2; ++which) {
+        const float* src = which ? values : keys;
+        char* base = static_cast<char*>(which ? b->vc : b->kc);
+        if (es == 4) {
+            // Host or device rows (cudaMemcpyDefault: unified addressing).
+            for (int g = 0; g < P.NKV; ++g)
+                BT_CUDA(cudaMemcpy2DAsync(base + b->kv_offset(seq, layer, g, start) * es, P.D * es,
+                                          src + (size_t)g * P.D, kvd * sizeof(float), P.D * es, count,
+                                          cudaMemcpyDefault, b->stream));
+        } else {
+            // FP32 rows gathered per head into device scratch, rounded to F16 on the device.
+            if (b->stage_f_elems < count * P.D) {
+                if (int rc = b->alloc(&b->stage_f, count * P.D)) return rc;
+                b->stage_f_elems = count * P.D;
+            }
+            for (int g = 0; g < P.NKV; ++g) {
+                BT_CUDA(cudaMemcpy2DAsync(b->stage_f, P.D * sizeof(float), src + (size_t)g * P.D,
+                                          kvd * sizeof(float), P.D * sizeof(float), count, cudaMemcpyDefault,
+                                          b->stream));
+                to_kv_kernel<__half><<<256, 256, 0, b->stream>>>(
+                    b->stage_f, reinterpret_cast<__half*>(base) + b->kv_offset(seq, layer, g, start), count * P.D);
+                BT_CUDA(cudaGetLastError());
+                BT_CUDA(cudaStreamSynchronize(b->stream));  // stage_f is reused by the next head
+            }
+        }
+    }
+    BT_CUDA(cudaStreamSynchronize(b->stream));  // the caller may reuse keys/values on return
+    return 0;
+}
+
+int dcb_batch_kv_read(const dcb_batch* b, int seq, int layer, size_t start, size_t count, float* keys, float* values) {
+    if (!b || !keys || !values) return bfail(DCB_ERR_ARGUMENT, "null argument");
+    if (int rc = check_seq(b, seq)) return rc;
+    const Params& P = b->M.P;
+    if (layer < 0 || layer >= P.L || start + count > b->capacity) return bfail(DCB_ERR_ARGUMENT, "KV rows out of range");
+    if (!count) return 0;
+    BT_CUDA(cudaSetDevice(b->device));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    const size_t kvd = (size_t)P.NKV * P.D, es = b->kv_elem();
+    for (int which = 0; which < 2; ++which) {
+        float* dst = which ? values : keys;
+        const char* base = static_cast<const char*>(which ? b->vc : b->kc);
+        if (es == 4) {
+            for (int g = 0; g < P.NKV; ++g)
+                BT_CUDA(cudaMemcpy2D(dst + (size_t)g * P.D, kvd * sizeof(float),
+                                     base + b->kv_offset(seq, layer, g, start) * es, P.D * es, P.D * es, count,
+                                     cudaMemcpyDefault));
+        } else {
+            std::vector<__half> hbuf(count * P.D);
+            for (int g = 0; g < P.NKV; ++g) {
+                BT_CUDA(cudaMemcpy(hbuf.data(), base + b->kv_offset(seq, layer, g, start) * es, count * P.D * es,
+                                   cudaMemcpyDeviceToHost));
+                for (size_t t = 0; t < count; ++t)
+                    for (int j = 0; j < P.D; ++j) dst[t * kvd + (size_t)g * P.D + j] = __half2float(hbuf[t * P.D + j]);
+            }
+        }
+    }
+    return 0;
+}
+
+int dcb_batch_step(dcb_batch* b, int n, const int* tokens, float* logits, int* argmax_out) {
+    if (!b) return bfail(DCB_ERR_ARGUMENT, "null batch");
+    if (n < 1 || n > b->slots) return bfail(DCB_ERR_ARGUMENT, "sequence count out of range");
+    const Params& P = b->M.P;
+    for (int s = 0; s < n; ++s)
+        if (b->pos_host[s] >= b->capacity) return bfail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    if (tokens)
+        for (int s = 0; s < n; ++s)
+            if (tokens[s] < 0 || tokens[s] >= P.V) return bfail(DCB_ERR_TOKEN, "token ID outside vocabulary");
+    BT_CUDA(cudaSetDevice(b->device));
+    if (int rc = build_graph(b, n, logits != nullptr)) return rc;
+    if (tokens) {
+        std::memcpy(b->h_io, tokens, (size_t)n * sizeof(int));
+        BT_CUDA(cudaMemcpyAsync(b->tokens, b->h_io, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, b->stream));
+    }
+    BT_CUDA(cudaGraphLaunch(b->exec, b->stream));
+    ++b->steps;
+    if (logits)
+        BT_CUDA(cudaMemcpyAsync(logits, b->logits, (size_t)n * P.V * sizeof(float), cudaMemcpyDeviceToHost, b->stream));
+    int* hout = b->h_io + b->slots + 1;
+    BT_CUDA(cudaMemcpyAsync(hout, b->argmax, (size_t)(b->slots + 1) * sizeof(int), cudaMemcpyDeviceToHost, b->stream));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    if (int rc = device_status(b, hout[b->slots])) {
+        // Positions advanced on the device with the abandoned step: put them back.
+        std::vector<int> p(b->slots);
+        for (int s = 0; s < b->slots; ++s) p[s] = (int)b->pos_host[s];
+        BT_CUDA(cudaMemcpyAsync(b->pos, p.data(), p.size() * sizeof(int), cudaMemcpyHostToDevice, b->stream));
+        BT_CUDA(cudaStreamSynchronize(b->stream));
+        return rc;
+    }
+    if (argmax_out) std::memcpy(argmax_out, hout, (size_t)n * sizeof(int));
+    for (int s = 0; s < n; ++s) ++b->pos_host[s];
+    return 0;
+}
+
+int dcb_batch_step_greedy(dcb_batch* b, int n, int steps) {
+    if (!b) return bfail(DCB_ERR_ARGUMENT, "null batch");
+    if (n < 1 || n > b->slots || steps < 0) return bfail(DCB_ERR_ARGUMENT, "sequence or step count out of range");
+    for (int s = 0; s < n; ++s)
+        if (b->pos_host[s] + (size_t)steps > b->capacity) return bfail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    BT_CUDA(cudaSetDevice(b->device));
+    if (int rc = build_graph(b, n, false)) return rc;
+    for (int i = 0; i < steps; ++i) BT_CUDA(cudaGraphLaunch(b->exec, b->stream));
+    b->steps += (uint64_t)steps;
+    for (int s = 0; s < n; ++s) b->pos_host[s] += (size_t)steps;
+    return 0;
+}
+
+int dcb_batch_read(dcb_batch* b, int n, int* tokens_out, float* logits) {
+    if (!b) return bfail(DCB_ERR_ARGUMENT, "null batch");
+    if (n < 0 || n > b->slots) return bfail(DCB_ERR_ARGUMENT, "sequence count out of range");
+    BT_CUDA(cudaSetDevice(b->device));
+    int* hout = b->h_io + b->slots + 1;
+    BT_CUDA(cudaMemcpyAsync(hout, b->argmax, (size_t)(b->slots + 1) * sizeof(int), cudaMemcpyDeviceToHost, b->stream));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    if (int rc = device_status(b, hout[b->slots])) return rc;
+    if (tokens_out) std::memcpy(tokens_out, hout, (size_t)n * sizeof(int));
+    if (logits)
+        BT_CUDA(cudaMemcpyAsync(logits, b->logits, (size_t)n * b->M.P.V * sizeof(float), cudaMemcpyDeviceToHost,
+                                b->stream));
+    BT_CUDA(cudaStreamSynchronize(b->stream));
+    return 0;
+}
+
+void* dcb_batch_stream(const dcb_batch* b) { return b ? b->stream : nullptr; }
+
+uint64_t dcb_batch_kernels_per_step(const dcb_batch* b, int n) {
+    (void)n;
+    if (!b) return 0;
+    return 1 + (uint64_t)b->M.P.L * 9 + 2;
+}
+
+}  // extern "C"

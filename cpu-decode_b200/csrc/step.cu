@@ -2,6 +2,7 @@
 // the step kernel's layout, owns the KV cache and the activation buffers, and
 // launches one cooperative step kernel (step_kernel.cuh) per token.
 #include "decode_b200.h"
+#include "model_view.h"
 #include "step_kernel.cuh"
 
 #include <cuda_runtime.h>
@@ -167,7 +168,9 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
 
 int device_error(dcb_engine* e, int err) {
     if (!err) return 0;
-    DCB_CUDA(cudaMemset(e->P.sync, 0, sizeof(Sync)));
+    // On the engine's stream: a legacy-stream memset is not ordered before its next launch.
+    DCB_CUDA(cudaMemsetAsync(e->P.sync, 0, sizeof(Sync), e->stream));
+    DCB_CUDA(cudaStreamSynchronize(e->stream));
     if (err == ERR_TOKEN) return fail(DCB_ERR_TOKEN, "token ID outside vocabulary");
     return fail(DCB_ERR_DEVICE_WAIT, "a device-side wait ran out of time; the step was abandoned");
 }
@@ -525,17 +528,19 @@ int dcb_kv_write(dcb_engine* e, int layer, size_t start, size_t count, const flo
         char* base = static_cast<char*>(which ? e->P.vcache : e->P.kcache);
         if (es == 4) {
             for (int g = 0; g < e->NKV; ++g)
-                DCB_CUDA(cudaMemcpy2D(base + kv_offset(e, layer, g, start) * es, e->D * es, src + (size_t)g * e->D,
-                                      kvd * sizeof(float), e->D * es, count, cudaMemcpyHostToDevice));
+                DCB_CUDA(cudaMemcpy2DAsync(base + kv_offset(e, layer, g, start) * es, e->D * es, src + (size_t)g * e->D,
+                                           kvd * sizeof(float), e->D * es, count, cudaMemcpyHostToDevice, e->stream));
         } else {
             std::vector<__half> h(count * kvd);
             for (size_t i = 0; i < h.size(); ++i) h[i] = __float2half_rn(src[i]);
             for (int g = 0; g < e->NKV; ++g)
-                DCB_CUDA(cudaMemcpy2D(base + kv_offset(e, layer, g, start) * es, e->D * es,
-                                      h.data() + (size_t)g * e->D, kvd * es, e->D * es, count,
-                                      cudaMemcpyHostToDevice));
+                DCB_CUDA(cudaMemcpy2DAsync(base + kv_offset(e, layer, g, start) * es, e->D * es,
+                                           h.data() + (size_t)g * e->D, kvd * es, e->D * es, count,
+                                           cudaMemcpyHostToDevice, e->stream));
+            DCB_CUDA(cudaStreamSynchronize(e->stream));  // h is released at the end of this block
         }
     }
+    DCB_CUDA(cudaStreamSynchronize(e->stream));  // the caller may reuse keys/values on return
     return 0;
 }
 
@@ -614,7 +619,8 @@ int dcb_set_kv_shard(dcb_engine* e, int rank, int world, size_t kv_begin, size_t
     }
     DCB_CUDA(cudaSetDevice(e->device));
     DCB_CUDA(cudaStreamSynchronize(e->stream));
-    DCB_CUDA(cudaMemcpy(const_cast<uint64_t**>(e->P.peers), ptrs, sizeof(ptrs), cudaMemcpyHostToDevice));
+    DCB_CUDA(cudaMemcpyAsync(const_cast<uint64_t**>(e->P.peers), ptrs, sizeof(ptrs), cudaMemcpyHostToDevice, e->stream));
+    DCB_CUDA(cudaStreamSynchronize(e->stream));
     e->kv_base = kv_begin;
     e->kv_end = kv_end;
     e->P.kv_base = (int)kv_begin;
@@ -656,8 +662,21 @@ int dcb_trace_read(dcb_engine* e, uint64_t* ready, uint64_t* done, int* phases) 
     const size_t per = (size_t)TRACE_MAX_PHASES * e->grid * sizeof(uint64_t);
     if (ready) DCB_CUDA(cudaMemcpy(ready, e->trace, per, cudaMemcpyDeviceToHost));
     if (done) DCB_CUDA(cudaMemcpy(done, e->trace + (size_t)TRACE_MAX_PHASES * e->grid, per, cudaMemcpyDeviceToHost));
-    if (ready || done) DCB_CUDA(cudaMemset(e->trace, 0, (size_t)2 * TRACE_MAX_PHASES * e->grid * sizeof(uint64_t)));
+    if (ready || done) {
+        DCB_CUDA(cudaMemsetAsync(e->trace, 0, (size_t)2 * TRACE_MAX_PHASES * e->grid * sizeof(uint64_t), e->stream));
+        DCB_CUDA(cudaStreamSynchronize(e->stream));
+    }
     return 0;
 }
 
 }  // extern "C"
+
+int dcb::model_view(const dcb_engine* e, ModelView* out) {
+    if (!e || !out) return fail(DCB_ERR_ARGUMENT, "null engine");
+    DCB_CUDA(cudaSetDevice(e->device));
+    out->device = e->device;
+    out->P = e->P;
+    out->layers.resize(e->L);
+    DCB_CUDA(cudaMemcpy(out->layers.data(), e->P.layers, (size_t)e->L * sizeof(LayerW), cudaMemcpyDeviceToHost));
+    return 0;
+}

@@ -229,7 +229,7 @@ __device__ __forceinline__ bool wait_expired(const BlockState& st, uint64_t& t0)
 // Thread 0 alone tests the barrier (512 threads testing one shared word
 // serialise on it); the closing __syncthreads orders the completed copies
 // before every thread's reads and lets all threads take the same decision.
-__device__ bool mbar_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
+static __device__ bool mbar_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
     if (threadIdx.x == 0) {
         uint64_t t0 = 0;
         unsigned spins = 0;
@@ -266,7 +266,7 @@ struct Staged {
 
 // All elements accepted: reduce (sum v^2, max |v*gain|) and quantise xf into
 // the planes (padding n..16*nch as zeros). Two barriers.
-__device__ Staged finish_stage(int n, int nch, const float* xf, int8_t* xq, int plane, float ss, float mx, float* red,
+static __device__ Staged finish_stage(int n, int nch, const float* xf, int8_t* xq, int plane, float ss, float mx, float* red,
                                float eps) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -452,7 +452,7 @@ __device__ bool warp_stage(const uint64_t* src, const uint8_t* row, float row_sc
 // One warp waits for phase `parity` of mbarrier m: lane 0 tests, then the
 // warp synchronises (ordering the completed copies before every lane's reads).
 // Bounded; false when the wait ran out (the abort flag is set).
-__device__ bool warp_slot_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
+static __device__ bool warp_slot_wait(uint64_t* m, uint32_t parity, const BlockState& st) {
     bool okw = true;
     if ((threadIdx.x & 31) == 0) {
         uint64_t t0 = 0;

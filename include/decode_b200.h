@@ -218,6 +218,44 @@ int dcb_rope(float* x, int heads, int dim, int position, float theta, int direct
  * std::max_element semantics (src/main.cpp:35-37). */
 int dcb_argmax(const float* x, int n, int* out, void* stream);
 
+/* ---- batched decode of independent sequences (one GPU) --------------------
+ * No counterpart in the reference, which decodes one sequence per Engine
+ * (src/model.cpp:258-329); a caller with many sequences would run one Engine
+ * each. Here up to 64 sequences (slots 0..max_seqs-1) step together: every
+ * projection is one int8 GEMM on the tensor cores over all sequences, each
+ * sequence attends over its own KV cache (capacity positions, kv_dtype), and
+ * the argmax of step t becomes sequence s's token of step t+1 on the device.
+ * The batch shares the weights of `model` (same device; keep `model` alive
+ * while the batch exists; its own KV capacity may be 1). Per sequence the
+ * results are those of dcb_step on an engine at the same position with the
+ * same KV rows (logits within the FP32 tolerance, not bit-identical). */
+typedef struct dcb_batch dcb_batch;
+int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int kv_dtype, dcb_batch** out);
+void dcb_batch_destroy(dcb_batch* b);
+/* Sequence slots (max_seqs rounded up to 16), capacity, attention split length. */
+int dcb_batch_info(const dcb_batch* b, int* slots, size_t* capacity, int* split_len);
+/* Position (rows 0..position-1 of the sequence's cache are its context). */
+int dcb_batch_set_position(dcb_batch* b, int seq, size_t position);
+size_t dcb_batch_position(const dcb_batch* b, int seq);
+/* KV rows [start, start+count) of `layer` of sequence seq: count rows of
+ * kv_heads*head_dim FP32 values, in host or device memory. */
+int dcb_batch_kv_write(dcb_batch* b, int seq, int layer, size_t start, size_t count, const float* keys,
+                       const float* values);
+int dcb_batch_kv_read(const dcb_batch* b, int seq, int layer, size_t start, size_t count, float* keys,
+                      float* values);
+/* One step of sequences 0..n-1: tokens[s] (host; NULL: each sequence's
+ * previous argmax), logits [n][vocab] (host, or NULL), argmax_out [n] (host,
+ * or NULL). Positions advance by one. Errors as dcb_step. */
+int dcb_batch_step(dcb_batch* b, int n, const int* tokens, float* logits, int* argmax_out);
+/* `steps` greedy steps of sequences 0..n-1 queued on the batch's stream
+ * without host round trips (each step's argmax is the next token); read the
+ * last tokens with dcb_batch_read, which also reports a device error. */
+int dcb_batch_step_greedy(dcb_batch* b, int n, int steps);
+int dcb_batch_read(dcb_batch* b, int n, int* tokens_out, float* logits);
+/* The batch's CUDA stream, and the kernels one step launches. */
+void* dcb_batch_stream(const dcb_batch* b);
+uint64_t dcb_batch_kernels_per_step(const dcb_batch* b, int n);
+
 #ifdef __cplusplus
 }
 #endif
