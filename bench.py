@@ -204,6 +204,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip the ctx 4096 extra measurement")
+    ap.add_argument("--no-batch", action="store_true", help="skip the batched 64-sequence measurement")
+    ap.add_argument("--ncu-batch", type=int, default=0, metavar="SEQS",
+                    help="the batched profiling case: SEQS sequences, --steps graph steps")
     ap.add_argument("--ncu-case", action="store_true",
                     help="the profiling case: KV rows 0..127 written from the host, then 5 decode launches")
     args = ap.parse_args()
@@ -212,6 +215,9 @@ def main() -> None:
         return
     if args.ncu_case:
         ncu_case()
+        return
+    if args.ncu_batch:
+        ncu_batch_case(args.ncu_batch, max(1, args.steps))
         return
 
     import torch
@@ -315,6 +321,8 @@ def main() -> None:
     assert nxt == generated_last, "host-driven and device-chained greedy streams diverged"
 
     extra = {}
+    if not args.no_batch:
+        extra["batched"] = batched_decode(dcb, eng, d, dist, rank, world, W)
     if dist and not args.no_long:
         split = kv_split_context(dcb, model, d, min(K, 32), W, local, dist, 32768)
         if rank == 0:
@@ -383,6 +391,41 @@ def ncu_case() -> None:
     eng.synchronize()
     print(json.dumps({"ncu_case": "decode_step_kernel ctx 128", "launches": eng.launch_count,
                       "last_token": int(tok.item())}))
+    eng.close()
+
+
+def ncu_batch_case(seqs: int, steps: int) -> None:
+    """The batched workload for a profiler: `seqs` sequences with the bench's
+    seeded contexts (uniform [512, 8192]), KV pre-filled on the device, then
+    `steps` graph steps. Capture with `-k regex:"gemm_i8|attention_kernel|
+    combine_stage|stage_kernel|argmax_kernel"`: one step is
+    1 + 9 x layers + 2 of these launches."""
+    import torch
+    dcb = load_package()
+    import cpu_decode_b200.synthetic as syn
+    model = ensure_model()
+    d = syn.QWEN05
+    eng = dcb.Engine(model, 1)
+    rng = np.random.default_rng(100)
+    ctxs = rng.integers(BATCH_CTX[0], BATCH_CTX[1] + 1, BATCH_SEQS)[:seqs]
+    bat = dcb.Batch(eng, seqs, int(ctxs.max()) + steps + 2)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2024)
+    maxc = int(ctxs.max())
+    for l in range(d.layers):
+        k = torch.randn(maxc, d.kv_dim, device="cuda", generator=gen)
+        v = torch.randn(maxc, d.kv_dim, device="cuda", generator=gen)
+        torch.cuda.synchronize()
+        for s in range(seqs):
+            bat.kv_write(s, l, 0, k.data_ptr(), v.data_ptr(), count=int(ctxs[s]))
+    for s in range(seqs):
+        bat.set_position(s, int(ctxs[s]))
+    bat.step(rng.integers(0, d.vocab, seqs).astype(np.int32), logits=False)
+    bat.step_greedy(seqs, steps - 1)
+    toks, _ = bat.read(seqs)
+    print(json.dumps({"ncu_case": f"batched decode, {seqs} sequences", "steps": steps,
+                      "kernels_per_step": bat.kernels_per_step(seqs), "last_tokens": toks[:4].tolist()}))
+    bat.close()
     eng.close()
 
 
@@ -480,6 +523,118 @@ def attention_sweep(dcb) -> dict:
                                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
             del k, v
     return out
+
+
+BATCH_SEQS = 64           # independent sequences per GPU
+BATCH_CTX = (512, 8192)   # per-sequence context, uniform
+BATCH_STEPS = 128         # greedy steps each
+
+
+def batched_decode(dcb, eng, d, dist, rank: int, world: int, warmup: int, kv: str = "f32") -> dict:
+    """Batched multi-stream decode: 64 independent sequences per GPU, contexts
+    uniform in [512, 8192] (seeded per rank), KV caches pre-filled with seeded
+    N(0,1) rows, 128 greedy steps, every projection one tcgen05 int8 GEMM over
+    all sequences. Data-parallel over ranks (replicated weights, no
+    collective); tokens/s = all ranks' sequences x steps / max-over-ranks time.
+    The step is one CUDA graph; steps chain on the device (each sequence's
+    argmax is its next token). e2e: dcb_batch_step with host token and argmax
+    buffers every step."""
+    import ctypes
+    import torch
+    K = BATCH_STEPS
+    rng = np.random.default_rng(100 + rank)
+    ctxs = rng.integers(BATCH_CTX[0], BATCH_CTX[1] + 1, BATCH_SEQS)
+    cap = int(ctxs.max()) + warmup + K + 2
+    bat = dcb.Batch(eng, BATCH_SEQS, cap, kv_dtype=kv)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2024 + rank)
+    maxc = int(ctxs.max())
+    for l in range(d.layers):
+        k = torch.randn(maxc, d.kv_dim, device="cuda", generator=gen)
+        v = torch.randn(maxc, d.kv_dim, device="cuda", generator=gen)
+        torch.cuda.synchronize()
+        for s in range(BATCH_SEQS):
+            bat.kv_write(s, l, 0, k.data_ptr(), v.data_ptr(), count=int(ctxs[s]))
+    del k, v
+    toks = rng.integers(0, d.vocab, BATCH_SEQS).astype(np.int32)
+
+    def reset():
+        for s in range(BATCH_SEQS):
+            bat.set_position(s, int(ctxs[s]))
+
+    stream = torch.cuda.ExternalStream(bat.stream)
+    reset()
+    bat.step(toks, logits=False)
+    bat.step_greedy(BATCH_SEQS, warmup - 1)
+    bat.read(BATCH_SEQS)
+    clocks = ClockSampler(torch.cuda.current_device())
+    burst_end = time.time() + 1.0
+    while time.time() < burst_end:
+        reset()
+        bat.step_greedy(BATCH_SEQS, 32)
+        bat.read(BATCH_SEQS)
+    reset()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s_ev.record(stream)
+    bat.step_greedy(BATCH_SEQS, K)
+    e_ev.record(stream)
+    torch.cuda.synchronize()
+    bat.read(BATCH_SEQS)
+    clock_info = clocks.stop()
+    ms = s_ev.elapsed_time(e_ev)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # Algorithmic bytes of one step on one GPU: every weight once (shared by all
+    # sequences), each sequence's embedding row, new K/V row and K/V rows 0..pos.
+    kvb = 4 if kv == "f32" else 2
+    per_token_kv = d.layers * 2 * d.kv_dim * kvb
+    weights_once = model_bytes_per_token(d, 0, kvb) - 2 * per_token_kv - (d.hidden + 4)
+    step_bytes = [weights_once + sum((d.hidden + 4) + per_token_kv * (1 + int(c) + i + 1) for c in ctxs)
+                  for i in range(K)]
+    avg_bytes = sum(step_bytes) / K
+    peak, peak_kind = measured_peaks()
+    gbs = avg_bytes / (ms / 1000.0 / K) / 1e9
+
+    # e2e through the C ABI with host buffers (tokens in, argmax out, every step).
+    reset()
+    lib = dcb.lib()
+    host_toks = toks.copy()
+    am = np.zeros(BATCH_SEQS, np.int32)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        rc = lib.dcb_batch_step(bat._h, BATCH_SEQS, host_toks.ctypes.data, None, am.ctypes.data)
+        if rc:
+            raise RuntimeError(lib.dcb_last_error().decode())
+        host_toks[:] = am
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    kernels = bat.kernels_per_step(BATCH_SEQS)
+    bat.close()
+    return {
+        "workload": "64 independent sequences per GPU, contexts uniform [512, 8192] (seeded), KV pre-filled with "
+                    "seeded N(0,1) rows, 128 greedy steps, FP32 KV, qwen2.5-0.5b-shape int8",
+        "gpus": world, "parallelism": f"dp{world}", "scaling": "weak",
+        "tokens_per_s": round(world * BATCH_SEQS * K / (ms / 1000.0), 1),
+        "ms_per_step": round(ms / K, 4),
+        "mean_context": float(np.mean(ctxs)),
+        "e2e": {"value": round(world * BATCH_SEQS * K / e2e_s, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4 * BATCH_SEQS, "d2h_bytes_per_step": 4 * (bat.slots + 1)},
+        "gpu_launches": int(kernels * K),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_step": int(avg_bytes), "kernel": "whole step (graph)"},
+        "clocks": clock_info,
+    }
 
 
 def _long_model_dir(model: Path) -> Path:

@@ -53,23 +53,28 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Tensor map over int8 rows: `inner` bytes of each row (the rest of its
-// `stride` is not read), `rows` rows; boxes of GK bytes x box_rows rows with
-// the 128-byte swizzle; out-of-range bytes read as zero.
-int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t stride, uint32_t box_rows) {
+// 2D tensor map: `inner` elements of each row (the rest of its `stride`
+// bytes is not read), `rows` rows; boxes of box_inner elements (128 bytes) x
+// box_rows rows with the 128-byte swizzle; out-of-range elements read as zero.
+int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType type, uint64_t inner, uint64_t rows,
+             uint64_t stride, uint32_t box_inner, uint32_t box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return bfail(DCB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride & 15) || box_rows < 1 || box_rows > 256)
         return bfail(DCB_ERR_ARGUMENT, "tensor map: misaligned base or stride");
     const cuuint64_t dims[2] = {inner, rows};
     const cuuint64_t strides[1] = {stride};
-    const cuuint32_t box[2] = {(cuuint32_t)GK, box_rows};
+    const cuuint32_t box[2] = {box_inner, box_rows};
     const cuuint32_t es[2] = {1, 1};
-    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const CUresult r = fn(m, type, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return bfail(DCB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
     return 0;
+}
+// Int8 rows in GK-byte boxes.
+int make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint64_t stride, uint32_t box_rows) {
+    return make_map(m, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, inner, rows, stride, GK, box_rows);
 }
 
 // FP32 rows -> the cache's element type, on the device.
@@ -95,10 +100,12 @@ struct dcb_batch {
     int *tokens = nullptr, *pos = nullptr, *argmax = nullptr, *err = nullptr;
     void *kc = nullptr, *vc = nullptr;
     float* stage_f = nullptr;  // FP32 rows waiting for conversion to F16 (kv_write from device memory)
+    float2* rope = nullptr;    // [slots][D/2] (cos, sin) of each sequence's position, per step
     size_t stage_f_elems = 0;
     int* h_io = nullptr;  // pinned: [slots] tokens in, then [slots] argmax + error word out
     std::vector<CUtensorMap> map_qkv, map_o, map_gu, map_down;
-    CUtensorMap map_head{}, map_ph{}, map_pi{};
+    CUtensorMap map_head{}, map_ph{}, map_pi{}, map_k{}, map_v{};
+    bool attn64 = false;  // head_dim 64, at most 8 query heads per KV head: attention64_kernel
     std::vector<size_t> pos_host;
     cudaGraphExec_t exec = nullptr;
     int graph_n = -1;
@@ -177,6 +184,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
     g.rope_inv = P.rope_inv;
     g.rope_den = P.rope_den;
     g.pos = b->pos;
+    g.rope = b->rope;
     g.kcache = b->kc;
     g.vcache = b->vc;
     g.amax = b->amax;
@@ -197,6 +205,12 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
         s.planes = b->ph;
         s.xsc = b->xsc;
         s.xinv = b->xinv;
+        s.pos = b->pos;
+        s.rope_inv = P.rope_inv;
+        s.rope_den = P.rope_den;
+        s.cached_rope = P.cached_rope;
+        s.half = D / 2;
+        s.rope = b->rope;
         stage_kernel<<<n, ST_NT, st_smem_h, b->stream>>>(s);
         BT_CUDA(cudaGetLastError());
     }
@@ -245,12 +259,28 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             if (int rc = launch_gemm<EPI_QKV, KV>(b, b->map_qkv[l], b->map_ph, 2 * P.qkv_pairs, P.Kh, a)) return rc;
         }
         aa.layer = l;
-        if (D == 64)
+        if (b->attn64) {
+            Attn64Args a6{};
+            a6.q = b->q;
+            a6.part = b->part;
+            a6.pos = b->pos;
+            a6.NH = P.NH;
+            a6.NKV = P.NKV;
+            a6.L = P.L;
+            a6.layer = l;
+            a6.capacity = (int)b->capacity;
+            a6.split_len = b->split_len;
+            a6.max_splits = b->max_splits;
+            a6.err = b->err;
+            attention64_kernel<KV><<<dim3(b->max_splits, P.NKV, n), A64_NT, a64_smem_bytes<KV>(), b->stream>>>(
+                b->map_k, b->map_v, a6);
+        } else if (D == 64) {
             attention_kernel<KV, 64><<<dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream>>>(aa);
-        else
+        } else {
             attention_kernel<KV, 0><<<dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream>>>(aa);
+        }
         BT_CUDA(cudaGetLastError());
-        combine_stage_kernel<<<n, ST_NT, cb_smem, b->stream>>>(ca);
+        combine_stage_kernel<<<n, CB_NT, cb_smem, b->stream>>>(ca);
         BT_CUDA(cudaGetLastError());
         // O + residual.
         {
@@ -407,11 +437,14 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
     b->slots = (int)rup((size_t)max_seqs, 16);
     b->capacity = capacity;
     b->kv_dtype = kv_dtype;
+    b->attn64 = P.D == 64 && P.NH / P.NKV <= A64_HP;
+    b->split_len = b->attn64 ? 512 : 256;
     b->max_splits = cdiv((int)capacity, b->split_len);
     const int S = b->slots;
     if (int rc = b->alloc(&b->x, (size_t)S * P.Kh)) return bail(rc);
     if (int rc = b->alloc(&b->h, (size_t)S * P.Ki)) return bail(rc);
     if (int rc = b->alloc(&b->q, (size_t)S * P.NH * P.D)) return bail(rc);
+    if (int rc = b->alloc(&b->rope, (size_t)S * (P.D / 2))) return bail(rc);
     if (int rc = b->alloc(&b->xsc, S)) return bail(rc);
     if (int rc = b->alloc(&b->xinv, S)) return bail(rc);
     if (int rc = b->alloc(&b->part, (size_t)S * P.NH * b->max_splits * (P.D + 2))) return bail(rc);
@@ -447,6 +480,22 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
     if (int rc = make_map(&b->map_head, P.embed, P.Kh, P.V, P.SH, GM)) return bail(rc);
     if (int rc = make_map(&b->map_ph, b->ph, P.Kh, 3 * (uint64_t)S, P.Kh, 3 * S)) return bail(rc);
     if (int rc = make_map(&b->map_pi, b->pi, P.Ki, 3 * (uint64_t)S, P.Ki, 3 * S)) return bail(rc);
+    if (b->attn64) {
+        // KV rows of every sequence, layer and head as one 2D array of 64-element rows.
+        const uint64_t rows = (uint64_t)S * P.L * P.NKV * capacity;
+        const bool f16 = kv_dtype == DCB_KV_F16;
+        const CUtensorMapDataType t = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        const uint32_t inner = f16 ? 64 : 32;  // 128-byte boxes
+        if (rows > 0x7fffffffull) return bail(bfail(DCB_ERR_UNSUPPORTED, "KV cache too large for one tensor map"));
+        if (int rc = make_map(&b->map_k, b->kc, t, 64, rows, 64 * b->kv_elem(), inner, A64_T)) return bail(rc);
+        if (int rc = make_map(&b->map_v, b->vc, t, 64, rows, 64 * b->kv_elem(), inner, A64_T)) return bail(rc);
+        if (f16)
+            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         a64_smem_bytes<__half>()));
+        else
+            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         a64_smem_bytes<float>()));
+    }
     const int smem = gemm_smem_bytes(S);
     if (int rc = allow_smem<EPI_QKV, float>(smem)) return bail(rc);
     if (int rc = allow_smem<EPI_QKV, __half>(smem)) return bail(rc);

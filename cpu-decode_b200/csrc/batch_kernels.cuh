@@ -65,6 +65,7 @@ struct GemmArgs {
     const float* rope_inv;  // [D/2]
     const float* rope_den;  // [D/2]
     const int* pos;         // [slots] position of each sequence's new token
+    const float2* rope;     // [slots][D/2] (cos, sin) of each sequence's position
     void* kcache;           // [slots][L][NKV][capacity][D]
     void* vcache;
     ArgBest* amax;  // HEAD: [tiles][slots] best (value, row) of each tile and sequence
@@ -161,6 +162,7 @@ __global__ void __launch_bounds__(GT, 1)
     __shared__ float s_xsc[MAX_SLOTS], s_xinv[MAX_SLOTS];
     __shared__ float s_bv[4][MAX_SLOTS];
     __shared__ int s_bi[4][MAX_SLOTS];
+    __shared__ int s_pos[MAX_SLOTS];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.x * GM;
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(GT, 1)
     for (int s = tid; s < a.slots; s += GT) {
         s_xsc[s] = s < a.nseq ? a.xsc[s] : 0.f;
         s_xinv[s] = (a.xinv && s < a.nseq) ? a.xinv[s] : 1.f;
+        if (EPI == EPI_QKV) s_pos[s] = s < a.nseq ? a.pos[s] : 0;
     }
     tc_fence_before();
     __syncthreads();
@@ -231,17 +234,42 @@ __global__ void __launch_bounds__(GT, 1)
     __syncthreads();
     tc_fence_after();
 
-    // ---- epilogue: thread = weight row m0 + 32*warp + lane
+    // ---- epilogue: thread = weight row m0 + 32*warp + lane. Every global
+    // value the epilogue needs is loaded before the stores of its group, so
+    // the loads of a group are in flight together.
     const int r = m0 + 32 * warp + lane;
     const bool rv = r < a.M;
     const float wsc = rv ? a.wscale[(size_t)r * a.wstride] : 0.f;
     const float bia = (rv && a.bias) ? a.bias[(size_t)r * a.bstride] : 0.f;
+    float* __restrict__ out = a.out;
+    // QKV: this row's RoPE pair index and frequency (src/model.cpp:222-224,269-274).
+    int q_kind = 0, q_hd = 0, q_j = 0;
+    if (EPI == EPI_QKV && rv) {
+        const int half = a.D >> 1, u = r >> 1;
+        const int qpairs = a.NH * half, kpairs = a.NKV * half;
+        q_kind = u < qpairs ? 0 : (u < qpairs + kpairs ? 1 : 2);
+        const int pu = q_kind == 0 ? u : (q_kind == 1 ? u - qpairs : u - qpairs - kpairs);
+        q_hd = pu / half;
+        q_j = pu - q_hd * half;
+    }
     const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
     for (int s0 = 0; s0 < a.nseq; s0 += 16) {
         uint32_t hi[16], md[16], lo[16];
         tmem_ld16(trow + (uint32_t)s0, hi);
         tmem_ld16(trow + (uint32_t)(a.slots + s0), md);
         tmem_ld16(trow + (uint32_t)(2 * a.slots + s0), lo);
+        float xo[16];
+        float2 cs16[16];
+        if (EPI == EPI_RESID) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xo[i] = (rv && s0 + i < a.nseq) ? out[(size_t)(s0 + i) * a.ldo + r] : 0.f;
+        }
+        if (EPI == EPI_QKV) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                cs16[i] = (rv && q_kind < 2 && s0 + i < a.nseq) ? a.rope[(size_t)(s0 + i) * (a.D >> 1) + q_j]
+                                                                : make_float2(1.f, 0.f);
+        }
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -250,45 +278,38 @@ __global__ void __launch_bounds__(GT, 1)
             const float acc = planes_to_float((int)hi[i], (int)md[i], (int)lo[i]);
             float y = acc * s_xsc[s] * s_xinv[s] * wsc + bia;
             if (EPI == EPI_PLAIN) {
-                if (rv && sv) a.out[(size_t)s * a.ldo + r] = y;
+                if (rv && sv) out[(size_t)s * a.ldo + r] = y;
             } else if (EPI == EPI_RESID) {
-                if (rv && sv) a.out[(size_t)s * a.ldo + r] += y;
+                if (rv && sv) out[(size_t)s * a.ldo + r] = xo[i] + y;
             } else if (EPI == EPI_GU) {
                 // rows (2j, 2j+1) = (gate_j, up_j) in adjacent lanes (src/model.cpp:306-308)
                 const float u = __shfl_xor_sync(FULL, y, 1);
-                if (rv && sv && !(lane & 1)) a.out[(size_t)s * a.ldo + (r >> 1)] = (y / (1.0f + expf(-y))) * u;
+                if (rv && sv && !(lane & 1)) out[(size_t)s * a.ldo + (r >> 1)] = (y / (1.0f + expf(-y))) * u;
             } else if (EPI == EPI_QKV) {
                 // rows (2u, 2u+1) = (j, j + D/2) of one head in adjacent lanes (src/model.cpp:277-302)
                 const float other = __shfl_xor_sync(FULL, y, 1);
                 if (rv && sv) {
-                    const int half = a.D >> 1, u = r >> 1;
-                    const int qpairs = a.NH * half, kpairs = a.NKV * half;
-                    const int kind = u < qpairs ? 0 : (u < qpairs + kpairs ? 1 : 2);
-                    const int pu = kind == 0 ? u : (kind == 1 ? u - qpairs : u - qpairs - kpairs);
-                    const int hd = pu / half, j = pu - hd * half;
+                    const int half = a.D >> 1;
                     const bool second = lane & 1;
                     const float y0 = second ? other : y, y1 = second ? y : other;
                     float val = second ? y1 : y0;
-                    const int p = a.pos[s];
-                    if (kind < 2) {
-                        const float angle =
-                            a.cached_rope ? __fmul_rn((float)p, a.rope_inv[j]) : __fdiv_rn((float)p, a.rope_den[j]);
-                        float sn, cs;
-                        sincosf(angle, &sn, &cs);
+                    const int p = s_pos[s];
+                    if (q_kind < 2) {
+                        const float cs = cs16[i].x, sn = cs16[i].y;
                         val = second ? __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn))
                                      : __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
                     }
-                    const int idx = j + (second ? half : 0);
-                    if (kind == 0) {
-                        a.out[(size_t)s * a.ldo + hd * a.D + idx] = val;
+                    const int idx = q_j + (second ? half : 0);
+                    if (q_kind == 0) {
+                        out[(size_t)s * a.ldo + q_hd * a.D + idx] = val;
                     } else {
-                        KV* cache = static_cast<KV*>(kind == 1 ? a.kcache : a.vcache) +
-                                    ((((size_t)s * a.L + a.layer) * a.NKV + hd) * a.capacity + p) * a.D;
+                        KV* cache = static_cast<KV*>(q_kind == 1 ? a.kcache : a.vcache) +
+                                    ((((size_t)s * a.L + a.layer) * a.NKV + q_hd) * a.capacity + p) * a.D;
                         kv_store(cache + idx, val);
                     }
                 }
             } else if (EPI == EPI_HEAD) {
-                if (rv && sv && a.out) a.out[(size_t)s * a.ldo + r] = y;
+                if (rv && sv && out) out[(size_t)s * a.ldo + r] = y;
                 float v = (rv && sv) ? y : -INFINITY;
                 int vi = r;
 #pragma unroll
@@ -345,6 +366,12 @@ struct StageArgs {
     float* xsc;          // [slots]
     float* xinv;         // [slots] RMSNorm factor (null: not a normalised input)
     int* err;
+    // embed mode: each sequence's RoPE (cos, sin) table for this step
+    const int* pos;
+    const float* rope_inv;  // [D/2] (cached angle formula) or
+    const float* rope_den;  // [D/2] (direct formula)
+    int cached_rope, half;
+    float2* rope;           // [slots][half]
 };
 
 __device__ __forceinline__ void block_sum_max(float& ss, float& mx, float* red) {
@@ -377,6 +404,15 @@ __global__ void __launch_bounds__(ST_NT) stage_kernel(const StageArgs a) {
     if (s >= a.nseq) return;
     const uint8_t* row = nullptr;
     float rsc = 0.f;
+    if (a.embed && a.rope && threadIdx.x < a.half) {
+        // RoPE angles of this sequence's position (src/model.cpp:269-274), once per step.
+        const int j = threadIdx.x;
+        const float p = (float)a.pos[s];
+        const float angle = a.cached_rope ? __fmul_rn(p, a.rope_inv[j]) : __fdiv_rn(p, a.rope_den[j]);
+        float sn, cs;
+        sincosf(angle, &sn, &cs);
+        a.rope[(size_t)s * a.half + j] = make_float2(cs, sn);
+    }
     if (a.embed) {
         int t = a.tokens[s];
         if ((unsigned)t >= (unsigned)a.vocab) {  // a device-supplied token out of range (src/model.cpp:259)
@@ -462,6 +498,289 @@ __global__ void __launch_bounds__(AT_NT) attention_kernel(const AttnArgs a) {
     });
 }
 
+// ---- attention for head_dim 64 -------------------------------------------------------
+// Block (split, kv head g, sequence s) over positions [split*split_len, ...)
+// up to pos[s], all gq <= 8 query heads of group g, in 64-position chunks that
+// TMA brings into a ring of shared-memory slots (K and V tiles with the
+// 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r % 8) within its
+// 128-byte row segment, so lane-private rows read without bank conflicts).
+// Per chunk:
+//   QK : warp w owns dims 8w..8w+7 (q of every head in registers), lane owns
+//        positions lane and lane+32; partial scores go to shared memory
+//   SM : warp h < gq sums head h's partials over the 8 warps, online softmax
+//        (base 2) over the chunk: new max, rescale, probabilities P[t][h]
+//   PV : warp w owns positions 8w..8w+7, lane owns dims 2*lane, 2*lane+1
+// then the warps' outputs are summed into the split's (max, sum, output).
+constexpr int A64_NT = 256;
+constexpr int A64_NW = A64_NT / 32;
+constexpr int A64_T = 64;    // positions per chunk
+constexpr int A64_HP = 8;    // query heads per group, padded
+constexpr int A64_RING = 65536;  // bytes of K/V chunk slots
+
+template <typename KV>
+__host__ __device__ constexpr int a64_tile_bytes() { return A64_T * 64 * (int)sizeof(KV); }  // one K or V chunk
+template <typename KV>
+__host__ __device__ constexpr int a64_slots() { return A64_RING / (2 * a64_tile_bytes<KV>()); }
+// Dynamic shared memory: 1 KB alignment slack, the ring, partial scores
+// [8 warps][8 heads][64], probabilities [64][8], rescale factors.
+template <typename KV>
+__host__ __device__ constexpr int a64_smem_bytes() {
+    return 1024 + A64_RING + A64_NW * A64_HP * A64_T * 4 + A64_T * A64_HP * 4 + 64;
+}
+
+struct Attn64Args {
+    const float* q;  // [slots][NH*64] rotated queries
+    float* part;     // [slots][NH][max_splits][66]
+    const int* pos;
+    int NH, NKV, L, layer, capacity, split_len, max_splits;
+    int* err;
+};
+
+// Byte offset of element (row r, dim d) in a swizzled chunk tile.
+template <typename KV>
+__device__ __forceinline__ int a64_off(int r, int d) {
+    if (sizeof(KV) == 4) {  // two 128-byte boxes per row: dims 0..31, then 32..63 (8 KB each)
+        const int c = (d & 31) >> 2;
+        return (d >> 5) * (A64_T * 128) + r * 128 + ((c ^ (r & 7)) << 4) + ((d & 3) << 2);
+    } else {  // one 128-byte box per row
+        const int c = d >> 3;
+        return r * 128 + ((c ^ (r & 7)) << 4) + ((d & 7) << 1);
+    }
+}
+__device__ __forceinline__ void a64_load8(const uint8_t* tile, int r, int d0, float (&o)[8], float) {
+    const float4 a = *reinterpret_cast<const float4*>(tile + a64_off<float>(r, d0));
+    const float4 b = *reinterpret_cast<const float4*>(tile + a64_off<float>(r, d0 + 4));
+    o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w, o[4] = b.x, o[5] = b.y, o[6] = b.z, o[7] = b.w;
+}
+__device__ __forceinline__ void a64_load8(const uint8_t* tile, int r, int d0, float (&o)[8], __half) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + a64_off<__half>(r, d0));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        o[2 * i] = f.x;
+        o[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ float2 a64_load2(const uint8_t* tile, int r, int d0, float) {
+    return *reinterpret_cast<const float2*>(tile + a64_off<float>(r, d0));
+}
+__device__ __forceinline__ float2 a64_load2(const uint8_t* tile, int r, int d0, __half) {
+    return __half22float2(*reinterpret_cast<const __half2*>(tile + a64_off<__half>(r, d0)));
+}
+
+template <typename KV>
+__global__ void __launch_bounds__(A64_NT, 2)
+    attention64_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const Attn64Args a) {
+    extern __shared__ uint8_t a64_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a64_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int TB = a64_tile_bytes<KV>(), NS = a64_slots<KV>();
+    float* sp = reinterpret_cast<float*>(sm + A64_RING);  // [warp][head][t] partial scores
+    float* P = sp + A64_NW * A64_HP * A64_T;               // [t][head] probabilities
+    float* s_alpha = P + A64_T * A64_HP;                   // [head] rescale of this chunk
+    __shared__ __align__(8) uint64_t full[8];
+    __shared__ float s_ml[2 * A64_HP];
+    __shared__ int s_abort;
+
+    const int sp_i = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int length = a.pos[s] + 1;
+    const int t0 = sp_i * a.split_len;
+    if (t0 >= length) return;
+    const int t1 = min(length, t0 + a.split_len);
+    const int nch = (t1 - t0 + A64_T - 1) / A64_T;
+    const int gq = a.NH / a.NKV;
+    const int row0 = (((s * a.L + a.layer) * a.NKV + g) * a.capacity) + t0;  // map row of position t0
+
+    auto issue = [&](int c) {  // thread 0: chunk c into slot c % NS
+        const int slot = c % NS;
+        uint8_t* kt = sm + slot * 2 * TB;
+        uint8_t* vt = kt + TB;
+        mbar_expect(&full[slot], 2 * TB);
+        const int y = row0 + c * A64_T;
+        if (sizeof(KV) == 4) {
+            tma2d(kt, &tmK, 0, y, &full[slot]);
+            tma2d(kt + TB / 2, &tmK, 32, y, &full[slot]);
+            tma2d(vt, &tmV, 0, y, &full[slot]);
+            tma2d(vt + TB / 2, &tmV, 32, y, &full[slot]);
+        } else {
+            tma2d(kt, &tmK, 0, y, &full[slot]);
+            tma2d(vt, &tmV, 0, y, &full[slot]);
+        }
+    };
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int c = 0; c < NS && c < nch; ++c) issue(c);
+    }
+    // q of every head for this warp's 8 dims, scaled by log2(e)/8.
+    float qr[A64_HP][8];
+    {
+        const float qscale = 1.4426950408889634f / 8.0f;
+        const float* qs = a.q + ((size_t)s * a.NH + (size_t)g * gq) * 64 + 8 * warp;
+#pragma unroll
+        for (int h = 0; h < A64_HP; ++h) {
+            if (h < gq) {
+                const float4 x = *reinterpret_cast<const float4*>(qs + (size_t)h * 64);
+                const float4 y = *reinterpret_cast<const float4*>(qs + (size_t)h * 64 + 4);
+                qr[h][0] = x.x * qscale, qr[h][1] = x.y * qscale, qr[h][2] = x.z * qscale, qr[h][3] = x.w * qscale;
+                qr[h][4] = y.x * qscale, qr[h][5] = y.y * qscale, qr[h][6] = y.z * qscale, qr[h][7] = y.w * qscale;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) qr[h][e] = 0.f;
+            }
+        }
+    }
+    float m_run = -INFINITY, l_run = 0.f;  // head `warp`'s softmax state (warps < gq)
+    float o[A64_HP][2];
+#pragma unroll
+    for (int h = 0; h < A64_HP; ++h) o[h][0] = o[h][1] = 0.f;
+    __syncthreads();
+
+    bool ok = true;
+    for (int c = 0; c < nch; ++c) {
+        const int slot = c % NS;
+        const uint8_t* kt = sm + slot * 2 * TB;
+        const uint8_t* vt = kt + TB;
+        if (tid == 0) {
+            uint64_t w0 = 0;
+            unsigned spins = 0;
+            while (!mbar_test(&full[slot], (uint32_t)(c / NS) & 1u)) {
+                if ((++spins & 63u) == 0) {
+                    const uint64_t now = globaltimer();
+                    if (!w0) {
+                        w0 = now;
+                    } else if (now - w0 > WAIT_LIMIT_NS) {
+                        atomicExch(a.err, ERR_WAIT);
+                        s_abort = 1;
+                        break;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (s_abort) {  // the wait ran out
+            ok = false;
+            break;
+        }
+        const int cbase = t0 + c * A64_T;
+        // QK partials: positions lane, lane + 32; dims 8*warp..8*warp+7.
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+            const int t = lane + 32 * pp;
+            float k8[8];
+            a64_load8(kt, t, 8 * warp, k8, KV());
+#pragma unroll
+            for (int h = 0; h < A64_HP; ++h) {
+                if (h < gq) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc = fmaf(qr[h][e], k8[e], acc);
+                    sp[(warp * A64_HP + h) * A64_T + t] = acc;
+                }
+            }
+        }
+        __syncthreads();
+        // Softmax over the chunk: warp h owns head h.
+        if (warp < gq) {
+            const int h = warp;
+            float sc[2];
+#pragma unroll
+            for (int pp = 0; pp < 2; ++pp) {
+                const int t = lane + 32 * pp;
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < A64_NW; ++w) v += sp[(w * A64_HP + h) * A64_T + t];
+                sc[pp] = cbase + t < t1 ? v : -INFINITY;
+            }
+            const float cmax = warp_max(fmaxf(sc[0], sc[1]));
+            const float m_new = fmaxf(m_run, cmax);
+            const float alpha = m_run > -INFINITY ? at_ex2(m_run - m_new) : 0.f;
+            const float p0 = sc[0] > -INFINITY ? at_ex2(sc[0] - m_new) : 0.f;
+            const float p1 = sc[1] > -INFINITY ? at_ex2(sc[1] - m_new) : 0.f;
+            l_run = fmaf(l_run, alpha, warp_sum(p0 + p1));
+            m_run = m_new;
+            P[lane * A64_HP + h] = p0;
+            P[(lane + 32) * A64_HP + h] = p1;
+            if (lane == 0) s_alpha[h] = alpha;
+        } else if (warp < A64_HP) {
+            const int h = warp;  // padded heads: zero probabilities
+            P[lane * A64_HP + h] = 0.f;
+            P[(lane + 32) * A64_HP + h] = 0.f;
+            if (lane == 0) s_alpha[h] = 0.f;
+        }
+        __syncthreads();
+        // PV: positions 8*warp..8*warp+7, dims 2*lane, 2*lane+1.
+        {
+            const float4 al0 = *reinterpret_cast<const float4*>(s_alpha);
+            const float4 al1 = *reinterpret_cast<const float4*>(s_alpha + 4);
+            const float alv[8] = {al0.x, al0.y, al0.z, al0.w, al1.x, al1.y, al1.z, al1.w};
+#pragma unroll
+            for (int h = 0; h < A64_HP; ++h) {
+                o[h][0] *= alv[h];
+                o[h][1] *= alv[h];
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int t = 8 * warp + i;
+                const float2 v2 = a64_load2(vt, t, 2 * lane, KV());
+                const float4 pa = *reinterpret_cast<const float4*>(P + t * A64_HP);
+                const float4 pb = *reinterpret_cast<const float4*>(P + t * A64_HP + 4);
+                const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                for (int h = 0; h < A64_HP; ++h) {
+                    o[h][0] = fmaf(pv[h], v2.x, o[h][0]);
+                    o[h][1] = fmaf(pv[h], v2.y, o[h][1]);
+                }
+            }
+        }
+        __syncthreads();  // slot consumed by every warp
+        if (tid == 0 && c + NS < nch) {
+            fence_proxy_async();
+            issue(c + NS);
+        }
+    }
+    if (!ok) {
+        // Copies still in flight land before the block exits (bounded).
+        if (tid == 0) {
+            const uint64_t w0 = globaltimer();
+            for (int c = 0; c < nch && c < NS; ++c) {
+                const int last = c + ((nch - 1 - c) / NS) * NS;
+                while (!mbar_test(&full[c % NS], (uint32_t)(last / NS) & 1u) && globaltimer() - w0 < WAIT_LIMIT_NS) {
+                }
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    // Sum the warps' outputs: [warp][head][64] through the partial-score area.
+    float* ow = sp;
+#pragma unroll
+    for (int h = 0; h < A64_HP; ++h) {
+        ow[(warp * A64_HP + h) * 64 + 2 * lane] = o[h][0];
+        ow[(warp * A64_HP + h) * 64 + 2 * lane + 1] = o[h][1];
+    }
+    if (warp < gq && lane == 0) {
+        s_ml[2 * warp] = m_run;
+        s_ml[2 * warp + 1] = l_run;
+    }
+    __syncthreads();
+    for (int e = tid; e < gq * 64; e += A64_NT) {
+        const int h = e >> 6, j = e & 63;
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < A64_NW; ++w) acc += ow[(w * A64_HP + h) * 64 + j];
+        float* pp = a.part + (((size_t)s * a.NH + (size_t)g * gq + h) * a.max_splits + sp_i) * 66;
+        if (j == 0) {
+            pp[0] = s_ml[2 * h];
+            pp[1] = s_ml[2 * h + 1];
+        }
+        pp[2 + j] = acc;
+    }
+}
+
 // One block per sequence: merge the splits of every head (in split order) and
 // stage the attention output (NH*D values) as planes for the O projection.
 struct CombineArgs {
@@ -471,43 +790,61 @@ struct CombineArgs {
     int8_t* planes;  // [3][slots][kp]
     float* xsc;
 };
-__global__ void __launch_bounds__(ST_NT) combine_stage_kernel(const CombineArgs a) {
+constexpr int CB_NT = 512;  // combine threads: one warp per head (up to 16 heads per pass)
+__global__ void __launch_bounds__(CB_NT) combine_stage_kernel(const CombineArgs a) {
     extern __shared__ float cb_sm[];  // [NH*D] outputs, then [NH][max_splits] weights
     __shared__ float red[64];
     const int s = blockIdx.x;
-    const int n = a.NH * a.D;
+    const int n = a.NH * a.D, D = a.D, W = D + 2;
     float* outv = cb_sm;
     float* wts = cb_sm + n;
     const int ns = (a.pos[s] + a.split_len) / a.split_len;  // splits covering positions 0..pos
-    const float* base = a.part + (size_t)s * a.NH * a.max_splits * (a.D + 2);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = ST_NT / 32;
-    // Per head: weight of split i = 2^(m_i - M) / sum_i 2^(m_i - M) l_i.
+    const float* base = a.part + (size_t)s * a.NH * a.max_splits * W;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = CB_NT / 32;
+    float mx = 0.f, ss = 0.f;
+    // Warp per head: weight of split i = 2^(m_i - M) / sum_i 2^(m_i - M) l_i
+    // (lanes over splits), then lanes over dimensions j = lane + 32k with the
+    // loads of eight splits in flight, summed in split order.
     for (int h = warp; h < a.NH; h += nw) {
-        const float* hb = base + (size_t)h * a.max_splits * (a.D + 2);
+        const float* hb = base + (size_t)h * a.max_splits * W;
+        float* hw = wts + h * a.max_splits;
         float M = -INFINITY;
-        for (int i = lane; i < ns; i += 32) M = fmaxf(M, hb[(size_t)i * (a.D + 2)]);
+        for (int i = lane; i < ns; i += 32) M = fmaxf(M, hb[(size_t)i * W]);
         M = warp_max(M);
         float Ls = 0.f;
         for (int i = lane; i < ns; i += 32) {
-            const float mi = hb[(size_t)i * (a.D + 2)];
+            const float mi = hb[(size_t)i * W];
             const float f = mi > -INFINITY ? at_ex2(mi - M) : 0.f;
-            wts[h * a.max_splits + i] = f;
-            Ls = fmaf(f, hb[(size_t)i * (a.D + 2) + 1], Ls);
+            hw[i] = f;
+            Ls = fmaf(f, hb[(size_t)i * W + 1], Ls);
         }
         Ls = warp_sum(Ls);
         __syncwarp();
         const float invL = 1.0f / Ls;
-        for (int i = lane; i < ns; i += 32) wts[h * a.max_splits + i] *= invL;
-    }
-    __syncthreads();
-    float mx = 0.f, ss = 0.f;
-    for (int e = threadIdx.x; e < n; e += ST_NT) {
-        const int h = e / a.D, j = e - h * a.D;
-        const float* hb = base + (size_t)h * a.max_splits * (a.D + 2) + 2 + j;
-        float acc = 0.f;
-        for (int i = 0; i < ns; ++i) acc = fmaf(wts[h * a.max_splits + i], hb[(size_t)i * (a.D + 2)], acc);
-        outv[e] = acc;
-        mx = fmaxf(mx, fabsf(acc));
+        float acc[AT_MAXD] = {0.f, 0.f, 0.f, 0.f};
+        for (int i0 = 0; i0 < ns; i0 += 8) {
+            float v[8][AT_MAXD];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int k = 0; k < AT_MAXD; ++k)
+                    v[u][k] = (i0 + u < ns && lane + 32 * k < D) ? hb[(size_t)(i0 + u) * W + 2 + lane + 32 * k] : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float f = i0 + u < ns ? hw[i0 + u] : 0.f;
+#pragma unroll
+                for (int k = 0; k < AT_MAXD; ++k) acc[k] = fmaf(f, v[u][k], acc[k]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < AT_MAXD; ++k) {
+            const int j = lane + 32 * k;
+            if (j < D) {
+                const float o = acc[k] * invL;
+                outv[h * D + j] = o;
+                mx = fmaxf(mx, fabsf(o));
+            }
+        }
     }
     block_sum_max(ss, mx, red);
     const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
@@ -515,7 +852,7 @@ __global__ void __launch_bounds__(ST_NT) combine_stage_kernel(const CombineArgs 
     int8_t* ph = a.planes + (size_t)s * a.kp;
     int8_t* pm = ph + (size_t)a.slots * a.kp;
     int8_t* pl = pm + (size_t)a.slots * a.kp;
-    for (int quad = threadIdx.x; quad < a.kp / 4; quad += ST_NT) {
+    for (int quad = threadIdx.x; quad < a.kp / 4; quad += CB_NT) {
         const int j = 4 * quad;
         const float4 v4 = make_float4(j < n ? outv[j] : 0.f, j + 1 < n ? outv[j + 1] : 0.f,
                                       j + 2 < n ? outv[j + 2] : 0.f, j + 3 < n ? outv[j + 3] : 0.f);

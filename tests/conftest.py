@@ -56,6 +56,23 @@ SMALL = synthetic.Dims(hidden=128, intermediate=320, layers=2, heads=4, kv_heads
 ODD = synthetic.Dims(hidden=72, intermediate=100, layers=2, heads=6, kv_heads=2, vocab=333, max_positions=128,
                      epsilon=1e-6, theta=10000.0)
 
+# head_dim 64 with 7 and 2 query heads per KV head: the batched engine's TMA
+# attention path (the Qwen shape's head geometry at a small width).
+G64 = synthetic.Dims(hidden=448, intermediate=512, layers=2, heads=7, kv_heads=1, vocab=1000, max_positions=4096,
+                     epsilon=1e-6, theta=1e6)
+G64B = synthetic.Dims(hidden=256, intermediate=384, layers=2, heads=4, kv_heads=2, vocab=777, max_positions=4096,
+                      epsilon=1e-6, theta=1e6)
+
+
+@pytest.fixture(scope="session")
+def g64_int8(tmp_path_factory) -> Path:
+    return synthetic.write_int8_model(tmp_path_factory.mktemp("g64") / "int8", G64, synthetic.random_values(17))
+
+
+@pytest.fixture(scope="session")
+def g64b_int8(tmp_path_factory) -> Path:
+    return synthetic.write_int8_model(tmp_path_factory.mktemp("g64b") / "int8", G64B, synthetic.random_values(19))
+
 
 @pytest.fixture(scope="session")
 def small_int8(tmp_path_factory) -> Path:

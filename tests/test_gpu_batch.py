@@ -63,6 +63,19 @@ def test_batch_matches_oracle_per_sequence(small_int8, kv):
         assert bat.position(s) == ctx + 4
 
 
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+@pytest.mark.parametrize("which", ["g64", "g64b"])
+def test_batch_head_dim_64(which, kv, g64_int8, g64b_int8):
+    """head_dim 64: the TMA-fed attention kernel, contexts across its
+    64-position chunks and 512-position splits."""
+    from conftest import G64, G64B
+    model, d = (g64_int8, G64) if which == "g64" else (g64b_int8, G64B)
+    contexts = [0, 1, 63, 64, 511, 512, 513, 1100]
+    eng, bat, orcs = _setup(model, d, contexts, 3, kv)
+    toks = np.random.default_rng(21).integers(0, d.vocab, len(contexts))
+    _run_and_compare(bat, orcs, toks, 3)
+
+
 def test_batch_all_64_slots(small_int8):
     contexts = list(np.random.default_rng(3).integers(0, 400, 64))
     eng, bat, orcs = _setup(small_int8, SMALL, contexts, 2)
