@@ -207,6 +207,7 @@ def main() -> None:
     ap.add_argument("--no-batch", action="store_true", help="skip the batched 64-sequence measurement")
     ap.add_argument("--ncu-batch", type=int, default=0, metavar="SEQS",
                     help="the batched profiling case: SEQS sequences, --steps graph steps")
+    ap.add_argument("--ncu-ctx", type=int, default=8192, help="largest context of the batched profiling case")
     ap.add_argument("--ncu-case", action="store_true",
                     help="the profiling case: KV rows 0..127 written from the host, then 5 decode launches")
     args = ap.parse_args()
@@ -217,7 +218,7 @@ def main() -> None:
         ncu_case()
         return
     if args.ncu_batch:
-        ncu_batch_case(args.ncu_batch, max(1, args.steps))
+        ncu_batch_case(args.ncu_batch, max(1, args.steps), args.ncu_ctx)
         return
 
     import torch
@@ -394,7 +395,7 @@ def ncu_case() -> None:
     eng.close()
 
 
-def ncu_batch_case(seqs: int, steps: int) -> None:
+def ncu_batch_case(seqs: int, steps: int, max_ctx: int = 8192) -> None:
     """The batched workload for a profiler: `seqs` sequences with the bench's
     seeded contexts (uniform [512, 8192]), KV pre-filled on the device, then
     `steps` graph steps. Capture with `-k regex:"gemm_i8|attention_kernel|
@@ -407,7 +408,7 @@ def ncu_batch_case(seqs: int, steps: int) -> None:
     d = syn.QWEN05
     eng = dcb.Engine(model, 1)
     rng = np.random.default_rng(100)
-    ctxs = rng.integers(BATCH_CTX[0], BATCH_CTX[1] + 1, BATCH_SEQS)[:seqs]
+    ctxs = np.minimum(rng.integers(BATCH_CTX[0], BATCH_CTX[1] + 1, BATCH_SEQS)[:seqs], max_ctx)
     bat = dcb.Batch(eng, seqs, int(ctxs.max()) + steps + 2)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(2024)

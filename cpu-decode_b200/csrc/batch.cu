@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 #include <algorithm>
 #include <cstring>
+#include <utility>
 #include <string>
 #include <vector>
 
@@ -92,6 +93,7 @@ struct dcb_batch {
     int slots = 0, kv_dtype = DCB_KV_F32;
     size_t capacity = 0;
     int split_len = 256, max_splits = 0;
+    int sms = 148;
     std::vector<void*> allocations;
     float *x = nullptr, *h = nullptr, *q = nullptr, *xsc = nullptr, *xinv = nullptr, *part = nullptr,
           *logits = nullptr;
@@ -141,15 +143,46 @@ struct dcb_batch {
 
 namespace {
 
+// Every kernel of a step is launched with programmatic stream serialization:
+// it may start (and run the part before its griddepcontrol.wait) while the
+// previous kernel finishes. `cluster` > 1 groups that many CTAs along x.
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, int threads, size_t smem, cudaStream_t stream, int cluster,
+           Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (cluster > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)cluster;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    BT_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+    return 0;
+}
+
+// Row tiles of 128 x all sequences; with fewer tiles than SMs the reduction
+// is split over a cluster of up to 8 CTAs per tile (one stage at least each).
 template <int EPI, typename KV>
 int launch_gemm(dcb_batch* b, const CUtensorMap& ma, const CUtensorMap& mb, int rows, int K, const GemmArgs& a0) {
     GemmArgs a = a0;
     a.M = rows;
     a.nk = cdiv(K, GK);
+    const int tiles = cdiv(rows, GM);
+    a.ksplit = EPI == EPI_HEAD ? 1 : std::max(1, std::min({8, a.nk, b->sms / tiles}));
     const int smem = gemm_smem_bytes(b->slots);
-    gemm_i8_kernel<EPI, KV><<<cdiv(rows, GM), GT, smem, b->stream>>>(ma, mb, a);
-    BT_CUDA(cudaGetLastError());
-    return 0;
+    return launch(gemm_i8_kernel<EPI, KV>, dim3(tiles * a.ksplit), GT, smem, b->stream, a.ksplit, ma, mb, a);
 }
 
 template <int EPI, typename KV>
@@ -211,8 +244,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
         s.cached_rope = P.cached_rope;
         s.half = D / 2;
         s.rope = b->rope;
-        stage_kernel<<<n, ST_NT, st_smem_h, b->stream>>>(s);
-        BT_CUDA(cudaGetLastError());
+        if (int rc = launch(stage_kernel, dim3(n), ST_NT, st_smem_h, b->stream, 1, s)) return rc;
     }
     AttnArgs aa{};
     aa.q = b->q;
@@ -272,16 +304,17 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             a6.split_len = b->split_len;
             a6.max_splits = b->max_splits;
             a6.err = b->err;
-            attention64_kernel<KV><<<dim3(b->max_splits, P.NKV, n), A64_NT, a64_smem_bytes<KV>(), b->stream>>>(
-                b->map_k, b->map_v, a6);
+            if (int rc = launch(attention64_kernel<KV>, dim3(b->max_splits, P.NKV, n), A64_NT, a64_smem_bytes<KV>(),
+                                b->stream, 1, b->map_k, b->map_v, a6))
+                return rc;
         } else if (D == 64) {
-            attention_kernel<KV, 64><<<dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream>>>(aa);
+            if (int rc = launch(attention_kernel<KV, 64>, dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream, 1, aa))
+                return rc;
         } else {
-            attention_kernel<KV, 0><<<dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream>>>(aa);
+            if (int rc = launch(attention_kernel<KV, 0>, dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream, 1, aa))
+                return rc;
         }
-        BT_CUDA(cudaGetLastError());
-        combine_stage_kernel<<<n, CB_NT, cb_smem, b->stream>>>(ca);
-        BT_CUDA(cudaGetLastError());
+        if (int rc = launch(combine_stage_kernel, dim3(n), CB_NT, cb_smem, b->stream, 1, ca)) return rc;
         // O + residual.
         {
             GemmArgs a = g;
@@ -301,8 +334,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             s.planes = b->ph;
             s.xsc = b->xsc;
             s.xinv = b->xinv;
-            stage_kernel<<<n, ST_NT, st_smem_h, b->stream>>>(s);
-            BT_CUDA(cudaGetLastError());
+            if (int rc = launch(stage_kernel, dim3(n), ST_NT, st_smem_h, b->stream, 1, s)) return rc;
         }
         // gate/up + SiLU.
         {
@@ -322,8 +354,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             s.lds = P.Ki;
             s.planes = b->pi;
             s.xsc = b->xsc;
-            stage_kernel<<<n, ST_NT, st_smem_i, b->stream>>>(s);
-            BT_CUDA(cudaGetLastError());
+            if (int rc = launch(stage_kernel, dim3(n), ST_NT, st_smem_i, b->stream, 1, s)) return rc;
         }
         // down + residual.
         {
@@ -345,8 +376,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             s.planes = b->ph;
             s.xsc = b->xsc;
             s.xinv = b->xinv;
-            stage_kernel<<<n, ST_NT, st_smem_h, b->stream>>>(s);
-            BT_CUDA(cudaGetLastError());
+            if (int rc = launch(stage_kernel, dim3(n), ST_NT, st_smem_h, b->stream, 1, s)) return rc;
         }
     }
     // Tied LM head + per-tile argmax, then the argmax per sequence.
@@ -367,9 +397,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
     ga.argmax = b->argmax;
     ga.tokens = b->tokens;
     ga.pos = b->pos;
-    argmax_kernel<<<n, ARG_NT, 0, b->stream>>>(ga);
-    BT_CUDA(cudaGetLastError());
-    return 0;
+    return launch(argmax_kernel, dim3(n), ARG_NT, 0, b->stream, 1, ga);
 }
 
 int build_graph(dcb_batch* b, int n, bool want_logits) {
@@ -429,6 +457,7 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
     const Params& P = b->M.P;
     b->device = b->M.device;
     BT_CUDA(cudaSetDevice(b->device));
+    BT_CUDA(cudaDeviceGetAttribute(&b->sms, cudaDevAttrMultiProcessorCount, b->device));
     int major = 0, minor = 0;
     BT_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, b->device));
     BT_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, b->device));

@@ -50,6 +50,7 @@ __host__ __device__ constexpr int gemm_smem_bytes(int slots) { return 1024 + GST
 struct GemmArgs {
     int M;      // weight rows
     int nk;     // reduction stages (ceil(K / GK))
+    int ksplit; // CTAs of a cluster sharing one row tile, each a slice of the stages (1 = no split)
     int nseq;   // active sequences (slots 0..nseq-1)
     int slots;  // sequence slots per plane (multiple of 16)
     const float* wscale;  // row r's scale at wscale[r * wstride]
@@ -130,6 +131,39 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Programmatic dependent launch: a kernel may start while its predecessor in
+// the stream still runs; griddep_wait() returns once the predecessor has
+// completed and its writes are visible. Work before it may only touch data
+// that no kernel of the same step writes (weights, earlier steps' KV rows).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Expected transaction bytes without an arrival (the phase cannot complete
+// before the arrival that comes with the rest of the stage).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* m, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
+}
+// Thread-block cluster: rank, barrier, and loads from another CTA's shared memory.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ int dsmem_ld(uint32_t addr) {
+    int v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
 // One thread waits for phase `parity` of m, at most WAIT_LIMIT_NS.
 static __device__ bool wait_phase(uint64_t* m, uint32_t parity, int* err) {
     uint64_t t0 = 0;
@@ -165,7 +199,15 @@ __global__ void __launch_bounds__(GT, 1)
     __shared__ int s_pos[MAX_SLOTS];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.x * GM;
+    // Split-K: the S CTAs of a cluster share row tile blockIdx.x / S; rank r
+    // takes stages [r*nk/S, (r+1)*nk/S) and, after the exact integer sums
+    // over the cluster, sequences [r*ceil(slots/S), ...) of the epilogue.
+    const int S = a.ksplit;
+    const int rank = S > 1 ? (int)cluster_rank() : 0;
+    const int m0 = (blockIdx.x / S) * GM;
+    const int kb = rank * a.nk / S, nkl = (rank + 1) * a.nk / S - kb;
+    const int per = (a.slots + S - 1) / S;
+    const int s_first = rank * per, s_last = min(a.nseq, s_first + per);
 
     if (tid == 0) {
         for (int s = 0; s < GSTAGES; ++s) {
@@ -181,26 +223,33 @@ __global__ void __launch_bounds__(GT, 1)
         tmem_alloc(&s_tmem, TMEM_COLS);
         tmem_relinquish();
     }
-    for (int s = tid; s < a.slots; s += GT) {
-        s_xsc[s] = s < a.nseq ? a.xsc[s] : 0.f;
-        s_xinv[s] = (a.xinv && s < a.nseq) ? a.xinv[s] : 1.f;
-        if (EPI == EPI_QKV) s_pos[s] = s < a.nseq ? a.pos[s] : 0;
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
-            // Producer: weight tile rows m0.., all sequences' planes, GK bytes of K per stage.
+            // Producer. The first stages' weight tiles do not depend on the
+            // previous kernel: they are requested before waiting for it.
+            const int npre = min(GSTAGES, nkl);
+            for (int i = 0; i < npre; ++i) {
+                mbar_expect_tx(&full[i], A_BYTES);
+                tma2d(sA + i * A_BYTES, &tmA, (kb + i) * GK, m0, &full[i]);
+            }
+            griddep_wait();
+            for (int i = 0; i < npre; ++i) {
+                mbar_expect(&full[i], (uint32_t)BB);
+                tma2d(sB + i * BB, &tmB, (kb + i) * GK, 0, &full[i]);
+            }
             const uint32_t bytes = (uint32_t)(A_BYTES + BB);
-            for (int kt = 0; kt < a.nk; ++kt) {
-                const int s = kt % GSTAGES;
-                if (kt >= GSTAGES && !wait_phase(&empty[s], (uint32_t)((kt / GSTAGES) - 1) & 1u, a.err)) break;
+            for (int i = npre; i < nkl; ++i) {
+                const int s = i % GSTAGES;
+                if (!wait_phase(&empty[s], (uint32_t)((i / GSTAGES) - 1) & 1u, a.err)) break;
                 mbar_expect(&full[s], bytes);
-                tma2d(sA + s * A_BYTES, &tmA, kt * GK, m0, &full[s]);
-                tma2d(sB + s * BB, &tmB, kt * GK, 0, &full[s]);
+                tma2d(sA + s * A_BYTES, &tmA, (kb + i) * GK, m0, &full[s]);
+                tma2d(sB + s * BB, &tmB, (kb + i) * GK, 0, &full[s]);
             }
         }
         __syncwarp();
@@ -208,31 +257,53 @@ __global__ void __launch_bounds__(GT, 1)
         if (lane == 0) {
             // MMA issuer: 4 MMAs of K = 32 per stage, accumulating in TMEM.
             const uint32_t idesc = idesc_i8(N);
-            for (int kt = 0; kt < a.nk; ++kt) {
-                const int s = kt % GSTAGES;
-                if (!wait_phase(&full[s], (uint32_t)(kt / GSTAGES) & 1u, a.err)) break;
+            for (int i = 0; i < nkl; ++i) {
+                const int s = i % GSTAGES;
+                if (!wait_phase(&full[s], (uint32_t)(i / GSTAGES) & 1u, a.err)) break;
                 tc_fence_after();
                 const uint64_t da = sw128_desc(sA + s * A_BYTES), db = sw128_desc(sB + s * BB);
 #pragma unroll
                 for (int kk = 0; kk < GK / 32; ++kk)
-                    umma_i8(tmem, da + 2 * kk, db + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
+                    umma_i8(tmem, da + 2 * kk, db + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
                 umma_commit(&empty[s]);
             }
             umma_commit(&done);
         }
         __syncwarp();
     }
+    griddep_wait();
+    for (int s = tid; s < a.slots; s += GT) {
+        s_xsc[s] = s < a.nseq ? a.xsc[s] : 0.f;
+        s_xinv[s] = (a.xinv && s < a.nseq) ? a.xinv[s] : 1.f;
+        if (EPI == EPI_QKV) s_pos[s] = s < a.nseq ? a.pos[s] : 0;
+    }
     if (tid == 0) {
         wait_phase(&done, 0, a.err);
         // Every load issued must have landed before the block may exit (only
         // relevant after an expired wait; otherwise these phases are complete).
-        for (int s = 0; s < GSTAGES && s < a.nk; ++s) {
-            const int last = s + ((a.nk - 1 - s) / GSTAGES) * GSTAGES;  // last stage index kt using slot s
+        for (int s = 0; s < GSTAGES && s < nkl; ++s) {
+            const int last = s + ((nkl - 1 - s) / GSTAGES) * GSTAGES;  // last local stage using slot s
             wait_phase(&full[s], (uint32_t)(last / GSTAGES) & 1u, a.err);
         }
     }
     __syncthreads();
     tc_fence_after();
+
+    // Split-K: this CTA's int32 partials (all N columns) into its own shared
+    // memory as [column][128 rows] (the pipeline buffers are free now), then
+    // visible to the cluster.
+    int* red = reinterpret_cast<int*>(g_sm);
+    if (S > 1) {
+        const uint32_t trow0 = tmem + ((uint32_t)(32 * warp) << 16);
+        for (int c0 = 0; c0 < N; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(trow0 + (uint32_t)c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) red[(c0 + i) * GM + 32 * warp + lane] = (int)v[i];
+        }
+        cluster_sync();
+    }
 
     // ---- epilogue: thread = weight row m0 + 32*warp + lane. Every global
     // value the epilogue needs is loaded before the stores of its group, so
@@ -253,30 +324,48 @@ __global__ void __launch_bounds__(GT, 1)
         q_j = pu - q_hd * half;
     }
     const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-    for (int s0 = 0; s0 < a.nseq; s0 += 16) {
+    for (int s0 = s_first; s0 < s_last; s0 += 16) {
         uint32_t hi[16], md[16], lo[16];
-        tmem_ld16(trow + (uint32_t)s0, hi);
-        tmem_ld16(trow + (uint32_t)(a.slots + s0), md);
-        tmem_ld16(trow + (uint32_t)(2 * a.slots + s0), lo);
+        if (S == 1) {
+            tmem_ld16(trow + (uint32_t)s0, hi);
+            tmem_ld16(trow + (uint32_t)(a.slots + s0), md);
+            tmem_ld16(trow + (uint32_t)(2 * a.slots + s0), lo);
+        } else {
+            // Exact sums of the cluster's partials, in rank order.
+#pragma unroll
+            for (int i = 0; i < 16; ++i) hi[i] = md[i] = lo[i] = 0u;
+            for (int q = 0; q < S; ++q) {
+                const uint32_t base = dsmem_addr(red, (uint32_t)q) + 4u * (uint32_t)(32 * warp + lane);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    if (s0 + i < s_last) {
+                        hi[i] += (uint32_t)dsmem_ld(base + 4u * (uint32_t)((s0 + i) * GM));
+                        md[i] += (uint32_t)dsmem_ld(base + 4u * (uint32_t)((a.slots + s0 + i) * GM));
+                        lo[i] += (uint32_t)dsmem_ld(base + 4u * (uint32_t)((2 * a.slots + s0 + i) * GM));
+                    }
+                }
+            }
+        }
         float xo[16];
         float2 cs16[16];
         if (EPI == EPI_RESID) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) xo[i] = (rv && s0 + i < a.nseq) ? out[(size_t)(s0 + i) * a.ldo + r] : 0.f;
+            for (int i = 0; i < 16; ++i) xo[i] = (rv && s0 + i < s_last) ? out[(size_t)(s0 + i) * a.ldo + r] : 0.f;
         }
         if (EPI == EPI_QKV) {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-                cs16[i] = (rv && q_kind < 2 && s0 + i < a.nseq) ? a.rope[(size_t)(s0 + i) * (a.D >> 1) + q_j]
+                cs16[i] = (rv && q_kind < 2 && s0 + i < s_last) ? a.rope[(size_t)(s0 + i) * (a.D >> 1) + q_j]
                                                                 : make_float2(1.f, 0.f);
         }
-        tmem_wait_ld();
+        if (S == 1) tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const int s = s0 + i;
-            const bool sv = s < a.nseq;
+            const bool sv = s < s_last;
+            const int si = sv ? s : 0;
             const float acc = planes_to_float((int)hi[i], (int)md[i], (int)lo[i]);
-            float y = acc * s_xsc[s] * s_xinv[s] * wsc + bia;
+            float y = acc * s_xsc[si] * s_xinv[si] * wsc + bia;
             if (EPI == EPI_PLAIN) {
                 if (rv && sv) out[(size_t)s * a.ldo + r] = y;
             } else if (EPI == EPI_RESID) {
@@ -293,7 +382,7 @@ __global__ void __launch_bounds__(GT, 1)
                     const bool second = lane & 1;
                     const float y0 = second ? other : y, y1 = second ? y : other;
                     float val = second ? y1 : y0;
-                    const int p = s_pos[s];
+                    const int p = s_pos[si];
                     if (q_kind < 2) {
                         const float cs = cs16[i].x, sn = cs16[i].y;
                         val = second ? __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn))
@@ -341,6 +430,8 @@ __global__ void __launch_bounds__(GT, 1)
             a.amax[(size_t)blockIdx.x * a.slots + tid] = {v, vi};
         }
     }
+    // No CTA leaves while a cluster peer may still read its partials.
+    if (S > 1) cluster_sync();
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
@@ -400,6 +491,8 @@ __device__ __forceinline__ void block_sum_max(float& ss, float& mx, float* red) 
 __global__ void __launch_bounds__(ST_NT) stage_kernel(const StageArgs a) {
     extern __shared__ float st_v[];  // [n] gained values
     __shared__ float red[64];
+    griddep_launch_dependents();
+    griddep_wait();
     const int s = blockIdx.x;
     if (s >= a.nseq) return;
     const uint8_t* row = nullptr;
@@ -472,6 +565,8 @@ struct AttnArgs {
 template <typename KV, int DT>
 __global__ void __launch_bounds__(AT_NT) attention_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) unsigned char at_sm[];
+    griddep_launch_dependents();
+    griddep_wait();
     const int sp = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
     const int D = DT ? DT : a.D;
     const int length = a.pos[s] + 1;
@@ -609,12 +704,22 @@ __global__ void __launch_bounds__(A64_NT, 2)
             tma2d(vt, &tmV, 0, y, &full[slot]);
         }
     };
+    // pos[] changes only at the end of a step, and the rows below pos were
+    // written by earlier steps: chunks wholly below pos are requested before
+    // waiting for the QKV projection, which writes row pos.
+    const int pos = length - 1;
+    griddep_launch_dependents();
     if (tid == 0) {
         s_abort = 0;
         for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int c = 0; c < NS && c < nch; ++c) issue(c);
+        for (int c = 0; c < NS && c < nch; ++c)
+            if (t0 + (c + 1) * A64_T <= pos) issue(c);
     }
+    griddep_wait();
+    if (tid == 0)
+        for (int c = 0; c < NS && c < nch; ++c)
+            if (t0 + (c + 1) * A64_T > pos) issue(c);
     // q of every head for this warp's 8 dims, scaled by log2(e)/8.
     float qr[A64_HP][8];
     {
@@ -794,6 +899,8 @@ constexpr int CB_NT = 512;  // combine threads: one warp per head (up to 16 head
 __global__ void __launch_bounds__(CB_NT) combine_stage_kernel(const CombineArgs a) {
     extern __shared__ float cb_sm[];  // [NH*D] outputs, then [NH][max_splits] weights
     __shared__ float red[64];
+    griddep_launch_dependents();
+    griddep_wait();
     const int s = blockIdx.x;
     const int n = a.NH * a.D, D = a.D, W = D + 2;
     float* outv = cb_sm;
@@ -875,6 +982,8 @@ struct ArgmaxArgs {
 __global__ void __launch_bounds__(ARG_NT) argmax_kernel(const ArgmaxArgs a) {
     __shared__ float sv[ARG_NT / 32];
     __shared__ int si[ARG_NT / 32];
+    griddep_launch_dependents();
+    griddep_wait();
     const int s = blockIdx.x;
     float v = -INFINITY;
     int vi = 0x7fffffff;
