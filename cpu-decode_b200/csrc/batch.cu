@@ -16,6 +16,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <utility>
 #include <string>
@@ -103,6 +104,10 @@ struct dcb_batch {
     void *kc = nullptr, *vc = nullptr;
     float* stage_f = nullptr;  // FP32 rows waiting for conversion to F16 (kv_write from device memory)
     float2* rope = nullptr;    // [slots][D/2] (cos, sin) of each sequence's position, per step
+    int* seq_done = nullptr;   // [slots] attention blocks finished per sequence (fused split merge)
+    int* gbar = nullptr;       // [3][2] grid barriers of the O, gate/up and down projections
+    bool fuse_combine = false; // split merge inside the attention kernel
+    bool fuse_stage = false;   // staging of the next input inside the O, gate/up and down projections
     size_t stage_f_elems = 0;
     int* h_io = nullptr;  // pinned: [slots] tokens in, then [slots] argmax + error word out
     std::vector<CUtensorMap> map_qkv, map_o, map_gu, map_down;
@@ -174,20 +179,69 @@ int launch(void (*kernel)(KArgs...), dim3 grid, int threads, size_t smem, cudaSt
 
 // Row tiles of 128 x all sequences; with fewer tiles than SMs the reduction
 // is split over a cluster of up to 8 CTAs per tile (one stage at least each).
+int gemm_split(const dcb_batch* b, int epi, int rows, int K) {
+    const int tiles = cdiv(rows, GM), nk = cdiv(K, GK);
+    return epi == EPI_HEAD ? 1 : std::max(1, std::min({8, nk, b->sms / tiles}));
+}
+
+template <int EPI>
+constexpr int stages_of() {
+    return EPI == EPI_HEAD ? HEAD_STAGES : GSTAGES;
+}
+
 template <int EPI, typename KV>
 int launch_gemm(dcb_batch* b, const CUtensorMap& ma, const CUtensorMap& mb, int rows, int K, const GemmArgs& a0) {
     GemmArgs a = a0;
     a.M = rows;
     a.nk = cdiv(K, GK);
     const int tiles = cdiv(rows, GM);
-    a.ksplit = EPI == EPI_HEAD ? 1 : std::max(1, std::min({8, a.nk, b->sms / tiles}));
-    const int smem = gemm_smem_bytes(b->slots);
-    return launch(gemm_i8_kernel<EPI, KV>, dim3(tiles * a.ksplit), GT, smem, b->stream, a.ksplit, ma, mb, a);
+    a.ksplit = gemm_split(b, EPI, rows, K);
+    constexpr int ST = stages_of<EPI>();
+    const int smem = gemm_smem_bytes(b->slots, ST);
+    if (a.st_planes)
+        return launch(gemm_i8_kernel<EPI, KV, ST, true>, dim3(tiles * a.ksplit), GT, smem, b->stream, a.ksplit, ma, mb,
+                      a);
+    return launch(gemm_i8_kernel<EPI, KV, ST>, dim3(tiles * a.ksplit), GT, smem, b->stream, a.ksplit, ma, mb, a);
+}
+
+// Can every CTA of this projection's grid be resident at once (needed by its
+// grid barrier)?
+template <int EPI, typename KV>
+bool co_resident(const dcb_batch* b, int rows, int K) {
+    const int S = gemm_split(b, EPI, rows, K), grid = cdiv(rows, GM) * S;
+    constexpr int ST = stages_of<EPI>();
+    const int smem = gemm_smem_bytes(b->slots, ST);
+    if (S == 1) {
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_i8_kernel<EPI, KV, ST, true>, GT, smem) !=
+            cudaSuccess)
+            return false;
+        return per_sm * b->sms >= grid;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GT);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = (unsigned)S;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_i8_kernel<EPI, KV, ST, true>, &cfg) != cudaSuccess) return false;
+    return clusters * S >= grid;
 }
 
 template <int EPI, typename KV>
-int allow_smem(int bytes) {
-    BT_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<EPI, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+int allow_smem(int slots) {
+    constexpr int ST = stages_of<EPI>();
+    BT_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<EPI, KV, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemm_smem_bytes(slots, ST)));
+    if (EPI == EPI_RESID || EPI == EPI_GU)
+        BT_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<EPI, KV, ST, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     gemm_smem_bytes(slots, ST)));
     return 0;
 }
 
@@ -304,9 +358,14 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             a6.split_len = b->split_len;
             a6.max_splits = b->max_splits;
             a6.err = b->err;
-            if (int rc = launch(attention64_kernel<KV>, dim3(b->max_splits, P.NKV, n), A64_NT, a64_smem_bytes<KV>(),
-                                b->stream, 1, b->map_k, b->map_v, a6))
-                return rc;
+            a6.seq_done = b->seq_done;
+            a6.cb = ca;
+            const dim3 grid(b->max_splits, P.NKV, n);
+            const int rc = b->fuse_combine ? launch(attention64_kernel<KV, true>, grid, A64_NT, a64_smem_bytes<KV>(),
+                                                    b->stream, 1, b->map_k, b->map_v, a6)
+                                           : launch(attention64_kernel<KV, false>, grid, A64_NT, a64_smem_bytes<KV>(),
+                                                    b->stream, 1, b->map_k, b->map_v, a6);
+            if (rc) return rc;
         } else if (D == 64) {
             if (int rc = launch(attention_kernel<KV, 64>, dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream, 1, aa))
                 return rc;
@@ -314,7 +373,8 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             if (int rc = launch(attention_kernel<KV, 0>, dim3(b->max_splits, P.NKV, n), AT_NT, at_smem, b->stream, 1, aa))
                 return rc;
         }
-        if (int rc = launch(combine_stage_kernel, dim3(n), CB_NT, cb_smem, b->stream, 1, ca)) return rc;
+        if (!(b->attn64 && b->fuse_combine))
+            if (int rc = launch(combine_stage_kernel, dim3(n), CB_NT, cb_smem, b->stream, 1, ca)) return rc;
         // O + residual.
         {
             GemmArgs a = g;
@@ -322,9 +382,21 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             a.wstride = P.SH / 4;
             a.out = b->x;
             a.ldo = P.Kh;
+            if (b->fuse_stage) {  // then the post-attention RMSNorm input of gate/up
+                a.gbar = b->gbar;
+                a.st_src = b->x;
+                a.st_lds = P.Kh;
+                a.st_n = H;
+                a.st_kp = P.Kh;
+                a.st_gain = post_norm;
+                a.st_planes = b->ph;
+                a.st_xsc = b->xsc;
+                a.st_xinv = b->xinv;
+                a.st_eps = P.eps;
+            }
             if (int rc = launch_gemm<EPI_RESID, KV>(b, b->map_o[l], b->map_ph, H, P.Kh, a)) return rc;
         }
-        {
+        if (!b->fuse_stage) {
             StageArgs s = sa;
             s.n = H;
             s.kp = P.Kh;
@@ -344,9 +416,18 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             a.xinv = b->xinv;
             a.out = b->h;
             a.ldo = P.Ki;
+            if (b->fuse_stage) {  // then the down projection's input
+                a.gbar = b->gbar + 2;
+                a.st_src = b->h;
+                a.st_lds = P.Ki;
+                a.st_n = I;
+                a.st_kp = P.Ki;
+                a.st_planes = b->pi;
+                a.st_xsc = b->xsc;
+            }
             if (int rc = launch_gemm<EPI_GU, KV>(b, b->map_gu[l], b->map_ph, 2 * I, P.Kh, a)) return rc;
         }
-        {
+        if (!b->fuse_stage) {
             StageArgs s = sa;
             s.n = I;
             s.kp = P.Ki;
@@ -363,10 +444,22 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             a.wstride = P.SI / 4;
             a.out = b->x;
             a.ldo = P.Kh;
+            if (b->fuse_stage) {  // then the next layer's input norm, or the final norm before the head
+                a.gbar = b->gbar + 4;
+                a.st_src = b->x;
+                a.st_lds = P.Kh;
+                a.st_n = H;
+                a.st_kp = P.Kh;
+                a.st_gain = l + 1 < P.L ? P.norms + (size_t)(l + 1) * 2 * P.Kh : P.norms + (size_t)P.L * 2 * P.Kh;
+                a.st_planes = b->ph;
+                a.st_xsc = b->xsc;
+                a.st_xinv = b->xinv;
+                a.st_eps = P.eps;
+            }
             if (int rc = launch_gemm<EPI_RESID, KV>(b, b->map_down[l], b->map_pi, H, P.Ki, a)) return rc;
         }
         // Next layer's input norm, or the final norm before the head.
-        {
+        if (!b->fuse_stage) {
             StageArgs s = sa;
             s.n = H;
             s.kp = P.Kh;
@@ -433,6 +526,9 @@ int check_seq(const dcb_batch* b, int s) {
 int device_status(dcb_batch* b, int err) {
     if (!err) return 0;
     BT_CUDA(cudaMemsetAsync(b->err, 0, sizeof(int), b->stream));
+    // An abandoned step may leave counters part-way: start them from zero.
+    BT_CUDA(cudaMemsetAsync(b->seq_done, 0, (size_t)b->slots * sizeof(int), b->stream));
+    BT_CUDA(cudaMemsetAsync(b->gbar, 0, 6 * sizeof(int), b->stream));
     BT_CUDA(cudaStreamSynchronize(b->stream));
     if (err == ERR_TOKEN) return bfail(DCB_ERR_TOKEN, "token ID outside vocabulary");
     return bfail(DCB_ERR_DEVICE_WAIT, "a device-side wait ran out of time; the step was abandoned");
@@ -474,6 +570,8 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
     if (int rc = b->alloc(&b->h, (size_t)S * P.Ki)) return bail(rc);
     if (int rc = b->alloc(&b->q, (size_t)S * P.NH * P.D)) return bail(rc);
     if (int rc = b->alloc(&b->rope, (size_t)S * (P.D / 2))) return bail(rc);
+    if (int rc = b->alloc(&b->seq_done, S)) return bail(rc);
+    if (int rc = b->alloc(&b->gbar, 6)) return bail(rc);
     if (int rc = b->alloc(&b->xsc, S)) return bail(rc);
     if (int rc = b->alloc(&b->xinv, S)) return bail(rc);
     if (int rc = b->alloc(&b->part, (size_t)S * P.NH * b->max_splits * (P.D + 2))) return bail(rc);
@@ -518,22 +616,45 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
         if (rows > 0x7fffffffull) return bail(bfail(DCB_ERR_UNSUPPORTED, "KV cache too large for one tensor map"));
         if (int rc = make_map(&b->map_k, b->kc, t, 64, rows, 64 * b->kv_elem(), inner, A64_T)) return bail(rc);
         if (int rc = make_map(&b->map_v, b->vc, t, 64, rows, 64 * b->kv_elem(), inner, A64_T)) return bail(rc);
-        if (f16)
-            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (f16) {
+            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<__half, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          a64_smem_bytes<__half>()));
-        else
-            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<__half, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         a64_smem_bytes<__half>()));
+        } else {
+            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<float, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          a64_smem_bytes<float>()));
+            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<float, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         a64_smem_bytes<float>()));
+        }
     }
-    const int smem = gemm_smem_bytes(S);
-    if (int rc = allow_smem<EPI_QKV, float>(smem)) return bail(rc);
-    if (int rc = allow_smem<EPI_QKV, __half>(smem)) return bail(rc);
-    if (int rc = allow_smem<EPI_RESID, float>(smem)) return bail(rc);
-    if (int rc = allow_smem<EPI_RESID, __half>(smem)) return bail(rc);
-    if (int rc = allow_smem<EPI_GU, float>(smem)) return bail(rc);
-    if (int rc = allow_smem<EPI_GU, __half>(smem)) return bail(rc);
-    if (int rc = allow_smem<EPI_HEAD, float>(smem)) return bail(rc);
-    if (int rc = allow_smem<EPI_HEAD, __half>(smem)) return bail(rc);
+    if (int rc = allow_smem<EPI_QKV, float>(S)) return bail(rc);
+    if (int rc = allow_smem<EPI_QKV, __half>(S)) return bail(rc);
+    if (int rc = allow_smem<EPI_RESID, float>(S)) return bail(rc);
+    if (int rc = allow_smem<EPI_RESID, __half>(S)) return bail(rc);
+    if (int rc = allow_smem<EPI_GU, float>(S)) return bail(rc);
+    if (int rc = allow_smem<EPI_GU, __half>(S)) return bail(rc);
+    if (int rc = allow_smem<EPI_HEAD, float>(S)) return bail(rc);
+    if (int rc = allow_smem<EPI_HEAD, __half>(S)) return bail(rc);
+    // Optional fusions (DCB_BATCH_FUSE=1): the split merge by the last
+    // attention block of each sequence, and the staging of the next input by
+    // the O, gate/up and down projections after a grid barrier. Measured on a
+    // B200 with 64 sequences they are slower than the separate kernels (the
+    // merge and the staging of a sequence then run on one block at the end of
+    // the kernel instead of in parallel), so they are off by default. The
+    // merge needs its scratch to fit the attention kernel's score area; the
+    // staging needs every CTA of a projection resident at once.
+    const char* fv = std::getenv("DCB_BATCH_FUSE");
+    if (fv && std::atoi(fv)) {
+        b->fuse_combine = b->attn64 && (size_t)(P.NH * 64 + P.NH * b->max_splits) * 4 <=
+                                           (size_t)A64_NW * A64_HP * A64_T * 4;
+        if (kv_dtype == DCB_KV_F16)
+            b->fuse_stage = co_resident<EPI_RESID, __half>(b, P.H, P.Kh) &&
+                            co_resident<EPI_GU, __half>(b, 2 * P.I, P.Kh) && co_resident<EPI_RESID, __half>(b, P.H, P.Ki);
+        else
+            b->fuse_stage = co_resident<EPI_RESID, float>(b, P.H, P.Kh) &&
+                            co_resident<EPI_GU, float>(b, 2 * P.I, P.Kh) && co_resident<EPI_RESID, float>(b, P.H, P.Ki);
+    }
     {
         const int at = (int)attention_smem_bytes(P.D, (int)b->kv_elem(), P.NH / P.NKV);
         auto set = [&](const void* f) {
@@ -722,7 +843,8 @@ void* dcb_batch_stream(const dcb_batch* b) { return b ? b->stream : nullptr; }
 uint64_t dcb_batch_kernels_per_step(const dcb_batch* b, int n) {
     (void)n;
     if (!b) return 0;
-    return 1 + (uint64_t)b->M.P.L * 9 + 2;
+    const uint64_t per_layer = 5 + (b->attn64 && b->fuse_combine ? 0 : 1) + (b->fuse_stage ? 0 : 3);
+    return 1 + (uint64_t)b->M.P.L * per_layer + 2;
 }
 
 }  // extern "C"

@@ -33,7 +33,8 @@ namespace batch {
 
 constexpr int GM = 128;        // weight rows per GEMM tile (UMMA M)
 constexpr int GK = 128;        // reduction bytes per pipeline stage (one 128-byte swizzle row)
-constexpr int GSTAGES = 4;     // pipeline depth
+constexpr int GSTAGES = 4;     // pipeline depth of the layer projections (one CTA per SM)
+constexpr int HEAD_STAGES = 2; // LM head: two CTAs per SM, one's loads under the other's prologue and epilogue
 constexpr int GT = 128;        // GEMM threads (four warps: one per 32 TMEM lanes)
 constexpr int MAX_SLOTS = 64;  // sequences per batch: N = 3 * slots <= 192
 constexpr uint32_t TMEM_COLS = 256;
@@ -45,7 +46,9 @@ enum Epi { EPI_PLAIN = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GU = 3, EPI_HEAD = 4 }
 
 __host__ __device__ constexpr int b_bytes(int slots) { return 3 * slots * GK; }
 // Dynamic shared memory of the GEMM: 1 KB alignment slack, then the A and B rings.
-__host__ __device__ constexpr int gemm_smem_bytes(int slots) { return 1024 + GSTAGES * (A_BYTES + b_bytes(slots)); }
+__host__ __device__ constexpr int gemm_smem_bytes(int slots, int stages = GSTAGES) {
+    return 1024 + stages * (A_BYTES + b_bytes(slots));
+}
 
 struct GemmArgs {
     int M;      // weight rows
@@ -71,6 +74,17 @@ struct GemmArgs {
     void* vcache;
     ArgBest* amax;  // HEAD: [tiles][slots] best (value, row) of each tile and sequence
     int* err;       // set to ERR_WAIT when a wait runs out
+    // Staging of the next projection's input once every tile is written (the
+    // STAGE instantiation): a grid barrier (all CTAs co-resident), then CTA c
+    // stages sequences c, c + grid, ... (RMSNorm factor, planes, scale).
+    int* gbar;  // [2]: arrivals, generation
+    const float* st_src;  // [slots][st_lds]
+    int st_lds, st_n, st_kp;
+    const float* st_gain;  // RMSNorm gains, or null
+    int8_t* st_planes;     // [3][slots][st_kp]
+    float* st_xsc;
+    float* st_xinv;  // or null
+    float st_eps;
 };
 
 // ---- tcgen05 / TMA primitives ------------------------------------------------------
@@ -182,8 +196,105 @@ static __device__ bool wait_phase(uint64_t* m, uint32_t parity, int* err) {
     return true;
 }
 
+__device__ __forceinline__ void block_sum_max(float& ss, float& mx, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(FULL, ss, o);
+        mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    }
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+        red[w] = ss;
+        red[32 + w] = mx;
+    }
+    __syncthreads();
+    ss = 0.f;
+    mx = 0.f;
+    for (int i = 0; i < nw; ++i) {
+        ss += red[i];
+        mx = fmaxf(mx, red[32 + i]);
+    }
+}
+
+__device__ __forceinline__ int ld_acquire_int(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_int(int* p, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Every CTA of the grid (all co-resident) arrives; the last one resets the
+// count and publishes a new generation. Bounded: false when the wait ran out.
+static __device__ bool grid_barrier(int* bar, int nblocks, int* err, int* s_flag) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const int gen = ld_acquire_int(bar + 1);
+        __threadfence();  // this block's writes before its arrival
+        if (atomicAdd(bar, 1) == nblocks - 1) {
+            atomicExch(bar, 0);
+            __threadfence();
+            st_release_int(bar + 1, gen + 1);
+        } else {
+            uint64_t t0 = 0;
+            unsigned spins = 0;
+            while (ld_acquire_int(bar + 1) == gen) {
+                if ((++spins & 63u) == 0) {
+                    const uint64_t now = globaltimer();
+                    if (!t0) {
+                        t0 = now;
+                    } else if (now - t0 > WAIT_LIMIT_NS) {
+                        atomicExch(err, ERR_WAIT);
+                        ok = 0;
+                        break;
+                    }
+                }
+            }
+        }
+        *s_flag = ok;
+    }
+    __syncthreads();
+    return *s_flag != 0;
+}
+
+// The whole block stages sequence s: v = src[0..n) (read through L2), the
+// RMSNorm factor of v (src/kernels.cpp:132-137), v*gain as planes.
+static __device__ void stage_vec(const float* src, int n, int kp, const float* gain, float eps, int8_t* planes, int slots,
+                          int s, float* xsc, float* xinv, float* buf, float* red) {
+    float ss = 0.f, mx = 0.f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const float v = __ldcg(src + j);
+        ss = fmaf(v, v, ss);
+        const float g = gain ? v * gain[j] : v;
+        buf[j] = g;
+        mx = fmaxf(mx, fabsf(g));
+    }
+    block_sum_max(ss, mx, red);
+    const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
+    if (threadIdx.x == 0) {
+        xsc[s] = mx > 0.f ? __frcp_rn(rs) : 1.0f;
+        if (xinv) xinv[s] = __frsqrt_rn(ss / (float)n + eps);
+    }
+    int8_t* ph = planes + (size_t)s * kp;
+    int8_t* pm = ph + (size_t)slots * kp;
+    int8_t* pl = pm + (size_t)slots * kp;
+    for (int quad = threadIdx.x; quad < kp / 4; quad += blockDim.x) {
+        const int j = 4 * quad;
+        const float4 v4 = make_float4(j < n ? buf[j] : 0.f, j + 1 < n ? buf[j + 1] : 0.f, j + 2 < n ? buf[j + 2] : 0.f,
+                                      j + 3 < n ? buf[j + 3] : 0.f);
+        uint32_t h, m, l;
+        fix_pack4(v4, rs, h, m, l);
+        reinterpret_cast<uint32_t*>(ph)[quad] = h;
+        reinterpret_cast<uint32_t*>(pm)[quad] = m;
+        reinterpret_cast<uint32_t*>(pl)[quad] = l;
+    }
+    __syncthreads();  // buf and red are reused by the next sequence
+}
+
 // ---- the GEMM ----------------------------------------------------------------------
-template <int EPI, typename KV>
+template <int EPI, typename KV, int GSTAGES, bool STAGE = false>
 __global__ void __launch_bounds__(GT, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
     extern __shared__ uint8_t g_sm_raw[];
@@ -197,6 +308,8 @@ __global__ void __launch_bounds__(GT, 1)
     __shared__ float s_bv[4][MAX_SLOTS];
     __shared__ int s_bi[4][MAX_SLOTS];
     __shared__ int s_pos[MAX_SLOTS];
+    __shared__ int s_flag;
+    __shared__ float s_red[64];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // Split-K: the S CTAs of a cluster share row tile blockIdx.x / S; rank r
@@ -430,8 +543,15 @@ __global__ void __launch_bounds__(GT, 1)
             a.amax[(size_t)blockIdx.x * a.slots + tid] = {v, vi};
         }
     }
-    // No CTA leaves while a cluster peer may still read its partials.
+    // No CTA leaves (or reuses its shared memory) while a cluster peer may
+    // still read its partials.
     if (S > 1) cluster_sync();
+    if (STAGE && grid_barrier(a.gbar, gridDim.x, a.err, &s_flag)) {
+        float* buf = reinterpret_cast<float*>(g_sm);
+        for (int s = blockIdx.x; s < a.nseq; s += gridDim.x)
+            stage_vec(a.st_src + (size_t)s * a.st_lds, a.st_n, a.st_kp, a.st_gain, a.st_eps, a.st_planes, a.slots, s,
+                      a.st_xsc, a.st_xinv, buf, s_red);
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
@@ -464,27 +584,6 @@ struct StageArgs {
     int cached_rope, half;
     float2* rope;           // [slots][half]
 };
-
-__device__ __forceinline__ void block_sum_max(float& ss, float& mx, float* red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        ss += __shfl_xor_sync(FULL, ss, o);
-        mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-    }
-    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) {
-        red[w] = ss;
-        red[32 + w] = mx;
-    }
-    __syncthreads();
-    ss = 0.f;
-    mx = 0.f;
-    for (int i = 0; i < nw; ++i) {
-        ss += red[i];
-        mx = fmaxf(mx, red[32 + i]);
-    }
-}
 
 // One block per sequence: v (embedded token row or src), sum v^2 for the
 // RMSNorm factor (src/kernels.cpp:132-137), v*gain quantised into the planes.
@@ -593,6 +692,97 @@ __global__ void __launch_bounds__(AT_NT) attention_kernel(const AttnArgs a) {
     });
 }
 
+// Merge the splits of every head of sequence s (in split order) and stage the
+// attention output (NH*D values) as planes for the O projection. Run by one
+// whole block; partials are read through L2 (other blocks of the same kernel
+// may have written them). smem: (NH*D + NH*max_splits) floats; red: 64 floats.
+struct CombineArgs {
+    const float* part;
+    const int* pos;
+    int NH, D, split_len, max_splits, slots, kp;
+    int8_t* planes;  // [3][slots][kp]
+    float* xsc;
+};
+static __device__ __noinline__ void combine_seq(const CombineArgs& a, int s, float* cb_sm, float* red) {
+    const int n = a.NH * a.D, D = a.D, W = D + 2;
+    float* outv = cb_sm;
+    float* wts = cb_sm + n;
+    const int ns = (a.pos[s] + a.split_len) / a.split_len;  // splits covering positions 0..pos
+    const float* base = a.part + (size_t)s * a.NH * a.max_splits * W;
+    const int nt = blockDim.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = nt / 32;
+    float mx = 0.f, ss = 0.f;
+    // Warp per head: weight of split i = 2^(m_i - M) / sum_i 2^(m_i - M) l_i
+    // (lanes over splits), then lanes over dimensions j = lane + 32k with the
+    // loads of eight splits in flight, summed in split order.
+    for (int h = warp; h < a.NH; h += nw) {
+        const float* hb = base + (size_t)h * a.max_splits * W;
+        float* hw = wts + h * a.max_splits;
+        float M = -INFINITY;
+        for (int i = lane; i < ns; i += 32) M = fmaxf(M, __ldcg(hb + (size_t)i * W));
+        M = warp_max(M);
+        float Ls = 0.f;
+        for (int i = lane; i < ns; i += 32) {
+            const float mi = __ldcg(hb + (size_t)i * W);
+            const float f = mi > -INFINITY ? at_ex2(mi - M) : 0.f;
+            hw[i] = f;
+            Ls = fmaf(f, __ldcg(hb + (size_t)i * W + 1), Ls);
+        }
+        Ls = warp_sum(Ls);
+        __syncwarp();
+        const float invL = 1.0f / Ls;
+        float acc[AT_MAXD] = {0.f, 0.f, 0.f, 0.f};
+        for (int i0 = 0; i0 < ns; i0 += 8) {
+            float v[8][AT_MAXD];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int k = 0; k < AT_MAXD; ++k)
+                    v[u][k] = (i0 + u < ns && lane + 32 * k < D) ? __ldcg(hb + (size_t)(i0 + u) * W + 2 + lane + 32 * k)
+                                                                 : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float f = i0 + u < ns ? hw[i0 + u] : 0.f;
+#pragma unroll
+                for (int k = 0; k < AT_MAXD; ++k) acc[k] = fmaf(f, v[u][k], acc[k]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < AT_MAXD; ++k) {
+            const int j = lane + 32 * k;
+            if (j < D) {
+                const float o = acc[k] * invL;
+                outv[h * D + j] = o;
+                mx = fmaxf(mx, fabsf(o));
+            }
+        }
+    }
+    block_sum_max(ss, mx, red);
+    const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
+    if (threadIdx.x == 0) a.xsc[s] = mx > 0.f ? __frcp_rn(rs) : 1.0f;
+    int8_t* ph = a.planes + (size_t)s * a.kp;
+    int8_t* pm = ph + (size_t)a.slots * a.kp;
+    int8_t* pl = pm + (size_t)a.slots * a.kp;
+    for (int quad = threadIdx.x; quad < a.kp / 4; quad += nt) {
+        const int j = 4 * quad;
+        const float4 v4 = make_float4(j < n ? outv[j] : 0.f, j + 1 < n ? outv[j + 1] : 0.f,
+                                      j + 2 < n ? outv[j + 2] : 0.f, j + 3 < n ? outv[j + 3] : 0.f);
+        uint32_t h, m, l;
+        fix_pack4(v4, rs, h, m, l);
+        reinterpret_cast<uint32_t*>(ph)[quad] = h;
+        reinterpret_cast<uint32_t*>(pm)[quad] = m;
+        reinterpret_cast<uint32_t*>(pl)[quad] = l;
+    }
+}
+
+constexpr int CB_NT = 512;  // combine threads: one warp per head (up to 16 heads per pass)
+__global__ void __launch_bounds__(CB_NT) combine_stage_kernel(const CombineArgs a) {
+    extern __shared__ float cb_sm[];  // [NH*D] outputs, then [NH][max_splits] weights
+    __shared__ float red[64];
+    griddep_launch_dependents();
+    griddep_wait();
+    combine_seq(a, blockIdx.x, cb_sm, red);
+}
+
 // ---- attention for head_dim 64 -------------------------------------------------------
 // Block (split, kv head g, sequence s) over positions [split*split_len, ...)
 // up to pos[s], all gq <= 8 query heads of group g, in 64-position chunks that
@@ -629,6 +819,10 @@ struct Attn64Args {
     const int* pos;
     int NH, NKV, L, layer, capacity, split_len, max_splits;
     int* err;
+    // Split merge in the kernel (FUSE): the last block to finish for a
+    // sequence (seq_done[s] counts them; it resets it) merges its splits.
+    int* seq_done;  // [slots]
+    CombineArgs cb;
 };
 
 // Byte offset of element (row r, dim d) in a swizzled chunk tile.
@@ -664,7 +858,7 @@ __device__ __forceinline__ float2 a64_load2(const uint8_t* tile, int r, int d0, 
     return __half22float2(*reinterpret_cast<const __half2*>(tile + a64_off<__half>(r, d0)));
 }
 
-template <typename KV>
+template <typename KV, bool FUSE>
 __global__ void __launch_bounds__(A64_NT, 2)
     attention64_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const Attn64Args a) {
@@ -676,7 +870,8 @@ __global__ void __launch_bounds__(A64_NT, 2)
     float* s_alpha = P + A64_T * A64_HP;                   // [head] rescale of this chunk
     __shared__ __align__(8) uint64_t full[8];
     __shared__ float s_ml[2 * A64_HP];
-    __shared__ int s_abort;
+    __shared__ int s_abort, s_last;
+    __shared__ float s_red[64];
 
     const int sp_i = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -884,90 +1079,18 @@ __global__ void __launch_bounds__(A64_NT, 2)
         }
         pp[2 + j] = acc;
     }
-}
-
-// One block per sequence: merge the splits of every head (in split order) and
-// stage the attention output (NH*D values) as planes for the O projection.
-struct CombineArgs {
-    const float* part;
-    const int* pos;
-    int NH, D, split_len, max_splits, slots, kp;
-    int8_t* planes;  // [3][slots][kp]
-    float* xsc;
-};
-constexpr int CB_NT = 512;  // combine threads: one warp per head (up to 16 heads per pass)
-__global__ void __launch_bounds__(CB_NT) combine_stage_kernel(const CombineArgs a) {
-    extern __shared__ float cb_sm[];  // [NH*D] outputs, then [NH][max_splits] weights
-    __shared__ float red[64];
-    griddep_launch_dependents();
-    griddep_wait();
-    const int s = blockIdx.x;
-    const int n = a.NH * a.D, D = a.D, W = D + 2;
-    float* outv = cb_sm;
-    float* wts = cb_sm + n;
-    const int ns = (a.pos[s] + a.split_len) / a.split_len;  // splits covering positions 0..pos
-    const float* base = a.part + (size_t)s * a.NH * a.max_splits * W;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = CB_NT / 32;
-    float mx = 0.f, ss = 0.f;
-    // Warp per head: weight of split i = 2^(m_i - M) / sum_i 2^(m_i - M) l_i
-    // (lanes over splits), then lanes over dimensions j = lane + 32k with the
-    // loads of eight splits in flight, summed in split order.
-    for (int h = warp; h < a.NH; h += nw) {
-        const float* hb = base + (size_t)h * a.max_splits * W;
-        float* hw = wts + h * a.max_splits;
-        float M = -INFINITY;
-        for (int i = lane; i < ns; i += 32) M = fmaxf(M, hb[(size_t)i * W]);
-        M = warp_max(M);
-        float Ls = 0.f;
-        for (int i = lane; i < ns; i += 32) {
-            const float mi = hb[(size_t)i * W];
-            const float f = mi > -INFINITY ? at_ex2(mi - M) : 0.f;
-            hw[i] = f;
-            Ls = fmaf(f, hb[(size_t)i * W + 1], Ls);
-        }
-        Ls = warp_sum(Ls);
-        __syncwarp();
-        const float invL = 1.0f / Ls;
-        float acc[AT_MAXD] = {0.f, 0.f, 0.f, 0.f};
-        for (int i0 = 0; i0 < ns; i0 += 8) {
-            float v[8][AT_MAXD];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-#pragma unroll
-                for (int k = 0; k < AT_MAXD; ++k)
-                    v[u][k] = (i0 + u < ns && lane + 32 * k < D) ? hb[(size_t)(i0 + u) * W + 2 + lane + 32 * k] : 0.f;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const float f = i0 + u < ns ? hw[i0 + u] : 0.f;
-#pragma unroll
-                for (int k = 0; k < AT_MAXD; ++k) acc[k] = fmaf(f, v[u][k], acc[k]);
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < AT_MAXD; ++k) {
-            const int j = lane + 32 * k;
-            if (j < D) {
-                const float o = acc[k] * invL;
-                outv[h * D + j] = o;
-                mx = fmaxf(mx, fabsf(o));
-            }
-        }
+    if (!FUSE) return;
+    __syncthreads();  // this block's partials are written
+    if (tid == 0) {
+        __threadfence();
+        const int total = a.NKV * ((length + a.split_len - 1) / a.split_len);  // blocks of sequence s
+        s_last = atomicAdd(a.seq_done + s, 1) == total - 1;
     }
-    block_sum_max(ss, mx, red);
-    const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
-    if (threadIdx.x == 0) a.xsc[s] = mx > 0.f ? __frcp_rn(rs) : 1.0f;
-    int8_t* ph = a.planes + (size_t)s * a.kp;
-    int8_t* pm = ph + (size_t)a.slots * a.kp;
-    int8_t* pl = pm + (size_t)a.slots * a.kp;
-    for (int quad = threadIdx.x; quad < a.kp / 4; quad += CB_NT) {
-        const int j = 4 * quad;
-        const float4 v4 = make_float4(j < n ? outv[j] : 0.f, j + 1 < n ? outv[j + 1] : 0.f,
-                                      j + 2 < n ? outv[j + 2] : 0.f, j + 3 < n ? outv[j + 3] : 0.f);
-        uint32_t h, m, l;
-        fix_pack4(v4, rs, h, m, l);
-        reinterpret_cast<uint32_t*>(ph)[quad] = h;
-        reinterpret_cast<uint32_t*>(pm)[quad] = m;
-        reinterpret_cast<uint32_t*>(pl)[quad] = l;
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        combine_seq(a.cb, s, sp, s_red);
+        if (tid == 0) a.seq_done[s] = 0;
     }
 }
 

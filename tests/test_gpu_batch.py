@@ -76,6 +76,19 @@ def test_batch_head_dim_64(which, kv, g64_int8, g64b_int8):
     _run_and_compare(bat, orcs, toks, 3)
 
 
+def test_batch_fused_path(g64_int8, monkeypatch):
+    """The optional fusions: the split merge by the last attention block of a
+    sequence, the staging of the next input inside the projections (after a
+    grid barrier)."""
+    from conftest import G64
+    monkeypatch.setenv("DCB_BATCH_FUSE", "1")
+    contexts = [0, 64, 600]
+    eng, bat, orcs = _setup(g64_int8, G64, contexts, 2)
+    assert bat.kernels_per_step(3) == 1 + 5 * G64.layers + 2
+    toks = np.random.default_rng(22).integers(0, G64.vocab, len(contexts))
+    _run_and_compare(bat, orcs, toks, 2)
+
+
 def test_batch_all_64_slots(small_int8):
     contexts = list(np.random.default_rng(3).integers(0, 400, 64))
     eng, bat, orcs = _setup(small_int8, SMALL, contexts, 2)
