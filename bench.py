@@ -18,9 +18,13 @@ rewind to the context and time.
   byte model) over its average launch time, against the measured HBM peak.
 * cpu_baseline: the reference's own CPU engine (built from its sources into
   oracle/_ref) timed on this host's cores on a bounded sample.
+* batched: 64 independent sequences per GPU (contexts 512-8192, KV pre-filled
+  with seeded N(0,1) rows, 128 greedy steps), every projection one tensor-core
+  GEMM over all of them; its own tokens/s, e2e and step roofline.
 
-Several GPUs (torchrun) run independent replicas, one sequence each, with no
-collective on the data path (weak scaling); the job time is the max over ranks.
+Several GPUs (torchrun) run independent replicas, one sequence each (and 64
+each in the batched measurement), with no collective on the data path (weak
+scaling); the job time is the max over ranks.
 `--impl reference` times the reference CPU engine instead (rank 0 only).
 """
 from __future__ import annotations
