@@ -84,12 +84,12 @@ def measured_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def profiled_traffic(name: str):
-    """DRAM bytes per launch from the committed ncu summary, if present."""
+def profiled_traffic(name: str, key: str = "dram_bytes_per_launch"):
+    """DRAM bytes per launch (or per step) from the committed ncu summary, if present."""
     p = ROOT / "profiles" / name
     if not p.exists():
         return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    m = re.search(key + r":\s*([0-9.eE+]+)", p.read_text())
     return float(m.group(1)) if m else None
 
 
@@ -637,7 +637,8 @@ def batched_decode(dcb, eng, d, dist, rank: int, world: int, warmup: int, kv: st
         "gpu_launches": int(kernels * K),
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_step": int(avg_bytes), "kernel": "whole step (graph)"},
+                     "algorithmic_bytes_per_step": int(avg_bytes), "kernel": "whole step (graph)",
+                     "traffic": profiled_traffic("batched_decode_64seq.md", "dram_bytes_per_step")},
         "clocks": clock_info,
     }
 
