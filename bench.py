@@ -327,7 +327,8 @@ def main() -> None:
 
     extra = {}
     if not args.no_batch:
-        extra["batched"] = batched_decode(dcb, eng, d, dist, rank, world, W)
+        extra["batched"] = batched_decode(dcb, eng, d, dist, rank, world, W, eng_model_dir=model,
+                                          cpu_sample=not args.no_cpu_baseline)
     if dist and not args.no_long:
         split = kv_split_context(dcb, model, d, min(K, 32), W, local, dist, 32768)
         if rank == 0:
@@ -535,7 +536,8 @@ BATCH_CTX = (512, 8192)   # per-sequence context, uniform
 BATCH_STEPS = 128         # greedy steps each
 
 
-def batched_decode(dcb, eng, d, dist, rank: int, world: int, warmup: int, kv: str = "f32") -> dict:
+def batched_decode(dcb, eng, d, dist, rank: int, world: int, warmup: int, kv: str = "f32",
+                   eng_model_dir: Path | None = None, cpu_sample: bool = False) -> dict:
     """Batched multi-stream decode: 64 independent sequences per GPU, contexts
     uniform in [512, 8192] (seeded per rank), KV caches pre-filled with seeded
     N(0,1) rows, 128 greedy steps, every projection one tcgen05 int8 GEMM over
@@ -625,6 +627,7 @@ def batched_decode(dcb, eng, d, dist, rank: int, world: int, warmup: int, kv: st
         e2e_s = float(t.item())
     kernels = bat.kernels_per_step(BATCH_SEQS)
     bat.close()
+    cpu = batched_cpu_baseline(eng_model_dir, d, ctxs[:2]) if (rank == 0 and cpu_sample) else None
     return {
         "workload": "64 independent sequences per GPU, contexts uniform [512, 8192] (seeded), KV pre-filled with "
                     "seeded N(0,1) rows, 128 greedy steps, FP32 KV, qwen2.5-0.5b-shape int8",
@@ -640,7 +643,38 @@ def batched_decode(dcb, eng, d, dist, rank: int, world: int, warmup: int, kv: st
                      "algorithmic_bytes_per_step": int(avg_bytes), "kernel": "whole step (graph)",
                      "traffic": profiled_traffic("batched_decode_64seq.md", "dram_bytes_per_step")},
         "clocks": clock_info,
+        "cpu_baseline": cpu,
     }
+
+
+def batched_cpu_baseline(model_dir: Path, d, contexts, steps: int = 2) -> dict:
+    """The reference has no batch: it decodes each sequence with its own
+    engine, and cannot take a pre-filled KV cache. The C restatement of its
+    step over a caller-owned cache stands in (kind "port"): two of the
+    batch's sequences at their own contexts (seeded N(0,1) KV rows), a few
+    greedy steps each, all host threads; tokens/s of that sample."""
+    sys.path.insert(0, str(ROOT))
+    import oracle
+    threads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(7)
+    total, elapsed = 0, 0.0
+    for ctx in contexts:
+        ctx = int(ctx)
+        orc = oracle.Oracle(model_dir, ctx + steps + 1, threads=threads)
+        kc, vc = orc.kv_view()
+        for l in range(d.layers):
+            kc[l, :ctx] = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+            vc[l, :ctx] = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+        orc.pos = ctx
+        tok = 1234
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            tok = oracle.argmax(orc.step(tok))
+        elapsed += time.perf_counter() - t0
+        total += steps
+    return {"value": round(total / elapsed, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"C restatement of the reference step, one sequence at a time: contexts "
+                      f"{[int(c) for c in contexts]}, {steps} greedy steps each"}
 
 
 def _long_model_dir(model: Path) -> Path:
