@@ -112,7 +112,7 @@ struct dcb_batch {
     int* h_io = nullptr;  // pinned: [slots] tokens in, then [slots] argmax + error word out
     std::vector<CUtensorMap> map_qkv, map_o, map_gu, map_down;
     CUtensorMap map_head{}, map_ph{}, map_pi{}, map_k{}, map_v{};
-    bool attn64 = false;  // head_dim 64, at most 8 query heads per KV head: attention64_kernel
+    bool attn64 = false;  // head_dim 64, at most 8 query heads per KV head: attention64_tc_kernel
     std::vector<size_t> pos_host;
     cudaGraphExec_t exec = nullptr;
     int graph_n = -1;
@@ -361,9 +361,9 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             a6.seq_done = b->seq_done;
             a6.cb = ca;
             const dim3 grid(b->max_splits, P.NKV, n);
-            const int rc = b->fuse_combine ? launch(attention64_kernel<KV, true>, grid, A64_NT, a64_smem_bytes<KV>(),
+            const int rc = b->fuse_combine ? launch(attention64_tc_kernel<KV, true>, grid, A64_NT, tc_smem_bytes(),
                                                     b->stream, 1, b->map_k, b->map_v, a6)
-                                           : launch(attention64_kernel<KV, false>, grid, A64_NT, a64_smem_bytes<KV>(),
+                                           : launch(attention64_tc_kernel<KV, false>, grid, A64_NT, tc_smem_bytes(),
                                                     b->stream, 1, b->map_k, b->map_v, a6);
             if (rc) return rc;
         } else if (D == 64) {
@@ -616,17 +616,11 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
         if (rows > 0x7fffffffull) return bail(bfail(DCB_ERR_UNSUPPORTED, "KV cache too large for one tensor map"));
         if (int rc = make_map(&b->map_k, b->kc, t, 64, rows, 64 * b->kv_elem(), inner, A64_T)) return bail(rc);
         if (int rc = make_map(&b->map_v, b->vc, t, 64, rows, 64 * b->kv_elem(), inner, A64_T)) return bail(rc);
-        if (f16) {
-            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<__half, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         a64_smem_bytes<__half>()));
-            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<__half, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         a64_smem_bytes<__half>()));
-        } else {
-            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<float, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         a64_smem_bytes<float>()));
-            BT_CUDA(cudaFuncSetAttribute(attention64_kernel<float, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         a64_smem_bytes<float>()));
-        }
+        for (const void* f : {(const void*)attention64_tc_kernel<float, false>,
+                              (const void*)attention64_tc_kernel<float, true>,
+                              (const void*)attention64_tc_kernel<__half, false>,
+                              (const void*)attention64_tc_kernel<__half, true>})
+            BT_CUDA(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem_bytes()));
     }
     if (int rc = allow_smem<EPI_QKV, float>(S)) return bail(rc);
     if (int rc = allow_smem<EPI_QKV, __half>(S)) return bail(rc);
@@ -646,8 +640,7 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
     // staging needs every CTA of a projection resident at once.
     const char* fv = std::getenv("DCB_BATCH_FUSE");
     if (fv && std::atoi(fv)) {
-        b->fuse_combine = b->attn64 && (size_t)(P.NH * 64 + P.NH * b->max_splits) * 4 <=
-                                           (size_t)A64_NW * A64_HP * A64_T * 4;
+        b->fuse_combine = b->attn64 && (size_t)(P.NH * 64 + P.NH * b->max_splits) * 4 <= (size_t)TC_RING_F32;
         if (kv_dtype == DCB_KV_F16)
             b->fuse_stage = co_resident<EPI_RESID, __half>(b, P.H, P.Kh) &&
                             co_resident<EPI_GU, __half>(b, 2 * P.I, P.Kh) && co_resident<EPI_RESID, __half>(b, P.H, P.Ki);

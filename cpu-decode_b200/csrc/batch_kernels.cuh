@@ -783,35 +783,19 @@ __global__ void __launch_bounds__(CB_NT) combine_stage_kernel(const CombineArgs 
     combine_seq(a, blockIdx.x, cb_sm, red);
 }
 
-// ---- attention for head_dim 64 -------------------------------------------------------
-// Block (split, kv head g, sequence s) over positions [split*split_len, ...)
+// ---- attention for head_dim 64: shared geometry ----------------------------------------
+// Block (split, KV head g, sequence s) over positions [split*split_len, ...)
 // up to pos[s], all gq <= 8 query heads of group g, in 64-position chunks that
 // TMA brings into a ring of shared-memory slots (K and V tiles with the
 // 128-byte swizzle: 16-byte chunk c of row r sits at c ^ (r % 8) within its
-// 128-byte row segment, so lane-private rows read without bank conflicts).
-// Per chunk:
-//   QK : warp w owns dims 8w..8w+7 (q of every head in registers), lane owns
-//        positions lane and lane+32; partial scores go to shared memory
-//   SM : warp h < gq sums head h's partials over the 8 warps, online softmax
-//        (base 2) over the chunk: new max, rescale, probabilities P[t][h]
-//   PV : warp w owns positions 8w..8w+7, lane owns dims 2*lane, 2*lane+1
-// then the warps' outputs are summed into the split's (max, sum, output).
+// 128-byte row segment, so rows read without bank conflicts).
 constexpr int A64_NT = 256;
 constexpr int A64_NW = A64_NT / 32;
 constexpr int A64_T = 64;    // positions per chunk
 constexpr int A64_HP = 8;    // query heads per group, padded
-constexpr int A64_RING = 65536;  // bytes of K/V chunk slots
 
 template <typename KV>
 __host__ __device__ constexpr int a64_tile_bytes() { return A64_T * 64 * (int)sizeof(KV); }  // one K or V chunk
-template <typename KV>
-__host__ __device__ constexpr int a64_slots() { return A64_RING / (2 * a64_tile_bytes<KV>()); }
-// Dynamic shared memory: 1 KB alignment slack, the ring, partial scores
-// [8 warps][8 heads][64], probabilities [64][8], rescale factors.
-template <typename KV>
-__host__ __device__ constexpr int a64_smem_bytes() {
-    return 1024 + A64_RING + A64_NW * A64_HP * A64_T * 4 + A64_T * A64_HP * 4 + 64;
-}
 
 struct Attn64Args {
     const float* q;  // [slots][NH*64] rotated queries
@@ -836,38 +820,72 @@ __device__ __forceinline__ int a64_off(int r, int d) {
         return r * 128 + ((c ^ (r & 7)) << 4) + ((d & 7) << 1);
     }
 }
-__device__ __forceinline__ void a64_load8(const uint8_t* tile, int r, int d0, float (&o)[8], float) {
-    const float4 a = *reinterpret_cast<const float4*>(tile + a64_off<float>(r, d0));
-    const float4 b = *reinterpret_cast<const float4*>(tile + a64_off<float>(r, d0 + 4));
-    o[0] = a.x, o[1] = a.y, o[2] = a.z, o[3] = a.w, o[4] = b.x, o[5] = b.y, o[6] = b.z, o[7] = b.w;
+// ---- attention for head_dim 64 on the tensor cores ----------------------------------
+// Block = split x KV head x sequence, 64-position chunks by TMA into a
+// swizzled ring; QK and PV are mma.sync m16n8k16 products (FP16 operands,
+// FP32 accumulators). An FP32
+// operand x is split as hi = f16(x), lo = f16(x - hi); the products
+// hi*hi + hi*lo + lo*hi keep about 22 bits (F16 K/V need no split: two
+// products). Per chunk:
+//   QK: warp w: positions 16(w%4).., dims 32(w/4)..+31 (two k-steps), all heads
+//       as the MMA's 8 columns; the two dim halves' partial scores in S
+//   SM: warp h < gq: online softmax of head h over the chunk (base 2) -> P
+//   PV: warp w: dims 16(w%4).., positions 32(w/4)..+31; O^T[dim][head]
+//       accumulates across chunks in the MMA fragments (rescaled per head)
+constexpr int TC_RING_F32 = 3 * 32768;  // three FP32 chunk slots (six F16)
+constexpr int TC_SS = 9;                 // S row stride (floats): [half][64 positions][9]
+constexpr int TC_PS = 12;                // P row stride (floats): [64 positions][12], conflict-free B loads
+__host__ __device__ constexpr int tc_smem_bytes() {
+    return 1024 + TC_RING_F32 + 2 * A64_T * TC_SS * 4 + A64_T * TC_PS * 4 + 64 + 2 * 64 * A64_HP * 4;
 }
-__device__ __forceinline__ void a64_load8(const uint8_t* tile, int r, int d0, float (&o)[8], __half) {
-    const uint4 v = *reinterpret_cast<const uint4*>(tile + a64_off<__half>(r, d0));
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        o[2 * i] = f.x;
-        o[2 * i + 1] = f.y;
-    }
+template <typename KV>
+__host__ __device__ constexpr int tc_slots() { return TC_RING_F32 / (2 * a64_tile_bytes<KV>()); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
-__device__ __forceinline__ float2 a64_load2(const uint8_t* tile, int r, int d0, float) {
-    return *reinterpret_cast<const float2*>(tile + a64_off<float>(r, d0));
+// (x0, x1) -> packed f16 hi and lo parts (low half = x0).
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
 }
-__device__ __forceinline__ float2 a64_load2(const uint8_t* tile, int r, int d0, __half) {
-    return __half22float2(*reinterpret_cast<const __half2*>(tile + a64_off<__half>(r, d0)));
+__device__ __forceinline__ uint32_t pack2(float x0, float x1) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// K/V element pair (row r, dims d, d+1), d even, of a swizzled chunk tile.
+__device__ __forceinline__ float2 tile_pair(const uint8_t* tile, int r, int d, float) {
+    return *reinterpret_cast<const float2*>(tile + a64_off<float>(r, d));
+}
+__device__ __forceinline__ uint32_t tile_pair_h(const uint8_t* tile, int r, int d) {
+    return *reinterpret_cast<const uint32_t*>(tile + a64_off<__half>(r, d));
+}
+__device__ __forceinline__ float tile_one(const uint8_t* tile, int r, int d, float) {
+    return *reinterpret_cast<const float*>(tile + a64_off<float>(r, d));
+}
+__device__ __forceinline__ float tile_one(const uint8_t* tile, int r, int d, __half) {
+    return __half2float(*reinterpret_cast<const __half*>(tile + a64_off<__half>(r, d)));
 }
 
 template <typename KV, bool FUSE>
 __global__ void __launch_bounds__(A64_NT, 2)
-    attention64_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                       const Attn64Args a) {
-    extern __shared__ uint8_t a64_raw[];
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a64_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int TB = a64_tile_bytes<KV>(), NS = a64_slots<KV>();
-    float* sp = reinterpret_cast<float*>(sm + A64_RING);  // [warp][head][t] partial scores
-    float* P = sp + A64_NW * A64_HP * A64_T;               // [t][head] probabilities
-    float* s_alpha = P + A64_T * A64_HP;                   // [head] rescale of this chunk
+    attention64_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                          const Attn64Args a) {
+    extern __shared__ uint8_t tc_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
+    constexpr bool F16 = sizeof(KV) == 2;
+    constexpr int TB = a64_tile_bytes<KV>(), NS = tc_slots<KV>();
+    float* S = reinterpret_cast<float*>(sm + TC_RING_F32);  // [2 halves][64][TC_SS]
+    float* P = S + 2 * A64_T * TC_SS;                        // [64][TC_PS]
+    float* s_alpha = P + A64_T * TC_PS;                      // [8]
+    float* ow = s_alpha + 16;                                // [2 halves][64 dims][8 heads] at the end
     __shared__ __align__(8) uint64_t full[8];
     __shared__ float s_ml[2 * A64_HP];
     __shared__ int s_abort, s_last;
@@ -875,21 +893,22 @@ __global__ void __launch_bounds__(A64_NT, 2)
 
     const int sp_i = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq8 = lane >> 2, t4 = lane & 3;  // MMA fragment row group, column pair
     const int length = a.pos[s] + 1;
     const int t0 = sp_i * a.split_len;
     if (t0 >= length) return;
     const int t1 = min(length, t0 + a.split_len);
     const int nch = (t1 - t0 + A64_T - 1) / A64_T;
     const int gq = a.NH / a.NKV;
-    const int row0 = (((s * a.L + a.layer) * a.NKV + g) * a.capacity) + t0;  // map row of position t0
+    const int row0 = (((s * a.L + a.layer) * a.NKV + g) * a.capacity) + t0;
 
-    auto issue = [&](int c) {  // thread 0: chunk c into slot c % NS
+    auto issue = [&](int c) {
         const int slot = c % NS;
         uint8_t* kt = sm + slot * 2 * TB;
         uint8_t* vt = kt + TB;
         mbar_expect(&full[slot], 2 * TB);
         const int y = row0 + c * A64_T;
-        if (sizeof(KV) == 4) {
+        if (!F16) {
             tma2d(kt, &tmK, 0, y, &full[slot]);
             tma2d(kt + TB / 2, &tmK, 32, y, &full[slot]);
             tma2d(vt, &tmV, 0, y, &full[slot]);
@@ -899,9 +918,6 @@ __global__ void __launch_bounds__(A64_NT, 2)
             tma2d(vt, &tmV, 0, y, &full[slot]);
         }
     };
-    // pos[] changes only at the end of a step, and the rows below pos were
-    // written by earlier steps: chunks wholly below pos are requested before
-    // waiting for the QKV projection, which writes row pos.
     const int pos = length - 1;
     griddep_launch_dependents();
     if (tid == 0) {
@@ -915,28 +931,26 @@ __global__ void __launch_bounds__(A64_NT, 2)
     if (tid == 0)
         for (int c = 0; c < NS && c < nch; ++c)
             if (t0 + (c + 1) * A64_T > pos) issue(c);
-    // q of every head for this warp's 8 dims, scaled by log2(e)/8.
-    float qr[A64_HP][8];
+
+    // QK roles: positions 16*mt.., dims 32*kh..; B fragments of q (scaled by
+    // log2(e)/8), head = fragment column gq8, for this warp's two k-steps.
+    const int mt = warp & 3, kh = warp >> 2;
+    uint32_t qb_hi[2][2], qb_lo[2][2];
     {
         const float qscale = 1.4426950408889634f / 8.0f;
-        const float* qs = a.q + ((size_t)s * a.NH + (size_t)g * gq) * 64 + 8 * warp;
+        const bool hv = gq8 < gq;
+        const float* qh = a.q + ((size_t)s * a.NH + (size_t)g * gq + (hv ? gq8 : 0)) * 64;
 #pragma unroll
-        for (int h = 0; h < A64_HP; ++h) {
-            if (h < gq) {
-                const float4 x = *reinterpret_cast<const float4*>(qs + (size_t)h * 64);
-                const float4 y = *reinterpret_cast<const float4*>(qs + (size_t)h * 64 + 4);
-                qr[h][0] = x.x * qscale, qr[h][1] = x.y * qscale, qr[h][2] = x.z * qscale, qr[h][3] = x.w * qscale;
-                qr[h][4] = y.x * qscale, qr[h][5] = y.y * qscale, qr[h][6] = y.z * qscale, qr[h][7] = y.w * qscale;
-            } else {
+        for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-                for (int e = 0; e < 8; ++e) qr[h][e] = 0.f;
+            for (int r = 0; r < 2; ++r) {
+                const int d = 32 * kh + 16 * ks + 2 * t4 + 8 * r;
+                const float x0 = hv ? qh[d] * qscale : 0.f, x1 = hv ? qh[d + 1] * qscale : 0.f;
+                split2(x0, x1, qb_hi[ks][r], qb_lo[ks][r]);
             }
-        }
     }
     float m_run = -INFINITY, l_run = 0.f;  // head `warp`'s softmax state (warps < gq)
-    float o[A64_HP][2];
-#pragma unroll
-    for (int h = 0; h < A64_HP; ++h) o[h][0] = o[h][1] = 0.f;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};     // O^T fragment: dims 16mt + gq8 (+8) x heads 2t4, 2t4+1
     __syncthreads();
 
     bool ok = true;
@@ -961,89 +975,115 @@ __global__ void __launch_bounds__(A64_NT, 2)
             }
         }
         __syncthreads();
-        if (s_abort) {  // the wait ran out
+        if (s_abort) {
             ok = false;
             break;
         }
         const int cbase = t0 + c * A64_T;
-        // QK partials: positions lane, lane + 32; dims 8*warp..8*warp+7.
+        // ---- QK: S[kh][position][head] partial over this warp's 32 dims
+        {
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            const int p0 = 16 * mt + gq8, p1 = p0 + 8;
 #pragma unroll
-        for (int pp = 0; pp < 2; ++pp) {
-            const int t = lane + 32 * pp;
-            float k8[8];
-            a64_load8(kt, t, 8 * warp, k8, KV());
-#pragma unroll
-            for (int h = 0; h < A64_HP; ++h) {
-                if (h < gq) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc = fmaf(qr[h][e], k8[e], acc);
-                    sp[(warp * A64_HP + h) * A64_T + t] = acc;
+            for (int ks = 0; ks < 2; ++ks) {
+                const int d = 32 * kh + 16 * ks + 2 * t4;
+                uint32_t ah[4], al[4];
+                if (!F16) {
+                    const float2 v0 = tile_pair(kt, p0, d, 0.f), v1 = tile_pair(kt, p1, d, 0.f);
+                    const float2 v2 = tile_pair(kt, p0, d + 8, 0.f), v3 = tile_pair(kt, p1, d + 8, 0.f);
+                    split2(v0.x, v0.y, ah[0], al[0]);
+                    split2(v1.x, v1.y, ah[1], al[1]);
+                    split2(v2.x, v2.y, ah[2], al[2]);
+                    split2(v3.x, v3.y, ah[3], al[3]);
+                    mma16816(sc, ah, qb_hi[ks]);
+                    mma16816(sc, ah, qb_lo[ks]);
+                    mma16816(sc, al, qb_hi[ks]);
+                } else {
+                    ah[0] = tile_pair_h(kt, p0, d);
+                    ah[1] = tile_pair_h(kt, p1, d);
+                    ah[2] = tile_pair_h(kt, p0, d + 8);
+                    ah[3] = tile_pair_h(kt, p1, d + 8);
+                    mma16816(sc, ah, qb_hi[ks]);
+                    mma16816(sc, ah, qb_lo[ks]);
                 }
             }
+            float* Sh = S + kh * A64_T * TC_SS;
+            Sh[p0 * TC_SS + 2 * t4] = sc[0];
+            Sh[p0 * TC_SS + 2 * t4 + 1] = sc[1];
+            Sh[p1 * TC_SS + 2 * t4] = sc[2];
+            Sh[p1 * TC_SS + 2 * t4 + 1] = sc[3];
         }
         __syncthreads();
-        // Softmax over the chunk: warp h owns head h.
+        // ---- softmax over the chunk: warp h owns head h
         if (warp < gq) {
             const int h = warp;
-            float sc[2];
+            float scv[2];
 #pragma unroll
             for (int pp = 0; pp < 2; ++pp) {
                 const int t = lane + 32 * pp;
-                float v = 0.f;
-#pragma unroll
-                for (int w = 0; w < A64_NW; ++w) v += sp[(w * A64_HP + h) * A64_T + t];
-                sc[pp] = cbase + t < t1 ? v : -INFINITY;
+                const float v = S[t * TC_SS + h] + S[(A64_T + t) * TC_SS + h];
+                scv[pp] = cbase + t < t1 ? v : -INFINITY;
             }
-            const float cmax = warp_max(fmaxf(sc[0], sc[1]));
+            const float cmax = warp_max(fmaxf(scv[0], scv[1]));
             const float m_new = fmaxf(m_run, cmax);
             const float alpha = m_run > -INFINITY ? at_ex2(m_run - m_new) : 0.f;
-            const float p0 = sc[0] > -INFINITY ? at_ex2(sc[0] - m_new) : 0.f;
-            const float p1 = sc[1] > -INFINITY ? at_ex2(sc[1] - m_new) : 0.f;
+            const float p0 = scv[0] > -INFINITY ? at_ex2(scv[0] - m_new) : 0.f;
+            const float p1 = scv[1] > -INFINITY ? at_ex2(scv[1] - m_new) : 0.f;
             l_run = fmaf(l_run, alpha, warp_sum(p0 + p1));
             m_run = m_new;
-            P[lane * A64_HP + h] = p0;
-            P[(lane + 32) * A64_HP + h] = p1;
+            P[lane * TC_PS + h] = p0;
+            P[(lane + 32) * TC_PS + h] = p1;
             if (lane == 0) s_alpha[h] = alpha;
         } else if (warp < A64_HP) {
-            const int h = warp;  // padded heads: zero probabilities
-            P[lane * A64_HP + h] = 0.f;
-            P[(lane + 32) * A64_HP + h] = 0.f;
-            if (lane == 0) s_alpha[h] = 0.f;
+            P[lane * TC_PS + warp] = 0.f;
+            P[(lane + 32) * TC_PS + warp] = 0.f;
+            if (lane == 0) s_alpha[warp] = 0.f;
         }
         __syncthreads();
-        // PV: positions 8*warp..8*warp+7, dims 2*lane, 2*lane+1.
+        // ---- PV: O^T[dims 16mt..][heads] += V^T[dims][positions 32kh..] P[positions][heads]
         {
-            const float4 al0 = *reinterpret_cast<const float4*>(s_alpha);
-            const float4 al1 = *reinterpret_cast<const float4*>(s_alpha + 4);
-            const float alv[8] = {al0.x, al0.y, al0.z, al0.w, al1.x, al1.y, al1.z, al1.w};
+            const float al0 = s_alpha[2 * t4], al1 = s_alpha[2 * t4 + 1];
+            o[0] *= al0;
+            o[1] *= al1;
+            o[2] *= al0;
+            o[3] *= al1;
+            const int dm0 = 16 * mt + gq8, dm1 = dm0 + 8;
 #pragma unroll
-            for (int h = 0; h < A64_HP; ++h) {
-                o[h][0] *= alv[h];
-                o[h][1] *= alv[h];
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int t = 8 * warp + i;
-                const float2 v2 = a64_load2(vt, t, 2 * lane, KV());
-                const float4 pa = *reinterpret_cast<const float4*>(P + t * A64_HP);
-                const float4 pb = *reinterpret_cast<const float4*>(P + t * A64_HP + 4);
-                const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-                for (int h = 0; h < A64_HP; ++h) {
-                    o[h][0] = fmaf(pv[h], v2.x, o[h][0]);
-                    o[h][1] = fmaf(pv[h], v2.y, o[h][1]);
+            for (int ks = 0; ks < 2; ++ks) {
+                const int k0 = 32 * kh + 16 * ks + 2 * t4;  // positions k0, k0+1, k0+8, k0+9
+                uint32_t bh[2], bl[2];
+                split2(P[k0 * TC_PS + gq8], P[(k0 + 1) * TC_PS + gq8], bh[0], bl[0]);
+                split2(P[(k0 + 8) * TC_PS + gq8], P[(k0 + 9) * TC_PS + gq8], bh[1], bl[1]);
+                const float v00 = tile_one(vt, k0, dm0, KV()), v01 = tile_one(vt, k0 + 1, dm0, KV());
+                const float v10 = tile_one(vt, k0, dm1, KV()), v11 = tile_one(vt, k0 + 1, dm1, KV());
+                const float v20 = tile_one(vt, k0 + 8, dm0, KV()), v21 = tile_one(vt, k0 + 9, dm0, KV());
+                const float v30 = tile_one(vt, k0 + 8, dm1, KV()), v31 = tile_one(vt, k0 + 9, dm1, KV());
+                uint32_t ah[4], al[4];
+                if (!F16) {
+                    split2(v00, v01, ah[0], al[0]);
+                    split2(v10, v11, ah[1], al[1]);
+                    split2(v20, v21, ah[2], al[2]);
+                    split2(v30, v31, ah[3], al[3]);
+                    mma16816(o, ah, bh);
+                    mma16816(o, ah, bl);
+                    mma16816(o, al, bh);
+                } else {
+                    ah[0] = pack2(v00, v01);
+                    ah[1] = pack2(v10, v11);
+                    ah[2] = pack2(v20, v21);
+                    ah[3] = pack2(v30, v31);
+                    mma16816(o, ah, bh);
+                    mma16816(o, ah, bl);
                 }
             }
         }
-        __syncthreads();  // slot consumed by every warp
+        __syncthreads();  // slot, S and P consumed by every warp
         if (tid == 0 && c + NS < nch) {
             fence_proxy_async();
             issue(c + NS);
         }
     }
     if (!ok) {
-        // Copies still in flight land before the block exits (bounded).
         if (tid == 0) {
             const uint64_t w0 = globaltimer();
             for (int c = 0; c < nch && c < NS; ++c) {
@@ -1055,12 +1095,14 @@ __global__ void __launch_bounds__(A64_NT, 2)
         __syncthreads();
         return;
     }
-    // Sum the warps' outputs: [warp][head][64] through the partial-score area.
-    float* ow = sp;
-#pragma unroll
-    for (int h = 0; h < A64_HP; ++h) {
-        ow[(warp * A64_HP + h) * 64 + 2 * lane] = o[h][0];
-        ow[(warp * A64_HP + h) * 64 + 2 * lane + 1] = o[h][1];
+    // Sum the two position halves of O^T, then write (max, sum, output) per head.
+    {
+        const int dm0 = 16 * mt + gq8, dm1 = dm0 + 8;
+        float* oh = ow + kh * 64 * A64_HP;
+        oh[dm0 * A64_HP + 2 * t4] = o[0];
+        oh[dm0 * A64_HP + 2 * t4 + 1] = o[1];
+        oh[dm1 * A64_HP + 2 * t4] = o[2];
+        oh[dm1 * A64_HP + 2 * t4 + 1] = o[3];
     }
     if (warp < gq && lane == 0) {
         s_ml[2 * warp] = m_run;
@@ -1069,9 +1111,7 @@ __global__ void __launch_bounds__(A64_NT, 2)
     __syncthreads();
     for (int e = tid; e < gq * 64; e += A64_NT) {
         const int h = e >> 6, j = e & 63;
-        float acc = 0.f;
-#pragma unroll
-        for (int w = 0; w < A64_NW; ++w) acc += ow[(w * A64_HP + h) * 64 + j];
+        const float acc = ow[j * A64_HP + h] + ow[64 * A64_HP + j * A64_HP + h];
         float* pp = a.part + (((size_t)s * a.NH + (size_t)g * gq + h) * a.max_splits + sp_i) * 66;
         if (j == 0) {
             pp[0] = s_ml[2 * h];
@@ -1089,7 +1129,7 @@ __global__ void __launch_bounds__(A64_NT, 2)
     __syncthreads();
     if (s_last) {
         __threadfence();
-        combine_seq(a.cb, s, sp, s_red);
+        combine_seq(a.cb, s, reinterpret_cast<float*>(sm), s_red);  // the ring is free now
         if (tid == 0) a.seq_done[s] = 0;
     }
 }
