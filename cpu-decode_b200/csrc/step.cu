@@ -60,6 +60,7 @@ struct dcb_engine {
     int* h_result = nullptr;  // pinned [2]: error, argmax (copied together from Sync)
     uint64_t* trace = nullptr;
     uint64_t launches = 0;
+    int par = 0;  // half of the down sums the next step uses
     int split_min = 64;   // positions per attention split, at least (one chunk)
 
     ~dcb_engine() {
@@ -160,6 +161,8 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
     choose_split(e, (int)e->attended(e->pos), &A.nsplit, &A.split_len);
     if (++e->seq >= (1u << 24)) e->seq = 1;  // tags are seq << 8 | layer
     A.seq = e->seq;
+    A.par = e->par;
+    e->par ^= 1;
     void* args[] = {(void*)&e->P, (void*)&A};
     DCB_CUDA(cudaLaunchCooperativeKernel(e->kernel, dim3(e->grid), dim3(NT), args, (size_t)e->smem, e->stream));
     ++e->launches;
@@ -170,6 +173,8 @@ int device_error(dcb_engine* e, int err) {
     if (!err) return 0;
     // On the engine's stream: a legacy-stream memset is not ordered before its next launch.
     DCB_CUDA(cudaMemsetAsync(e->P.sync, 0, sizeof(Sync), e->stream));
+    // An abandoned step may have left down sums behind: start both halves from zero.
+    DCB_CUDA(cudaMemsetAsync(e->P.dacc, 0, (size_t)2 * e->L * e->P.Hp * sizeof(uint64_t), e->stream));
     DCB_CUDA(cudaStreamSynchronize(e->stream));
     if (err == ERR_TOKEN) return fail(DCB_ERR_TOKEN, "token ID outside vocabulary");
     return fail(DCB_ERR_DEVICE_WAIT, "a device-side wait ran out of time; the step was abandoned");
@@ -222,7 +227,6 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     e->sms = dev_sms;
     e->grid = dev_sms;
     const int H = e->H, I = e->I, D = e->D, half = D / 2, G = e->grid;
-    if (ceil_div(H, G) > DOWN_MAX_ROWS) return bail(fail(DCB_ERR_UNSUPPORTED, "hidden size too large for this GPU"));
     Params& P = e->P;
     P.H = H;
     P.I = I;
@@ -281,6 +285,34 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         if (int rc = upload(e, &d8, buf)) return bail(rc);
         W.down = d8;
     }
+    // Down projection for the split-K step: block b's columns [b*I/G, (b+1)*I/G)
+    // of every row, DW bytes per row (zero past the block's columns), one
+    // down_slice-byte region per (layer, block); per-row scales apart.
+    {
+        const int DW = (int)round_up((size_t)ceil_div(I, G), 4);
+        if (DW > NT) return bail(fail(DCB_ERR_UNSUPPORTED, "intermediate size too large for this GPU"));
+        if (H > DOWN_RPT * NT) return bail(fail(DCB_ERR_UNSUPPORTED, "hidden size above 1024 is not supported"));
+        // The sum words count the blocks in 8 bits.
+        if (G > 255) return bail(fail(DCB_ERR_UNSUPPORTED, "more than 255 multiprocessors is not supported"));
+        P.down_dw = DW;
+        P.down_slice = (int)round_up((size_t)H * DW, 16);
+        buf.assign((size_t)e->L * G * P.down_slice, 0);
+        std::vector<float> dscale((size_t)e->L * H);
+        for (int l = 0; l < e->L; ++l) {
+            const dcb_layer_desc& S = m->layer[l];
+            for (int bb = 0; bb < G; ++bb) {
+                const int c0 = (int)((long long)bb * I / G), c1 = (int)((long long)(bb + 1) * I / G);
+                uint8_t* dst = &buf[((size_t)l * G + bb) * P.down_slice];
+                for (int r = 0; r < H; ++r)
+                    std::memcpy(dst + (size_t)r * DW, S.down + (size_t)r * I + c0, (size_t)(c1 - c0));
+            }
+            std::copy(S.down_scales, S.down_scales + H, dscale.begin() + (size_t)l * H);
+        }
+        uint8_t* d8;
+        if (int rc = upload(e, &d8, buf)) return bail(rc);
+        P.down_cols = d8;
+        if (int rc = upload_floats(e, &P.down_scale, dscale)) return bail(rc);
+    }
     {
         LayerW* d_layers = nullptr;
         if (int rc = e->alloc(&d_layers, lw.size())) return bail(rc);
@@ -322,7 +354,6 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         P.kcache = kc;
         P.vcache = vc;
     }
-    if (int rc = e->alloc(&P.ll_xa, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_xb, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_q, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_kv, 2 * e->NKV * D)) return bail(rc);
@@ -339,6 +370,8 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         DCB_CUDA(cudaMemcpy(peers, own, sizeof(own), cudaMemcpyHostToDevice));
         P.peers = peers;
     }
+    P.Hp = (int)round_up((size_t)H, 32);
+    if (int rc = e->alloc(&P.dacc, (size_t)2 * e->L * P.Hp)) return bail(rc);
     if (int rc = e->alloc(&P.logits, e->V)) return bail(rc);
     if (int rc = e->alloc(&P.amax, G)) return bail(rc);
     if (int rc = e->alloc(&P.sync, 1)) return bail(rc);
@@ -351,7 +384,7 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     DCB_CUDA(cudaFuncGetAttributes(&fattr, e->kernel));
     const size_t budget = (size_t)max_optin - fattr.sharedSizeBytes;  // dynamic shared memory available
     const size_t gu_slot = (size_t)ceil_div(I, G) * 2 * P.SH;
-    const size_t down_slot = (size_t)ceil_div(H, G) * P.SI;
+    const size_t down_slot = (size_t)P.down_slice;
     const size_t qkv_slot = (size_t)ceil_div(P.qkv_pairs, G) * 2 * P.SH;
     const size_t o_slot = (size_t)ceil_div(H, G) * P.SH;
     size_t off = 0;
@@ -376,16 +409,13 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     const size_t gpart_bytes = round_up(2 * (size_t)P.gpart_floats * sizeof(float), 128);
     const size_t xr_bytes = round_up((size_t)P.Kh * sizeof(float), 128);
     const size_t misc_bytes = round_up((size_t)(384 + NW * (D + 2)) * sizeof(float), 128);
-    const size_t tail = xs_bytes + xq_bytes + gpart_bytes + xr_bytes + misc_bytes;
-    // The attention ring takes what is left (2..ATT_MAX_BUFS chunks); DOWN's
-    // intermediate-sized input staging overlays it, so it is at least that big.
+    const size_t h_bytes = round_up((size_t)P.down_dw * sizeof(float), 128);
+    const size_t tail = xs_bytes + xq_bytes + gpart_bytes + xr_bytes + misc_bytes + h_bytes;
+    // The attention ring takes what is left (2..ATT_MAX_BUFS chunks).
     P.att_chunk_bytes = (int)(2 * (size_t)ATT_CHUNK * D * e->kv_elem());
-    P.down_x_off = (int)round_up((size_t)P.Ki * sizeof(float), 128);
-    P.down_plane = (int)round_up((size_t)P.Ki, 128);
-    const size_t down_stage = round_up((size_t)P.down_x_off + 3 * (size_t)P.down_plane, 128);
     const size_t room = budget > off + tail ? budget - off - tail : 0;
     P.att_bufs = (int)std::min<size_t>(ATT_MAX_BUFS, std::max<size_t>(2, room / P.att_chunk_bytes));
-    off = round_up(off + std::max((size_t)P.att_bufs * P.att_chunk_bytes, down_stage), 128);
+    off = round_up(off + (size_t)P.att_bufs * P.att_chunk_bytes, 128);
     P.off_xs = (int)off;
     P.trace_layer = std::min(5, e->L - 1);
     if (const char* v = std::getenv("DCB_SPLIT_MIN")) e->split_min = std::max(ATT_CHUNK, std::atoi(v) / ATT_CHUNK * ATT_CHUNK);
@@ -398,6 +428,8 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     off += xr_bytes;
     P.off_misc = (int)off;
     off += misc_bytes;
+    P.off_h = (int)off;
+    off += h_bytes;
     e->smem = (int)off;
     if ((size_t)e->smem > budget) return bail(fail(DCB_ERR_UNSUPPORTED, "model too large for shared memory staging"));
     if (cudaFuncSetAttribute(e->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem) != cudaSuccess)

@@ -8,7 +8,9 @@
 //          KV split; split 0 merges the splits' (max, sum, output))
 //   O    : O GEMV + residual
 //   GU   : RMSNorm prologue, gate/up GEMV, SiLU(gate)*up
-//   DOWN : down GEMV + residual
+//   DOWN : split-K over the blocks: each block multiplies its own SiLU(gate)*up
+//          values by its columns of W_down and adds the products into exact
+//          fixed-point sums; the next layer reads x_b + sums
 // then the final RMSNorm, the tied LM head and the argmax.
 //
 // Data movement, B200-first:
@@ -20,6 +22,8 @@
 //    {value, tag}: a producer stores each element once with its tag, consumers
 //    poll exactly the elements they need until the tag of this step and layer
 //    shows. One L2 round trip per dependency; a stale value is never used.
+//    The down projection's output is a sum over all blocks instead: 64-bit
+//    integer atomics into L2 and a per-layer count of the blocks done.
 //  * The LM head (136 MB at the Qwen shape) streams straight from HBM: every
 //    warp keeps the 16-byte chunks of its next row group in flight while it
 //    reduces the current one.
@@ -46,8 +50,8 @@ constexpr int HEAD_R = 4;           // LM-head rows a warp reduces per group (th
 constexpr int HEAD_L2_ROWS = 256;   // LM-head rows per block prefetched into L2 during the last layer
 constexpr int HEAD_MAXC = 2;        // 16-byte chunks per lane of a hidden-size row (hidden <= 1024)
 constexpr int TRACE_MAX_PHASES = 512;
+constexpr int DOWN_RPT = 2;    // down output rows per thread (H <= DOWN_RPT * NT)
 constexpr int MAXD = 4;        // head_dim <= 128: lane owns dims lane + 32k
-constexpr int DOWN_MAX_ROWS = 8;  // down rows per block (H <= 8 * grid)
 
 // Per-layer weights, packed rows: [K int8 | FP32 scale | FP32 bias | 8 pad].
 struct LayerW {
@@ -87,7 +91,6 @@ struct Params {
     const float* rope_den;  // [D/2] theta^(2j/D)    (direct angle formula)
     void* kcache;           // [L][NKV][capacity][D], head-major
     void* vcache;
-    uint64_t* ll_xa;    // [H]   residual stream entering a layer (and the head)
     uint64_t* ll_xb;    // [H]   residual stream after attention
     uint64_t* ll_q;     // [H]   rotated queries
     uint64_t* ll_kv;    // [2*NKV*D] the new K and V rows
@@ -101,12 +104,19 @@ struct Params {
     // shared memory layout (bytes)
     int off_gu, off_down, off_qkv, off_o, off_att, off_xs, off_xq, off_gpart, off_xr, off_misc;
     int xq_plane;      // bytes per fixed-point plane of a hidden-sized vector (>= Kh)
-    int down_x_off;    // DOWN input staging inside the attention buffers: floats at off_att,
-    int down_plane;    // planes at off_att + down_x_off, down_plane bytes each (>= Ki)
     int gpart_floats;  // floats per block-GEMV partial buffer (NW * max rows of a phase)
     int att_chunk_bytes;
     int att_bufs;     // chunk buffers in the attention ring (2..ATT_MAX_BUFS)
     int trace_layer;  // layer whose phases get detailed marks when tracing
+    // Down projection as split-K over the blocks: block b holds columns
+    // [b*I/G, (b+1)*I/G) of W_down for all H rows, DW int8 per row (zero
+    // padded), one down_slice-byte region per block and layer. Its products
+    // with the block's own SiLU(gate)*up values are added, scaled per row, into
+    // the self-counting sum words dacc[parity][layer][Hp].
+    const uint8_t* down_cols;  // [L][G][down_slice]
+    const float* down_scale;   // [L][H] per-row scales of W_down
+    uint64_t* dacc;            // [2][L][Hp]
+    int down_dw, down_slice, Hp, off_h;
 };
 
 struct StepArgs {
@@ -119,6 +129,7 @@ struct StepArgs {
     int split_len;
     unsigned seq;
     float* host_logits;  // mapped pinned host memory the LM head also writes, or null
+    int par;             // which half of dacc this step sums into (the other half is cleared for the next)
 };
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
@@ -305,53 +316,6 @@ static __device__ Staged finish_stage(int n, int nch, const float* xf, int8_t* x
     return out;
 }
 
-// Block-cooperative: wait until the n tagged words at src carry `tag`, accept
-// them and stage the vector. Words are polled in groups of W per thread, all
-// loads of a group in flight together; with GAIN, the RMSNorm gains of the
-// same elements (global memory, gain[j]) are loaded alongside the first poll.
-// Returns false when the step must abort.
-template <int W, bool GAIN>
-__device__ bool gather_stage(const uint64_t* src, int n, uint32_t tag, float* xr, float* xf, int8_t* xq, int plane,
-                             int nch, const float* gain, float* red, float eps, Staged& out, const BlockState& st) {
-    uint64_t t0 = 0;
-    unsigned rounds = 0;
-    float ss = 0.f, mx = 0.f;
-    for (int base = 0; base < n; base += W * NT) {
-        uint64_t w[W];
-        float g[W];
-        unsigned pending = 0;
-#pragma unroll
-        for (int k = 0; k < W; ++k) {
-            const int j = base + threadIdx.x + k * NT;
-            g[k] = 1.f;
-            if (j < n) {
-                w[k] = ll_load(src + j);
-                if (GAIN) g[k] = __ldg(gain + j);
-                pending |= 1u << k;
-            }
-        }
-        while (true) {
-#pragma unroll
-            for (int k = 0; k < W; ++k) {
-                if ((pending >> k) & 1u) {
-                    if ((uint32_t)(w[k] >> 32) == tag) {
-                        accept(base + threadIdx.x + k * NT, __uint_as_float((uint32_t)w[k]), xr, xf, g[k], ss, mx);
-                        pending &= ~(1u << k);
-                    }
-                }
-            }
-            if (!pending) break;
-            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
-#pragma unroll
-            for (int k = 0; k < W; ++k)
-                if ((pending >> k) & 1u) w[k] = ll_load(src + base + threadIdx.x + k * NT);
-        }
-        if (should_abort(st)) break;
-    }
-    out = finish_stage(n, nch, xf, xq, plane, ss, mx, red, eps);
-    return !should_abort(st);
-}
-
 // ---- per-warp staging of a GEMV input ---------------------------------------------
 // Warp w owns K-chunks [w*nch/NW, (w+1)*nch/NW) of the input (16 elements
 // each), the same chunks block_gemv gives it. warp_stage waits for exactly
@@ -465,6 +429,177 @@ static __device__ bool warp_slot_wait(uint64_t* m, uint32_t parity, const BlockS
     }
     __syncwarp();
     return __shfl_sync(FULL, okw, 0);
+}
+
+// ---- split-K down projection: self-counting fixed-point sums over blocks ------------
+// Each output row of the down projection is one 64-bit word in L2 that every
+// block adds its share v into with one fire-and-forget reduction:
+//   2^56 + (rint(v * 2^26) + 2^47)      (|v| < 2^21 = 2097152, clamped)
+// The top 8 bits count the blocks added so far; the low 56 bits hold the sum
+// in offset fixed point (no carry reaches the count for up to 255 blocks).
+// Integer addition is exact, so the total does not depend on the order in
+// which the additions reach L2 (every run, and every GPU of a KV split, gets
+// the same bits), and a reader knows the word is complete when its count
+// equals the number of blocks: no fence, no flag.
+constexpr int DACC_CNT_SHIFT = 56;
+constexpr double DACC_ONE = 67108864.0;  // 2^26: one unit of the sum
+constexpr long long DACC_BIAS = 1LL << 47;
+constexpr uint64_t DACC_LOW = (1ull << DACC_CNT_SHIFT) - 1;
+
+__device__ __forceinline__ void dacc_add(uint64_t* p, float v) {
+    long long q = __double2ll_rn((double)v * DACC_ONE);
+    q = q > DACC_BIAS - 1 ? DACC_BIAS - 1 : (q < 1 - DACC_BIAS ? 1 - DACC_BIAS : q);
+    const uint64_t c = (1ull << DACC_CNT_SHIFT) + (uint64_t)(q + DACC_BIAS);
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(c) : "memory");
+}
+__device__ __forceinline__ unsigned dacc_count(uint64_t w) { return (unsigned)(w >> DACC_CNT_SHIFT); }
+__device__ __forceinline__ float dacc_value(uint64_t w) {
+    const long long q = (long long)(w & DACC_LOW) - (long long)dacc_count(w) * DACC_BIAS;
+    return (float)((double)q * (1.0 / DACC_ONE));
+}
+
+// Per-warp staging of x = xr + down sums (the residual stream entering a
+// layer): warp w takes the same K-chunks as in warp_stage, polls their sum
+// words until every block (`expect`) has added its share, keeps the new raw
+// values in xr, folds in the RMSNorm gain, quantises with its own scale
+// (wscale) and leaves its share of sum x^2 in ss_out[warp]. Returns false
+// when the wait ran out (the abort flag is set); one decision per warp.
+static __device__ bool warp_stage_sum(const uint64_t* acc, unsigned expect, int n, float* xr, float* xf, int8_t* xq,
+                                      int plane, int nch, const float* gain, float* ss_out, float& wscale,
+                                      const BlockState& st) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = warp * nch / NW, c1 = (warp + 1) * nch / NW;
+    const int e0 = 16 * c0, e1 = min(16 * c1, n);
+    bool okw = true;
+    float ss = 0.f, mx = 0.f;
+    uint64_t t0 = 0;
+    unsigned rounds = 0;
+    for (int base = e0; base < e1; base += 64) {
+        uint64_t w[2];
+        float g[2];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int j = base + lane + 32 * k;
+            g[k] = 0.f;
+            w[k] = 0;
+            if (j < e1) {
+                w[k] = ll_load(acc + j);
+                g[k] = __ldg(gain + j);
+                pending |= 1u << k;
+            }
+        }
+        while (true) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                if (((pending >> k) & 1u) && dacc_count(w[k]) == expect) pending &= ~(1u << k);
+            if (!pending) break;
+            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) {
+                okw = false;
+                break;
+            }
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                if ((pending >> k) & 1u) w[k] = ll_load(acc + base + lane + 32 * k);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int j = base + lane + 32 * k;
+            if (j < e1) {
+                const float v = xr[j] + dacc_value(w[k]);
+                xr[j] = v;
+                const float gv = v * g[k];
+                xf[j] = gv;
+                ss = fmaf(v, v, ss);
+                mx = fmaxf(mx, fabsf(gv));
+            }
+        }
+        if (!okw) break;
+    }
+    okw = __all_sync(FULL, okw);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ss += __shfl_xor_sync(FULL, ss, o);
+        mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    }
+    if (lane == 0) ss_out[warp] = ss;
+    const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
+    wscale = mx > 0.f ? __frcp_rn(rs) : 1.0f;
+    __syncwarp();
+    for (int quad = 4 * c0 + lane; quad < 4 * c1; quad += 32) {
+        const int j = 4 * quad;
+        const float4 v4 = j + 3 < n ? *reinterpret_cast<const float4*>(xf + j)
+                                    : make_float4(j < n ? xf[j] : 0.f, j + 1 < n ? xf[j + 1] : 0.f,
+                                                  j + 2 < n ? xf[j + 2] : 0.f, 0.f);
+        uint32_t ph, pm, pl;
+        fix_pack4(v4, rs, ph, pm, pl);
+        reinterpret_cast<uint32_t*>(xq)[quad] = ph;
+        reinterpret_cast<uint32_t*>(xq + plane)[quad] = pm;
+        reinterpret_cast<uint32_t*>(xq + 2 * plane)[quad] = pl;
+    }
+    __syncwarp();
+    return okw;
+}
+
+// This block's share of the down projection (src/model.cpp:309, the matvec of
+// src/kernels.cpp:107-120 split over K): for every output row r < H,
+// scale_r * sum_{j < DW} w[r][j] * h[j] with the block's column slice (H rows
+// of DW int8 in shared memory, zero past its columns) and its SiLU(gate)*up
+// values h (DW floats, zero past its columns), added into acc[r] by fire-and-
+// forget reductions. Thread t owns rows t + i*NT; scale[i] is row
+// t + i*NT's scale, loaded by the caller well ahead.
+static __device__ void down_partial(const uint8_t* slice, int DW, int H, const float* h, const float (&scale)[DOWN_RPT],
+                                    uint64_t* acc) {
+#pragma unroll
+    for (int i = 0; i < DOWN_RPT; ++i) {
+        const int r = threadIdx.x + i * NT;
+        if (r < H) {
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(slice + (size_t)r * DW);
+            float2 a = make_float2(0.f, 0.f);
+            for (int k = 0; k < DW / 4; ++k) a = dot4(w[k], *reinterpret_cast<const float4*>(h + 4 * k), a);
+            dacc_add(acc + r, (a.x + a.y) * scale[i]);
+        }
+    }
+}
+
+// Block-wide staging of x = xr + down sums (the final norm's input): thread t
+// polls the sum words t, t + NT (H <= 2*NT) until `expect` blocks have added,
+// then the vector is reduced and quantised as in finish_stage. Returns false
+// when the step must abort.
+static __device__ bool stage_sum(const uint64_t* acc, unsigned expect, int n, int nch, const float* xr, float* xf,
+                                 int8_t* xq, int plane, const float* gain, float* red, float eps, Staged& out,
+                                 const BlockState& st) {
+    float ss = 0.f, mx = 0.f;
+    uint64_t w[2];
+    unsigned pending = 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int j = threadIdx.x + k * NT;
+        w[k] = 0;
+        if (j < n) {
+            w[k] = ll_load(acc + j);
+            pending |= 1u << k;
+        }
+    }
+    uint64_t t0 = 0;
+    unsigned rounds = 0;
+    while (true) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            if (((pending >> k) & 1u) && dacc_count(w[k]) == expect) pending &= ~(1u << k);
+        if (!pending) break;
+        if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            if ((pending >> k) & 1u) w[k] = ll_load(acc + threadIdx.x + k * NT);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int j = threadIdx.x + k * NT;
+        if (j < n) accept(j, xr[j] + dacc_value(w[k]), nullptr, xf, __ldg(gain + j), ss, mx);
+    }
+    out = finish_stage(n, nch, xf, xq, plane, ss, mx, red, eps);
+    return !should_abort(st);
 }
 
 // 1/sqrt(mean(v^2) + eps) from the warps' shares of sum v^2 (src/kernels.cpp:132-137).
@@ -944,11 +1079,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     float* xf = reinterpret_cast<float*>(sm + P.off_xs);       // staged values before quantisation
     int8_t* xq = reinterpret_cast<int8_t*>(sm + P.off_xq);     // fixed-point planes of the staged vector
     const int QP = P.xq_plane;
-    // DOWN's input (intermediate-sized) is staged in the attention buffers, which
-    // hold no copies between the end of this layer's attention and the next
-    // layer's prefetch (issued after a block barrier and a proxy fence).
-    float* xf_i = reinterpret_cast<float*>(sm + P.off_att);
-    int8_t* xq_i = reinterpret_cast<int8_t*>(sm + P.off_att + P.down_x_off);
     float* gpart = reinterpret_cast<float*>(sm + P.off_gpart);  // block-GEMV partial sums, two buffers
     float* xr = reinterpret_cast<float*>(sm + P.off_xr);
     float* misc = reinterpret_cast<float*>(sm + P.off_misc);
@@ -969,15 +1099,19 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
 
     const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int H = P.H, I = P.I, D = P.D, half = D / 2, kvd = P.NKV * D;
-    const int nch_h = P.Kh / 16, nch_i = P.Ki / 16;
+    const int nch_h = P.Kh / 16;
     const BlockState st{&s_abort, P.sync};
 
     // This block's rows in every phase.
     const int qa = part_lo(b, G, P.qkv_pairs), qn = part_lo(b + 1, G, P.qkv_pairs) - qa;
     const int oa = part_lo(b, G, H), on = part_lo(b + 1, G, H) - oa;
     const int ga = part_lo(b, G, I), gn = part_lo(b + 1, G, I) - ga;
-    const int da = part_lo(b, G, H), dn = part_lo(b + 1, G, H) - da;
     const int ha = part_lo(b, G, P.V), hn = part_lo(b + 1, G, P.V) - ha;
+    // This step's down sums (the other half is cleared at the end); a sum word
+    // is complete when every block that holds down columns has added to it.
+    uint64_t* const dacc = P.dacc + (size_t)A.par * P.L * P.Hp;
+    const unsigned dblocks = (unsigned)min(G, I);
+    float* const s_h = reinterpret_cast<float*>(sm + P.off_h);  // [down_dw] this block's SiLU(gate)*up
 
     // This block's attention unit (at most one).
     AttnPlan ap{};
@@ -1003,7 +1137,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         if (qn) fill_slot(s_qkv, W.qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH, mb_qkv, s_fills + 2);
         if (on) fill_slot(s_o, W.o + (size_t)oa * P.SH, (uint32_t)on * P.SH, mb_o, s_fills + 3);
         if (gn) fill_slot(s_gu, W.gu + (size_t)ga * 2 * P.SH, (uint32_t)gn * 2 * P.SH, mb_gu, s_fills + 0);
-        if (dn) fill_slot(s_down, W.down + (size_t)da * P.SI, (uint32_t)dn * P.SI, mb_down, s_fills + 1);
+        if (gn) fill_slot(s_down, P.down_cols + (size_t)b * P.down_slice, (uint32_t)P.down_slice, mb_down, s_fills + 1);
     }
     // RoPE cos/sin of this position, once per step (src/model.cpp:269-274).
     if (tid < half) {
@@ -1033,6 +1167,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // RMSNorm gains of layer l (global memory; read while the words are polled).
         const float* in_norm = P.norms + (size_t)l * 2 * P.Kh;
         const float* post_norm = in_norm + P.Kh;
+        // Row scales of this layer's down projection for the rows this thread
+        // adds (tid + i*NT): loaded now, used after the gate/up phase.
+        float dscale[DOWN_RPT];
+#pragma unroll
+        for (int i = 0; i < DOWN_RPT; ++i) {
+            const int r = tid + i * NT;
+            dscale[i] = gn && r < H ? __ldg(P.down_scale + (size_t)l * H + r) : 0.f;
+        }
 
         // HBM has slack during the last layer: start this block's first LM-head rows into L2.
         if (tid == 0 && A.head && l == P.L - 1 && hn)
@@ -1045,15 +1187,23 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                 att_issue<KV>(P, A, ap, l, c, s_att, mb_att, s_fills + MB_ATT);
         }
 
-        // ---- QKV (src/model.cpp:276-302); x entering layer l carries `tag`.
+        // ---- QKV (src/model.cpp:276-302). x entering layer 0 is the embedding
+        // row; entering layer l > 0 it is x_b of layer l-1 (xr) plus the down
+        // sums of layer l-1, read once every block has added its share.
         // Each warp stages its own chunks of x (RMSNorm gain folded in) and
         // starts its share of the GEMV; 1/rms scales the row totals.
         trace_detail(P, l, 0, 0);
         if (qn || on) {
-            float wsc;
-            const uint8_t* er = l == 0 ? P.embed + (size_t)token * P.SH : nullptr;
-            const bool okw = warp_stage<2, true>(P.ll_xa, er, er ? row_scale(er, P.Kh) : 0.f, H, tag, xr, xf, xq, QP,
-                                                 nch_h, in_norm, s_ss, wsc, st);
+            float wsc = 1.f;
+            bool okw;
+            if (l == 0) {
+                const uint8_t* er = P.embed + (size_t)token * P.SH;
+                okw = warp_stage<2, true>(nullptr, er, row_scale(er, P.Kh), H, tag, xr, xf, xq, QP, nch_h, in_norm,
+                                          s_ss, wsc, st);
+            } else {
+                okw = warp_stage_sum(dacc + (size_t)(l - 1) * P.Hp, dblocks, H, xr, xf, xq, QP, nch_h, in_norm,
+                                     s_ss, wsc, st);
+            }
             trace_detail(P, l, 0, 1);
             if (qn) {
                 trace_detail(P, l, 0, 2);
@@ -1154,10 +1304,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         }
         trace_mark(P, 1, ph + 3);
 
-        // ---- gate/up + SiLU (src/model.cpp:306-308)
-        if (gn || dn) {
+        // ---- gate/up + SiLU (src/model.cpp:306-308), then this block's share of
+        // down (src/model.cpp:309-310): its columns of W_down times its own
+        // SiLU(gate)*up values, for all H rows, into the down sums of layer l.
+        // Every block gathers x_b (kept raw in xr): x entering layer l+1, and the
+        // final norm's input, is xr plus those sums.
+        {
             trace_detail(P, l, 3, 0);
-            float wsc;
+            float wsc = 1.f;
             const bool okw = warp_stage<2, true>(P.ll_xb, nullptr, 0.f, H, tag, xr, xf, xq, QP, nch_h, post_norm, s_ss,
                                                  wsc, st);
             trace_detail(P, l, 3, 1);
@@ -1171,12 +1325,16 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                     ok = false;
                     break;
                 }
-                if (tid < gn) {
-                    const float inv = rms_inv(s_ss, H, P.eps);
-                    const uint8_t* r0 = s_gu + (size_t)tid * 2 * P.SH;
-                    const float g = gemv_row(gpart, 2 * gn, 2 * tid) * inv * row_scale(r0, P.Kh);
-                    const float u = gemv_row(gpart, 2 * gn, 2 * tid + 1) * inv * row_scale(r0 + P.SH, P.Kh);
-                    ll_store(P.ll_h + ga + tid, (g / (1.0f + expf(-g))) * u, tag);
+                if (tid < P.down_dw) {
+                    float hv = 0.f;  // zero past this block's columns
+                    if (tid < gn) {
+                        const float inv = rms_inv(s_ss, H, P.eps);
+                        const uint8_t* r0 = s_gu + (size_t)tid * 2 * P.SH;
+                        const float g = gemv_row(gpart, 2 * gn, 2 * tid) * inv * row_scale(r0, P.Kh);
+                        const float u = gemv_row(gpart, 2 * gn, 2 * tid + 1) * inv * row_scale(r0 + P.SH, P.Kh);
+                        hv = (g / (1.0f + expf(-g))) * u;
+                    }
+                    s_h[tid] = hv;
                 }
                 trace_detail(P, l, 3, 4);
                 __syncthreads();
@@ -1188,40 +1346,37 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                                   s_fills + 0);
                 }
                 trace_detail(P, l, 3, 6);
+            } else {
+                __syncthreads();
+                if (should_abort(st)) {
+                    ok = false;
+                    break;
+                }
             }
         }
         trace_mark(P, 1, ph + 4);
 
-        // ---- down + residual (src/model.cpp:309-310); x entering layer l+1 carries tag + 1.
-        if (dn) {
-            trace_detail(P, l, 4, 0);
-            float wsc;
-            const bool okw = warp_stage<10, false>(P.ll_h, nullptr, 0.f, I, tag, nullptr, xf_i, xq_i, P.down_plane,
-                                                   nch_i, nullptr, nullptr, wsc, st);
-            trace_detail(P, l, 4, 1);
-            const bool okg = okw && warp_slot_wait(mb_down, (uint32_t)l & 1u, st);
+        {
             trace_mark(P, 0, ph + 5);
+            trace_detail(P, l, 4, 0);
+            if (gn) {
+                if (!mbar_wait(mb_down, (uint32_t)l & 1u, st)) {
+                    ok = false;
+                    break;
+                }
+                trace_detail(P, l, 4, 1);
+                down_partial(s_down, P.down_dw, H, s_h, dscale, dacc + (size_t)l * P.Hp);
+            }
             trace_detail(P, l, 4, 2);
-            block_gemv<8, 2>(s_down, P.SI, dn, nch_i, xq_i, P.down_plane, gpart, wsc, okg);
-            if (should_abort(st)) {
-                ok = false;
-                break;
+            __syncthreads();  // the down slot is consumed
+            if (tid == 0) {
+                if (gn && l + 1 < P.L) {
+                    fence_proxy_async();
+                    fill_slot(s_down, P.down_cols + ((size_t)(l + 1) * G + b) * P.down_slice, (uint32_t)P.down_slice,
+                              mb_down, s_fills + 1);
+                }
             }
             trace_detail(P, l, 4, 3);
-            if (tid < dn) {
-                const int r = da + tid;
-                ll_store(P.ll_xa + r, xr[r] + gemv_row(gpart, dn, tid) * row_scale(s_down + (size_t)tid * P.SI, P.Ki),
-                         tag + 1);
-            }
-            __syncthreads();
-            trace_detail(P, l, 4, 4);
-            if (tid == 0) {
-                fence_proxy_async();
-                if (l + 1 < P.L)
-                    fill_slot(s_down, P.layers[l + 1].down + (size_t)da * P.SI, (uint32_t)dn * P.SI, mb_down,
-                              s_fills + 1);
-            }
-            trace_detail(P, l, 4, 5);
         }
         trace_mark(P, 1, ph + 5);
     }
@@ -1231,9 +1386,9 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         float best_v = -INFINITY;
         int best_i = 0x7fffffff;
         if (hn) {
-            Staged sf;
-            if (!gather_stage<2, true>(P.ll_xa, H, seq_tag | (uint32_t)(P.L + 1), nullptr, xf, xq, QP, nch_h,
-                                       P.norms + (size_t)P.L * 2 * P.Kh, red, P.eps, sf, st))
+            Staged sf{1.f, 1.f};
+            if (!stage_sum(dacc + (size_t)(P.L - 1) * P.Hp, dblocks, H, nch_h, xr, xf, xq, QP,
+                           P.norms + (size_t)P.L * 2 * P.Kh, red, P.eps, sf, st))
                 ok = false;
             const float inv = sf.inv * sf.scale;
             if (ok) {
@@ -1349,6 +1504,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         const LayerW& W0 = P.layers[0];
         if (qn) prefetch_l2(W0.qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH);
         if (on) prefetch_l2(W0.o + (size_t)oa * P.SH, (uint32_t)on * P.SH);
+    }
+
+    // Clear the other half of the down sums for the next step (this step's
+    // half is cleared by the next one). Done on abort too.
+    {
+        uint64_t* z = P.dacc + (size_t)(A.par ^ 1) * P.L * P.Hp;
+        const int n = P.L * P.Hp;
+        for (int i = part_lo(b, G, n) + tid; i < part_lo(b + 1, G, n); i += NT) z[i] = 0ull;
     }
 
     // On abort, wait (bounded) for this block's copies in flight before the
