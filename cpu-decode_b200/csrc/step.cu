@@ -37,6 +37,14 @@ int fail(int code, const std::string& msg) {
 
 size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 int ceil_div(int a, int b) { return (a + b - 1) / b; }
+// Bytes per row of a column slice of n int8: a multiple of 4 with an odd
+// number of 4-byte words, so a warp reading one word of 32 consecutive rows
+// touches 32 different shared-memory banks.
+int slice_row_bytes(int n) {
+    int w = ceil_div(n, 4);
+    if (w % 2 == 0) ++w;
+    return 4 * w;
+}
 }  // namespace
 
 struct dcb_engine {
@@ -144,7 +152,7 @@ int validate(const dcb_model_desc* m) {
 void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len) {
     const int chunks = ceil_div(length, ATT_CHUNK);
     // Split 0 gathers the other splits' (D+2)-float partials into the chunk buffers.
-    const int table_max = 1 + e->P.att_bufs * e->P.att_chunk_bytes / (int)((e->D + 2) * sizeof(float));
+    const int table_max = 1 + e->P.wo_off / (int)((e->D + 2) * sizeof(float));
     const int n = std::max(1, std::min({ceil_div(length, e->split_min), e->grid / e->NH, table_max}));
     *split_len = ceil_div(chunks, n) * ATT_CHUNK;
     *nsplit = ceil_div(length, *split_len);
@@ -174,7 +182,7 @@ int device_error(dcb_engine* e, int err) {
     // On the engine's stream: a legacy-stream memset is not ordered before its next launch.
     DCB_CUDA(cudaMemsetAsync(e->P.sync, 0, sizeof(Sync), e->stream));
     // An abandoned step may have left down sums behind: start both halves from zero.
-    DCB_CUDA(cudaMemsetAsync(e->P.dacc, 0, (size_t)2 * e->L * e->P.Hp * sizeof(uint64_t), e->stream));
+    DCB_CUDA(cudaMemsetAsync(e->P.dacc, 0, (size_t)2 * e->L * 2 * e->P.Hp * sizeof(uint64_t), e->stream));
     DCB_CUDA(cudaStreamSynchronize(e->stream));
     if (err == ERR_TOKEN) return fail(DCB_ERR_TOKEN, "token ID outside vocabulary");
     return fail(DCB_ERR_DEVICE_WAIT, "a device-side wait ran out of time; the step was abandoned");
@@ -289,11 +297,13 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     // of every row, DW bytes per row (zero past the block's columns), one
     // down_slice-byte region per (layer, block); per-row scales apart.
     {
-        const int DW = (int)round_up((size_t)ceil_div(I, G), 4);
+        const int DW = slice_row_bytes(ceil_div(I, G));
         if (DW > NT) return bail(fail(DCB_ERR_UNSUPPORTED, "intermediate size too large for this GPU"));
         if (H > DOWN_RPT * NT) return bail(fail(DCB_ERR_UNSUPPORTED, "hidden size above 1024 is not supported"));
-        // The sum words count the blocks in 8 bits.
+        // The sum words count the blocks (down) or heads (O) in 8 bits; every
+        // head needs a block of its own.
         if (G > 255) return bail(fail(DCB_ERR_UNSUPPORTED, "more than 255 multiprocessors is not supported"));
+        if (e->NH > G) return bail(fail(DCB_ERR_UNSUPPORTED, "more query heads than multiprocessors"));
         P.down_dw = DW;
         P.down_slice = (int)round_up((size_t)H * DW, 16);
         buf.assign((size_t)e->L * G * P.down_slice, 0);
@@ -312,6 +322,27 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         if (int rc = upload(e, &d8, buf)) return bail(rc);
         P.down_cols = d8;
         if (int rc = upload_floats(e, &P.down_scale, dscale)) return bail(rc);
+    }
+    // O projection for the split-K-over-heads step: per (layer, head) the
+    // head's D columns of every row, o_dw bytes per row (zero past D, an odd
+    // number of words); per-row scales apart.
+    {
+        P.o_dw = slice_row_bytes(D);
+        P.o_slice = (int)round_up((size_t)H * P.o_dw, 16);
+        buf.assign((size_t)e->L * e->NH * P.o_slice, 0);
+        std::vector<float> oscale((size_t)e->L * H);
+        for (int l = 0; l < e->L; ++l) {
+            const dcb_layer_desc& S = m->layer[l];
+            for (int h = 0; h < e->NH; ++h) {
+                uint8_t* dst = &buf[((size_t)l * e->NH + h) * P.o_slice];
+                for (int r = 0; r < H; ++r) std::memcpy(dst + (size_t)r * P.o_dw, S.o + (size_t)r * H + h * D, D);
+            }
+            std::copy(S.o_scales, S.o_scales + H, oscale.begin() + (size_t)l * H);
+        }
+        uint8_t* d8;
+        if (int rc = upload(e, &d8, buf)) return bail(rc);
+        P.o_cols = d8;
+        if (int rc = upload_floats(e, &P.o_scale, oscale)) return bail(rc);
     }
     {
         LayerW* d_layers = nullptr;
@@ -354,10 +385,8 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         P.kcache = kc;
         P.vcache = vc;
     }
-    if (int rc = e->alloc(&P.ll_xb, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_q, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_kv, 2 * e->NKV * D)) return bail(rc);
-    if (int rc = e->alloc(&P.ll_attn, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_h, I)) return bail(rc);
     if (int rc = e->alloc(&P.ll_part, (size_t)e->NH * (G + 1) * (D + 2))) return bail(rc);
     // KV-split exchange: [2 slots][NH][MAX_WORLD][D+2] tagged words, and the
@@ -371,7 +400,7 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         P.peers = peers;
     }
     P.Hp = (int)round_up((size_t)H, 32);
-    if (int rc = e->alloc(&P.dacc, (size_t)2 * e->L * P.Hp)) return bail(rc);
+    if (int rc = e->alloc(&P.dacc, (size_t)2 * e->L * 2 * P.Hp)) return bail(rc);
     if (int rc = e->alloc(&P.logits, e->V)) return bail(rc);
     if (int rc = e->alloc(&P.amax, G)) return bail(rc);
     if (int rc = e->alloc(&P.sync, 1)) return bail(rc);
@@ -386,7 +415,6 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     const size_t gu_slot = (size_t)ceil_div(I, G) * 2 * P.SH;
     const size_t down_slot = (size_t)P.down_slice;
     const size_t qkv_slot = (size_t)ceil_div(P.qkv_pairs, G) * 2 * P.SH;
-    const size_t o_slot = (size_t)ceil_div(H, G) * P.SH;
     size_t off = 0;
     P.off_gu = (int)off;
     off = round_up(off + gu_slot, 128);
@@ -394,14 +422,12 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     off = round_up(off + down_slot, 128);
     P.off_qkv = (int)off;
     off = round_up(off + qkv_slot, 128);
-    P.off_o = (int)off;
-    off = round_up(off + o_slot, 128);
     P.off_att = (int)off;
     // Vectors after the attention ring: staged floats, fixed-point planes,
     // GEMV partials (two buffers), raw residual, attention scratch.
     P.xq_plane = (int)round_up((size_t)P.Kh, 128);
     {
-        const int max_rows = std::max({2 * ceil_div(P.qkv_pairs, G), ceil_div(H, G), 2 * ceil_div(I, G)});
+        const int max_rows = std::max(2 * ceil_div(P.qkv_pairs, G), 2 * ceil_div(I, G));
         P.gpart_floats = NW * max_rows;
     }
     const size_t xs_bytes = round_up((size_t)P.Kh * sizeof(float), 128);
@@ -415,6 +441,14 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     P.att_chunk_bytes = (int)(2 * (size_t)ATT_CHUNK * D * e->kv_elem());
     const size_t room = budget > off + tail ? budget - off - tail : 0;
     P.att_bufs = (int)std::min<size_t>(ATT_MAX_BUFS, std::max<size_t>(2, room / P.att_chunk_bytes));
+    // W_o's columns of a head sit at the end of the attention buffers; the
+    // split-merge and KV-split tables at their start must stay below them.
+    {
+        const long long wo = (long long)P.att_bufs * P.att_chunk_bytes - P.o_slice;
+        const long long tables = (long long)(1 + MAX_WORLD) * (D + 2) * sizeof(float);
+        if (wo < tables) return bail(fail(DCB_ERR_UNSUPPORTED, "model too large for shared memory staging"));
+        P.wo_off = (int)(wo / 16 * 16);
+    }
     off = round_up(off + (size_t)P.att_bufs * P.att_chunk_bytes, 128);
     P.off_xs = (int)off;
     P.trace_layer = std::min(5, e->L - 1);

@@ -6,7 +6,9 @@
 //          written to the cache at `pos`
 //   ATTN : GQA attention over positions 0..pos (one block per query head and
 //          KV split; split 0 merges the splits' (max, sum, output))
-//   O    : O GEMV + residual
+//   O    : split-K over the heads: the block that finishes head h's attention
+//          multiplies it by W_o's columns of head h and adds the products into
+//          exact fixed-point sums; the gate/up phase reads x_a + sums
 //   GU   : RMSNorm prologue, gate/up GEMV, SiLU(gate)*up
 //   DOWN : split-K over the blocks: each block multiplies its own SiLU(gate)*up
 //          values by its columns of W_down and adds the products into exact
@@ -22,8 +24,8 @@
 //    {value, tag}: a producer stores each element once with its tag, consumers
 //    poll exactly the elements they need until the tag of this step and layer
 //    shows. One L2 round trip per dependency; a stale value is never used.
-//    The down projection's output is a sum over all blocks instead: 64-bit
-//    integer atomics into L2 and a per-layer count of the blocks done.
+//    The O and down projections' outputs are sums over blocks instead:
+//    64-bit integer reductions into L2 words that count their own additions.
 //  * The LM head (136 MB at the Qwen shape) streams straight from HBM: every
 //    warp keeps the 16-byte chunks of its next row group in flight while it
 //    reduces the current one.
@@ -91,10 +93,8 @@ struct Params {
     const float* rope_den;  // [D/2] theta^(2j/D)    (direct angle formula)
     void* kcache;           // [L][NKV][capacity][D], head-major
     void* vcache;
-    uint64_t* ll_xb;    // [H]   residual stream after attention
     uint64_t* ll_q;     // [H]   rotated queries
     uint64_t* ll_kv;    // [2*NKV*D] the new K and V rows
-    uint64_t* ll_attn;  // [H]   attention output
     uint64_t* ll_h;     // [I]   SiLU(gate)*up
     uint64_t* ll_part;    // [NH][nsplit][D+2] tagged attention split partials (m, l, o)
     float* logits;        // [V]
@@ -102,7 +102,7 @@ struct Params {
     Sync* sync;
     uint64_t* trace;  // [2][TRACE_MAX_PHASES][grid] ready/done ns, or null
     // shared memory layout (bytes)
-    int off_gu, off_down, off_qkv, off_o, off_att, off_xs, off_xq, off_gpart, off_xr, off_misc;
+    int off_gu, off_down, off_qkv, off_att, off_xs, off_xq, off_gpart, off_xr, off_misc;
     int xq_plane;      // bytes per fixed-point plane of a hidden-sized vector (>= Kh)
     int gpart_floats;  // floats per block-GEMV partial buffer (NW * max rows of a phase)
     int att_chunk_bytes;
@@ -112,11 +112,18 @@ struct Params {
     // [b*I/G, (b+1)*I/G) of W_down for all H rows, DW int8 per row (zero
     // padded), one down_slice-byte region per block and layer. Its products
     // with the block's own SiLU(gate)*up values are added, scaled per row, into
-    // the self-counting sum words dacc[parity][layer][Hp].
+    // the self-counting sum words of the layer.
     const uint8_t* down_cols;  // [L][G][down_slice]
     const float* down_scale;   // [L][H] per-row scales of W_down
-    uint64_t* dacc;            // [2][L][Hp]
-    int down_dw, down_slice, Hp, off_h;
+    // O projection as split-K over the heads: W_o's columns of head h for all
+    // H rows, o_dw int8 per row (zero past D), o_slice bytes per (layer, head),
+    // copied into the end of the attention buffers (offset wo_off) of the
+    // block that finishes head h (split 0).
+    const uint8_t* o_cols;     // [L][NH][o_slice]
+    const float* o_scale;      // [L][H] per-row scales of W_o
+    // Sum words [2 halves][L][2: O, down][Hp].
+    uint64_t* dacc;
+    int down_dw, down_slice, Hp, off_h, o_dw, o_slice, wo_off;
 };
 
 struct StepArgs {
@@ -541,14 +548,14 @@ static __device__ bool warp_stage_sum(const uint64_t* acc, unsigned expect, int 
     return okw;
 }
 
-// This block's share of the down projection (src/model.cpp:309, the matvec of
-// src/kernels.cpp:107-120 split over K): for every output row r < H,
+// A block's share of a projection split over K (the matvec of
+// src/kernels.cpp:107-120 by columns): for every output row r < H,
 // scale_r * sum_{j < DW} w[r][j] * h[j] with the block's column slice (H rows
-// of DW int8 in shared memory, zero past its columns) and its SiLU(gate)*up
-// values h (DW floats, zero past its columns), added into acc[r] by fire-and-
-// forget reductions. Thread t owns rows t + i*NT; scale[i] is row
+// of DW int8 in shared memory, zero past its columns) and its input values h
+// (DW floats, zero past its columns), added into the sum word acc[r] by a
+// fire-and-forget reduction. Thread t owns rows t + i*NT; scale[i] is row
 // t + i*NT's scale, loaded by the caller well ahead.
-static __device__ void down_partial(const uint8_t* slice, int DW, int H, const float* h, const float (&scale)[DOWN_RPT],
+static __device__ void slice_partial(const uint8_t* slice, int DW, int H, const float* h, const float (&scale)[DOWN_RPT],
                                     uint64_t* acc) {
 #pragma unroll
     for (int i = 0; i < DOWN_RPT; ++i) {
@@ -752,10 +759,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
 constexpr float LOG2E = 1.4426950408889634f;
 
 // DT: head_dim known at compile time (64), or 0 for any even head_dim <= 128.
+// The block's attention output (split 0 of a head, after the merges) is left
+// in misc[0..D). wo_src (split 0, when W_o's columns were not copied at the
+// start of the layer): copied to att + wo_off once the chunks are consumed.
 template <typename KV, int DT>
 __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPlan& ap, int l, uint32_t tag,
                                 uint8_t* att, uint64_t* mb_att, unsigned* issued, float* misc,
-                                const BlockState& st) {
+                                const uint8_t* wo_src, uint64_t* mb_wo, unsigned* wo_fills, const BlockState& st) {
     constexpr int MD = DT ? (DT + 31) / 32 : MAXD;  // 32-dim groups a lane covers
     const int D = DT ? DT : P.D, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int kvd = P.NKV * D, NB = P.att_bufs;
@@ -900,6 +910,12 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
     for (int k = 0; k < MD; ++k)
         if (lane + 32 * k < D) wpart[warp * (D + 2) + 2 + lane + 32 * k] = o[k];
     __syncthreads();
+    // Every warp is done with the chunk buffers: split 0 brings in W_o's
+    // columns of this head now unless they came at the start of the layer.
+    if (threadIdx.x == 0 && wo_src) {
+        fence_proxy_async();
+        fill_slot(att + P.wo_off, wo_src, (uint32_t)P.o_slice, mb_wo, wo_fills);
+    }
     const int split = blockIdx.x % A.nsplit;
     float own_m = 0.f, own_l = 0.f, own_acc = 0.f;  // split 0 of several: its own partial (threads j < D)
     if (threadIdx.x < ((D + 31) & ~31)) {
@@ -920,7 +936,7 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
         }
         if (j < D) {
             if (A.nsplit == 1 && P.world == 1) {
-                ll_store(P.ll_attn + (size_t)ap.h * D + j, acc / Lsum, tag);
+                misc[j] = acc / Lsum;
             } else if (split == 0) {
                 own_m = M;
                 own_l = Lsum;
@@ -989,7 +1005,7 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
                 den = fmaf(f, table[i * (D + 2) + 1], den);
             }
             if (P.world == 1) {
-                ll_store(P.ll_attn + (size_t)ap.h * D + j, num / den, tag);
+                misc[j] = num / den;
             } else {
                 own_m = Mx;
                 own_l = den;
@@ -1062,7 +1078,7 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
                 num = fmaf(f, tab[q * (D + 2) + 2 + j], num);
                 den = fmaf(f, tab[q * (D + 2) + 1], den);
             }
-            ll_store(P.ll_attn + (size_t)ap.h * D + j, num / den, tag);
+            misc[j] = num / den;
         }
     }
     return true;
@@ -1074,7 +1090,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     uint8_t* s_gu = sm + P.off_gu;
     uint8_t* s_down = sm + P.off_down;
     uint8_t* s_qkv = sm + P.off_qkv;
-    uint8_t* s_o = sm + P.off_o;
     uint8_t* s_att = sm + P.off_att;
     float* xf = reinterpret_cast<float*>(sm + P.off_xs);       // staged values before quantisation
     int8_t* xq = reinterpret_cast<int8_t*>(sm + P.off_xq);     // fixed-point planes of the staged vector
@@ -1082,14 +1097,15 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     float* gpart = reinterpret_cast<float*>(sm + P.off_gpart);  // block-GEMV partial sums, two buffers
     float* xr = reinterpret_cast<float*>(sm + P.off_xr);
     float* misc = reinterpret_cast<float*>(sm + P.off_misc);
-    // mbarriers: four weight slots, then the attention chunk ring (one arrival + bytes each).
+    // mbarriers: three weight slots and W_o's head columns, then the attention
+    // chunk ring (one arrival + bytes each).
     constexpr int MB_ATT = 4;
     constexpr int NMB = MB_ATT + ATT_MAX_BUFS;
     __shared__ __align__(8) uint64_t mb[NMB];
     uint64_t* mb_gu = mb + 0;
     uint64_t* mb_down = mb + 1;
     uint64_t* mb_qkv = mb + 2;
-    uint64_t* mb_o = mb + 3;
+    uint64_t* mb_wo = mb + 3;
     uint64_t* mb_att = mb + MB_ATT;
     __shared__ float s_cos[64], s_sin[64];
     __shared__ __align__(16) float red[2 * NW + 8];  // read as float4 in finish_stage
@@ -1104,12 +1120,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
 
     // This block's rows in every phase.
     const int qa = part_lo(b, G, P.qkv_pairs), qn = part_lo(b + 1, G, P.qkv_pairs) - qa;
-    const int oa = part_lo(b, G, H), on = part_lo(b + 1, G, H) - oa;
     const int ga = part_lo(b, G, I), gn = part_lo(b + 1, G, I) - ga;
     const int ha = part_lo(b, G, P.V), hn = part_lo(b + 1, G, P.V) - ha;
-    // This step's down sums (the other half is cleared at the end); a sum word
-    // is complete when every block that holds down columns has added to it.
-    uint64_t* const dacc = P.dacc + (size_t)A.par * P.L * P.Hp;
+    // This step's sum words (the other half is cleared at the end): per layer
+    // the O sums, complete when every head has added, then the down sums,
+    // complete when every block that holds down columns has added.
+    uint64_t* const dacc = P.dacc + (size_t)A.par * P.L * 2 * P.Hp;
+    auto osum = [&](int l) { return dacc + (size_t)(2 * l) * P.Hp; };
+    auto dsum = [&](int l) { return dacc + (size_t)(2 * l + 1) * P.Hp; };
     const unsigned dblocks = (unsigned)min(G, I);
     float* const s_h = reinterpret_cast<float*>(sm + P.off_h);  // [down_dw] this block's SiLU(gate)*up
 
@@ -1125,6 +1143,11 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         ap.nissued = min(ap.nchunks, max(0, (A.pos - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK));
         ap.bulk = ((size_t)D * sizeof(KV)) % 16 == 0;
     }
+    // Split 0 of a head finishes it and adds its O share. W_o's columns come at
+    // the start of a layer when this layer's chunks leave the buffers at
+    // wo_off free, else once the chunks are consumed.
+    const bool o_head = has_att && b % A.nsplit == 0;
+    const bool wo_early = o_head && (size_t)ap.nchunks * P.att_chunk_bytes <= (size_t)P.wo_off;
 
     if (tid == 0) {
         s_abort = 0;
@@ -1135,7 +1158,6 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         const LayerW& W = P.layers[0];
         if (qn) fill_slot(s_qkv, W.qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH, mb_qkv, s_fills + 2);
-        if (on) fill_slot(s_o, W.o + (size_t)oa * P.SH, (uint32_t)on * P.SH, mb_o, s_fills + 3);
         if (gn) fill_slot(s_gu, W.gu + (size_t)ga * 2 * P.SH, (uint32_t)gn * 2 * P.SH, mb_gu, s_fills + 0);
         if (gn) fill_slot(s_down, P.down_cols + (size_t)b * P.down_slice, (uint32_t)P.down_slice, mb_down, s_fills + 1);
     }
@@ -1167,14 +1189,16 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // RMSNorm gains of layer l (global memory; read while the words are polled).
         const float* in_norm = P.norms + (size_t)l * 2 * P.Kh;
         const float* post_norm = in_norm + P.Kh;
-        // Row scales of this layer's down projection for the rows this thread
-        // adds (tid + i*NT): loaded now, used after the gate/up phase.
-        float dscale[DOWN_RPT];
+        // Row scales of this layer's O and down projections for the rows this
+        // thread adds (tid + i*NT): loaded now, used after attention and gate/up.
+        float oscale[DOWN_RPT], dscale[DOWN_RPT];
 #pragma unroll
         for (int i = 0; i < DOWN_RPT; ++i) {
             const int r = tid + i * NT;
+            oscale[i] = o_head && r < H ? __ldg(P.o_scale + (size_t)l * H + r) : 0.f;
             dscale[i] = gn && r < H ? __ldg(P.down_scale + (size_t)l * H + r) : 0.f;
         }
+        const uint8_t* wo_src = o_head ? P.o_cols + ((size_t)l * P.NH + ap.h) * P.o_slice : nullptr;
 
         // HBM has slack during the last layer: start this block's first LM-head rows into L2.
         if (tid == 0 && A.head && l == P.L - 1 && hn)
@@ -1185,15 +1209,17 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
             fence_proxy_async();  // the previous layer read and wrote these buffers
             for (int c = 0; c < min(P.att_bufs, ap.nchunks); ++c)
                 att_issue<KV>(P, A, ap, l, c, s_att, mb_att, s_fills + MB_ATT);
+            if (wo_early) fill_slot(s_att + P.wo_off, wo_src, (uint32_t)P.o_slice, mb_wo, s_fills + 3);
         }
 
         // ---- QKV (src/model.cpp:276-302). x entering layer 0 is the embedding
         // row; entering layer l > 0 it is x_b of layer l-1 (xr) plus the down
         // sums of layer l-1, read once every block has added its share.
         // Each warp stages its own chunks of x (RMSNorm gain folded in) and
-        // starts its share of the GEMV; 1/rms scales the row totals.
+        // starts its share of the GEMV; 1/rms scales the row totals. Every
+        // block keeps x in xr: x_b = xr + O sums.
         trace_detail(P, l, 0, 0);
-        if (qn || on) {
+        {
             float wsc = 1.f;
             bool okw;
             if (l == 0) {
@@ -1201,11 +1227,16 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                 okw = warp_stage<2, true>(nullptr, er, row_scale(er, P.Kh), H, tag, xr, xf, xq, QP, nch_h, in_norm,
                                           s_ss, wsc, st);
             } else {
-                okw = warp_stage_sum(dacc + (size_t)(l - 1) * P.Hp, dblocks, H, xr, xf, xq, QP, nch_h, in_norm,
-                                     s_ss, wsc, st);
+                okw = warp_stage_sum(dsum(l - 1), dblocks, H, xr, xf, xq, QP, nch_h, in_norm, s_ss, wsc, st);
             }
             trace_detail(P, l, 0, 1);
-            if (qn) {
+            if (!qn) {
+                __syncthreads();
+                if (should_abort(st)) {
+                    ok = false;
+                    break;
+                }
+            } else {
                 trace_detail(P, l, 0, 2);
                 const bool okg = okw && warp_slot_wait(mb_qkv, (uint32_t)l & 1u, st);
                 trace_mark(P, 0, ph + 1);
@@ -1261,59 +1292,48 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         }
         trace_mark(P, 1, ph + 1);
 
-        // ---- ATTN over positions 0..pos (src/kernels.cpp:150-179)
+        // ---- ATTN over positions 0..pos (src/kernels.cpp:150-179), then the
+        // O projection (src/model.cpp:304) split over heads: the block that
+        // finishes head h adds W_o[:, h*D .. h*D+D) times the head's output into
+        // the O sums of layer l.
         if (has_att) {
             trace_mark(P, 0, ph + 2);
+            const uint8_t* late = wo_early ? nullptr : wo_src;
             const bool att_ok =
-                D == 64 ? attention_block<KV, 64>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, st)
-                        : attention_block<KV, 0>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, st);
+                D == 64 ? attention_block<KV, 64>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, late, mb_wo,
+                                                  s_fills + 3, st)
+                        : attention_block<KV, 0>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, late, mb_wo,
+                                                 s_fills + 3, st);
             if (!att_ok) {
                 ok = false;
                 break;
             }
         }
         trace_mark(P, 1, ph + 2);
-
-        // ---- O projection + residual (src/model.cpp:304-305)
-        if (on) {
-            trace_detail(P, l, 2, 0);
-            float wsc;
-            const bool okw = warp_stage<2, false>(P.ll_attn, nullptr, 0.f, H, tag, nullptr, xf, xq, QP, nch_h, nullptr,
-                                                  nullptr, wsc, st);
-            trace_detail(P, l, 2, 1);
-            const bool okg = okw && warp_slot_wait(mb_o, (uint32_t)l & 1u, st);
+        if (o_head) {
             trace_mark(P, 0, ph + 3);
-            trace_detail(P, l, 2, 2);
-            block_gemv<8, 2>(s_o, P.SH, on, nch_h, xq, QP, gpart, wsc, okg);
-            if (should_abort(st)) {
+            trace_detail(P, l, 2, 0);
+            if (tid >= D && tid < P.o_dw) misc[tid] = 0.f;  // the head's output, zero past D
+            if (!mbar_wait(mb_wo, (uint32_t)l & 1u, st)) {
                 ok = false;
                 break;
             }
-            if (tid < on) {
-                const int r = oa + tid;
-                ll_store(P.ll_xb + r, xr[r] + gemv_row(gpart, on, tid) * row_scale(s_o + (size_t)tid * P.SH, P.Kh), tag);
-            }
-            trace_detail(P, l, 2, 3);
-            __syncthreads();
-            trace_detail(P, l, 2, 4);
-            if (tid == 0 && l + 1 < P.L) {
-                fence_proxy_async();
-                fill_slot(s_o, P.layers[l + 1].o + (size_t)oa * P.SH, (uint32_t)on * P.SH, mb_o, s_fills + 3);
-            }
-            trace_detail(P, l, 2, 5);
+            trace_detail(P, l, 2, 1);
+            slice_partial(s_att + P.wo_off, P.o_dw, H, misc, oscale, osum(l));
+            trace_detail(P, l, 2, 2);
         }
         trace_mark(P, 1, ph + 3);
 
-        // ---- gate/up + SiLU (src/model.cpp:306-308), then this block's share of
-        // down (src/model.cpp:309-310): its columns of W_down times its own
+        // ---- gate/up + SiLU (src/model.cpp:305-308; x_b = x_a + O sums, kept raw
+        // in xr by every block), then this block's share of down
+        // (src/model.cpp:309-310): its columns of W_down times its own
         // SiLU(gate)*up values, for all H rows, into the down sums of layer l.
-        // Every block gathers x_b (kept raw in xr): x entering layer l+1, and the
-        // final norm's input, is xr plus those sums.
+        // x entering layer l+1, and the final norm's input, is xr plus those sums.
         {
             trace_detail(P, l, 3, 0);
             float wsc = 1.f;
-            const bool okw = warp_stage<2, true>(P.ll_xb, nullptr, 0.f, H, tag, xr, xf, xq, QP, nch_h, post_norm, s_ss,
-                                                 wsc, st);
+            const bool okw =
+                warp_stage_sum(osum(l), (unsigned)P.NH, H, xr, xf, xq, QP, nch_h, post_norm, s_ss, wsc, st);
             trace_detail(P, l, 3, 1);
             if (gn) {
                 trace_detail(P, l, 3, 2);
@@ -1365,7 +1385,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                     break;
                 }
                 trace_detail(P, l, 4, 1);
-                down_partial(s_down, P.down_dw, H, s_h, dscale, dacc + (size_t)l * P.Hp);
+                slice_partial(s_down, P.down_dw, H, s_h, dscale, dsum(l));
             }
             trace_detail(P, l, 4, 2);
             __syncthreads();  // the down slot is consumed
@@ -1387,7 +1407,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         int best_i = 0x7fffffff;
         if (hn) {
             Staged sf{1.f, 1.f};
-            if (!stage_sum(dacc + (size_t)(P.L - 1) * P.Hp, dblocks, H, nch_h, xr, xf, xq, QP,
+            if (!stage_sum(dsum(P.L - 1), dblocks, H, nch_h, xr, xf, xq, QP,
                            P.norms + (size_t)P.L * 2 * P.Kh, red, P.eps, sf, st))
                 ok = false;
             const float inv = sf.inv * sf.scale;
@@ -1503,14 +1523,13 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
         // Warm L2 with this block's first-layer rows for the next token.
         const LayerW& W0 = P.layers[0];
         if (qn) prefetch_l2(W0.qkv + (size_t)qa * 2 * P.SH, (uint32_t)qn * 2 * P.SH);
-        if (on) prefetch_l2(W0.o + (size_t)oa * P.SH, (uint32_t)on * P.SH);
     }
 
     // Clear the other half of the down sums for the next step (this step's
     // half is cleared by the next one). Done on abort too.
     {
-        uint64_t* z = P.dacc + (size_t)(A.par ^ 1) * P.L * P.Hp;
-        const int n = P.L * P.Hp;
+        uint64_t* z = P.dacc + (size_t)(A.par ^ 1) * P.L * 2 * P.Hp;
+        const int n = P.L * 2 * P.Hp;
         for (int i = part_lo(b, G, n) + tid; i < part_lo(b + 1, G, n); i += NT) z[i] = 0ull;
     }
 
