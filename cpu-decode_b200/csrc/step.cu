@@ -70,6 +70,11 @@ struct dcb_engine {
     uint64_t launches = 0;
     int par = 0;  // half of the down sums the next step uses
     int split_min = 64;   // positions per attention split, at least (one chunk)
+    // Group attention units (one block per KV group and split, all its query
+    // heads at once): allowed for this model (gqa_ok), used from group_min
+    // attended positions on, splits of at least group_split_min positions.
+    bool gqa_ok = false;
+    int group_min = 1024, group_split_min = 64;
 
     ~dcb_engine() {
         cudaSetDevice(device);
@@ -148,9 +153,26 @@ int validate(const dcb_model_desc* m) {
 }
 
 // KV split: one block per (query head, split), at most one unit per block;
-// each split covers at least split_min positions (a multiple of 64).
-void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len) {
+// each split covers at least split_min positions (a multiple of 64). From
+// group_min positions on (one GPU, head_dim 64), one block per (KV group,
+// split) instead, with at least one split per query head of the group (the
+// splits' blocks j < heads per group merge head j).
+void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len, int* group) {
     const int chunks = ceil_div(length, ATT_CHUNK);
+    *group = 0;
+    if (e->gqa_ok && e->P.world == 1 && length >= e->group_min) {
+        const int hpg = e->NH / e->NKV;
+        const int table_g = std::min(GQA_MERGE_MAX, e->P.wo_off / (int)((e->D + 2) * sizeof(float)));
+        const int n = std::max(1, std::min({ceil_div(length, e->group_split_min), e->grid / e->NKV, table_g}));
+        const int len = ceil_div(chunks, n) * ATT_CHUNK;
+        const int ns = ceil_div(length, len);
+        if (ns >= hpg) {
+            *group = 1;
+            *nsplit = ns;
+            *split_len = len;
+            return;
+        }
+    }
     // Split 0 gathers the other splits' (D+2)-float partials into the chunk buffers.
     const int table_max = 1 + e->P.wo_off / (int)((e->D + 2) * sizeof(float));
     const int n = std::max(1, std::min({ceil_div(length, e->split_min), e->grid / e->NH, table_max}));
@@ -166,7 +188,7 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
     A.pos = (int)e->pos;
     A.head = head;
     A.argmax_dev = argmax_dev;
-    choose_split(e, (int)e->attended(e->pos), &A.nsplit, &A.split_len);
+    choose_split(e, (int)e->attended(e->pos), &A.nsplit, &A.split_len, &A.group);
     if (++e->seq >= (1u << 24)) e->seq = 1;  // tags are seq << 8 | layer
     A.seq = e->seq;
     A.par = e->par;
@@ -453,6 +475,19 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     P.off_xs = (int)off;
     P.trace_layer = std::min(5, e->L - 1);
     if (const char* v = std::getenv("DCB_SPLIT_MIN")) e->split_min = std::max(ATT_CHUNK, std::atoi(v) / ATT_CHUNK * ATT_CHUNK);
+    if (const char* v = std::getenv("DCB_GROUP_MIN")) e->group_min = std::max(1, std::atoi(v));
+    if (const char* v = std::getenv("DCB_GROUP_SPLIT_MIN"))
+        e->group_split_min = std::max(ATT_CHUNK, std::atoi(v) / ATT_CHUNK * ATT_CHUNK);
+    // Group units stage q in the staged-vector buffer and the scores in the
+    // GEMV partial buffers (both idle during attention).
+    {
+        const int hpg = e->NH / e->NKV;
+        e->gqa_ok = D == 64 && hpg <= GQA_MAX && P.Kh >= hpg * D &&
+                    2 * P.gpart_floats >= GQA_MAX * GQA_PASS * ATT_CHUNK;
+        // Chunks per pass: leave at least one buffer loading while a pass computes.
+        P.gqa_pass = std::max(1, std::min(GQA_PASS, P.att_bufs - 1));
+        if (const char* v = std::getenv("DCB_GQA_PASS")) P.gqa_pass = std::max(1, std::min({GQA_PASS, P.att_bufs, std::atoi(v)}));
+    }
     off += xs_bytes;
     P.off_xq = (int)off;
     off += xq_bytes;

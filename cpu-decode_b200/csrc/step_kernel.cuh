@@ -54,6 +54,9 @@ constexpr int HEAD_MAXC = 2;        // 16-byte chunks per lane of a hidden-size 
 constexpr int TRACE_MAX_PHASES = 512;
 constexpr int DOWN_RPT = 2;    // down output rows per thread (H <= DOWN_RPT * NT)
 constexpr int MAXD = 4;        // head_dim <= 128: lane owns dims lane + 32k
+constexpr int GQA_MAX = 8;     // query heads per KV group of a group attention unit, at most
+constexpr int GQA_PASS = 3;    // resident chunks a group attention unit takes per pass, at most
+constexpr int GQA_MERGE_MAX = 160;  // splits a group unit's merge weighs (misc holds the weights)
 
 // Per-layer weights, packed rows: [K int8 | FP32 scale | FP32 bias | 8 pad].
 struct LayerW {
@@ -124,6 +127,7 @@ struct Params {
     // Sum words [2 halves][L][2: O, down][Hp].
     uint64_t* dacc;
     int down_dw, down_slice, Hp, off_h, o_dw, o_slice, wo_off;
+    int gqa_pass;  // resident chunks a group attention unit takes per pass (<= GQA_PASS, < att_bufs when possible)
 };
 
 struct StepArgs {
@@ -137,6 +141,7 @@ struct StepArgs {
     unsigned seq;
     float* host_logits;  // mapped pinned host memory the LM head also writes, or null
     int par;             // which half of dacc this step sums into (the other half is cleared for the next)
+    int group;           // attention units are (KV group, split) instead of (query head, split)
 };
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
@@ -1084,6 +1089,302 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
     return true;
 }
 
+
+// ---- attention unit of a whole KV group (long contexts, head_dim 64) -------------
+// Block (g, split) reads each cached chunk of its range once for all hpg query
+// heads of KV group g (hpg <= GQA_MAX), in passes of up to GQA_PASS resident
+// chunks:
+//   A: a warp takes 32 positions and 4 of the heads; lane = position, its
+//      64-dim dot products walk the K row in a lane-rotated order (no bank
+//      conflicts); q is pre-scaled by log2(e)/8 in shared memory (qt);
+//   B: warp h turns head h's scores of the pass into 2^(s - m) with the running
+//      max m and adds them to the running sum;
+//   C: thread (h, d) rescales and accumulates o_h[d] += p_t * V[t][d].
+// The new row (position pos) is first written into its chunk buffer, so every
+// position is read the same way. Each split publishes (m, l, o) of every head
+// as tagged words; block (g, j), j < hpg, then merges head g*hpg + j over all
+// splits in split order and leaves the result in misc[0..64). stile: the
+// [GQA_MAX][GQA_PASS*64] score tile.
+template <typename KV>
+__device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPlan& ap, int l, uint32_t tag,
+                                uint8_t* att, uint64_t* mb_att, unsigned* issued, float* misc, float* qt,
+                                float* stile, const uint8_t* wo_src, uint64_t* mb_wo, unsigned* wo_fills,
+                                const BlockState& st) {
+    constexpr int D = 64, SROW = GQA_PASS * ATT_CHUNK;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
+    const int hpg = P.NH / P.NKV, NB = P.att_bufs, split = blockIdx.x % A.nsplit;
+    float* s_new = misc + 128;   // [2][D] new K and V rows (rounded to KV)
+    float* hm = misc + 384;      // [GQA_MAX] running max per head
+    float* hl = hm + GQA_MAX;    // running sum
+    float* ha = hl + GQA_MAX;    // rescale of the current pass
+    trace_detail(P, l, 1, 0);
+    {
+        // q of the group's heads and the new K/V rows of the group: one round trip.
+        const int nq = hpg * D, nwords = nq + 2 * D;
+        uint64_t w[2];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = tid + k * NT;
+            w[k] = 0;
+            if (i < nwords) {
+                w[k] = ll_load(i < nq ? P.ll_q + (size_t)ap.g * nq + i
+                                      : P.ll_kv + (i < nq + D ? 0 : P.NKV * D) + (size_t)ap.g * D + (i - nq) % D);
+                pending |= 1u << k;
+            }
+        }
+        uint64_t t0 = 0;
+        unsigned rounds = 0;
+        while (true) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) pending &= ~(1u << k);
+            if (!pending) break;
+            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                if ((pending >> k) & 1u) {
+                    const int i = tid + k * NT;
+                    w[k] = ll_load(i < nq ? P.ll_q + (size_t)ap.g * nq + i
+                                          : P.ll_kv + (i < nq + D ? 0 : P.NKV * D) + (size_t)ap.g * D + (i - nq) % D);
+                }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = tid + k * NT;
+            if (i < nwords) {
+                const float v = __uint_as_float((uint32_t)w[k]);
+                if (i < nq) qt[i] = v * (LOG2E / 8.0f);
+                else s_new[i - nq] = round_to(v, KV());
+            }
+        }
+        if (tid < GQA_MAX) {
+            hm[tid] = -INFINITY;
+            hl[tid] = 0.f;
+        }
+        __syncthreads();
+        if (should_abort(st)) return false;
+    }
+    trace_detail(P, l, 1, 1);
+    float o0 = 0.f, o1 = 0.f;  // thread (h, d) = (tid / 64, tid % 64), tid < hpg * 64: even and odd positions
+    const int nissued = ap.nissued;
+    const int pass = P.gqa_pass;
+    for (int c = 0; c < ap.nchunks; c += pass) {
+        const int cb = min(pass, ap.nchunks - c);
+        __syncthreads();  // the previous pass is done with the buffers and the score tile
+        for (int u = 0; u < cb; ++u) {
+            const int cu = c + u, c0 = ap.t0 + cu * ATT_CHUNK;
+            const int ncache = max(0, min(min(ATT_CHUNK, ap.t1 - c0), A.pos - c0));
+            if (ncache <= 0) continue;
+            const int buf = cu % NB;
+            const int per_layer = (nissued - buf + NB - 1) / NB;  // fills of this buffer per layer
+            if (!mbar_wait(mb_att + buf, (uint32_t)(l * per_layer + cu / NB) & 1u, st)) return false;
+        }
+        trace_detail(P, l, 1, c == 0 ? 2 : 4);
+        {
+            // The new row into its chunk buffer, where the cached rows end.
+            const int pc = (A.pos - ap.t0) / ATT_CHUNK - c;
+            if (A.pos >= ap.t0 && A.pos < ap.t1 && pc >= 0 && pc < cb && tid < 2 * D) {
+                KV* kb = reinterpret_cast<KV*>(att + (size_t)((c + pc) % NB) * P.att_chunk_bytes);
+                const int t = (A.pos - ap.t0) % ATT_CHUNK;
+                kv_store(kb + (tid < D ? 0 : (size_t)ATT_CHUNK * D) + (size_t)t * D + tid % D, s_new[tid]);
+            }
+        }
+        __syncthreads();
+        // A: scores of the pass into the tile (-inf past a chunk's last position).
+        // Warp w takes positions 4w..4w+3 of every chunk of the pass: the 8 lanes
+        // of group grp own dims 8*part .. 8*part+7 of position 4w+grp, read them
+        // once, and for each head add q_h over those dims and reduce over the 8
+        // lanes (q is read from shared memory, the same 8 dims by 4 lanes).
+        {
+            const int grp = lane >> 3, part = lane & 7, t = warp * 4 + grp;
+            for (int u = 0; u < cb; ++u) {
+                const int c0 = ap.t0 + (c + u) * ATT_CHUNK;
+                const int n = min(ATT_CHUNK, ap.t1 - c0);
+                float kk[8];
+                if (t < n) {
+                    const KV* kr = reinterpret_cast<const KV*>(att + (size_t)((c + u) % NB) * P.att_chunk_bytes) +
+                                   (size_t)t * D + 8 * part;
+                    float a[4], bq[4];
+                    load4(kr, a);
+                    load4(kr + 4, bq);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        kk[e] = a[e];
+                        kk[4 + e] = bq[e];
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) kk[e] = 0.f;
+                }
+                for (int h = 0; h < hpg; ++h) {
+                    const float4 q0 = *reinterpret_cast<const float4*>(qt + h * D + 8 * part);
+                    const float4 q1 = *reinterpret_cast<const float4*>(qt + h * D + 8 * part + 4);
+                    float sc = q0.x * kk[0];
+                    sc = fmaf(q0.y, kk[1], sc);
+                    sc = fmaf(q0.z, kk[2], sc);
+                    sc = fmaf(q0.w, kk[3], sc);
+                    sc = fmaf(q1.x, kk[4], sc);
+                    sc = fmaf(q1.y, kk[5], sc);
+                    sc = fmaf(q1.z, kk[6], sc);
+                    sc = fmaf(q1.w, kk[7], sc);
+                    sc += __shfl_xor_sync(FULL, sc, 4);
+                    sc += __shfl_xor_sync(FULL, sc, 2);
+                    sc += __shfl_xor_sync(FULL, sc, 1);
+                    if (part == 0) stile[h * SROW + u * ATT_CHUNK + t] = t < n ? sc : -INFINITY;
+                }
+            }
+        }
+        __syncthreads();
+        // B: per head, 2^(s - m) with the running max, and the running sum.
+        if (warp < hpg) {
+            float* row = stile + warp * SROW;
+            const int np = cb * ATT_CHUNK;
+            float mx = -INFINITY;
+            for (int q = lane; q < np; q += 32) mx = fmaxf(mx, row[q]);
+            mx = warp_max(mx);
+            const float mo = hm[warp], mn = fmaxf(mo, mx);
+            float sum = 0.f;
+            for (int q = lane; q < np; q += 32) {
+                const float e = ex2_approx(row[q] - mn);
+                row[q] = e;
+                sum += e;
+            }
+            sum = warp_sum(sum);
+            if (lane == 0) {
+                const float al = ex2_approx(mo - mn);
+                ha[warp] = al;
+                hl[warp] = fmaf(hl[warp], al, sum);
+                hm[warp] = mn;
+            }
+        }
+        __syncthreads();
+        // C: o_h[d] += p_t * V[t][d] over the pass's positions.
+        if (tid < hpg * D) {
+            const int h = tid >> 6, d = tid & 63;
+            o0 *= ha[h];
+            o1 *= ha[h];
+            const float* prow = stile + h * SROW;
+            for (int u = 0; u < cb; ++u) {
+                const int c0 = ap.t0 + (c + u) * ATT_CHUNK;
+                const int n = min(ATT_CHUNK, ap.t1 - c0);
+                const KV* vb = reinterpret_cast<const KV*>(att + (size_t)((c + u) % NB) * P.att_chunk_bytes) +
+                               (size_t)ATT_CHUNK * D + d;
+                const float* pu = prow + u * ATT_CHUNK;
+                int t = 0;
+#pragma unroll 2
+                for (; t + 4 <= n; t += 4) {
+                    const float4 pv = *reinterpret_cast<const float4*>(pu + t);
+                    o0 = fmaf(pv.x, kv_to_float(vb[(size_t)t * D]), o0);
+                    o1 = fmaf(pv.y, kv_to_float(vb[(size_t)(t + 1) * D]), o1);
+                    o0 = fmaf(pv.z, kv_to_float(vb[(size_t)(t + 2) * D]), o0);
+                    o1 = fmaf(pv.w, kv_to_float(vb[(size_t)(t + 3) * D]), o1);
+                }
+                for (; t < n; ++t) o0 = fmaf(pu[t], kv_to_float(vb[(size_t)t * D]), o0);
+            }
+        }
+        trace_detail(P, l, 1, c == 0 ? 3 : 5);
+        if (c + NB < ap.nchunks) {
+            __syncthreads();  // the pass's buffers are consumed by every warp
+            if (tid == 0)
+                for (int u = 0; u < cb; ++u)
+                    if (c + u + NB < ap.nchunks) {
+                        if (u == 0) fence_proxy_async();
+                        att_issue<KV>(P, A, ap, l, c + u + NB, att, mb_att, issued);
+                    }
+        }
+    }
+    // (m, l, unnormalised o) of every head of the group for this split.
+    if (tid < hpg * D) {
+        const int h = tid >> 6, d = tid & 63;
+        uint64_t* pw = P.ll_part + ((size_t)(ap.g * hpg + h) * A.nsplit + split) * (D + 2);
+        ll_store(pw + 2 + d, o0 + o1, tag);
+        if (d == 0) {
+            ll_store(pw, hm[h], tag);
+            ll_store(pw + 1, hl[h], tag);
+        }
+    }
+    trace_detail(P, l, 1, 6);
+    if (split >= hpg) return true;
+    // Block (g, j) merges head g*hpg + j over all splits: W_o's columns of that
+    // head come into the end of the chunk buffers now (unless they came at the
+    // start of the layer), the splits' partials into their start.
+    __syncthreads();
+    if (tid == 0 && wo_src) {
+        fence_proxy_async();
+        fill_slot(att + P.wo_off, wo_src, (uint32_t)P.o_slice, mb_wo, wo_fills);
+    }
+    {
+        const int nwords = A.nsplit * (D + 2);
+        const uint64_t* src = P.ll_part + (size_t)(ap.g * hpg + split) * A.nsplit * (D + 2);
+        float* table = reinterpret_cast<float*>(att);
+        constexpr int WT = 4;
+        for (int base = 0; base < nwords; base += WT * NT) {
+            uint64_t w[WT];
+            unsigned pending = 0;
+#pragma unroll
+            for (int k = 0; k < WT; ++k) {
+                const int i = base + tid + k * NT;
+                if (i < nwords) {
+                    w[k] = ll_load(src + i);
+                    pending |= 1u << k;
+                }
+            }
+            uint64_t t0 = 0;
+            unsigned rounds = 0;
+            while (true) {
+#pragma unroll
+                for (int k = 0; k < WT; ++k)
+                    if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
+                        table[base + tid + k * NT] = __uint_as_float((uint32_t)w[k]);
+                        pending &= ~(1u << k);
+                    }
+                if (!pending) break;
+                if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+#pragma unroll
+                for (int k = 0; k < WT; ++k)
+                    if ((pending >> k) & 1u) w[k] = ll_load(src + base + tid + k * NT);
+            }
+        }
+        __syncthreads();
+        if (should_abort(st)) return false;
+        // Merge in split order, spread over the block: the largest m (warp 0),
+        // each split's weight 2^(m_s - M) once, then thread (d, q) sums splits
+        // q, q + 8, ... of dimension d (and q's share of the weights' sum), and
+        // thread d adds the 8 shares in order.
+        float* wgt = misc + 384;           // [nsplit <= GQA_MERGE_MAX] weights
+        float* part = wgt + GQA_MERGE_MAX; // [8][D + 1] shares of num (D) and den (1)
+        if (warp == 0) {
+            float mx = -INFINITY;
+            for (int i = lane; i < A.nsplit; i += 32) mx = fmaxf(mx, table[i * (D + 2)]);
+            mx = warp_max(mx);
+            for (int i = lane; i < A.nsplit; i += 32) wgt[i] = ex2_approx(table[i * (D + 2)] - mx);
+        }
+        __syncthreads();
+        {
+            const int d = tid & 63, q = tid >> 6;  // q < 8
+            float num = 0.f, den = 0.f;
+            for (int i = q; i < A.nsplit; i += 8) {
+                num = fmaf(wgt[i], table[i * (D + 2) + 2 + d], num);
+                if (d == 0) den = fmaf(wgt[i], table[i * (D + 2) + 1], den);
+            }
+            part[q * (D + 1) + d] = num;
+            if (d == 0) part[q * (D + 1) + D] = den;
+        }
+        __syncthreads();
+        if (tid < D) {
+            float num = 0.f, den = 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                num += part[q * (D + 1) + tid];
+                den += part[q * (D + 1) + D];
+            }
+            misc[tid] = num / den;
+        }
+    }
+    return true;
+}
+
 template <typename KV>
 __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, const StepArgs A) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -1132,11 +1433,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     float* const s_h = reinterpret_cast<float*>(sm + P.off_h);  // [down_dw] this block's SiLU(gate)*up
 
     // This block's attention unit (at most one).
+    // Units are (query head, split), or (KV group, split) when A.group.
     AttnPlan ap{};
-    const bool has_att = b < P.NH * A.nsplit;
+    const int hpg = P.NH / P.NKV;
+    const bool has_att = b < (A.group ? P.NKV : P.NH) * A.nsplit;
     if (has_att) {
-        ap.h = b / A.nsplit;
-        ap.g = ap.h / (P.NH / P.NKV);
+        const int unit = b / A.nsplit, usplit = b % A.nsplit;
+        ap.g = A.group ? unit : unit / hpg;
+        ap.h = A.group ? ap.g * hpg + min(usplit, hpg - 1) : unit;
         ap.t0 = P.kv_base + (b % A.nsplit) * A.split_len;
         ap.t1 = min(min(A.pos + 1, P.kv_end), ap.t0 + A.split_len);
         ap.nchunks = (ap.t1 - ap.t0 + ATT_CHUNK - 1) / ATT_CHUNK;
@@ -1146,7 +1450,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     // Split 0 of a head finishes it and adds its O share. W_o's columns come at
     // the start of a layer when this layer's chunks leave the buffers at
     // wo_off free, else once the chunks are consumed.
-    const bool o_head = has_att && b % A.nsplit == 0;
+    const bool o_head = has_att && (A.group ? b % A.nsplit < hpg : b % A.nsplit == 0);
     const bool wo_early = o_head && (size_t)ap.nchunks * P.att_chunk_bytes <= (size_t)P.wo_off;
 
     if (tid == 0) {
@@ -1300,10 +1604,12 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
             trace_mark(P, 0, ph + 2);
             const uint8_t* late = wo_early ? nullptr : wo_src;
             const bool att_ok =
-                D == 64 ? attention_block<KV, 64>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, late, mb_wo,
-                                                  s_fills + 3, st)
-                        : attention_block<KV, 0>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, late, mb_wo,
-                                                 s_fills + 3, st);
+                A.group   ? attention_group<KV>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, xf, gpart, late,
+                                                mb_wo, s_fills + 3, st)
+                : D == 64 ? attention_block<KV, 64>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, late,
+                                                    mb_wo, s_fills + 3, st)
+                          : attention_block<KV, 0>(P, A, ap, l, tag, s_att, mb_att, s_fills + MB_ATT, misc, late, mb_wo,
+                                                   s_fills + 3, st);
             if (!att_ok) {
                 ok = false;
                 break;
