@@ -214,12 +214,17 @@ def main() -> None:
     ap.add_argument("--ncu-ctx", type=int, default=8192, help="largest context of the batched profiling case")
     ap.add_argument("--ncu-case", action="store_true",
                     help="the profiling case: KV rows 0..127 written from the host, then 5 decode launches")
+    ap.add_argument("--ncu-long", type=int, default=0, metavar="CTX",
+                    help="the long-context profiling case: KV rows 0..CTX-1 pre-filled, then 5 decode launches")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
         return
     if args.ncu_case:
         ncu_case()
+        return
+    if args.ncu_long:
+        ncu_case(args.ncu_long)
         return
     if args.ncu_batch:
         ncu_batch_case(args.ncu_batch, max(1, args.steps), args.ncu_ctx)
@@ -373,29 +378,30 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def ncu_case() -> None:
-    """Five decode launches at context 128 with few launches before them (the
-    KV rows come from the host, no prefill): launches 4 and 5 are the ones a
-    profiler captures (`-k regex:decode_step -s 3 -c 2`)."""
+def ncu_case(ctx: int = CONTEXT) -> None:
+    """Five decode launches at context `ctx` (128 by default) with few launches
+    before them (the KV rows come from the host as seeded N(0,1) values, no
+    prefill): launches 4 and 5 are the ones a profiler captures
+    (`-k regex:decode_step -s 3 -c 2`)."""
     import torch
     dcb = load_package()
     import cpu_decode_b200.synthetic as syn
-    model = ensure_model()
+    model = ensure_model() if ctx <= CONTEXT else _long_model_dir(ensure_model())
     d = syn.QWEN05
-    eng = dcb.Engine(model, CONTEXT + 8)
+    eng = dcb.Engine(model, ctx + 8)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     eng.set_stream(stream.cuda_stream)
-    rng = np.random.default_rng(128)
+    rng = np.random.default_rng(ctx)
     for l in range(d.layers):
-        eng.kv_write(l, 0, rng.standard_normal((CONTEXT, d.kv_dim), dtype=np.float32),
-                     rng.standard_normal((CONTEXT, d.kv_dim), dtype=np.float32))
-    eng.set_position(CONTEXT)
+        eng.kv_write(l, 0, rng.standard_normal((ctx, d.kv_dim), dtype=np.float32),
+                     rng.standard_normal((ctx, d.kv_dim), dtype=np.float32))
+    eng.set_position(ctx)
     tok = torch.full((1,), prompt_tokens()[-1], dtype=torch.int32, device="cuda")
     for _ in range(5):
         eng.step_async(token_dev=tok.data_ptr(), head=True, argmax_dev=tok.data_ptr())
     eng.synchronize()
-    print(json.dumps({"ncu_case": "decode_step_kernel ctx 128", "launches": eng.launch_count,
+    print(json.dumps({"ncu_case": f"decode_step_kernel ctx {ctx}", "launches": eng.launch_count,
                       "last_token": int(tok.item())}))
     eng.close()
 

@@ -1193,9 +1193,10 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
         __syncthreads();
         // A: scores of the pass into the tile (-inf past a chunk's last position).
         // Warp w takes positions 4w..4w+3 of every chunk of the pass: the 8 lanes
-        // of group grp own dims 8*part .. 8*part+7 of position 4w+grp, read them
+        // of group grp own dims 4*part .. +3 and 32 + 4*part .. +3 of position
+        // 4w+grp (8 lanes read 128 contiguous bytes: no bank conflicts), read them
         // once, and for each head add q_h over those dims and reduce over the 8
-        // lanes (q is read from shared memory, the same 8 dims by 4 lanes).
+        // lanes (q is read from shared memory, the same dims by 4 lanes).
         {
             const int grp = lane >> 3, part = lane & 7, t = warp * 4 + grp;
             for (int u = 0; u < cb; ++u) {
@@ -1204,10 +1205,10 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
                 float kk[8];
                 if (t < n) {
                     const KV* kr = reinterpret_cast<const KV*>(att + (size_t)((c + u) % NB) * P.att_chunk_bytes) +
-                                   (size_t)t * D + 8 * part;
+                                   (size_t)t * D + 4 * part;
                     float a[4], bq[4];
                     load4(kr, a);
-                    load4(kr + 4, bq);
+                    load4(kr + 32, bq);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         kk[e] = a[e];
@@ -1218,8 +1219,8 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
                     for (int e = 0; e < 8; ++e) kk[e] = 0.f;
                 }
                 for (int h = 0; h < hpg; ++h) {
-                    const float4 q0 = *reinterpret_cast<const float4*>(qt + h * D + 8 * part);
-                    const float4 q1 = *reinterpret_cast<const float4*>(qt + h * D + 8 * part + 4);
+                    const float4 q0 = *reinterpret_cast<const float4*>(qt + h * D + 4 * part);
+                    const float4 q1 = *reinterpret_cast<const float4*>(qt + h * D + 32 + 4 * part);
                     float sc = q0.x * kk[0];
                     sc = fmaf(q0.y, kk[1], sc);
                     sc = fmaf(q0.z, kk[2], sc);
