@@ -154,13 +154,14 @@ int validate(const dcb_model_desc* m) {
 
 // KV split: one block per (query head, split), at most one unit per block;
 // each split covers at least split_min positions (a multiple of 64). From
-// group_min positions on (one GPU, head_dim 64), one block per (KV group,
-// split) instead, with at least one split per query head of the group (the
-// splits' blocks j < heads per group merge head j).
+// group_min positions on (head_dim 64), one block per (KV group, split)
+// instead, with at least one split per query head of the group (the splits'
+// blocks j < heads per group merge head j). Either way each head's merged
+// result is then exchanged with the other GPUs of a KV split the same way.
 void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len, int* group) {
     const int chunks = ceil_div(length, ATT_CHUNK);
     *group = 0;
-    if (e->gqa_ok && e->P.world == 1 && length >= e->group_min) {
+    if (e->gqa_ok && length >= e->group_min) {
         const int hpg = e->NH / e->NKV;
         const int table_g = std::min(GQA_MERGE_MAX, e->P.wo_off / (int)((e->D + 2) * sizeof(float)));
         const int n = std::max(1, std::min({ceil_div(length, e->group_split_min), e->grid / e->NKV, table_g}));
@@ -454,7 +455,9 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     }
     const size_t xs_bytes = round_up((size_t)P.Kh * sizeof(float), 128);
     const size_t xq_bytes = round_up(3 * (size_t)P.xq_plane, 128);
-    const size_t gpart_bytes = round_up(2 * (size_t)P.gpart_floats * sizeof(float), 128);
+    // The GEMV partial buffers also hold a group attention unit's score tile.
+    const size_t gqa_tile = D == 64 ? (size_t)GQA_MAX * GQA_PASS * ATT_CHUNK * sizeof(float) : 0;
+    const size_t gpart_bytes = round_up(std::max(2 * (size_t)P.gpart_floats * sizeof(float), gqa_tile), 128);
     const size_t xr_bytes = round_up((size_t)P.Kh * sizeof(float), 128);
     const size_t misc_bytes = round_up((size_t)(384 + NW * (D + 2)) * sizeof(float), 128);
     const size_t h_bytes = round_up((size_t)P.down_dw * sizeof(float), 128);
@@ -482,8 +485,7 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     // GEMV partial buffers (both idle during attention).
     {
         const int hpg = e->NH / e->NKV;
-        e->gqa_ok = D == 64 && hpg <= GQA_MAX && P.Kh >= hpg * D &&
-                    2 * P.gpart_floats >= GQA_MAX * GQA_PASS * ATT_CHUNK;
+        e->gqa_ok = D == 64 && hpg <= GQA_MAX && P.Kh >= hpg * D;
         // Chunks per pass: leave at least one buffer loading while a pass computes.
         P.gqa_pass = std::max(1, std::min(GQA_PASS, P.att_bufs - 1));
         if (const char* v = std::getenv("DCB_GQA_PASS")) P.gqa_pass = std::max(1, std::min({GQA_PASS, P.att_bufs, std::atoi(v)}));

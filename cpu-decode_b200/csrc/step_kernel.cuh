@@ -763,6 +763,79 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // with ex2, so that exp(s - m) = 2^((s - m) * log2(e)).
 constexpr float LOG2E = 1.4426950408889634f;
 
+// KV sequence split over GPUs: this GPU's (m, l, o) of head h (threads
+// j < D hold own_m, own_l and dimension j of own_acc) goes to every rank's
+// exchange buffer (system-scope tagged words over NVLink); then all ranks'
+// partials are polled from the local buffer and merged in rank order, so every
+// GPU ends with the same attention output, left in misc[0..D). Slots alternate
+// with the global layer count: a rank one layer ahead writes the other slot.
+// The start of att is used as scratch.
+static __device__ bool exchange_head(const Params& P, const StepArgs& A, int h, int D, int l, uint32_t tag, uint8_t* att,
+                                     float own_m, float own_l, float own_acc, float* misc, const BlockState& st) {
+    {
+        __syncthreads();  // the split tables above are consumed
+        float* own = reinterpret_cast<float*>(att);  // [D+2]: m, l, o
+        float* tab = own + (D + 2);                   // [world][D+2]
+        if ((int)threadIdx.x < D) {
+            own[2 + threadIdx.x] = own_acc;
+            if (threadIdx.x == 0) {
+                own[0] = own_m;
+                own[1] = own_l;
+            }
+        }
+        __syncthreads();
+        const int slot = (int)((A.seq * (unsigned)P.L + (unsigned)l) & 1u);
+        const int nw = P.world * (D + 2);
+        for (int i = threadIdx.x; i < nw; i += NT) {
+            const int q = i / (D + 2), k = i - q * (D + 2);
+            ll_store_sys(P.peers[q] + (((size_t)slot * P.NH + h) * P.world + P.rank) * (D + 2) + k, own[k], tag);
+        }
+        const uint64_t* src = P.exch + ((size_t)slot * P.NH + h) * P.world * (D + 2);
+        constexpr int WT = 4;  // world * (D+2) <= 8 * 130 < 4 * NT
+        uint64_t w[WT];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < WT; ++k) {
+            const int i = threadIdx.x + k * NT;
+            if (i < nw) {
+                w[k] = ll_load_sys(src + i);
+                pending |= 1u << k;
+            }
+        }
+        uint64_t t0 = 0;
+        unsigned rounds = 0;
+        while (pending) {
+#pragma unroll
+            for (int k = 0; k < WT; ++k)
+                if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
+                    tab[threadIdx.x + k * NT] = __uint_as_float((uint32_t)w[k]);
+                    pending &= ~(1u << k);
+                }
+            if (!pending) break;
+            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
+#pragma unroll
+            for (int k = 0; k < WT; ++k)
+                if ((pending >> k) & 1u) w[k] = ll_load_sys(src + threadIdx.x + k * NT);
+        }
+        __syncthreads();
+        if (should_abort(st)) return false;
+        if ((int)threadIdx.x < D) {
+            const int j = threadIdx.x;
+            float Mx = -INFINITY;
+            for (int q = 0; q < P.world; ++q) Mx = fmaxf(Mx, tab[q * (D + 2)]);
+            float num = 0.f, den = 0.f;
+            for (int q = 0; q < P.world; ++q) {
+                const float mq = tab[q * (D + 2)];
+                const float f = mq > -INFINITY ? ex2_approx(mq - Mx) : 0.f;
+                num = fmaf(f, tab[q * (D + 2) + 2 + j], num);
+                den = fmaf(f, tab[q * (D + 2) + 1], den);
+            }
+            misc[j] = num / den;
+        }
+    }
+    return true;
+}
+
 // DT: head_dim known at compile time (64), or 0 for any even head_dim <= 128.
 // The block's attention output (split 0 of a head, after the merges) is left
 // in misc[0..D). wo_src (split 0, when W_o's columns were not copied at the
@@ -1020,73 +1093,7 @@ __device__ bool attention_block(const Params& P, const StepArgs& A, const AttnPl
     }
     }
     if (P.world == 1) return true;
-    // KV sequence split over GPUs: this GPU's (m, l, o) of head h goes to every
-    // rank's exchange buffer (system-scope tagged words over NVLink); then all
-    // ranks' partials are polled from the local buffer and merged in rank order,
-    // so every GPU ends with the same attention output. Slots alternate with the
-    // global layer count: a rank one layer ahead writes the other slot.
-    {
-        __syncthreads();  // the split tables above are consumed
-        float* own = reinterpret_cast<float*>(att);  // [D+2]: m, l, o
-        float* tab = own + (D + 2);                   // [world][D+2]
-        if ((int)threadIdx.x < D) {
-            own[2 + threadIdx.x] = own_acc;
-            if (threadIdx.x == 0) {
-                own[0] = own_m;
-                own[1] = own_l;
-            }
-        }
-        __syncthreads();
-        const int slot = (int)((A.seq * (unsigned)P.L + (unsigned)l) & 1u);
-        const int nw = P.world * (D + 2);
-        for (int i = threadIdx.x; i < nw; i += NT) {
-            const int q = i / (D + 2), k = i - q * (D + 2);
-            ll_store_sys(P.peers[q] + (((size_t)slot * P.NH + ap.h) * P.world + P.rank) * (D + 2) + k, own[k], tag);
-        }
-        const uint64_t* src = P.exch + ((size_t)slot * P.NH + ap.h) * P.world * (D + 2);
-        constexpr int WT = 4;  // world * (D+2) <= 8 * 130 < 4 * NT
-        uint64_t w[WT];
-        unsigned pending = 0;
-#pragma unroll
-        for (int k = 0; k < WT; ++k) {
-            const int i = threadIdx.x + k * NT;
-            if (i < nw) {
-                w[k] = ll_load_sys(src + i);
-                pending |= 1u << k;
-            }
-        }
-        uint64_t t0 = 0;
-        unsigned rounds = 0;
-        while (pending) {
-#pragma unroll
-            for (int k = 0; k < WT; ++k)
-                if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
-                    tab[threadIdx.x + k * NT] = __uint_as_float((uint32_t)w[k]);
-                    pending &= ~(1u << k);
-                }
-            if (!pending) break;
-            if ((++rounds & 7u) == 0 && wait_expired(st, t0)) break;
-#pragma unroll
-            for (int k = 0; k < WT; ++k)
-                if ((pending >> k) & 1u) w[k] = ll_load_sys(src + threadIdx.x + k * NT);
-        }
-        __syncthreads();
-        if (should_abort(st)) return false;
-        if ((int)threadIdx.x < D) {
-            const int j = threadIdx.x;
-            float Mx = -INFINITY;
-            for (int q = 0; q < P.world; ++q) Mx = fmaxf(Mx, tab[q * (D + 2)]);
-            float num = 0.f, den = 0.f;
-            for (int q = 0; q < P.world; ++q) {
-                const float mq = tab[q * (D + 2)];
-                const float f = mq > -INFINITY ? ex2_approx(mq - Mx) : 0.f;
-                num = fmaf(f, tab[q * (D + 2) + 2 + j], num);
-                den = fmaf(f, tab[q * (D + 2) + 1], den);
-            }
-            misc[j] = num / den;
-        }
-    }
-    return true;
+    return exchange_head(P, A, ap.h, D, l, tag, att, own_m, own_l, own_acc, misc, st);
 }
 
 
@@ -1355,10 +1362,12 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
         // thread d adds the 8 shares in order.
         float* wgt = misc + 384;           // [nsplit <= GQA_MERGE_MAX] weights
         float* part = wgt + GQA_MERGE_MAX; // [8][D + 1] shares of num (D) and den (1)
+        float* smx = part + 8 * (D + 1);   // the largest m
         if (warp == 0) {
             float mx = -INFINITY;
             for (int i = lane; i < A.nsplit; i += 32) mx = fmaxf(mx, table[i * (D + 2)]);
             mx = warp_max(mx);
+            if (lane == 0) *smx = mx;
             for (int i = lane; i < A.nsplit; i += 32) wgt[i] = ex2_approx(table[i * (D + 2)] - mx);
         }
         __syncthreads();
@@ -1373,15 +1382,16 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
             if (d == 0) part[q * (D + 1) + D] = den;
         }
         __syncthreads();
+        float num = 0.f, den = 0.f;
         if (tid < D) {
-            float num = 0.f, den = 0.f;
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 num += part[q * (D + 1) + tid];
                 den += part[q * (D + 1) + D];
             }
-            misc[tid] = num / den;
+            if (P.world == 1) misc[tid] = num / den;
         }
+        if (P.world > 1) return exchange_head(P, A, ap.g * hpg + split, D, l, tag, att, *smx, den, num, misc, st);
     }
     return true;
 }

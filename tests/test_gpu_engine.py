@@ -172,3 +172,34 @@ def test_long_context_prefilled_kv(qwen05_int8, tmp_path, kv):
         np.testing.assert_allclose(got, exp, atol=LOGIT_ATOL)
         assert best == oracle.argmax(exp)
         tok = best
+
+
+@pytest.mark.parametrize("which,ctx", [("g64", 1000), ("g64", 1100), ("g64", 2300), ("g64b", 1500)])
+def test_group_attention_units_match_oracle(which, ctx, g64_int8, g64b_int8):
+    """head_dim 64 with 7 (g64) and 2 (g64b) query heads per KV head, KV
+    pre-filled with seeded N(0,1) rows: below 1024 attended positions the
+    step uses one block per (query head, split), from 1024 on one block per
+    (KV group, split); partial last chunks and split counts that do not divide
+    the context are included."""
+    from conftest import G64, G64B
+    model, d = (g64_int8, G64) if which == "g64" else (g64b_int8, G64B)
+    steps = 3
+    eng = dcb.Engine(model, ctx + steps)
+    orc = oracle.Oracle(model, ctx + steps, threads=8)
+    kc, vc = orc.kv_view()
+    rng = np.random.default_rng(ctx)
+    for l in range(d.layers):
+        k = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+        v = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+        kc[l, :ctx] = k
+        vc[l, :ctx] = v
+        eng.kv_write(l, 0, k, v)
+    eng.set_position(ctx)
+    orc.pos = ctx
+    tok = 5
+    for _ in range(steps):
+        got, best = eng.step(tok)
+        exp = orc.step(tok)
+        np.testing.assert_allclose(got, exp, atol=LOGIT_ATOL)
+        assert best == oracle.argmax(exp)
+        tok = best

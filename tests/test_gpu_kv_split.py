@@ -1,8 +1,10 @@
 """One decode stream with its KV cache split over two GPUs: two processes,
-one engine each, KV positions [0, 150) and [150, ...) of a 300-position
-pre-filled context; 8 greedy steps through the C ABI. Rank 0 then runs the
-same steps on one unsplit engine and compares logits and tokens. Needs two
-GPUs (skipped otherwise)."""
+one engine each, KV positions [0, ctx/2) and [ctx/2, ...) of a pre-filled
+context; 8 greedy steps through the C ABI. Rank 0 then runs the same steps on
+one unsplit engine and compares logits and tokens. Two cases: a 300-position
+context (attention units per query head) and a 2304-position one with
+head_dim 64 (units per KV group on every rank). Needs two GPUs (skipped
+otherwise)."""
 from __future__ import annotations
 
 import json
@@ -11,11 +13,12 @@ import socket
 import numpy as np
 import pytest
 
-from conftest import dcb, synthetic, SMALL
+from conftest import dcb, synthetic, SMALL, G64
 
 pytestmark = pytest.mark.gpu
 
-CTX, STEPS = 300, 8
+STEPS = 8
+CASES = {"small": (SMALL, 300), "g64": (G64, 2304)}
 
 
 def _gpu_count() -> int:
@@ -32,10 +35,10 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _kv(d):
-    rng = np.random.default_rng(300)
-    return [(rng.standard_normal((CTX, d.kv_dim), dtype=np.float32),
-             rng.standard_normal((CTX, d.kv_dim), dtype=np.float32)) for _ in range(d.layers)]
+def _kv(d, ctx):
+    rng = np.random.default_rng(ctx)
+    return [(rng.standard_normal((ctx, d.kv_dim), dtype=np.float32),
+             rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)) for _ in range(d.layers)]
 
 
 def _run(engine, first_token):
@@ -46,13 +49,13 @@ def _run(engine, first_token):
     return np.stack(logits)
 
 
-def _rank_main(rank: int, world: int, port: int, model: str, out: str) -> None:
+def _rank_main(rank: int, world: int, port: int, model: str, out: str, case: str) -> None:
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
-    d = SMALL
-    kv = _kv(d)
+    d, CTX = CASES[case]
+    kv = _kv(d, CTX)
     begin, end = dcb.kv_shard_ranges(CTX, world)[rank]
     cap = (end if end is not None else CTX + STEPS + 2) - begin
     eng = dcb.Engine(model, cap, device=rank)
@@ -81,11 +84,13 @@ def _rank_main(rank: int, world: int, port: int, model: str, out: str) -> None:
 
 
 @pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
-def test_kv_split_over_two_gpus_matches_one_engine(small_int8, tmp_path):
+@pytest.mark.parametrize("case", ["small", "g64"])
+def test_kv_split_over_two_gpus_matches_one_engine(case, small_int8, g64_int8, tmp_path):
     import torch.multiprocessing as mp
     out = str(tmp_path / "kv")
-    mp.start_processes(_rank_main, args=(2, _free_port(), str(small_int8), out), nprocs=2, start_method="spawn")
+    model = small_int8 if case == "small" else g64_int8
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(model), out, case), nprocs=2, start_method="spawn")
     split, whole = np.load(out + ".split.npy"), np.load(out + ".whole.npy")
-    assert split.shape == (STEPS, SMALL.vocab)
+    assert split.shape == (STEPS, CASES[case][0].vocab)
     np.testing.assert_allclose(split, whole, atol=1e-4, rtol=1e-4)
     assert (split.argmax(axis=1) == whole.argmax(axis=1)).all()
