@@ -240,6 +240,193 @@ __device__ __forceinline__ void attention_split_body(unsigned char* at_sm, const
     }
 }
 
+// Queries of KV group g (gq heads of d dims) into sq, rotated at position
+// length-1 when asked (cached angle formula of src/model.cpp:222-224,271) and
+// scaled by log2(e)/sqrt(d).
+__device__ __forceinline__ void at_stage_queries(const AttnIO& io, int g, int gq, int D, float* sq) {
+    const float qscale = 1.4426950408889634f / sqrtf((float)D);
+    for (int e = threadIdx.x; e < gq * D; e += AT_NT) {
+        const int hl = e / D, j = e - hl * D;
+        const float* qh = io.q + (size_t)(g * gq + hl) * D;
+        float v = qh[j];
+        if (io.rope_theta > 0.f) {
+            const int half = D / 2, jj = j < half ? j : j - half;
+            const float inv = 1.0f / powf(io.rope_theta, (float)(2 * jj) / (float)D);
+            const float angle = __fmul_rn((float)(io.length - 1), inv);
+            float sn, cs;
+            sincosf(angle, &sn, &cs);
+            const float a = qh[jj], b = qh[jj + half];
+            v = j < half ? __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn)) : __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+        }
+        sq[e] = v * qscale;
+    }
+}
+
+// Shared memory of attention_group_kernel: two chunk buffers of K and V rows
+// (head_dim 64), the group's scaled queries, the [AT_GH][AT_T] score tile and
+// the per-head running max, sum and rescale.
+__host__ __device__ constexpr size_t attention_group_smem_bytes(int es, int gq) {
+    return 2 * 2 * (size_t)AT_T * 64 * es + (size_t)gq * 64 * sizeof(float) +
+           ((size_t)AT_GH * AT_T + 3 * AT_GH) * sizeof(float);
+}
+
+// Split-KV attention for head_dim 64 and up to AT_GH query heads per KV head:
+// block (KV head g, split s) reads each 64-position chunk of its split once for
+// all gq heads. Per chunk, after the copy lands:
+//   scores: warp w takes positions 4w..4w+3; the 8 lanes of a position own dims
+//     4p..4p+3 and 32+4p..32+4p+3 (8 lanes read 128 contiguous bytes), read K
+//     once and, for each head, reduce q.k over the 8 lanes into the score tile;
+//   softmax: warp h turns head h's 64 scores into 2^(s - m) with its running
+//     max m and adds them to its running sum;
+//   P.V: thread (h, j) rescales and accumulates o_h[j] over the chunk.
+// Light on registers, so two blocks share an SM and their copies overlap.
+template <typename KV>
+__global__ void __launch_bounds__(AT_NT, 2) attention_group_kernel(AttnIO io) {
+    extern __shared__ __align__(16) unsigned char at_sm[];
+    constexpr int D = 64;
+    const int g = blockIdx.x / io.nsplit, s = blockIdx.x % io.nsplit;
+    const int gq = io.heads / io.kv_heads, kvd = io.kv_heads * D;
+    const int t0 = s * io.split_len, t1 = min(io.length, t0 + io.split_len);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t buf_elems = 2 * (size_t)AT_T * D;
+    KV* bufs = reinterpret_cast<KV*>(at_sm);
+    float* sq = reinterpret_cast<float*>(at_sm + 2 * buf_elems * sizeof(KV));
+    float* tile = sq + gq * D;          // [AT_GH][AT_T]
+    float* hm = tile + AT_GH * AT_T;    // [AT_GH] running max
+    float* hl = hm + AT_GH;             // running sum
+    float* ha = hl + AT_GH;             // rescale of the current chunk
+    const KV* kg = static_cast<const KV*>(io.keys) + (size_t)g * D;
+    const KV* vg = static_cast<const KV*>(io.values) + (size_t)g * D;
+    at_stage_queries(io, g, gq, D, sq);
+    if (tid < AT_GH) {
+        hm[tid] = -INFINITY;
+        hl[tid] = 0.f;
+    }
+    const bool async16 = (kvd * sizeof(KV)) % 16 == 0 && (reinterpret_cast<uintptr_t>(kg) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(vg) & 15) == 0;
+    const int nchunks = (t1 - t0 + AT_T - 1) / AT_T;
+    auto issue = [&](int c) {
+        const int c0 = t0 + c * AT_T, n = min(AT_T, t1 - c0);
+        KV* kb = bufs + (size_t)(c & 1) * buf_elems;
+        KV* vb = kb + (size_t)AT_T * D;
+        if (async16) {
+            constexpr int EP = 16 / sizeof(KV);
+            constexpr int pieces = D / EP;
+            for (int e = tid; e < n * pieces; e += AT_NT) {
+                const int t = e / pieces, pc = e - t * pieces;
+                const size_t src = (size_t)(c0 + t) * kvd + (size_t)pc * EP;
+                cp_async16(kb + (size_t)t * D + pc * EP, kg + src);
+                cp_async16(vb + (size_t)t * D + pc * EP, vg + src);
+            }
+        } else {
+            for (int e = tid; e < n * D; e += AT_NT) {
+                const int t = e / D, j = e - t * D;
+                kb[(size_t)t * D + j] = kg[(size_t)(c0 + t) * kvd + j];
+                vb[(size_t)t * D + j] = vg[(size_t)(c0 + t) * kvd + j];
+            }
+        }
+        cp_async_commit();
+    };
+    const int grp = lane >> 3, part = lane & 7;
+    float o0 = 0.f, o1 = 0.f;  // thread (h, j) = (tid / 64, tid % 64), tid < gq * 64
+    issue(0);
+    for (int c = 0; c < nchunks; ++c) {
+        if (c + 1 < nchunks) {
+            issue(c + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();  // chunk c landed for every thread (and the queries are staged)
+        const int n = min(AT_T, t1 - (t0 + c * AT_T));
+        const KV* kb = bufs + (size_t)(c & 1) * buf_elems;
+        const KV* vb = kb + (size_t)AT_T * D;
+        {
+            const int t = warp * 4 + grp;
+            float kk[8];
+            if (t < n) {
+                float a[4], b[4];
+                at_load4(kb + (size_t)t * D + 4 * part, a);
+                at_load4(kb + (size_t)t * D + 32 + 4 * part, b);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    kk[e] = a[e];
+                    kk[4 + e] = b[e];
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) kk[e] = 0.f;
+            }
+            for (int h = 0; h < gq; ++h) {
+                const float4 q0 = *reinterpret_cast<const float4*>(sq + h * D + 4 * part);
+                const float4 q1 = *reinterpret_cast<const float4*>(sq + h * D + 32 + 4 * part);
+                float sc = q0.x * kk[0];
+                sc = fmaf(q0.y, kk[1], sc);
+                sc = fmaf(q0.z, kk[2], sc);
+                sc = fmaf(q0.w, kk[3], sc);
+                sc = fmaf(q1.x, kk[4], sc);
+                sc = fmaf(q1.y, kk[5], sc);
+                sc = fmaf(q1.z, kk[6], sc);
+                sc = fmaf(q1.w, kk[7], sc);
+                sc += __shfl_xor_sync(FULL, sc, 4);
+                sc += __shfl_xor_sync(FULL, sc, 2);
+                sc += __shfl_xor_sync(FULL, sc, 1);
+                if (part == 0) tile[h * AT_T + t] = t < n ? sc : -INFINITY;
+            }
+        }
+        __syncthreads();
+        if (warp < gq) {
+            float* row = tile + warp * AT_T;
+            const float s0 = row[lane], s1 = row[lane + 32];
+            const float mx = warp_max(fmaxf(s0, s1));
+            const float mo = hm[warp], mn = fmaxf(mo, mx);
+            const float e0 = at_ex2(s0 - mn), e1 = at_ex2(s1 - mn);
+            row[lane] = e0;
+            row[lane + 32] = e1;
+            const float sum = warp_sum(e0 + e1);
+            if (lane == 0) {
+                const float al = at_ex2(mo - mn);
+                ha[warp] = al;
+                hl[warp] = fmaf(hl[warp], al, sum);
+                hm[warp] = mn;
+            }
+        }
+        __syncthreads();
+        if (tid < gq * D) {
+            const int h = tid >> 6, j = tid & 63;
+            o0 *= ha[h];
+            o1 *= ha[h];
+            const float* pr = tile + h * AT_T;
+            const KV* vj = vb + j;
+            int t = 0;
+#pragma unroll 2
+            for (; t + 4 <= n; t += 4) {
+                const float4 pv = *reinterpret_cast<const float4*>(pr + t);
+                o0 = fmaf(pv.x, at_float(vj[(size_t)t * D]), o0);
+                o1 = fmaf(pv.y, at_float(vj[(size_t)(t + 1) * D]), o1);
+                o0 = fmaf(pv.z, at_float(vj[(size_t)(t + 2) * D]), o0);
+                o1 = fmaf(pv.w, at_float(vj[(size_t)(t + 3) * D]), o1);
+            }
+            for (; t < n; ++t) o0 = fmaf(pr[t], at_float(vj[(size_t)t * D]), o0);
+        }
+        __syncthreads();  // buffer c & 1 and the tile consumed before chunk c + 2 and the next scores
+    }
+    if (tid < gq * D) {
+        const int h = g * gq + (tid >> 6), j = tid & 63;
+        const float acc = o0 + o1;
+        if (io.nsplit == 1) {
+            io.out[(size_t)h * D + j] = acc / hl[tid >> 6];
+        } else {
+            float* pp = io.part + ((size_t)h * io.nsplit + s) * (D + 2);
+            if (j == 0) {
+                pp[0] = hm[tid >> 6];
+                pp[1] = hl[tid >> 6];
+            }
+            pp[2 + j] = acc;
+        }
+    }
+}
+
 // DT: head_dim known at compile time (64), or 0 for any even head_dim <= 128.
 template <typename KV, int DT>
 __global__ void __launch_bounds__(AT_NT) attention_split_kernel(AttnIO io) {

@@ -232,6 +232,18 @@ cudaError_t launch_split(const AttnIO& io, size_t smem, cudaStream_t st) {
     return cudaLaunchKernel(k, dim3(io.kv_heads * io.nsplit), dim3(AT_NT), args, smem, st);
 }
 
+template <typename KV>
+cudaError_t launch_group(const AttnIO& io, size_t smem, cudaStream_t st) {
+    const void* k = (const void*)attention_group_kernel<KV>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    AttnIO a = io;
+    void* args[] = {(void*)&a};
+    return cudaLaunchKernel(k, dim3(io.kv_heads * io.nsplit), dim3(AT_NT), args, smem, st);
+}
+
 // The split kernel, then (several splits) the combine kernel, on stream st.
 int launch_attention(const AttnIO& io, int kv_dtype, cudaStream_t st) {
     const int es = kv_dtype == DCB_KV_F16 ? 2 : 4;
@@ -242,10 +254,15 @@ int launch_attention(const AttnIO& io, int kv_dtype, cudaStream_t st) {
     if (smem + 1024 > (size_t)optin)
         return fail(DCB_ERR_UNSUPPORTED, "attention needs more shared memory than a block has");
     cudaError_t e;
-    if (kv_dtype == DCB_KV_F16)
+    if (io.d == 64 && io.heads / io.kv_heads <= AT_GH) {
+        // head_dim 64, up to AT_GH query heads per KV head: the group kernel.
+        const size_t gs = attention_group_smem_bytes(es, io.heads / io.kv_heads);
+        e = kv_dtype == DCB_KV_F16 ? launch_group<__half>(io, gs, st) : launch_group<float>(io, gs, st);
+    } else if (kv_dtype == DCB_KV_F16) {
         e = io.d == 64 ? launch_split<__half, 64>(io, smem, st) : launch_split<__half, 0>(io, smem, st);
-    else
+    } else {
         e = io.d == 64 ? launch_split<float, 64>(io, smem, st) : launch_split<float, 0>(io, smem, st);
+    }
     if (e != cudaSuccess) return cuda_fail(e, "attention launch");
     if (io.nsplit > 1) {
         AttnIO a = io;
