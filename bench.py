@@ -216,6 +216,8 @@ def main() -> None:
                     help="the profiling case: KV rows 0..127 written from the host, then 5 decode launches")
     ap.add_argument("--ncu-long", type=int, default=0, metavar="CTX",
                     help="the long-context profiling case: KV rows 0..CTX-1 pre-filled, then 5 decode launches")
+    ap.add_argument("--ncu-attention", type=int, default=0, metavar="L",
+                    help="the isolated-attention profiling case: 5 calls at L positions, FP32 KV")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -225,6 +227,9 @@ def main() -> None:
         return
     if args.ncu_long:
         ncu_case(args.ncu_long)
+        return
+    if args.ncu_attention:
+        ncu_attention_case(args.ncu_attention)
         return
     if args.ncu_batch:
         ncu_batch_case(args.ncu_batch, max(1, args.steps), args.ncu_ctx)
@@ -535,6 +540,26 @@ def attention_sweep(dcb) -> dict:
                                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
             del k, v
     return out
+
+
+def ncu_attention_case(length: int) -> None:
+    """Five calls of the isolated attention at `length` positions (the sweep's
+    shape: 14 query heads over 2 KV heads, head_dim 64, FP32 KV, N(0,1) q/K/V,
+    RoPE theta 1e6): a profiler captures the third."""
+    import torch
+    dcb = load_package()
+    torch.cuda.set_stream(torch.cuda.Stream())
+    heads, kvh, dim = 14, 2, 64
+    g = torch.Generator(device="cuda").manual_seed(2)
+    k = torch.randn(length, kvh * dim, device="cuda", generator=g)
+    v = torch.randn(length, kvh * dim, device="cuda", generator=g)
+    q = torch.randn(heads * dim, device="cuda", generator=g)
+    o = torch.empty(heads * dim, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(5):
+        dcb.attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), "f32", o.data_ptr(), length, heads, kvh, dim, 1e6, stream)
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_case": f"isolated attention, {length} positions", "out0": float(o[0].item())}))
 
 
 BATCH_SEQS = 64           # independent sequences per GPU
