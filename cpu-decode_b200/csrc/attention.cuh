@@ -63,6 +63,11 @@ __device__ __forceinline__ void at_load4(const __half* p, float (&o)[4]) {
 }
 __device__ __forceinline__ float at_float(float v) { return v; }
 __device__ __forceinline__ float at_float(__half v) { return __half2float(v); }
+// Two adjacent elements (8- or 4-byte aligned) as FP32.
+__device__ __forceinline__ float2 at_float2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 at_float2(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
 
 // The pass over one split shared by the isolated operator and the batched
 // engine: K/V rows t0..t1-1 of one KV head (row t at kg + t*rs and vg + t*rs),
@@ -278,7 +283,8 @@ __host__ __device__ constexpr size_t attention_group_smem_bytes(int es, int gq) 
 //     once and, for each head, reduce q.k over the 8 lanes into the score tile;
 //   softmax: warp h turns head h's 64 scores into 2^(s - m) with its running
 //     max m and adds them to its running sum;
-//   P.V: thread (h, j) rescales and accumulates o_h[j] over the chunk.
+//   P.V: thread (h, j2) rescales and accumulates o_h[2j2], o_h[2j2+1] over the
+//     chunk (one 8-byte V load per two FMAs).
 // Light on registers, so two blocks share an SM and their copies overlap.
 template <typename KV>
 __global__ void __launch_bounds__(AT_NT, 2) attention_group_kernel(AttnIO io) {
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(AT_NT, 2) attention_group_kernel(AttnIO io) {
         cp_async_commit();
     };
     const int grp = lane >> 3, part = lane & 7;
-    float o0 = 0.f, o1 = 0.f;  // thread (h, j) = (tid / 64, tid % 64), tid < gq * 64
+    float2 o0 = make_float2(0.f, 0.f), o1 = o0;  // thread (h, j2) = (tid / 32, tid % 32), tid < gq * 32: dims 2j2, 2j2+1
     issue(0);
     for (int c = 0; c < nchunks; ++c) {
         if (c + 1 < nchunks) {
@@ -392,37 +398,52 @@ __global__ void __launch_bounds__(AT_NT, 2) attention_group_kernel(AttnIO io) {
             }
         }
         __syncthreads();
-        if (tid < gq * D) {
-            const int h = tid >> 6, j = tid & 63;
-            o0 *= ha[h];
-            o1 *= ha[h];
+        if (tid < gq * 32) {
+            const int h = tid >> 5, j2 = tid & 31;
+            const float al = ha[h];
+            o0.x *= al;
+            o0.y *= al;
+            o1.x *= al;
+            o1.y *= al;
             const float* pr = tile + h * AT_T;
-            const KV* vj = vb + j;
+            const KV* vj = vb + 2 * j2;
             int t = 0;
 #pragma unroll 2
             for (; t + 4 <= n; t += 4) {
                 const float4 pv = *reinterpret_cast<const float4*>(pr + t);
-                o0 = fmaf(pv.x, at_float(vj[(size_t)t * D]), o0);
-                o1 = fmaf(pv.y, at_float(vj[(size_t)(t + 1) * D]), o1);
-                o0 = fmaf(pv.z, at_float(vj[(size_t)(t + 2) * D]), o0);
-                o1 = fmaf(pv.w, at_float(vj[(size_t)(t + 3) * D]), o1);
+                const float2 v0 = at_float2(vj + (size_t)t * D), v1 = at_float2(vj + (size_t)(t + 1) * D);
+                const float2 v2 = at_float2(vj + (size_t)(t + 2) * D), v3 = at_float2(vj + (size_t)(t + 3) * D);
+                o0.x = fmaf(pv.x, v0.x, o0.x);
+                o0.y = fmaf(pv.x, v0.y, o0.y);
+                o1.x = fmaf(pv.y, v1.x, o1.x);
+                o1.y = fmaf(pv.y, v1.y, o1.y);
+                o0.x = fmaf(pv.z, v2.x, o0.x);
+                o0.y = fmaf(pv.z, v2.y, o0.y);
+                o1.x = fmaf(pv.w, v3.x, o1.x);
+                o1.y = fmaf(pv.w, v3.y, o1.y);
             }
-            for (; t < n; ++t) o0 = fmaf(pr[t], at_float(vj[(size_t)t * D]), o0);
+            for (; t < n; ++t) {
+                const float2 vt = at_float2(vj + (size_t)t * D);
+                o0.x = fmaf(pr[t], vt.x, o0.x);
+                o0.y = fmaf(pr[t], vt.y, o0.y);
+            }
         }
         __syncthreads();  // buffer c & 1 and the tile consumed before chunk c + 2 and the next scores
     }
-    if (tid < gq * D) {
-        const int h = g * gq + (tid >> 6), j = tid & 63;
-        const float acc = o0 + o1;
+    if (tid < gq * 32) {
+        const int hh = tid >> 5, h = g * gq + hh, j = 2 * (tid & 31);
+        const float a0 = o0.x + o1.x, a1 = o0.y + o1.y;
         if (io.nsplit == 1) {
-            io.out[(size_t)h * D + j] = acc / hl[tid >> 6];
+            io.out[(size_t)h * D + j] = a0 / hl[hh];
+            io.out[(size_t)h * D + j + 1] = a1 / hl[hh];
         } else {
             float* pp = io.part + ((size_t)h * io.nsplit + s) * (D + 2);
             if (j == 0) {
-                pp[0] = hm[tid >> 6];
-                pp[1] = hl[tid >> 6];
+                pp[0] = hm[hh];
+                pp[1] = hl[hh];
             }
-            pp[2 + j] = acc;
+            pp[2 + j] = a0;
+            pp[3 + j] = a1;
         }
     }
 }

@@ -700,6 +700,11 @@ __device__ __forceinline__ void trace_detail(const Params& P, int layer, int k, 
 
 __device__ __forceinline__ float kv_to_float(float v) { return v; }
 __device__ __forceinline__ float kv_to_float(__half v) { return __half2float(v); }
+// Two adjacent KV elements (8- or 4-byte aligned) as FP32.
+__device__ __forceinline__ float2 kv_to_float2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float2 kv_to_float2(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
 __device__ __forceinline__ float round_to(float v, float) { return v; }
 __device__ __forceinline__ float round_to(float v, __half) { return __half2float(__float2half_rn(v)); }
 
@@ -1173,7 +1178,7 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
         if (should_abort(st)) return false;
     }
     trace_detail(P, l, 1, 1);
-    float o0 = 0.f, o1 = 0.f;  // thread (h, d) = (tid / 64, tid % 64), tid < hpg * 64: even and odd positions
+    float2 o0 = make_float2(0.f, 0.f), o1 = o0;  // thread (h, d2) = (tid / 32, tid % 32), tid < hpg * 32: dims 2d2, 2d2+1
     const int nissued = ap.nissued;
     const int pass = P.gqa_pass;
     for (int c = 0; c < ap.nchunks; c += pass) {
@@ -1267,28 +1272,42 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
             }
         }
         __syncthreads();
-        // C: o_h[d] += p_t * V[t][d] over the pass's positions.
-        if (tid < hpg * D) {
-            const int h = tid >> 6, d = tid & 63;
-            o0 *= ha[h];
-            o1 *= ha[h];
+        // C: o_h[2d2..2d2+1] += p_t * V[t][2d2..2d2+1] over the pass's positions
+        // (one 8-byte V load per two FMAs).
+        if (tid < hpg * 32) {
+            const int h = tid >> 5, d2 = tid & 31;
+            const float al = ha[h];
+            o0.x *= al;
+            o0.y *= al;
+            o1.x *= al;
+            o1.y *= al;
             const float* prow = stile + h * SROW;
             for (int u = 0; u < cb; ++u) {
                 const int c0 = ap.t0 + (c + u) * ATT_CHUNK;
                 const int n = min(ATT_CHUNK, ap.t1 - c0);
                 const KV* vb = reinterpret_cast<const KV*>(att + (size_t)((c + u) % NB) * P.att_chunk_bytes) +
-                               (size_t)ATT_CHUNK * D + d;
+                               (size_t)ATT_CHUNK * D + 2 * d2;
                 const float* pu = prow + u * ATT_CHUNK;
                 int t = 0;
 #pragma unroll 2
                 for (; t + 4 <= n; t += 4) {
                     const float4 pv = *reinterpret_cast<const float4*>(pu + t);
-                    o0 = fmaf(pv.x, kv_to_float(vb[(size_t)t * D]), o0);
-                    o1 = fmaf(pv.y, kv_to_float(vb[(size_t)(t + 1) * D]), o1);
-                    o0 = fmaf(pv.z, kv_to_float(vb[(size_t)(t + 2) * D]), o0);
-                    o1 = fmaf(pv.w, kv_to_float(vb[(size_t)(t + 3) * D]), o1);
+                    const float2 v0 = kv_to_float2(vb + (size_t)t * D), v1 = kv_to_float2(vb + (size_t)(t + 1) * D);
+                    const float2 v2 = kv_to_float2(vb + (size_t)(t + 2) * D), v3 = kv_to_float2(vb + (size_t)(t + 3) * D);
+                    o0.x = fmaf(pv.x, v0.x, o0.x);
+                    o0.y = fmaf(pv.x, v0.y, o0.y);
+                    o1.x = fmaf(pv.y, v1.x, o1.x);
+                    o1.y = fmaf(pv.y, v1.y, o1.y);
+                    o0.x = fmaf(pv.z, v2.x, o0.x);
+                    o0.y = fmaf(pv.z, v2.y, o0.y);
+                    o1.x = fmaf(pv.w, v3.x, o1.x);
+                    o1.y = fmaf(pv.w, v3.y, o1.y);
                 }
-                for (; t < n; ++t) o0 = fmaf(pu[t], kv_to_float(vb[(size_t)t * D]), o0);
+                for (; t < n; ++t) {
+                    const float2 vt = kv_to_float2(vb + (size_t)t * D);
+                    o0.x = fmaf(pu[t], vt.x, o0.x);
+                    o0.y = fmaf(pu[t], vt.y, o0.y);
+                }
             }
         }
         trace_detail(P, l, 1, c == 0 ? 3 : 5);
@@ -1303,10 +1322,11 @@ __device__ bool attention_group(const Params& P, const StepArgs& A, const AttnPl
         }
     }
     // (m, l, unnormalised o) of every head of the group for this split.
-    if (tid < hpg * D) {
-        const int h = tid >> 6, d = tid & 63;
+    if (tid < hpg * 32) {
+        const int h = tid >> 5, d = 2 * (tid & 31);
         uint64_t* pw = P.ll_part + ((size_t)(ap.g * hpg + h) * A.nsplit + split) * (D + 2);
-        ll_store(pw + 2 + d, o0 + o1, tag);
+        ll_store(pw + 2 + d, o0.x + o1.x, tag);
+        ll_store(pw + 3 + d, o0.y + o1.y, tag);
         if (d == 0) {
             ll_store(pw, hm[h], tag);
             ll_store(pw + 1, hl[h], tag);
