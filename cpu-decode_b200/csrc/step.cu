@@ -410,7 +410,6 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     }
     if (int rc = e->alloc(&P.ll_q, H)) return bail(rc);
     if (int rc = e->alloc(&P.ll_kv, 2 * e->NKV * D)) return bail(rc);
-    if (int rc = e->alloc(&P.ll_h, I)) return bail(rc);
     if (int rc = e->alloc(&P.ll_part, (size_t)e->NH * (G + 1) * (D + 2))) return bail(rc);
     // KV-split exchange: [2 slots][NH][MAX_WORLD][D+2] tagged words, and the
     // ranks' buffers (this engine's own until dcb_set_kv_shard).

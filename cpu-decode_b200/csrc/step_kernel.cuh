@@ -98,7 +98,6 @@ struct Params {
     void* vcache;
     uint64_t* ll_q;     // [H]   rotated queries
     uint64_t* ll_kv;    // [2*NKV*D] the new K and V rows
-    uint64_t* ll_h;     // [I]   SiLU(gate)*up
     uint64_t* ll_part;    // [NH][nsplit][D+2] tagged attention split partials (m, l, o)
     float* logits;        // [V]
     ArgBest* amax;        // [grid]
