@@ -43,6 +43,11 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
 }
 
+// One 128-byte line at p into L2 (no register, nothing to wait for).
+__device__ __forceinline__ void prefetch_line_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Prefetch this block's 1/nblocks slice of [base, base+bytes), 16-byte aligned.
 __device__ __forceinline__ void prefetch_slice(const void* base, size_t bytes, int block, int nblocks) {
     if (!base || bytes < 16) return;

@@ -1781,8 +1781,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                     }
                 };
                 if (warp < ngroups) load_group(warp, wc, sc);
+                const int lines = (P.SH + 127) / 128;  // 128-byte lines per row
                 for (int gi = warp; gi < ngroups; gi += NW) {
                     if (gi + NW < ngroups) load_group(gi + NW, wn, sn);
+                    // The group after next into L2, one line per lane.
+                    if (gi + 2 * NW < ngroups && lane < HEAD_R * lines) {
+                        const int r = ha + (gi + 2 * NW) * HEAD_R + lane / lines;
+                        if (r < ha + hn) prefetch_line_l2(P.embed + (size_t)r * P.SH + (size_t)(lane % lines) * 128);
+                    }
                     float vmine = 0.f;  // lane rr keeps row rr's logit: one store per group
 #pragma unroll
                     for (int rr = 0; rr < HEAD_R; ++rr) {
