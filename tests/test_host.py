@@ -149,3 +149,44 @@ def test_missing_tensor_and_bad_scales_rejected(tmp_path, tiny_int8):
 def test_engine_fails_loudly_without_a_gpu(tiny_int8):
     rc, msg = _open(tiny_int8)
     assert rc != 0 and msg  # a CUDA error, never a silent CPU path
+
+
+def _sum_word(v: float) -> int:
+    """One contribution to a step-kernel sum word: 2^56 + (rint(v * 2^26) + 2^47),
+    the integer clamped to |q| < 2^47 (the encoding of dacc_add in
+    csrc/step_kernel.cuh)."""
+    bias = 1 << 47
+    q = int(np.rint(np.float64(v) * 2.0 ** 26))
+    q = max(1 - bias, min(bias - 1, q))
+    return (1 << 56) + q + bias
+
+
+def _decode(w: int) -> tuple[int, float]:
+    count = w >> 56
+    q = (w & ((1 << 56) - 1)) - count * (1 << 47)
+    return count, q / 2.0 ** 26
+
+
+def test_sum_words_are_exact_order_free_and_self_counting():
+    """The O and down projections' outputs are summed over blocks as 64-bit
+    integer additions into L2 words that count their own contributions: the
+    sum must not depend on the order of the additions, the count field must
+    equal the number of contributors, and no carry may reach it."""
+    rng = np.random.default_rng(7)
+    mask = (1 << 64) - 1
+    for n, scale in ((148, 1e-2), (148, 3.0), (14, 40.0), (255, 2.0 ** 21 - 1)):
+        v = rng.uniform(-scale, scale, n)
+        words = [_sum_word(x) for x in v]
+        w1 = sum(words) & mask
+        w2 = sum(words[i] for i in rng.permutation(n)) & mask
+        assert w1 == w2
+        count, total = _decode(w1)
+        assert count == n
+        exact = sum(int(np.rint(x * 2.0 ** 26)) for x in v) / 2.0 ** 26
+        assert total == exact
+        assert abs(total - float(np.sum(v))) <= n * 2.0 ** -27 + 1e-9 * abs(float(np.sum(v)))
+    # The largest magnitudes from 255 contributors stay below the count field.
+    top = sum(_sum_word(2.0 ** 21) for _ in range(255)) & mask
+    assert _decode(top)[0] == 255
+    bottom = sum(_sum_word(-2.0 ** 21) for _ in range(255)) & mask
+    assert _decode(bottom)[0] == 255
