@@ -343,6 +343,14 @@ def main() -> None:
         split = kv_split_context(dcb, model, d, min(K, 32), W, local, dist, 32768)
         if rank == 0:
             extra["ctx32768_kv_split"] = split
+    if rank == 0:
+        # HBM read bandwidth of this GPU by the engine's own probe (the
+        # reference's tools/bandwidth.cpp sweep), beside the measured peak.
+        probe = dcb.read_bandwidth(mib=2048, passes=8, repeats=5, device=local)
+        rates = sorted(x["GB_per_s"] for x in probe["samples"])
+        extra["hbm_read_probe"] = {"GB_per_s_median": round(rates[len(rates) // 2], 1),
+                                   "GB_per_s_max": round(rates[-1], 1), "array_bytes": probe["array_bytes"],
+                                   "passes": probe["passes"], "kernel": probe["kernel"]}
     if not args.no_long and rank == 0:
         extra["ctx4096"] = long_context(dcb, model, d, K, W, local, 4096)
         extra["ctx32768"] = long_context(dcb, model, d, min(K, 32), W, local, 32768)

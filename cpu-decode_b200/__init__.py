@@ -34,6 +34,7 @@ EXPORTS = (
     "dcb_step_async", "dcb_synchronize", "dcb_rewind", "dcb_reset", "dcb_position", "dcb_set_stream", "dcb_stream",
     "dcb_logits_device", "dcb_kv_write", "dcb_kv_read", "dcb_set_position", "dcb_launch_info", "dcb_launch_count",
     "dcb_gemv_i8", "dcb_attention", "dcb_attention_noalloc", "dcb_rmsnorm", "dcb_rope", "dcb_argmax",
+    "dcb_read_bandwidth",
     "dcb_trace_enable", "dcb_trace_read", "dcb_exchange_buffer", "dcb_ipc_handle", "dcb_ipc_open", "dcb_ipc_close",
     "dcb_set_kv_shard", "dcb_batch_create", "dcb_batch_destroy", "dcb_batch_info", "dcb_batch_set_position",
     "dcb_batch_position", "dcb_batch_kv_write", "dcb_batch_kv_read", "dcb_batch_step", "dcb_batch_step_greedy",
@@ -88,6 +89,7 @@ def lib() -> C.CDLL:
     L.dcb_rmsnorm.argtypes = [vp, vp, vp, i32, C.c_float, vp]
     L.dcb_rope.argtypes = [vp, i32, i32, i32, C.c_float, i32, vp]
     L.dcb_argmax.argtypes = [vp, i32, vp, vp]
+    L.dcb_read_bandwidth.argtypes = [i32, C.c_size_t, i32, i32, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
     L.dcb_trace_enable.argtypes = [vp, i32]
     L.dcb_trace_read.argtypes = [vp, vp, vp, C.POINTER(i32)]
     L.dcb_exchange_buffer.argtypes = [vp, C.POINTER(vp), C.POINTER(sz)]
@@ -401,3 +403,18 @@ def rope(x: int, heads: int, dim: int, pos: int, theta: float, direct: bool, str
 
 def argmax(x: int, n: int, out: int, stream: int | None = None):
     _check(lib().dcb_argmax(x, n, out, stream))
+
+
+def read_bandwidth(mib: int = 1024, passes: int = 8, repeats: int = 5, device: int = 0) -> dict:
+    """HBM read bandwidth of `device` from a read-only sweep of an mib-MiB array
+    (the reference's tools/bandwidth.cpp, on the GPU), in the reference's record
+    format: {"kind": "read_bandwidth", ..., "samples": [{"seconds", "GB_per_s"}],
+    "checksum"}."""
+    gbs = (C.c_double * repeats)()
+    cs = C.c_uint64()
+    _check(lib().dcb_read_bandwidth(int(device), int(mib), int(passes), int(repeats), gbs, C.byref(cs)))
+    nbytes = int(mib) << 20
+    return {"kind": "read_bandwidth", "kernel": "ld.global.nc.v4", "device": int(device), "array_bytes": nbytes,
+            "passes": int(passes),
+            "samples": [{"seconds": nbytes * passes / (g * 1e9), "GB_per_s": g} for g in gbs],
+            "checksum": int(cs.value)}

@@ -181,6 +181,42 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* x, int n, int
     }
 }
 
+// ---- read-bandwidth probe ---------------------------------------------------------
+constexpr int PROBE_NT = 512, PROBE_BLOCKS_PER_SM = 4, PROBE_ILP = 4;
+
+// Word i = i * 6364136223846793005 + 1 (tools/bandwidth.cpp:83-84).
+__global__ void fill_probe_kernel(uint64_t* p, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = i * 6364136223846793005ull + 1ull;
+}
+
+// `passes` sweeps of n 16-byte pieces, PROBE_ILP streaming loads in flight per
+// thread, XOR-folded so nothing is skipped; one XOR per warp into *sum.
+__global__ void __launch_bounds__(PROBE_NT) read_probe_kernel(const int4* __restrict__ p, size_t n, int passes,
+                                                           unsigned long long* sum) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    uint64_t acc = 0;
+    for (int pass = 0; pass < passes; ++pass) {
+        size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        for (; i + (PROBE_ILP - 1) * stride < n; i += PROBE_ILP * stride) {
+            int4 v[PROBE_ILP];
+#pragma unroll
+            for (int k = 0; k < PROBE_ILP; ++k) v[k] = ld_stream(p + i + k * stride);
+#pragma unroll
+            for (int k = 0; k < PROBE_ILP; ++k)
+                acc ^= (((uint64_t)(uint32_t)v[k].y << 32) | (uint32_t)v[k].x) ^
+                       (((uint64_t)(uint32_t)v[k].w << 32) | (uint32_t)v[k].z);
+        }
+        for (; i < n; i += stride) {
+            const int4 v = ld_stream(p + i);
+            acc ^= (((uint64_t)(uint32_t)v.y << 32) | (uint32_t)v.x) ^ (((uint64_t)(uint32_t)v.w << 32) | (uint32_t)v.z);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc ^= __shfl_xor_sync(FULL, acc, o);
+    if ((threadIdx.x & 31) == 0 && acc) atomicXor(sum, (unsigned long long)acc);
+}
+
 // Multiprocessor count of each device, looked up once.
 std::atomic<int> g_sm_count[64];
 int sm_count() {
@@ -349,6 +385,58 @@ int dcb_argmax(const float* x, int n, int* out, void* stream) {
     argmax_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(x, n, out);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_fail(e, "argmax launch");
+}
+
+int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* gb_per_s, uint64_t* checksum) {
+    if (mib < 32 || mib > 65536 || passes < 1 || repeats < 1 || !gb_per_s)
+        return fail(DCB_ERR_ARGUMENT, "invalid sweep parameters");
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "read probe device");
+    const size_t bytes = mib << 20, words = bytes / sizeof(uint64_t);
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    uint64_t* data = nullptr;
+    unsigned long long* sum = nullptr;
+    cudaStream_t st = nullptr;
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    int rc = 0;
+    auto check = [&](cudaError_t err, const char* what) {
+        if (err != cudaSuccess && !rc) rc = cuda_fail(err, what);
+        return rc == 0;
+    };
+    const int grid = std::max(1, sms) * PROBE_BLOCKS_PER_SM;
+    auto sweep = [&](int count) {
+        read_probe_kernel<<<grid, PROBE_NT, 0, st>>>(reinterpret_cast<const int4*>(data), bytes / 16, count, sum);
+        return check(cudaGetLastError(), "read probe launch");
+    };
+    if (check(cudaMalloc(&data, bytes), "read probe array") && check(cudaMalloc(&sum, sizeof(*sum)), "read probe sum") &&
+        check(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking), "read probe stream") &&
+        check(cudaEventCreate(&t0), "read probe event") && check(cudaEventCreate(&t1), "read probe event")) {
+        fill_probe_kernel<<<grid, PROBE_NT, 0, st>>>(data, words);
+        if (check(cudaGetLastError(), "read probe fill") && sweep(3)) {
+            for (int r = 0; r < repeats && rc == 0; ++r) {
+                float ms = 0.f;
+                if (check(cudaEventRecord(t0, st), "read probe event") && sweep(passes) &&
+                    check(cudaEventRecord(t1, st), "read probe event") &&
+                    check(cudaEventSynchronize(t1), "read probe sweep") &&
+                    check(cudaEventElapsedTime(&ms, t0, t1), "read probe time"))
+                    gb_per_s[r] = (double)bytes * passes / (ms / 1000.0) / 1e9;
+            }
+            // The checksum of one sweep (an odd count: repeated sweeps would cancel).
+            unsigned long long host = 0;
+            if (rc == 0 && check(cudaMemsetAsync(sum, 0, sizeof(*sum), st), "read probe sum") && sweep(1) &&
+                check(cudaMemcpyAsync(&host, sum, sizeof(host), cudaMemcpyDeviceToHost, st), "read probe sum") &&
+                check(cudaStreamSynchronize(st), "read probe sum") && checksum)
+                *checksum = host;
+        }
+    }
+    if (st) cudaStreamSynchronize(st);
+    if (t0) cudaEventDestroy(t0);
+    if (t1) cudaEventDestroy(t1);
+    if (st) cudaStreamDestroy(st);
+    if (data) cudaFree(data);
+    if (sum) cudaFree(sum);
+    return rc;
 }
 
 }  // extern "C"

@@ -218,6 +218,18 @@ int dcb_rope(float* x, int heads, int dim, int position, float theta, int direct
  * std::max_element semantics (src/main.cpp:35-37). */
 int dcb_argmax(const float* x, int n, int* out, void* stream);
 
+/* Read-only STREAM-style sweep of HBM on `device`, replacing the reference's
+ * host read-bandwidth probe (tools/bandwidth.cpp:58-109, read512 :37-56) as the
+ * roofline denominator. An array of mib MiB (32..65536; above the 126 MB L2
+ * for an honest number) is filled with word i = i*6364136223846793005 + 1, as
+ * the reference does; after a 3-pass warm-up, each of `repeats` samples times
+ * `passes` full sweeps of 16-byte streaming loads with CUDA events and stores
+ * bytes*passes/seconds/1e9 in gb_per_s[r]. *checksum receives the XOR of all
+ * words (one sweep). Allocates and frees its array (a measurement tool, not a
+ * serving path); runs on its own stream and synchronises. Invalid sizes give
+ * DCB_ERR_ARGUMENT ("invalid sweep parameters", the reference's message). */
+int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* gb_per_s, uint64_t* checksum);
+
 /* ---- batched decode of independent sequences (one GPU) --------------------
  * No counterpart in the reference, which decodes one sequence per Engine
  * (src/model.cpp:258-329); a caller with many sequences would run one Engine

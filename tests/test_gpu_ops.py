@@ -100,3 +100,18 @@ def test_rmsnorm_rope_argmax():
         dcb.argmax(dv.data_ptr(), n, o.data_ptr())
         torch.cuda.synchronize()
         assert int(o.item()) == oracle.argmax(v)
+
+
+def test_read_bandwidth_probe_sweeps_the_whole_array():
+    """The HBM read probe (tools/bandwidth.cpp's sweep on the GPU): the XOR of
+    all words of the i*6364136223846793005+1 pattern matches numpy, every sample
+    is a positive rate, and sizes out of range are refused with the reference's
+    message."""
+    mib = 64
+    r = dcb.read_bandwidth(mib=mib, passes=2, repeats=3)
+    n = (mib << 20) // 8
+    words = np.arange(n, dtype=np.uint64) * np.uint64(6364136223846793005) + np.uint64(1)
+    assert r["checksum"] == int(np.bitwise_xor.reduce(words))
+    assert len(r["samples"]) == 3 and all(s["GB_per_s"] > 0 for s in r["samples"])
+    with pytest.raises(ValueError, match="invalid sweep parameters"):
+        dcb.read_bandwidth(mib=16)

@@ -190,3 +190,11 @@ def test_sum_words_are_exact_order_free_and_self_counting():
     assert _decode(top)[0] == 255
     bottom = sum(_sum_word(-2.0 ** 21) for _ in range(255)) & mask
     assert _decode(bottom)[0] == 255
+
+
+@pytest.mark.parametrize("mib,passes,repeats", [(16, 1, 1), (65537, 1, 1), (64, 0, 1), (64, 1, 0)])
+def test_read_bandwidth_probe_rejects_invalid_sweeps(mib, passes, repeats):
+    """The HBM read probe checks its sizes before touching a device, with the
+    reference's message (tools/bandwidth.cpp:72-73)."""
+    with pytest.raises(ValueError, match="invalid sweep parameters"):
+        dcb.read_bandwidth(mib=mib, passes=passes, repeats=repeats)
