@@ -3,6 +3,7 @@
 // launches one cooperative step kernel (step_kernel.cuh) per token.
 #include "decode_b200.h"
 #include "model_view.h"
+#include "role_kernel.cuh"
 #include "step_kernel.cuh"
 
 #include <cuda_runtime.h>
@@ -75,6 +76,12 @@ struct dcb_engine {
     // attended positions on, splits of at least group_split_min positions.
     bool gqa_ok = false;
     int group_min = 1024, group_split_min = 64;
+    // The two-role step kernel (role_kernel.cuh): used for one GPU when every
+    // attended position fits in an attention block's resident buffers.
+    RoleParams R{};
+    bool role_ok = false, role_on = true;
+    void* role_kernel = nullptr;
+    int role_smem = 0, role_max_pos = 0;
 
     ~dcb_engine() {
         cudaSetDevice(device);
@@ -181,6 +188,12 @@ void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len, 
     *nsplit = ceil_div(length, *split_len);
 }
 
+// The two-role kernel takes the step when it is set up, one GPU keeps the
+// whole sequence and every attended position fits in its resident buffers.
+bool use_role(const dcb_engine* e) {
+    return e->role_ok && e->role_on && e->P.world == 1 && e->kv_base == 0 && e->pos + 1 <= (size_t)e->role_max_pos;
+}
+
 int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax_dev, float* host_logits = nullptr) {
     StepArgs A{};
     A.host_logits = host_logits;
@@ -194,6 +207,13 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
     A.seq = e->seq;
     A.par = e->par;
     e->par ^= 1;
+    if (use_role(e)) {
+        void* args[] = {(void*)&e->R, (void*)&A};
+        DCB_CUDA(cudaLaunchCooperativeKernel(e->role_kernel, dim3(e->grid), dim3(NT), args, (size_t)e->role_smem,
+                                             e->stream));
+        ++e->launches;
+        return 0;
+    }
     void* args[] = {(void*)&e->P, (void*)&A};
     DCB_CUDA(cudaLaunchCooperativeKernel(e->kernel, dim3(e->grid), dim3(NT), args, (size_t)e->smem, e->stream));
     ++e->launches;
@@ -215,6 +235,190 @@ int check_device_error(dcb_engine* e) {
     int err = 0;
     DCB_CUDA(cudaMemcpy(&err, &e->P.sync->error, sizeof(int), cudaMemcpyDeviceToHost));
     return device_error(e, err);
+}
+
+// The two-role kernel's layout: per attention block (2 per query head) its
+// QKV rows packed in the order the kernel reads them, per FFN block its
+// columns of W_down; both sized from the grid. Shapes the kernel does not
+// take (or that do not fit in shared memory) leave role_ok false: the step
+// kernel of step_kernel.cuh then runs every step.
+int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
+    const Params& P = e->P;
+    RoleParams& R = e->R;
+    const int H = e->H, I = e->I, D = e->D, half = D / 2, G = e->grid, NH = e->NH, NKV = e->NKV;
+    const int hpg = NH / NKV;
+    R.NA = 2 * NH;
+    R.NG = G - R.NA;
+    if (R.NG < 1 || H % 4 || NH > 255 || H > SLICE_RPT * SLICE_T) return 0;
+    R.H = H;
+    R.I = I;
+    R.L = e->L;
+    R.NH = NH;
+    R.NKV = NKV;
+    R.D = D;
+    R.V = e->V;
+    R.Kh = P.Kh;
+    R.SH = P.SH;
+    R.eps = P.eps;
+    R.cached_rope = P.cached_rope;
+    R.capacity = P.capacity;
+    R.q_first = (half + 1) / 2;
+    R.o_first = (int)round_up((size_t)(H / 2), 4);
+    R.o_dw = P.o_dw;
+    R.o_slice = P.o_slice;
+    R.o_cols = P.o_cols;
+    R.o_scale = P.o_scale;
+    R.layers = P.layers;
+    R.down_scale = P.down_scale;
+    R.embed = P.embed;
+    R.norms = P.norms;
+    R.rope_inv = P.rope_inv;
+    R.rope_den = P.rope_den;
+    R.kcache = P.kcache;
+    R.vcache = P.vcache;
+    R.ll_q = P.ll_q;
+    R.ll_kv = P.ll_kv;
+    R.dacc = P.dacc;
+    R.Hp = P.Hp;
+    R.logits = P.logits;
+    R.amax = P.amax;
+    R.sync = P.sync;
+    R.trace = nullptr;
+    R.trace_layer = P.trace_layer;
+    R.xq_plane = P.xq_plane;
+    auto plo = [](int b, int n, int total) { return (int)((long long)b * total / n); };
+    // QKV rows per attention block a = 2h + s: q pairs [q0, q0 + nq) of head h,
+    // then k/v pairs [kv0, kv0 + nkv) of its group (u < D/2: k, else v).
+    struct Share { int h, g, q0, nq, kv0, nkv; };
+    std::vector<Share> sh(R.NA);
+    int ra_max = 0;
+    for (int a = 0; a < R.NA; ++a) {
+        Share& x = sh[a];
+        x.h = a / 2;
+        const int s = a % 2;
+        x.g = x.h / hpg;
+        x.q0 = s ? R.q_first : 0;
+        x.nq = s ? half - R.q_first : R.q_first;
+        const int mi = 2 * (x.h % hpg) + s;
+        x.kv0 = plo(mi, 2 * hpg, D);
+        x.nkv = plo(mi + 1, 2 * hpg, D) - x.kv0;
+        ra_max = std::max(ra_max, 2 * (x.nq + x.nkv));
+    }
+    const int gmax = ceil_div(I, R.NG);
+    if (ra_max > 2 * RA_ROWS_MAX || 2 * gmax > 2 * RG_ROWS_MAX || gmax > NT) return 0;
+    R.ra_stride = ra_max;
+    R.dw = slice_row_bytes(gmax);
+    if (R.dw > 4 * (ROLE_PLANE / 4) - 16 || R.o_dw > ROLE_PLANE - 16) return 0;
+    R.down_slice = (int)round_up((size_t)H * R.dw, 16);
+    R.dcontrib = 0;
+    for (int f = 0; f < R.NG; ++f) R.dcontrib += plo(f + 1, R.NG, I) > plo(f, R.NG, I);
+    if (R.dcontrib > 255) return 0;
+    // KV rows and the resident chunk buffers.
+    const size_t es = e->kv_elem();
+    R.bulk_kv = ((size_t)D * es) % 16 == 0;
+    R.chunk_bytes = (int)round_up(2 * (size_t)ATT_CHUNK * D * es, 128);
+    // Shared memory: vectors both roles use, then either role's region.
+    cudaFuncAttributes fattr;
+    const bool f16 = e->kv_dtype == DCB_KV_F16;
+    void* k = D <= 32   ? (f16 ? (void*)role_step_kernel<__half, 1> : (void*)role_step_kernel<float, 1>)
+              : D <= 64 ? (f16 ? (void*)role_step_kernel<__half, 2> : (void*)role_step_kernel<float, 2>)
+                        : (f16 ? (void*)role_step_kernel<__half, 4> : (void*)role_step_kernel<float, 4>);
+    if (cudaFuncGetAttributes(&fattr, k) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
+    const size_t budget = (size_t)max_optin - fattr.sharedSizeBytes;
+    size_t off = 0;
+    R.off_xf = (int)off;
+    off = round_up(off + (size_t)P.Kh * 4, 128);
+    R.off_xq = (int)off;
+    off = round_up(off + 3 * (size_t)P.xq_plane, 128);
+    R.off_xr = (int)off;
+    off = round_up(off + (size_t)P.Kh * 4, 128);
+    R.off_misc = (int)off;
+    off = round_up(off + ROLE_MISC_BYTES, 128);
+    const size_t base = off;
+    R.a_qkv = (int)off;
+    off = round_up(off + (size_t)ra_max * P.SH, 128);
+    R.a_o = (int)off;
+    off = round_up(off + (size_t)std::max(R.o_first, H - R.o_first) * R.o_dw, 128);
+    R.a_part = (int)off;
+    off = round_up(off + (size_t)std::max(NW * ra_max, NW * (D + 1)) * 4, 128);
+    R.a_sc = (int)off;
+    off = round_up(off + (size_t)RES_POS_MAX * 4, 128);
+    R.a_ring = (int)off;
+    const size_t attn_fixed = off;
+    off = base;
+    R.g_gu = (int)off;
+    off = round_up(off + (size_t)2 * gmax * P.SH, 128);
+    R.g_down = (int)off;
+    off = round_up(off + (size_t)R.down_slice, 128);
+    R.g_part = (int)off;
+    off = round_up(off + (size_t)NW * 2 * gmax * 4, 128);
+    R.g_h = (int)off;
+    off = round_up(off + (size_t)std::max(R.dw, 32) * 4, 128);
+    const size_t ffn_end = off;
+    if (attn_fixed >= budget || ffn_end > budget) return 0;
+    R.nbufs = (int)std::min<size_t>(RES_BUFS_MAX, (budget - attn_fixed) / R.chunk_bytes);
+    if (R.nbufs < 1) return 0;
+    const size_t smem = std::max(attn_fixed + (size_t)R.nbufs * R.chunk_bytes, ffn_end);
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, NT, smem) != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        return 0;
+    }
+    // Packed QKV rows per (layer, attention block), zero rows past its count.
+    std::vector<uint8_t> buf((size_t)e->L * R.NA * ra_max * P.SH, 0);
+    for (int l = 0; l < e->L; ++l) {
+        const dcb_layer_desc& S = m->layer[l];
+        for (int a = 0; a < R.NA; ++a) {
+            const Share& x = sh[a];
+            uint8_t* dst = &buf[((size_t)l * R.NA + a) * ra_max * P.SH];
+            int row = 0;
+            auto put = [&](const int8_t* w, const float* sc, const float* bi, int r) {
+                pack_row(dst + (size_t)(row++) * P.SH, w + (size_t)r * H, H, sc[r], bi[r]);
+            };
+            for (int j = x.q0; j < x.q0 + x.nq; ++j) {
+                put(S.q, S.q_scales, S.q_bias, x.h * D + j);
+                put(S.q, S.q_scales, S.q_bias, x.h * D + j + half);
+            }
+            for (int u = x.kv0; u < x.kv0 + x.nkv; ++u) {
+                if (u < half) {
+                    put(S.k, S.k_scales, S.k_bias, x.g * D + u);
+                    put(S.k, S.k_scales, S.k_bias, x.g * D + u + half);
+                } else {
+                    put(S.v, S.v_scales, S.v_bias, x.g * D + u - half);
+                    put(S.v, S.v_scales, S.v_bias, x.g * D + u);
+                }
+            }
+        }
+    }
+    uint8_t* d8;
+    if (int rc = upload(e, &d8, buf)) return rc;
+    R.qkv = d8;
+    // W_down column slices per (layer, FFN block), dw bytes per row.
+    buf.assign((size_t)e->L * R.NG * R.down_slice, 0);
+    for (int l = 0; l < e->L; ++l) {
+        const dcb_layer_desc& S = m->layer[l];
+        for (int f = 0; f < R.NG; ++f) {
+            const int c0 = plo(f, R.NG, I), c1 = plo(f + 1, R.NG, I);
+            uint8_t* dst = &buf[((size_t)l * R.NG + f) * R.down_slice];
+            for (int r = 0; r < H; ++r) std::memcpy(dst + (size_t)r * R.dw, S.down + (size_t)r * I + c0, (size_t)(c1 - c0));
+        }
+    }
+    if (int rc = upload(e, &d8, buf)) return rc;
+    R.down_cols = d8;
+    e->role_kernel = k;
+    e->role_smem = (int)smem;
+    e->role_max_pos = R.nbufs * ATT_CHUNK;
+    e->role_ok = true;
+    if (const char* v = std::getenv("DCB_ROLE")) e->role_on = std::atoi(v) != 0;
+    R.coarse_down = 8;
+    R.coarse_o = 2;
+    if (const char* v = std::getenv("DCB_COARSE_DOWN")) R.coarse_down = std::atoi(v);
+    if (const char* v = std::getenv("DCB_COARSE_O")) R.coarse_o = std::atoi(v);
+    return 0;
 }
 
 // Head-major cache offset (elements) of (layer, kv head, position).
@@ -508,6 +712,8 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->kernel, NT, e->smem) != cudaSuccess || per_sm < 1)
         return bail(fail(DCB_ERR_UNSUPPORTED, "step kernel cannot be resident"));
 
+    if (int rc = setup_role(e, m, max_optin)) return bail(rc);
+
     if (cudaMallocHost(&e->h_result, 4 * sizeof(int)) != cudaSuccess)
         return bail(fail(DCB_ERR_CUDA, "cudaMallocHost failed"));
     if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -736,7 +942,7 @@ int dcb_launch_info(const dcb_engine* e, int* blocks, int* threads, int* smem_by
     if (!e) return fail(DCB_ERR_ARGUMENT, "null engine");
     if (blocks) *blocks = e->grid;
     if (threads) *threads = NT;
-    if (smem_bytes) *smem_bytes = e->smem;
+    if (smem_bytes) *smem_bytes = e->role_ok && e->role_on ? e->role_smem : e->smem;
     if (sms) *sms = e->sms;
     return 0;
 }
@@ -752,6 +958,7 @@ int dcb_trace_enable(dcb_engine* e, int on) {
         if (int rc = e->alloc(&e->trace, (size_t)2 * TRACE_MAX_PHASES * e->grid)) return rc;
     }
     e->P.trace = on ? e->trace : nullptr;
+    e->R.trace = e->P.trace;
     return 0;
 }
 

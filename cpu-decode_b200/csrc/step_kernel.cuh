@@ -191,6 +191,7 @@ __device__ __forceinline__ void fill_slot(void* dst, const void* src, uint32_t b
     ++*fills;
     mbar_expect(m, bytes);
     constexpr uint32_t piece = 32768;
+#pragma unroll 1
     for (uint32_t o = 0; o < bytes; o += piece) {
         const uint32_t n = bytes - o < piece ? bytes - o : piece;
         bulk_load(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, n, m);
@@ -475,6 +476,8 @@ __device__ __forceinline__ float dacc_value(uint64_t w) {
 // values in xr, folds in the RMSNorm gain, quantises with its own scale
 // (wscale) and leaves its share of sum x^2 in ss_out[warp]. Returns false
 // when the wait ran out (the abort flag is set); one decision per warp.
+// ADD false: the sums are the whole vector (x = sums; xr only receives it).
+template <bool ADD = true>
 static __device__ bool warp_stage_sum(const uint64_t* acc, unsigned expect, int n, float* xr, float* xf, int8_t* xq,
                                       int plane, int nch, const float* gain, float* ss_out, float& wscale,
                                       const BlockState& st) {
@@ -517,7 +520,7 @@ static __device__ bool warp_stage_sum(const uint64_t* acc, unsigned expect, int 
         for (int k = 0; k < 2; ++k) {
             const int j = base + lane + 32 * k;
             if (j < e1) {
-                const float v = xr[j] + dacc_value(w[k]);
+                const float v = ADD ? xr[j] + dacc_value(w[k]) : dacc_value(w[k]);
                 xr[j] = v;
                 const float gv = v * g[k];
                 xf[j] = gv;
@@ -576,7 +579,8 @@ static __device__ void slice_partial(const uint8_t* slice, int DW, int H, const 
 // Block-wide staging of x = xr + down sums (the final norm's input): thread t
 // polls the sum words t, t + NT (H <= 2*NT) until `expect` blocks have added,
 // then the vector is reduced and quantised as in finish_stage. Returns false
-// when the step must abort.
+// when the step must abort. ADD false: x = sums (xr is not read).
+template <bool ADD = true>
 static __device__ bool stage_sum(const uint64_t* acc, unsigned expect, int n, int nch, const float* xr, float* xf,
                                  int8_t* xq, int plane, const float* gain, float* red, float eps, Staged& out,
                                  const BlockState& st) {
@@ -607,7 +611,7 @@ static __device__ bool stage_sum(const uint64_t* acc, unsigned expect, int n, in
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
         const int j = threadIdx.x + k * NT;
-        if (j < n) accept(j, xr[j] + dacc_value(w[k]), nullptr, xf, __ldg(gain + j), ss, mx);
+        if (j < n) accept(j, (ADD ? xr[j] : 0.f) + dacc_value(w[k]), nullptr, xf, __ldg(gain + j), ss, mx);
     }
     out = finish_stage(n, nch, xf, xq, plane, ss, mx, red, eps);
     return !should_abort(st);
