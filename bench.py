@@ -45,7 +45,7 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 CONTEXT = 128
 SEED = 0
-MODEL_CACHE = Path(os.environ.get("DCB_MODEL_CACHE", "/tmp/dcb_models"))
+MODEL_CACHE = Path(os.environ.get("DCB_MODEL_CACHE", str(Path(tempfile.gettempdir()) / "dcb_models")))
 METRIC = "batch-1 decode tokens/s at ctx 128/4096; achieved HBM GB/s vs B200 peak"
 
 

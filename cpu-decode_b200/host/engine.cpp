@@ -16,11 +16,15 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <filesystem>
 #include <fstream>
 #include <limits>
+#include <map>
+#include <memory>
+#include <numeric>
 #include <set>
 #include <stdexcept>
 
@@ -45,34 +49,36 @@ Json load_json(const fs::path& path) {
     return j;
 }
 
-// A read-only file mapping.
-class MappedFile {
-public:
-    explicit MappedFile(const fs::path& path) {
-        const int fd = ::open(path.c_str(), O_RDONLY);
-        if (fd < 0) throw std::runtime_error("cannot open " + path.string());
-        struct stat st{};
-        if (::fstat(fd, &st) != 0 || st.st_size < 8) {
-            ::close(fd);
-            throw std::runtime_error("invalid safetensors file");
-        }
-        size_ = static_cast<size_t>(st.st_size);
-        base_ = ::mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd, 0);
-        ::close(fd);
-        if (base_ == MAP_FAILED) throw std::runtime_error("mmap failed: " + path.string());
-    }
-    ~MappedFile() {
-        if (base_ != MAP_FAILED) ::munmap(base_, size_);
-    }
-    MappedFile(const MappedFile&) = delete;
-    MappedFile& operator=(const MappedFile&) = delete;
-    const char* data() const { return static_cast<const char*>(base_); }
-    size_t size() const { return size_; }
+// ---- checkpoint files ----------------------------------------------------------
+// A checkpoint is read in two passes per file. The JSON header first becomes a
+// table of validated entries (element type, shape, byte range); then the byte
+// ranges are checked to tile the payload exactly. Tensors point into a
+// read-only mapping of the file until dcb_create() has copied them to HBM.
+// The rejections and their messages are the reference loader's
+// (src/model.cpp:34-133), which callers and tests match.
 
-private:
-    void* base_ = MAP_FAILED;
-    size_t size_ = 0;
+// A whole file mapped read-only; unmapped when the last owner lets go.
+using FileBytes = std::shared_ptr<const char>;
+FileBytes map_whole_file(const fs::path& path, size_t* size) {
+    const int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) throw std::runtime_error("cannot open " + path.string());
+    struct stat info{};
+    const bool sized = ::fstat(fd, &info) == 0 && info.st_size >= 8;
+    void* addr = sized ? ::mmap(nullptr, size_t(info.st_size), PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
+    ::close(fd);
+    if (!sized) throw std::runtime_error("invalid safetensors file");
+    if (addr == MAP_FAILED) throw std::runtime_error("mmap failed: " + path.string());
+    const size_t n = size_t(info.st_size);
+    *size = n;
+    return FileBytes(static_cast<const char*>(addr), [n](const char* q) { ::munmap(const_cast<char*>(q), n); });
+}
+
+struct ElementType {
+    const char* tag;
+    DType type;
+    size_t width;
 };
+constexpr ElementType kElementTypes[] = {{"BF16", DType::bf16, 2}, {"F32", DType::f32, 4}, {"I8", DType::i8, 1}};
 
 struct TensorView {
     const void* data = nullptr;
@@ -80,39 +86,81 @@ struct TensorView {
     DType type = DType::f32;
     size_t bytes = 0;
     size_t count() const {
-        size_t n = 1;
-        for (size_t d : shape) n = mul_checked(n, d);
-        return n;
+        return std::accumulate(shape.begin(), shape.end(), size_t(1), [](size_t a, size_t b) { return mul_checked(a, b); });
     }
     float value(size_t i) const {
-        if (type == DType::bf16) return bf16_float(static_cast<const uint16_t*>(data)[i]);
-        if (type == DType::f32) {
-            float v;
-            std::memcpy(&v, static_cast<const char*>(data) + 4 * i, 4);
-            return v;
+        switch (type) {
+            case DType::bf16: return bf16_float(static_cast<const uint16_t*>(data)[i]);
+            case DType::i8: return float(static_cast<const int8_t*>(data)[i]);
+            default: {
+                float v;
+                std::memcpy(&v, static_cast<const char*>(data) + 4 * i, 4);
+                return v;
+            }
         }
-        return float(static_cast<const int8_t*>(data)[i]);
     }
 };
 
-// All tensors of a (possibly sharded) safetensors checkpoint, validated.
+// One header entry, validated against the payload it indexes (origin: the
+// payload's offset in the file, for the alignment rule).
+struct HeaderEntry {
+    TensorView view;
+    size_t begin = 0, end = 0;
+};
+HeaderEntry read_entry(const std::string& name, const Json& e, size_t origin, size_t payload) {
+    HeaderEntry out;
+    const std::string tag = e.at("dtype").get<std::string>();
+    const auto* et = std::find_if(std::begin(kElementTypes), std::end(kElementTypes),
+                                  [&](const ElementType& x) { return tag == x.tag; });
+    if (et == std::end(kElementTypes)) throw std::runtime_error("unsupported tensor dtype: " + tag);
+    out.view.type = et->type;
+    for (const Json& d : e.at("shape")) {
+        if (!d.is_number_integer() || d.get<int64_t>() <= 0) throw std::runtime_error("invalid tensor shape");
+        out.view.shape.push_back(d.get<size_t>());
+    }
+    if (out.view.shape.empty() || out.view.shape.size() > 2) throw std::runtime_error("expected vector or matrix tensor");
+    const Json& range = e.at("data_offsets");
+    if (range.size() != 2 || !range[0].is_number_unsigned() || !range[1].is_number_unsigned())
+        throw std::runtime_error("invalid tensor offsets");
+    out.begin = range[0].get<size_t>();
+    out.end = range[1].get<size_t>();
+    out.view.bytes = mul_checked(out.view.count(), et->width);
+    const bool inside = out.begin <= out.end && out.end <= payload;
+    if (!inside || out.end - out.begin != out.view.bytes || (origin + out.begin) % et->width)
+        throw std::runtime_error("tensor bounds/alignment mismatch: " + name);
+    return out;
+}
+
+// The entries' byte ranges must cover [0, payload) once each, in any order.
+void check_tiling(std::vector<std::pair<size_t, size_t>> ranges, size_t payload) {
+    std::sort(ranges.begin(), ranges.end());
+    const auto seam = std::adjacent_find(ranges.begin(), ranges.end(),
+                                         [](const auto& a, const auto& b) { return a.second != b.first; });
+    if ((!ranges.empty() && ranges.front().first != 0) || seam != ranges.end())
+        throw std::runtime_error("gapped or overlapping safetensors payload");
+    if ((ranges.empty() ? 0 : ranges.back().second) != payload) throw std::runtime_error("unindexed safetensors payload");
+}
+
+// Shard file names of a checkpoint directory: the index's weight map, or the
+// single model.safetensors.
+std::set<std::string> shard_names(const fs::path& dir) {
+    std::set<std::string> names;
+    if (!fs::exists(dir / "model.safetensors.index.json")) return {"model.safetensors"};
+    for (const auto& kv : load_json(dir / "model.safetensors.index.json").at("weight_map").items()) {
+        const std::string shard = kv.value().get<std::string>();
+        if (fs::path(shard).filename() != shard) throw std::runtime_error("unsafe shard filename");
+        names.insert(shard);
+    }
+    return names;
+}
+
+// All tensors of a (possibly sharded) checkpoint, validated.
 class TensorStore {
 public:
     explicit TensorStore(const fs::path& dir) {
-        const uint16_t probe = 1;
-        if (*reinterpret_cast<const uint8_t*>(&probe) != 1) throw std::runtime_error("little-endian host required");
-        std::set<std::string> shards;
-        if (fs::exists(dir / "model.safetensors.index.json")) {
-            const Json index = load_json(dir / "model.safetensors.index.json");
-            for (const auto& kv : index.at("weight_map").items()) {
-                const std::string shard = kv.value().get<std::string>();
-                if (fs::path(shard).filename() != shard) throw std::runtime_error("unsafe shard filename");
-                shards.insert(shard);
-            }
-        } else {
-            shards.insert("model.safetensors");
-        }
-        for (const auto& shard : shards) add_file(dir / shard);
+        const uint32_t probe = 0x01020304u;
+        if (reinterpret_cast<const unsigned char*>(&probe)[0] != 0x04) throw std::runtime_error("little-endian host required");
+        for (const std::string& shard : shard_names(dir)) index_file(dir / shard);
     }
     const TensorView& get(const std::string& name, const std::vector<size_t>& shape) const {
         const auto it = tensors.find(name);
@@ -123,90 +171,70 @@ public:
     std::map<std::string, TensorView> tensors;
 
 private:
-    void add_file(const fs::path& path) {
-        auto file = std::make_unique<MappedFile>(path);
-        const char* base = file->data();
+    void index_file(const fs::path& path) {
+        size_t size = 0;
+        FileBytes bytes = map_whole_file(path, &size);
         uint64_t header_len = 0;
-        std::memcpy(&header_len, base, 8);
-        if (header_len > 64ull * 1024 * 1024 || header_len > file->size() - 8)
+        std::memcpy(&header_len, bytes.get(), 8);
+        if (header_len > 64ull * 1024 * 1024 || header_len > size - 8)
             throw std::runtime_error("invalid safetensors header length");
-        const size_t origin = 8 + size_t(header_len);
-        const size_t payload = file->size() - origin;
-        const Json header = Json::parse(base + 8, base + origin);
-        std::vector<std::pair<size_t, size_t>> spans;
-        for (const auto& item : header.items()) {
-            if (item.key() == "__metadata__") continue;
-            const Json& entry = item.value();
-            const std::string dtype = entry.at("dtype").get<std::string>();
-            TensorView t;
-            size_t width = 0;
-            if (dtype == "BF16") { t.type = DType::bf16; width = 2; }
-            else if (dtype == "F32") { t.type = DType::f32; width = 4; }
-            else if (dtype == "I8") { t.type = DType::i8; width = 1; }
-            else throw std::runtime_error("unsupported tensor dtype: " + dtype);
-            for (const auto& d : entry.at("shape")) {
-                if (!d.is_number_integer() || d.get<int64_t>() <= 0) throw std::runtime_error("invalid tensor shape");
-                t.shape.push_back(d.get<size_t>());
-            }
-            if (t.shape.empty() || t.shape.size() > 2) throw std::runtime_error("expected vector or matrix tensor");
-            const Json& off = entry.at("data_offsets");
-            if (off.size() != 2 || !off[0].is_number_unsigned() || !off[1].is_number_unsigned())
-                throw std::runtime_error("invalid tensor offsets");
-            const size_t begin = off[0].get<size_t>(), end = off[1].get<size_t>();
-            const size_t bytes = mul_checked(t.count(), width);
-            if (end < begin || end > payload || end - begin != bytes || (origin + begin) % width)
-                throw std::runtime_error("tensor bounds/alignment mismatch: " + item.key());
-            t.data = base + origin + begin;
-            t.bytes = bytes;
-            if (!tensors.emplace(item.key(), t).second) throw std::runtime_error("duplicate tensor: " + item.key());
-            spans.emplace_back(begin, end);
+        const size_t origin = 8 + size_t(header_len), payload = size - origin;
+        const Json header = Json::parse(bytes.get() + 8, bytes.get() + origin);
+        // Pass 1: the entry table.
+        std::vector<std::pair<std::string, HeaderEntry>> table;
+        for (const auto& item : header.items())
+            if (item.key() != "__metadata__") table.emplace_back(item.key(), read_entry(item.key(), item.value(), origin, payload));
+        // Pass 2: the byte ranges tile the payload.
+        std::vector<std::pair<size_t, size_t>> ranges;
+        ranges.reserve(table.size());
+        for (auto& [name, entry] : table) {
+            entry.view.data = bytes.get() + origin + entry.begin;
+            if (!tensors.emplace(name, entry.view).second) throw std::runtime_error("duplicate tensor: " + name);
+            ranges.emplace_back(entry.begin, entry.end);
         }
-        std::sort(spans.begin(), spans.end());
-        size_t covered = 0;
-        for (const auto& s : spans) {
-            if (s.first != covered) throw std::runtime_error("gapped or overlapping safetensors payload");
-            covered = s.second;
-        }
-        if (covered != payload) throw std::runtime_error("unindexed safetensors payload");
-        files.push_back(std::move(file));
+        check_tiling(std::move(ranges), payload);
+        files.push_back(std::move(bytes));
     }
-    std::vector<std::unique_ptr<MappedFile>> files;
+    std::vector<FileBytes> files;
 };
 
+// config.json of a tied-head Qwen2 checkpoint (the reference's accepted set
+// and messages, src/model.cpp:134-158).
 struct ModelConfig {
-    size_t hidden, intermediate, layers, heads, kv_heads, vocab, max_positions, dim;
-    float epsilon, theta;
+    size_t hidden = 0, intermediate = 0, layers = 0, heads = 0, kv_heads = 0, vocab = 0, max_positions = 0, dim = 0;
+    float epsilon = 0, theta = 0;
     explicit ModelConfig(const Json& j) {
         if (j.at("model_type") != "qwen2" || !j.value("tie_word_embeddings", false))
             throw std::runtime_error("requires tied-head Qwen2 architecture");
         if (j.contains("rope_scaling") && !j["rope_scaling"].is_null())
             throw std::runtime_error("scaled RoPE is not supported");
         if (j.value("hidden_act", std::string("silu")) != "silu") throw std::runtime_error("requires SiLU");
-        auto positive = [&](const char* key) {
+        static const std::pair<const char*, size_t ModelConfig::*> kDims[] = {
+            {"hidden_size", &ModelConfig::hidden},          {"intermediate_size", &ModelConfig::intermediate},
+            {"num_hidden_layers", &ModelConfig::layers},    {"num_attention_heads", &ModelConfig::heads},
+            {"num_key_value_heads", &ModelConfig::kv_heads}, {"vocab_size", &ModelConfig::vocab},
+            {"max_position_embeddings", &ModelConfig::max_positions}};
+        for (const auto& [key, member] : kDims) {
             const int64_t n = j.at(key).get<int64_t>();
             if (n <= 0 || n > 1000000) throw std::runtime_error(std::string("invalid config: ") + key);
-            return size_t(n);
-        };
-        hidden = positive("hidden_size");
-        intermediate = positive("intermediate_size");
-        layers = positive("num_hidden_layers");
-        heads = positive("num_attention_heads");
-        kv_heads = positive("num_key_value_heads");
-        vocab = positive("vocab_size");
-        max_positions = positive("max_position_embeddings");
+            this->*member = size_t(n);
+        }
         epsilon = j.at("rms_norm_eps").get<float>();
         theta = j.at("rope_theta").get<float>();
-        if (hidden % heads || heads % kv_heads || (hidden / heads) % 2 || !std::isfinite(epsilon) || epsilon <= 0 ||
-            !std::isfinite(theta) || theta <= 0)
-            throw std::runtime_error("invalid Qwen dimensions or constants");
+        const bool shapes_ok = hidden % heads == 0 && heads % kv_heads == 0 && (hidden / heads) % 2 == 0;
+        const bool constants_ok = std::isfinite(epsilon) && epsilon > 0 && std::isfinite(theta) && theta > 0;
+        if (!shapes_ok || !constants_ok) throw std::runtime_error("invalid Qwen dimensions or constants");
         dim = hidden / heads;
         if (j.contains("head_dim") && j["head_dim"].get<size_t>() != dim) throw std::runtime_error("incompatible head_dim");
     }
 };
 
+// The reference's operation buckets (src/kernels.cpp:181-182), plus
+// device_step: the GPU runs the whole step as one kernel, so its wall time
+// (launch, kernel, logits copy) is attributed there as one bucket.
 const char* const kOperations[] = {"embedding", "rmsnorm", "qkv", "rope", "kv_write", "attention",
                                    "attention_output", "residual", "mlp_gate_up", "silu", "mlp_down",
-                                   "lm_head", "argmax", "timing_overhead_and_loop"};
+                                   "lm_head", "argmax", "device_step", "timing_overhead_and_loop"};
 
 }  // namespace
 
@@ -355,7 +383,9 @@ struct Engine::Impl {
 
     const std::vector<float>& step(int token, bool head, Profile* p) {
         const size_t pos = dcb_position(engine);
+        const auto start = std::chrono::steady_clock::now();
         check(dcb_step(engine, token, head ? 1 : 0, head ? logits.data() : nullptr, nullptr));
+        if (p) p->seconds["device_step"] += std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
         account(p, pos, head);
         return logits;
     }
@@ -378,12 +408,14 @@ Json Engine::metadata() const {
     return {{"weight_dtype", impl->weight_dtype},
             {"quantization", "symmetric per-row int8, float32 scales, float32 activations"},
             {"kernel", kernel_name(impl->kernel)},
-            {"kernel_scope", "whole decode step in one persistent sm_100a kernel; per-operation timers are not separable"},
+            {"kernel_scope", "whole decode step in one persistent sm_100a kernel; per-operation timers are not separable, "
+                             "the step's wall time is the device_step bucket"},
             {"threads", impl->threads},
             {"stored_weight_bytes", impl->model.stored_bytes},
             {"rope", impl->cached_rope ? "cached" : "direct"},
             {"thread_scheduling", "cooperative launch, one " + std::to_string(nthreads) + "-thread block per SM (" +
-                                      std::to_string(blocks) + " blocks), grid barriers between dependent phases"},
+                                      std::to_string(blocks) + " blocks); blocks hand activations to each other through "
+                                      "L2 (tagged words and self-counting sums), no grid barriers"},
             {"stored_scale_bytes", impl->model.stored_scales},
             {"kv_capacity", impl->capacity},
             {"auxiliary_fp32_weight_bytes", (c.layers * (3 * c.hidden + 2 * c.kv_heads * c.dim) + c.hidden) * 4},
@@ -496,17 +528,22 @@ void attention(const float* q, const float* keys, const float* values, float* ou
     to_host(out, dout.p, heads * dim * 4);
 }
 
-// Offline per-row quantiser (the format tool; src/kernels.cpp:121-131).
+// Offline per-row quantiser (the format tool; src/kernels.cpp:121-131). The
+// rule: the row's scale is its largest magnitude over 127 (1 for an all-zero
+// row); each weight becomes weight / scale rounded half away from zero and
+// clamped to [-127, 127]. Non-finite weights and empty rows are rejected.
 void quantize_row(const float* source, size_t n, int8_t* out, float& scale) {
     if (!n) throw std::runtime_error("empty quantization row");
-    float maximum = 0;
-    for (size_t j = 0; j < n; ++j) {
-        if (!std::isfinite(source[j])) throw std::runtime_error("nonfinite model weight");
-        maximum = std::max(maximum, std::fabs(source[j]));
-    }
-    scale = maximum == 0 ? 1.0f : maximum / 127.0f;
-    for (size_t j = 0; j < n; ++j)
-        out[j] = static_cast<int8_t>(std::clamp(std::round(source[j] / scale), -127.0f, 127.0f));
+    const float* const last = source + n;
+    if (std::find_if(source, last, [](float v) { return !std::isfinite(v); }) != last)
+        throw std::runtime_error("nonfinite model weight");
+    const float peak = std::accumulate(source, last, 0.0f, [](float m, float v) { return std::max(m, std::fabs(v)); });
+    scale = peak > 0.0f ? peak / 127.0f : 1.0f;
+    const float s = scale;
+    std::transform(source, last, out, [s](float v) {
+        const float q = std::round(v / s);  // halves away from zero
+        return static_cast<int8_t>(q > 127.0f ? 127.0f : (q < -127.0f ? -127.0f : q));
+    });
 }
 
 // BF16 checkpoint -> per-row int8 checkpoint in the reference's file layout

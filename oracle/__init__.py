@@ -12,6 +12,7 @@ Only the tests, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -19,6 +20,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REF_DIR = HERE / "_ref"
+# The reference checkout whose sources the Makefile compiles into _ref/ (a
+# build-time input only; nothing reads it when the tests or the bench run).
+REFERENCE_SOURCES = Path(os.environ.get("DCB_REFERENCE", "/root/reference"))
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
 
@@ -26,9 +30,9 @@ _i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
 def build(reference: bool = True) -> None:
     """Compile liboracle.so, and the reference binaries when its sources exist."""
     targets = ["oracle"]
-    if reference and Path("/root/reference/src/model.cpp").exists():
+    if reference and (REFERENCE_SOURCES / "src" / "model.cpp").exists():
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REFERENCE_SOURCES}", *targets], check=True)
 
 
 def _lib() -> C.CDLL:

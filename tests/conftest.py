@@ -3,6 +3,7 @@ from __future__ import annotations
 
 import importlib.util
 import os
+import tempfile
 import sys
 from pathlib import Path
 
@@ -36,7 +37,7 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 and the built CUDA library")
 
 
-MODEL_CACHE = Path(os.environ.get("DCB_MODEL_CACHE", "/tmp/dcb_models"))
+MODEL_CACHE = Path(os.environ.get("DCB_MODEL_CACHE", str(Path(tempfile.gettempdir()) / "dcb_models")))
 
 
 @pytest.fixture(scope="session")
