@@ -2,6 +2,9 @@
 // attention, RMSNorm, RoPE and argmax, each on caller-provided device memory.
 // They share the device code of the fused step kernel, so the GEMV sweep and
 // the attention sweep measure the same inner loops.
+#include <mutex>
+#include <set>
+#include <utility>
 #include "decode_b200.h"
 #include "attention.cuh"
 #include "device.cuh"
@@ -230,6 +233,29 @@ int sm_count() {
     return n;
 }
 
+// Raise kernel k's dynamic shared-memory cap, once per device, to what the
+// device allows next to the kernel's static shared memory. Only ever raised:
+// threads launching the same kernel with different sizes cannot lower it
+// under one another, and later calls touch no attribute.
+std::mutex g_cap_mutex;
+std::set<std::pair<int, const void*>> g_cap_done;
+cudaError_t ensure_smem_cap(const void* k) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_cap_mutex);
+    if (g_cap_done.count({dev, k})) return cudaSuccess;
+    int optin = 0;
+    cudaFuncAttributes fa;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess ||
+        (e = cudaFuncGetAttributes(&fa, k)) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes)) !=
+            cudaSuccess)
+        return e;
+    g_cap_done.insert({dev, k});
+    return cudaSuccess;
+}
+
 template <int R, int U>
 int launch_gemv(const int8_t* w, const float* s, const float* b, const float* x, float* y, int rows, int cols,
                 cudaStream_t st) {
@@ -238,7 +264,7 @@ int launch_gemv(const int8_t* w, const float* s, const float* b, const float* x,
     const size_t smem = 3 * (size_t)cols;
     const void* k = (const void*)gemv_dp4a_kernel<R, U>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem_cap(k);
         if (e != cudaSuccess) return cuda_fail(e, "gemv shared memory");
     }
     void* args[] = {(void*)&w, (void*)&s, (void*)&b, (void*)&x, (void*)&y, (void*)&rows, (void*)&cols};
@@ -260,7 +286,7 @@ template <typename KV, int DT>
 cudaError_t launch_split(const AttnIO& io, size_t smem, cudaStream_t st) {
     const void* k = (const void*)attention_split_kernel<KV, DT>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem_cap(k);
         if (e != cudaSuccess) return e;
     }
     AttnIO a = io;
@@ -272,7 +298,7 @@ template <typename KV>
 cudaError_t launch_group(const AttnIO& io, size_t smem, cudaStream_t st) {
     const void* k = (const void*)attention_group_kernel<KV>;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem_cap(k);
         if (e != cudaSuccess) return e;
     }
     AttnIO a = io;
@@ -390,7 +416,10 @@ int dcb_argmax(const float* x, int n, int* out, void* stream) {
 int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* gb_per_s, uint64_t* checksum) {
     if (mib < 32 || mib > 65536 || passes < 1 || repeats < 1 || !gb_per_s)
         return fail(DCB_ERR_ARGUMENT, "invalid sweep parameters");
-    cudaError_t e = cudaSetDevice(device);
+    int caller_device = 0;
+    cudaError_t e = cudaGetDevice(&caller_device);
+    if (e != cudaSuccess) return cuda_fail(e, "current device");
+    e = cudaSetDevice(device);
     if (e != cudaSuccess) return cuda_fail(e, "read probe device");
     const size_t bytes = mib << 20, words = bytes / sizeof(uint64_t);
     int sms = 0;
@@ -436,6 +465,7 @@ int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* 
     if (st) cudaStreamDestroy(st);
     if (data) cudaFree(data);
     if (sum) cudaFree(sum);
+    cudaSetDevice(caller_device);  // the calling thread keeps its device
     return rc;
 }
 
@@ -447,7 +477,6 @@ int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* 
 // device memory per call. The array holds the split partials (heads x splits
 // x (dim + 2) floats); a call writes every word it reads, so nothing in it has
 // to start at zero.
-#include <mutex>
 
 namespace {
 constexpr size_t NOALLOC_BYTES = DCB_ATTENTION_NOALLOC_SCRATCH_BYTES;
@@ -464,19 +493,9 @@ struct NoallocDevice {
 };
 NoallocDevice g_noalloc[NOALLOC_MAX_DEVICES];
 
-template <typename KV, int DT>
-cudaError_t raise_smem_cap(int optin) {
-    cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, attention_split_kernel<KV, DT>);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(attention_split_kernel<KV, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                optin - (int)fa.sharedSizeBytes);
-}
-
-// Once per device, with that device current: the scratch's device address and
-// the kernel attributes (the dynamic shared memory cap raised to what the
-// device allows next to the kernels' static shared memory, so that later
-// calls leave the attributes as they are).
+// Once per device, with that device current: the scratch's device address
+// (the kernels' shared-memory caps are raised once per device by the launch
+// helpers, as for dcb_attention).
 void noalloc_setup(NoallocDevice& d, int dev) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
@@ -486,17 +505,9 @@ void noalloc_setup(NoallocDevice& d, int dev) {
         return;
     }
     d.scratch = static_cast<char*>(p);
-    int optin = 0;
-    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
-        (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) {
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) {
         d.status = e;
         d.what = "device attributes";
-        return;
-    }
-    if ((e = raise_smem_cap<float, 64>(optin)) != cudaSuccess || (e = raise_smem_cap<float, 0>(optin)) != cudaSuccess ||
-        (e = raise_smem_cap<__half, 64>(optin)) != cudaSuccess || (e = raise_smem_cap<__half, 0>(optin)) != cudaSuccess) {
-        d.status = e;
-        d.what = "attention kernel attributes";
     }
 }
 }  // namespace

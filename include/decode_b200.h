@@ -201,8 +201,8 @@ int dcb_attention(const float* q_in, const void* keys, const void* values, int k
  * (streams without ordering between them, or concurrent host threads) race on
  * it; issue them on one stream or order them with events. The first call on
  * each device does setup (it looks up the scratch's address with that device
- * current and sets kernel attributes) and should come before any stream
- * capture. */
+ * current and raises the attention kernels' shared-memory caps, once per
+ * device and never lowered) and should come before any stream capture. */
 enum { DCB_ATTENTION_NOALLOC_SCRATCH_BYTES = 1 << 20 };
 int dcb_attention_noalloc(const float* q_in, const void* keys, const void* values, int kv_dtype, float* out,
                           int length, int heads, int kv_heads, int dim, float rope_theta, void* stream);
@@ -225,9 +225,14 @@ int dcb_argmax(const float* x, int n, int* out, void* stream);
  * the reference does; after a 3-pass warm-up, each of `repeats` samples times
  * `passes` full sweeps of 16-byte streaming loads with CUDA events and stores
  * bytes*passes/seconds/1e9 in gb_per_s[r]. *checksum receives the XOR of all
- * words (one sweep). Allocates and frees its array (a measurement tool, not a
- * serving path); runs on its own stream and synchronises. Invalid sizes give
- * DCB_ERR_ARGUMENT ("invalid sweep parameters", the reference's message). */
+ * words from one extra sweep; the reference instead prints the XOR of its last
+ * timed repeat of `passes` sweeps, which is 0 for an even count, so only the
+ * one-sweep value checks the data. The size range is wider than the
+ * reference's (its limit is 1024 MiB, under which the B200's 126 MB L2 still
+ * holds much of a small array; figures reported here use 2 GiB). Allocates
+ * and frees its array (a measurement tool, not a serving path); runs on its
+ * own stream, synchronises, and leaves the calling thread's current device as
+ * it was. Invalid sizes give DCB_ERR_ARGUMENT ("invalid sweep parameters"). */
 int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* gb_per_s, uint64_t* checksum);
 
 /* ---- batched decode of independent sequences (one GPU) --------------------
