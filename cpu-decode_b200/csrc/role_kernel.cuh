@@ -198,32 +198,78 @@ __device__ __forceinline__ void slice_rows(const uint8_t* slice, int dw, int r0,
         const int r = r0 + (int)threadIdx.x + i * SLICE_T;
         if (r >= r1) break;
         const uint32_t* w = reinterpret_cast<const uint32_t*>(slice + (size_t)(r - r0) * dw);
-        float2 a = make_float2(0.f, 0.f), c2 = make_float2(0.f, 0.f);
+        float2 a0 = make_float2(0.f, 0.f), a1 = a0, a2 = a0, a3 = a0;
         int k = 0;
-#pragma unroll 4
-        for (; k + 1 < nw; k += 2) {
-            a = dot4(w[k], v4[k], a);
-            c2 = dot4(w[k + 1], v4[k + 1], c2);
+#pragma unroll 2
+        for (; k + 3 < nw; k += 4) {
+            a0 = dot4(w[k], v4[k], a0);
+            a1 = dot4(w[k + 1], v4[k + 1], a1);
+            a2 = dot4(w[k + 2], v4[k + 2], a2);
+            a3 = dot4(w[k + 3], v4[k + 3], a3);
         }
-        if (k < nw) a = dot4(w[k], v4[k], a);
-        float t = ((a.x + a.y) + (c2.x + c2.y)) * scale[i];
+        for (; k < nw; ++k) a0 = dot4(w[k], v4[k], a0);
+        float t = (((a0.x + a0.y) + (a1.x + a1.y)) + ((a2.x + a2.y) + (a3.x + a3.y))) * scale[i];
         if (fold) t += fold[r];
         dacc_add(acc + r, t);
     }
 }
 
+// Block GEMV of R packed rows in shared memory (stride S bytes, nch chunks of
+// 16 int8 each) with the staged planes: warp w covers chunks
+// [w*nch/NW, (w+1)*nch/NW) (at most ROLE_CPW), lane r the rows r + 32p,
+// p < PR, with every chunk's loads issued before its dp4a (the chunk loop is
+// unrolled). partial[w*R + r] = the warp's share times its staging scale;
+// the closing barrier publishes them. run false: only the barrier.
+constexpr int ROLE_CPW = 4;  // chunks per warp, at most (hidden <= 1024)
+template <int PR>
+__device__ __forceinline__ void role_gemv(const uint8_t* rows, int S, int R, int nch, const int8_t* xq, int plane,
+                                          float* partial, float wscale, bool run) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c0 = warp * nch / NW, c1 = (warp + 1) * nch / NW;
+    if (run) {
+        int ah[PR], am[PR], al[PR];
+#pragma unroll
+        for (int p = 0; p < PR; ++p) ah[p] = am[p] = al[p] = 0;
+#pragma unroll
+        for (int cc = 0; cc < ROLE_CPW; ++cc) {
+            const int c = c0 + cc;
+            if (c < c1) {
+                int4 h, m, l;
+                load_planes(xq, plane, c, h, m, l);
+#pragma unroll
+                for (int p = 0; p < PR; ++p) {
+                    const int r = lane + 32 * p;
+                    if (r < R)
+                        dp4a16(*reinterpret_cast<const int4*>(rows + (size_t)r * S + (size_t)c * 16), h, m, l, ah[p],
+                               am[p], al[p]);
+                }
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < PR; ++p) {
+            const int r = lane + 32 * p;
+            if (r < R) partial[warp * R + r] = planes_to_float(ah[p], am[p], al[p]) * wscale;
+        }
+    }
+    __syncthreads();
+}
+
 // Exact attention of one query head over positions [0, n) resident in the
 // chunk ring (the new row already written into its chunk), the reference's
 // src/kernels.cpp:150-179: scores q.k (q pre-scaled by log2(e)/sqrt(D)), the
-// maximum, 2^(s - max), their sum, then the weighted sum of V rows. Two passes
-// over all resident positions: no running rescale. Output in out[0..D).
-// sc: n scores; part: [16][D + 1] floats of partial sums.
+// maximum, 2^(s - max), their sum, then the weighted sum of V rows. Every
+// position is resident, so there is no running rescale:
+//   1. scores into sc[t] (8 lanes per position), each warp keeping the
+//      maximum of the scores it produced;
+//   2. the block maximum from the warps' maxima; thread t turns sc[t] into
+//      p_t = 2^(s_t - max) once;
+//   3. P.V: warp w takes positions t = w mod 16, lane d2 dims 2*d2, 2*d2+1
+//      (+64 per step); the 16 partial sums and weight sums are added in order.
+// Output in out[0..D). sc: n floats; part: [16][D + 1] floats; wmax: 16 floats.
 template <typename KV, int MD>
-__device__ __forceinline__ void attend_resident(const uint8_t* ring, int chunk_bytes, int D, int n, const float* sq, float* sc,
-                                float* part, float* out) {
+__device__ __forceinline__ void attend_resident(const uint8_t* ring, int chunk_bytes, int D, int n, const float* sq,
+                                                float* sc, float* part, float* wmax, float* out) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // Scores: the 8 lanes of group grp take position 4*warp + grp (+ 64 per
-    // pass); lane part p owns dims 32k + 4p + e, read as one vector.
     {
         const int grp = lane >> 3, pp = lane & 7;
         float qv[MD][4];
@@ -234,6 +280,7 @@ __device__ __forceinline__ void attend_resident(const uint8_t* ring, int chunk_b
                 const int j = 32 * k + 4 * pp + e;
                 qv[k][e] = j < D ? sq[j] : 0.f;
             }
+        float m_w = -INFINITY;
         for (int t0 = 0; t0 < n; t0 += ATT_CHUNK) {
             const int t = t0 + warp * 4 + grp;
             const KV* kb = reinterpret_cast<const KV*>(ring + (size_t)(t0 / ATT_CHUNK) * chunk_bytes);
@@ -257,31 +304,36 @@ __device__ __forceinline__ void attend_resident(const uint8_t* ring, int chunk_b
             s += __shfl_xor_sync(FULL, s, 4);
             s += __shfl_xor_sync(FULL, s, 2);
             s += __shfl_xor_sync(FULL, s, 1);
-            if (pp == 0 && t < n) sc[t] = s;
+            if (t < n) {
+                if (pp == 0) sc[t] = s;
+                m_w = fmaxf(m_w, s);
+            }
         }
+        m_w = fmaxf(m_w, __shfl_xor_sync(FULL, m_w, 8));
+        m_w = fmaxf(m_w, __shfl_xor_sync(FULL, m_w, 16));
+        if (lane == 0) wmax[warp] = m_w;
     }
     __syncthreads();
-    // Every warp finds the maximum itself (no barrier for it).
-    float M = -INFINITY;
-    for (int t = lane; t < n; t += 32) M = fmaxf(M, sc[t]);
-    M = warp_max(M);
-    // P.V: warp = position group (positions t = warp mod 16), lane = dim pair:
-    // dims 2*(lane + 32i) and +1; one 8-byte V load per two FMAs.
-    const int pg = warp, d2 = lane;
+    {
+        float M = lane < NW ? wmax[lane] : -INFINITY;
+        M = warp_max(M);
+        for (int t = tid; t < n; t += NT) sc[t] = ex2_approx(sc[t] - M);
+    }
+    __syncthreads();
     constexpr int ND2 = (MD + 1) / 2;
     float2 acc[ND2];
 #pragma unroll
     for (int i = 0; i < ND2; ++i) acc[i] = make_float2(0.f, 0.f);
     float lsum = 0.f;
-#pragma unroll 2
-    for (int t = pg; t < n; t += NW) {
-        const float p = ex2_approx(sc[t] - M);
+#pragma unroll 4
+    for (int t = warp; t < n; t += NW) {
+        const float p = sc[t];
         lsum += p;
         const KV* vr = reinterpret_cast<const KV*>(ring + (size_t)(t / ATT_CHUNK) * chunk_bytes) +
                        (size_t)ATT_CHUNK * D + (size_t)(t % ATT_CHUNK) * D;
 #pragma unroll
         for (int i = 0; i < ND2; ++i) {
-            const int d = 2 * (d2 + 32 * i);
+            const int d = 2 * (lane + 32 * i);
             if (d + 1 < D) {
                 const float2 v = kv_to_float2(vr + d);
                 acc[i].x = fmaf(p, v.x, acc[i].x);
@@ -293,11 +345,11 @@ __device__ __forceinline__ void attend_resident(const uint8_t* ring, int chunk_b
     }
 #pragma unroll
     for (int i = 0; i < ND2; ++i) {
-        const int d = 2 * (d2 + 32 * i);
-        if (d < D) part[pg * (D + 1) + d] = acc[i].x;
-        if (d + 1 < D) part[pg * (D + 1) + d + 1] = acc[i].y;
+        const int d = 2 * (lane + 32 * i);
+        if (d < D) part[warp * (D + 1) + d] = acc[i].x;
+        if (d + 1 < D) part[warp * (D + 1) + d + 1] = acc[i].y;
     }
-    if (lane == 0) part[pg * (D + 1) + D] = lsum;
+    if (lane == 0) part[warp * (D + 1) + D] = lsum;
     __syncthreads();
     if (tid < D) {
         float num = 0.f, den = 0.f;
@@ -589,7 +641,7 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
     rdetail_sync(P, l, 0, 1);
     const bool okg = wsc > 0.f && warp_slot_wait(c.mb + 0, (uint32_t)l & 1u, c.st);
     rdetail_sync(P, l, 0, 2);
-    block_gemv<1, 2>(c.slot0, P.SH, c.ra, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
+    role_gemv<(RA_ROWS_MAX + 31) / 32>(c.slot0, P.SH, c.ra, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
     rdetail(P, l, 0, 3);
     if (should_abort(c.st)) return false;
     attn_epilogue<KV>(P, A, c, l, tag);
@@ -604,7 +656,7 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
     if (!attn_gather<KV>(P, A, c, l, tag)) return false;
     rtrace(P, 0, ph + 2);
     rdetail(P, l, 1, 1);
-    attend_resident<KV, MD>(c.ring, P.chunk_bytes, P.D, c.n_att, c.misc, c.sc, c.part, c.misc + 384);
+    attend_resident<KV, MD>(c.ring, P.chunk_bytes, P.D, c.n_att, c.misc, c.sc, c.part, c.red, c.misc + 384);
     rdetail(P, l, 1, 2);
     if (tid == COPY_T && P.bulk_kv && l + 1 < P.L) {
         fence_proxy_async();
@@ -634,7 +686,7 @@ __device__ __forceinline__ bool ffn_layer(const RoleParams& P, const RoleCtx& c,
     rdetail_sync(P, l, 3, 1);
     const bool okg = wsc > 0.f && warp_slot_wait(c.mb + 0, (uint32_t)l & 1u, c.st);
     rdetail_sync(P, l, 3, 2);
-    block_gemv<1, 3>(c.slot0, P.SH, 2 * c.gn, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
+    role_gemv<(RG_ROWS_MAX + 31) / 32>(c.slot0, P.SH, 2 * c.gn, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
     rdetail(P, l, 3, 3);
     if (should_abort(c.st)) return false;
     ffn_epilogue(P, c);
@@ -757,6 +809,8 @@ __device__ __forceinline__ bool role_lm_head(const RoleParams& P, const StepArgs
         reinterpret_cast<int*>(c.red)[NW + warp] = best_i;
     }
     __syncthreads();
+    __shared__ ArgBest s_best;
+    __shared__ int s_last;
     if (tid == 0) {
         for (int w = 0; w < NW; ++w) {
             const float v = c.red[w];
@@ -766,24 +820,10 @@ __device__ __forceinline__ bool role_lm_head(const RoleParams& P, const StepArgs
                 best_i = i;
             }
         }
-        P.amax[b] = {best_v, best_i};
-        __threadfence();
-        const unsigned prev = atomicAdd(&P.sync->amax_done, 1u);
-        if (prev == (unsigned)G - 1) {
-            __threadfence();
-            ArgBest r = {-INFINITY, 0x7fffffff};
-            for (int k = 0; k < G; ++k) {
-                ArgBest t;
-                t.v = __ldcg(&P.amax[k].v);
-                t.i = __ldcg(&P.amax[k].i);
-                if (better(t.v, t.i, r.v, r.i)) r = t;
-            }
-            if (r.i == 0x7fffffff) r.i = 0;
-            P.sync->result = r.i;
-            if (A.argmax_dev) *A.argmax_dev = r.i;
-            P.sync->amax_done = 0;
-        }
+        s_best = {best_v, best_i};
     }
+    __syncthreads();
+    grid_argmax<NT>(s_best, P.amax, P.sync, A.argmax_dev, reinterpret_cast<ArgBest*>(c.misc), &s_last);
     rtrace(P, 1, 5 * P.L + 1);
     return true;
 }
@@ -831,6 +871,9 @@ __global__ void __launch_bounds__(NT, 1)
     RoleCtx c;
     const int b = blockIdx.x, tid = threadIdx.x, H = P.H;
     const bool is_attn = b < P.NA;
+    // A dependent LM-head kernel may be scheduled as soon as blocks leave; it
+    // waits for this grid's completion before reading anything.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     {
         c.xf = reinterpret_cast<float*>(sm + P.off_xf);
         c.xq = reinterpret_cast<int8_t*>(sm + P.off_xq);
@@ -901,7 +944,7 @@ __global__ void __launch_bounds__(NT, 1)
     bool ok = true;
     const bool idle = !is_attn && c.gn == 0;  // FFN blocks without gate/up rows (tiny models) sit the layers out
     for (int l = 0; l < P.L && !idle; ++l) {
-        if (tid == 0 && A.head && l == P.L - 1) {
+        if (tid == 0 && (A.head || A.head_follows) && l == P.L - 1) {
             // HBM has slack during the last layer: start this block's first LM-head rows into L2.
             const int ha = part_lo(b, gridDim.x, P.V), hn = part_lo(b + 1, gridDim.x, P.V) - ha;
             if (hn) prefetch_slice(P.embed + (size_t)ha * P.SH, (size_t)min(hn, HEAD_L2_ROWS) * P.SH, 0, 1);

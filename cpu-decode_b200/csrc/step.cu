@@ -3,6 +3,7 @@
 // launches one cooperative step kernel (step_kernel.cuh) per token.
 #include "decode_b200.h"
 #include "model_view.h"
+#include "head_kernel.cuh"
 #include "role_kernel.cuh"
 #include "step_kernel.cuh"
 
@@ -82,6 +83,11 @@ struct dcb_engine {
     bool role_ok = false, role_on = true;
     void* role_kernel = nullptr;
     int role_smem = 0, role_max_pos = 0;
+    // The LM head as its own kernel after a two-role step (head_kernel.cuh),
+    // chained by programmatic dependent launch; 2 blocks per SM.
+    HeadParams HP{};
+    bool head_sep = false;
+    int head_grid = 0;
 
     ~dcb_engine() {
         cudaSetDevice(device);
@@ -208,10 +214,28 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
     A.par = e->par;
     e->par ^= 1;
     if (use_role(e)) {
+        const bool sep = head && e->head_sep;
+        A.head_follows = sep ? 1 : 0;
+        if (sep) A.head = 0;
         void* args[] = {(void*)&e->R, (void*)&A};
         DCB_CUDA(cudaLaunchCooperativeKernel(e->role_kernel, dim3(e->grid), dim3(NT), args, (size_t)e->role_smem,
                                              e->stream));
         ++e->launches;
+        if (sep) {
+            HeadArgs HA{A.par, argmax_dev, host_logits};
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(e->head_grid);
+            cfg.blockDim = dim3(HEADK_NT);
+            cfg.dynamicSmemBytes = 3 * (size_t)e->P.Kh;
+            cfg.stream = e->stream;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            DCB_CUDA(cudaLaunchKernelEx(&cfg, head_kernel, e->HP, HA));
+            ++e->launches;
+        }
         return 0;
     }
     void* args[] = {(void*)&e->P, (void*)&A};
@@ -305,7 +329,8 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
         ra_max = std::max(ra_max, 2 * (x.nq + x.nkv));
     }
     const int gmax = ceil_div(I, R.NG);
-    if (ra_max > 2 * RA_ROWS_MAX || 2 * gmax > 2 * RG_ROWS_MAX || gmax > NT) return 0;
+    // The block GEMVs give each lane at most (rows + 31) / 32 rows of these caps.
+    if (ra_max > RA_ROWS_MAX || 2 * gmax > RG_ROWS_MAX) return 0;
     R.ra_stride = ra_max;
     R.dw = slice_row_bytes(gmax);
     if (R.dw > 4 * (ROLE_PLANE / 4) - 16 || R.o_dw > ROLE_PLANE - 16) return 0;
@@ -409,13 +434,46 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     }
     if (int rc = upload(e, &d8, buf)) return rc;
     R.down_cols = d8;
+    // The separate LM-head kernel (argmax candidates of its own).
+    {
+        HeadParams& HP = e->HP;
+        HP.H = H;
+        HP.Kh = P.Kh;
+        HP.SH = P.SH;
+        HP.V = e->V;
+        HP.L = e->L;
+        HP.Hp = P.Hp;
+        HP.eps = P.eps;
+        HP.expect = (unsigned)R.dcontrib;
+        HP.embed = P.embed;
+        HP.final_norm = P.norms + (size_t)e->L * 2 * P.Kh;
+        HP.dacc = P.dacc;
+        HP.logits = P.logits;
+        HP.sync = P.sync;
+        e->head_grid = 2 * e->sms;
+        ArgBest* amax = nullptr;
+        if (int rc = e->alloc(&amax, e->head_grid)) return rc;
+        HP.amax = amax;
+        int per_sm = 0;
+        const size_t hsmem = 3 * (size_t)P.Kh;
+        e->head_sep = P.Kh <= 32 * HEADK_C * 16 &&
+                      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, head_kernel, HEADK_NT, hsmem) == cudaSuccess &&
+                      per_sm >= 1;
+        // Measured slower in place than the step kernel's own LM head (the
+        // kernel boundary and a cold start outweigh its two blocks per SM), so
+        // it is opt-in.
+        const char* v = std::getenv("DCB_HEAD_KERNEL");
+        e->head_sep = e->head_sep && v && std::atoi(v) != 0;
+        cudaGetLastError();
+    }
     e->role_kernel = k;
     e->role_smem = (int)smem;
     e->role_max_pos = R.nbufs * ATT_CHUNK;
     e->role_ok = true;
     if (const char* v = std::getenv("DCB_ROLE")) e->role_on = std::atoi(v) != 0;
-    R.coarse_down = 8;
-    R.coarse_o = 2;
+    // The coarse waits end at the first contribution of a sum word.
+    R.coarse_down = R.dcontrib - 1;
+    R.coarse_o = NH - 1;
     if (const char* v = std::getenv("DCB_COARSE_DOWN")) R.coarse_down = std::atoi(v);
     if (const char* v = std::getenv("DCB_COARSE_O")) R.coarse_o = std::atoi(v);
     return 0;

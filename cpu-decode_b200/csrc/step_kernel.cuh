@@ -141,11 +141,57 @@ struct StepArgs {
     float* host_logits;  // mapped pinned host memory the LM head also writes, or null
     int par;             // which half of dacc this step sums into (the other half is cleared for the next)
     int group;           // attention units are (KV group, split) instead of (query head, split)
+    int head_follows;    // (two-role kernel) an LM-head kernel follows this launch: warm L2 with its rows
 };
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
 __device__ __forceinline__ int part_lo(int b, int G, int n) { return (int)((long long)b * n / G); }
+
+// The grid's argmax once every block has a candidate (its best value and
+// first index): each block stores its own into amax[block]; the last block to
+// count itself in sync->amax_done merges all of them with every thread (one
+// load pair each, warp shuffles, one shared-memory step; the first index wins
+// ties, as std::max_element), publishes the result and re-arms the counter.
+// The merge is block-parallel: one thread walking the candidates would pay an
+// L2 round trip per candidate. scratch: T/32 entries; flag: one shared int.
+// Every thread of the block calls it.
+template <int T>
+__device__ void grid_argmax(ArgBest best, ArgBest* amax, Sync* sync, int* argmax_dev, ArgBest* scratch, int* flag) {
+    const int tid = threadIdx.x, G = gridDim.x, lane = tid & 31;
+    if (tid == 0) {
+        amax[blockIdx.x] = best;
+        __threadfence();
+        *flag = atomicAdd(&sync->amax_done, 1u) == (unsigned)G - 1;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    ArgBest r = {-INFINITY, 0x7fffffff};
+    for (int k = tid; k < G; k += T) {
+        ArgBest t;
+        t.v = __ldcg(&amax[k].v);
+        t.i = __ldcg(&amax[k].i);
+        if (better(t.v, t.i, r.v, r.i)) r = t;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgBest t;
+        t.v = __shfl_xor_sync(FULL, r.v, o);
+        t.i = __shfl_xor_sync(FULL, r.i, o);
+        if (better(t.v, t.i, r.v, r.i)) r = t;
+    }
+    if (lane == 0) scratch[tid >> 5] = r;
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 0; w < T / 32; ++w)
+            if (better(scratch[w].v, scratch[w].i, r.v, r.i)) r = scratch[w];
+        if (r.i == 0x7fffffff) r.i = 0;
+        sync->result = r.i;
+        if (argmax_dev) *argmax_dev = r.i;
+        sync->amax_done = 0;
+    }
+}
 
 // ---- mbarrier + bulk copy ------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -1447,6 +1493,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
     __shared__ float s_ss[NW];  // the warps' shares of sum x^2 for the RMSNorm of a phase
     __shared__ int s_abort;
     __shared__ unsigned s_fills[NMB];  // fills issued per mbarrier (thread 0)
+    __shared__ ArgBest s_best;
+    __shared__ int s_last;
 
     const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int H = P.H, I = P.I, D = P.D, half = D / 2, kvd = P.NKV * D;
@@ -1844,24 +1892,10 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const Params P, cons
                         best_i = i;
                     }
                 }
-                P.amax[b] = {best_v, best_i};
-                __threadfence();
-                const unsigned prev = atomicAdd(&P.sync->amax_done, 1u);
-                if (prev == (unsigned)G - 1) {
-                    __threadfence();
-                    ArgBest r = {-INFINITY, 0x7fffffff};
-                    for (int c = 0; c < G; ++c) {
-                        ArgBest t;
-                        t.v = __ldcg(&P.amax[c].v);
-                        t.i = __ldcg(&P.amax[c].i);
-                        if (better(t.v, t.i, r.v, r.i)) r = t;
-                    }
-                    if (r.i == 0x7fffffff) r.i = 0;
-                    P.sync->result = r.i;
-                    if (A.argmax_dev) *A.argmax_dev = r.i;
-                    P.sync->amax_done = 0;
-                }
+                s_best = {best_v, best_i};
             }
+            __syncthreads();
+            grid_argmax<NT>(s_best, P.amax, P.sync, A.argmax_dev, reinterpret_cast<ArgBest*>(misc), &s_last);
         }
         trace_mark(P, 1, 5 * P.L + 1);
     }
