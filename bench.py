@@ -132,21 +132,47 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def host_cpu() -> dict:
+    """The host's CPU model and logical core count (as tools/measure.py:61-70 records)."""
+    name = ""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                name = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"model": name, "logical_cpus": os.cpu_count(), "usable_cpus": len(os.sched_getaffinity(0))}
+
+
+def reference_bench(model_dir: Path, steps: int, repeats: int, threads: int) -> dict:
+    """`cpu-decode bench` of the reference, built from its sources (oracle/_ref),
+    as BASELINE's plan runs it: ctx 128, `steps` greedy steps, `repeats`
+    repeats, the median tokens/s."""
+    exe = ROOT / "oracle" / "_ref" / "cpu-decode"
+    kernel = "simd512x4" if "avx512bw" in Path("/proc/cpuinfo").read_text() else "simd256"
+    tokens = ",".join(str(t) for t in prompt_tokens())
+    out = subprocess.run([str(exe), "bench", "--model", str(model_dir), "--tokens", tokens, "--context", str(CONTEXT),
+                          "--steps", str(steps), "--repeats", str(repeats), "--threads", str(threads), "--kernel",
+                          kernel], capture_output=True, text=True, check=True)
+    res = json.loads(out.stdout)
+    rates = [sample["tokens_per_second"] for sample in res["samples"]]
+    return {"tokens_per_s": round(statistics.median(rates), 3), "repeats": len(rates), "kernel": kernel,
+            "threads": threads}
+
+
 def cpu_baseline(model_dir: Path, steps: int = 16) -> dict:
-    """The reference CPU engine on this host's cores, bounded sample."""
+    """The reference CPU engine on this host's cores, on a bounded sample: all
+    usable threads, and one thread, 3 repeats each (median)."""
     exe = ROOT / "oracle" / "_ref" / "cpu-decode"
     threads = len(os.sched_getaffinity(0))
-    tokens = ",".join(str(t) for t in prompt_tokens())
     if exe.exists():
-        cpuinfo = Path("/proc/cpuinfo").read_text()
-        kernel = "simd512x4" if "avx512bw" in cpuinfo else "simd256"
-        out = subprocess.run([str(exe), "bench", "--model", str(model_dir), "--tokens", tokens, "--context",
-                              str(CONTEXT), "--steps", str(steps), "--repeats", "1", "--threads", str(threads),
-                              "--kernel", kernel], capture_output=True, text=True, check=True)
-        res = json.loads(out.stdout)
-        tps = res["samples"][0]["tokens_per_second"]
-        return {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
-                "sample": f"reference cpu-decode bench --kernel {kernel}: ctx {CONTEXT}, {steps} greedy steps, 1 repeat"}
+        full = reference_bench(model_dir, steps, 3, threads)
+        one = reference_bench(model_dir, steps, 3, 1)
+        return {"value": full["tokens_per_s"], "unit": "tokens/s", "cores": threads, "kind": "reference",
+                "value_1_thread": one["tokens_per_s"], "host_cpu": host_cpu(),
+                "sample": f"reference cpu-decode bench --kernel {full['kernel']}: ctx {CONTEXT}, {steps} greedy "
+                          f"steps, median of 3 repeats, at {threads} threads and at 1 thread"}
     sys.path.insert(0, str(ROOT))
     import oracle
     orc = oracle.Oracle(model_dir, CONTEXT + steps + 1, threads=threads)
@@ -159,7 +185,16 @@ def cpu_baseline(model_dir: Path, steps: int = 16) -> dict:
         nxt = oracle.argmax(orc.step(nxt))
     dt = time.perf_counter() - t0
     return {"value": round(steps / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "host_cpu": host_cpu(),
             "sample": f"C restatement of the reference step: ctx {CONTEXT}, {steps} greedy steps"}
+
+
+def headline_config(world: int) -> dict:
+    """The workload of the headline line, identical in both arms."""
+    return {"workload": "qwen2.5-0.5b-shape int8 (24x896, 14/2 heads, FFN 4864, vocab 151936), "
+                        "batch 1, 128-token prompt + greedy decode, FP32 KV",
+            "context": CONTEXT, "global_batch": world, "parallelism": f"replicas{world}",
+            "l2": "inputs larger than L2 (496 MB of weights per step)"}
 
 
 def prompt_tokens() -> list[int]:
@@ -175,6 +210,10 @@ def ensure_model() -> Path:
 
 
 def run_reference(args) -> None:
+    """The reference's CPU engine (its `cpu-decode bench`, built from its
+    sources) on this host's cores: the same steps, config, metric and unit as
+    the B200 arm; median of 3 repeats at all usable threads, with the
+    1-thread figure beside it. Rank 0 alone runs it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -184,18 +223,19 @@ def run_reference(args) -> None:
     if not exe.exists():
         print(json.dumps({"impl": "reference", "unavailable": "reference CPU build (oracle/_ref) is missing"}))
         return
-    samples = []
-    for _ in range(max(1, args.warmup) + 1):
-        samples.append(cpu_baseline(model, steps=min(steps, 16)))
-    base = samples[-1]
-    v = base["value"]
+    threads = len(os.sched_getaffinity(0))
+    full = reference_bench(model, steps, 3, threads)
+    one = reference_bench(model, steps, 3, 1)
+    v = full["tokens_per_s"]
+    base = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference", "value_1_thread": one["tokens_per_s"],
+            "host_cpu": host_cpu(),
+            "sample": f"reference cpu-decode bench --kernel {full['kernel']}: ctx {CONTEXT}, {steps} greedy steps, "
+                      f"median of 3 repeats (1 warm-up step each, as the CLI runs it)"}
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": min(steps, 16), "warmup": args.warmup, "ms_per_step": round(1000.0 / v, 4),
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / v, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights, f32 math",
-            "data": "synthetic (seeded random-init weights and tokens)",
-            "config": {"workload": "qwen2.5-0.5b-shape int8, batch 1, ctx 128 prompt + greedy decode, FP32 KV",
-                       "context": CONTEXT},
-            "cpu_baseline": base,
+            "data": "synthetic (seeded random-init weights N(0,0.02) and uniform token ids)",
+            "config": headline_config(args.gpus), "cpu_baseline": base,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -335,14 +375,14 @@ def main() -> None:
     e2e_value = world * K / e2e_s
     assert nxt == generated_last, "host-driven and device-chained greedy streams diverged"
 
-    extra = {}
+    extra, tail = {}, {}
     if not args.no_batch:
-        extra["batched"] = batched_decode(dcb, eng, d, dist, rank, world, W, eng_model_dir=model,
-                                          cpu_sample=not args.no_cpu_baseline)
+        tail["batched"] = batched_decode(dcb, eng, d, dist, rank, world, W, eng_model_dir=model,
+                                         cpu_sample=not args.no_cpu_baseline and world == 1)
     if dist and not args.no_long:
         split = kv_split_context(dcb, model, d, min(K, 32), W, local, dist, 32768)
         if rank == 0:
-            extra["ctx32768_kv_split"] = split
+            tail["ctx32768_kv_split"] = split
     if rank == 0:
         # HBM read bandwidth of this GPU by the engine's own probe (the
         # reference's tools/bandwidth.cpp sweep), beside the measured peak.
@@ -363,27 +403,33 @@ def main() -> None:
             "warmup": W, "ms_per_step": round(ms / K, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 weights, f32 math",
             "data": "synthetic (seeded random-init weights N(0,0.02) and uniform token ids)",
-            "config": {"workload": "qwen2.5-0.5b-shape int8 (24x896, 14/2 heads, FFN 4864, vocab 151936), "
-                                   "batch 1, 128-token prompt + greedy decode, FP32 KV",
-                       "context": CONTEXT, "global_batch": world, "parallelism": f"replicas{world}",
-                       "l2": "inputs larger than L2 (496 MB of weights per step)"},
+            "config": headline_config(world),
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": d.vocab * 4 + 8},
             "gpu_launches": int(gpu_launches),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": int(avg_bytes),
-                         "traffic": profiled_traffic("decode_step_kernel_ctx128.md"),
-                         "kernel": "decode_step_kernel"},
+                         "traffic": profiled_traffic("role_step_kernel_ctx128.md"),
+                         "kernel": "role_step_kernel"},
             "clocks": clock_info,
             "launch": eng.launch_info(),
         }
-        line.update(extra)
-        if not args.no_cpu_baseline:
+        # The reported CPU baseline runs at N=1 only: with other ranks alive
+        # on the host it would measure contention, not the reference.
+        if not args.no_cpu_baseline and world == 1:
             try:
                 line["cpu_baseline"] = cpu_baseline(model)
             except Exception as exc:  # reported, never fatal
                 line["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+        line.update(extra)
+        if world > 1:
+            line["scaling_limiter"] = (
+                "batch-1 decode does not shard: the headline runs one independent replica per GPU (weak "
+                "scaling, no collective); the multi-GPU work is `batched` (64 sequences per GPU, data parallel) "
+                "and `ctx32768_kv_split` (one 32K stream, KV split over the GPUs, strong scaling bounded by the "
+                "replicated dense part of every step and a per-layer NVLink exchange)")
+        line.update(tail)  # last, so the multi-GPU results end the line
         print(json.dumps(line))
     eng.close()
     if dist:
@@ -778,13 +824,43 @@ def kv_split_context(dcb, model, d, K, W, device, dist, ctx: int) -> dict:
         lmax, lmin = last.clone(), last.clone()
         dist.all_reduce(lmax, op=dist.ReduceOp.MAX)
         dist.all_reduce(lmin, op=dist.ReduceOp.MIN)
+        # Parity: a few host-driven steps with logits on the split (every rank
+        # steps together), then one unsplit engine on rank 0 over the same
+        # rows and tokens.
+        S = 3
+        eng.set_position(ctx)
+        nxt = 1234
+        split_logits, split_tokens = [], []
+        for _ in range(S):
+            lg, best = eng.step(nxt)
+            split_logits.append(lg.copy())
+            split_tokens.append(int(best))
+            nxt = int(best)
         dist.barrier()
         eng.close()
         for p in peers:
             dcb.ipc_close(p)
+        parity = None
+        if rank == 0:
+            one = dcb.Engine(long_dir, ctx + S + 2, kv_dtype=kvt, device=device)
+            rng = np.random.default_rng(ctx)
+            for l in range(d.layers):
+                k = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+                v = rng.standard_normal((ctx, d.kv_dim), dtype=np.float32)
+                one.kv_write(l, 0, k, v)
+            one.set_position(ctx)
+            nxt, diff, toks = 1234, 0.0, []
+            for i in range(S):
+                lg, best = one.step(nxt)
+                diff = max(diff, float(np.abs(lg - split_logits[i]).max()))
+                toks.append(int(best))
+                nxt = int(best)
+            one.close()
+            parity = {"steps": S, "max_abs_logit_diff": diff, "tokens_equal": toks == split_tokens}
+        dist.barrier()
         t = float(ms.item())
         out[kvt] = {"gpus": world, "tokens_per_s": round(K / (t / 1000.0), 2), "ms_per_step": round(t / K, 5),
-                    "ranks_agree": bool(lmax.item() == lmin.item())}
+                    "ranks_agree": bool(lmax.item() == lmin.item()), "vs_one_gpu": parity}
     return out
 
 

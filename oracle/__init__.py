@@ -32,6 +32,8 @@ def build(reference: bool = True) -> None:
     targets = ["oracle"]
     if reference and (REFERENCE_SOURCES / "src" / "model.cpp").exists():
         targets.append("ref")
+        if (HERE.parent / "cpu-decode_b200" / "libdecode_b200.so").exists():
+            targets.append("dropin")
     subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REFERENCE_SOURCES}", *targets], check=True)
 
 
