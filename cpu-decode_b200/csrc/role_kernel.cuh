@@ -34,8 +34,8 @@
 
 namespace dcb {
 
-constexpr int RA_ROWS_MAX = 64;   // QKV rows of one attention block, at most (lane rows, two passes)
-constexpr int RG_ROWS_MAX = 96;   // gate/up rows of one FFN block, at most (lane rows, three passes)
+constexpr int RA_ROWS_MAX = 64;   // QKV rows of one attention block, at most (4 tiles of 16)
+constexpr int RG_ROWS_MAX = 96;   // gate/up rows of one FFN block, at most (6 tiles of 16)
 constexpr int RES_BUFS_MAX = 8;   // resident KV chunk buffers, at most
 constexpr int RES_POS_MAX = RES_BUFS_MAX * ATT_CHUNK;  // positions one attention block keeps resident
 // The block's last thread issues every bulk copy and never a global store or
@@ -114,16 +114,20 @@ __device__ __forceinline__ AttnRows attn_rows(const RoleParams& P, int a) {
     return r;
 }
 
+// Trace records exist only in the traced instantiation (TR), so the product
+// kernel carries none of their code.
+template <bool TR>
 __device__ __forceinline__ void rtrace(const RoleParams& P, int which, int phase) {
-    if (P.trace && threadIdx.x == 0)
+    if (TR && P.trace && threadIdx.x == 0)
         P.trace[((size_t)which * TRACE_MAX_PHASES + phase) * gridDim.x + blockIdx.x] = globaltimer();
 }
 
 // Detailed marks m (< 8) inside phase k (< 5) of the traced layer: slot
 // TRACE_DETAIL + 8k + m of the ready record (as step_kernel.cuh's trace_detail).
 // The marks are SM clock counts (cheap; compare marks of one block only).
+template <bool TR>
 __device__ __forceinline__ void rdetail(const RoleParams& P, int layer, int k, int m) {
-    if (P.trace && layer == P.trace_layer && threadIdx.x == 0)
+    if (TR && P.trace && layer == P.trace_layer && threadIdx.x == 0)
         P.trace[((size_t)TRACE_DETAIL + 8 * k + m) * gridDim.x + blockIdx.x] = clock64();
 }
 
@@ -145,41 +149,49 @@ __device__ __forceinline__ bool coarse_wait(const uint64_t* w, unsigned first, c
 }
 
 // A block-wide mark: when tracing, every thread has reached this point.
+template <bool TR>
 __device__ __forceinline__ void rdetail_sync(const RoleParams& P, int layer, int k, int m) {
-    if (P.trace) {
+    if (TR && P.trace) {
         __syncthreads();
-        rdetail(P, layer, k, m);
+        rdetail<TR>(P, layer, k, m);
     }
 }
 
-// Stage a short vector v[0..n) (n <= 32*4, one warp) as fixed-point planes
-// (16*nch bytes each, zero past n) with its own scale; returns the scale.
-__device__ __forceinline__ float warp_stage_short(const float* v, int n, int8_t* xq, int plane, int nch) {
-    const int lane = threadIdx.x & 31;
-    float mx = 0.f;
-#pragma unroll 1
-    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, fabsf(v[j]));
-    mx = warp_max(mx);
-    const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
-#pragma unroll 1
-    for (int quad = lane; quad < nch * 4; quad += 32) {
-        const int j = 4 * quad;
-        const float4 v4 = make_float4(j < n ? v[j] : 0.f, j + 1 < n ? v[j + 1] : 0.f, j + 2 < n ? v[j + 2] : 0.f,
-                                      j + 3 < n ? v[j + 3] : 0.f);
-        uint32_t ph, pm, pl;
-        fix_pack4(v4, rs, ph, pm, pl);
-        reinterpret_cast<uint32_t*>(xq)[quad] = ph;
-        reinterpret_cast<uint32_t*>(xq + plane)[quad] = pm;
-        reinterpret_cast<uint32_t*>(xq + 2 * plane)[quad] = pl;
-    }
-    return mx > 0.f ? __frcp_rn(rs) : 1.0f;
+// ---- int8 tensor-core fragments (mma.sync m16n8k16, s8 x s8 -> s32) ----
+// A staged vector's three fixed-point planes are the first three columns of
+// the B operand (columns 3..7 zero), so one MMA yields the hi, mid and lo
+// plane sums of 16 rows over 16 columns: the same exact integer sums as three
+// dp4a chains. A fragments come from row-major int8 rows in shared memory by
+// ldmatrix (rows 16-byte aligned; an odd number of 16-byte units per row keeps
+// each 8-row matrix in distinct banks).
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a)
+                 : "memory");
+}
+__device__ __forceinline__ void mma_i8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(b));
+}
+// B fragment of 16 staged columns starting at byte c16: lane (g, q) holds
+// plane g's bytes c16 + 4q .. + 3 (zero for g >= 3).
+__device__ __forceinline__ uint32_t plane_frag(const int8_t* xq, int plane, int c16) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    return g < 3 ? *reinterpret_cast<const uint32_t*>(xq + g * plane + c16 + 4 * q) : 0u;
+}
+// The value of one accumulator tile's row for lanes q < 2 (row g + 8q of the
+// tile): lane q = 0 holds hi, mid of rows g and g + 8, lane q = 1 their lo.
+// Every lane takes part in the shuffles.
+__device__ __forceinline__ float tile_row_value(const int (&c)[4]) {
+    const int lo_g = __shfl_xor_sync(FULL, c[0], 1);
+    const int hi_g8 = __shfl_xor_sync(FULL, c[2], 1);
+    const int md_g8 = __shfl_xor_sync(FULL, c[3], 1);
+    return (threadIdx.x & 1) == 0 ? planes_to_float(c[0], c[1], lo_g) : planes_to_float(hi_g8, md_g8, c[2]);
 }
 
-// Rows [r0, r1) of a column slice (rows of dw bytes in shared memory, zero
-// past the columns) times a staged short vector (planes of `plane` bytes, dw
-// bytes used), scaled per row (scale[r] * vscale), plus fold[r] when set,
-// added into the sum words acc[r]. One row per thread at a time; an odd
-// number of words per row keeps the 32 lanes' reads in 32 banks.
 // Rows [r0, r1) of a column slice (dw bytes per row in shared memory: an odd
 // number of words, zero past the slice's columns) times v[0, dw) (floats,
 // zero past the columns), scaled per row, plus fold[r] when set, added into
@@ -214,41 +226,45 @@ __device__ __forceinline__ void slice_rows(const uint8_t* slice, int dw, int r0,
     }
 }
 
-// Block GEMV of R packed rows in shared memory (stride S bytes, nch chunks of
-// 16 int8 each) with the staged planes: warp w covers chunks
-// [w*nch/NW, (w+1)*nch/NW) (at most ROLE_CPW), lane r the rows r + 32p,
-// p < PR, with every chunk's loads issued before its dp4a (the chunk loop is
-// unrolled). partial[w*R + r] = the warp's share times its staging scale;
-// the closing barrier publishes them. run false: only the barrier.
+// Block GEMV of R packed rows in shared memory (stride S bytes, an odd number
+// of 16-byte units; nch chunks of 16 int8) with the staged planes: warp w
+// covers chunks [w*nch/NW, (w+1)*nch/NW) (at most ROLE_CPW) for every tile of
+// 16 rows (MT tiles at most), one MMA per tile and chunk.
+// partial[w*R + r] = the warp's share times its staging scale; the closing
+// barrier publishes them. run false: only the barrier.
 constexpr int ROLE_CPW = 4;  // chunks per warp, at most (hidden <= 1024)
-template <int PR>
+template <int MT>
 __device__ __forceinline__ void role_gemv(const uint8_t* rows, int S, int R, int nch, const int8_t* xq, int plane,
                                           float* partial, float wscale, bool run) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c0 = warp * nch / NW, c1 = (warp + 1) * nch / NW;
+    const int nt = (R + 15) >> 4;
     if (run) {
-        int ah[PR], am[PR], al[PR];
+        int acc[MT][4];
 #pragma unroll
-        for (int p = 0; p < PR; ++p) ah[p] = am[p] = al[p] = 0;
+        for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
+#pragma unroll 1
+        for (int c = c0; c < c1; ++c) {
+            {
+                const uint32_t bf = plane_frag(xq, plane, 16 * c);
 #pragma unroll
-        for (int cc = 0; cc < ROLE_CPW; ++cc) {
-            const int c = c0 + cc;
-            if (c < c1) {
-                int4 h, m, l;
-                load_planes(xq, plane, c, h, m, l);
-#pragma unroll
-                for (int p = 0; p < PR; ++p) {
-                    const int r = lane + 32 * p;
-                    if (r < R)
-                        dp4a16(*reinterpret_cast<const int4*>(rows + (size_t)r * S + (size_t)c * 16), h, m, l, ah[p],
-                               am[p], al[p]);
+                for (int t = 0; t < MT; t += 2) {
+                    if (t < nt) {
+                        uint32_t a[4];
+                        ldsm_x4(a, rows + (size_t)min(16 * t + lane, R - 1) * S + 16 * c);
+                        mma_i8(acc[t], a[0], a[1], bf);
+                        if (t + 1 < MT && t + 1 < nt) mma_i8(acc[t + 1], a[2], a[3], bf);
+                    }
                 }
             }
         }
 #pragma unroll
-        for (int p = 0; p < PR; ++p) {
-            const int r = lane + 32 * p;
-            if (r < R) partial[warp * R + r] = planes_to_float(ah[p], am[p], al[p]) * wscale;
+        for (int t = 0; t < MT; ++t) {
+            if (t < nt) {
+                const float v = tile_row_value(acc[t]);
+                const int r = 16 * t + (lane >> 2) + 8 * (lane & 3);
+                if ((lane & 3) < 2 && r < R) partial[warp * R + r] = v * wscale;
+            }
         }
     }
     __syncthreads();
@@ -591,11 +607,11 @@ __device__ __forceinline__ bool attn_gather(const RoleParams& P, const StepArgs&
 
 // One block's share of a sum: rows [r0, r1) of the slot behind mbarrier 1
 // (dw bytes each) times the float vector v (zero past its columns), scaled
-// per row (s0..s2 as slice_rows), plus fold, added into acc. The slot wait is
+// per row (rs, as slice_rows), plus fold, added into acc. The slot wait is
 // one thread's test; the closing barrier marks the slot consumed. Returns
 // false when the slot wait ran out (uniform).
 __device__ __forceinline__ bool sum_share(const RoleParams& P, const RoleCtx& c, const float* v, const uint8_t* slot,
-                                          int dw, int r0, int r1, float s0, float s1, float s2, const float* fold,
+                                          int dw, int r0, int r1, const float (&rs)[SLICE_RPT], const float* fold,
                                           uint64_t* acc, uint32_t parity) {
     if (threadIdx.x == 0) {
         uint64_t t0 = 0;
@@ -605,7 +621,7 @@ __device__ __forceinline__ bool sum_share(const RoleParams& P, const RoleCtx& c,
     }
     __syncthreads();
     if (should_abort(c.st)) return false;
-    slice_rows(slot, dw, r0, r1, v, s0, s1, s2, fold, acc);
+    slice_rows(slot, dw, r0, r1, v, rs[0], rs[1], rs[2], fold, acc);
     __syncthreads();
     return true;
 }
@@ -628,92 +644,94 @@ __device__ __forceinline__ void ffn_epilogue(const RoleParams& P, const RoleCtx&
 }
 
 // ---- one layer of each role ----
-template <typename KV, int MD>
+template <typename KV, int MD, bool TR>
 __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l, int token,
-                                        float s0, float s1, float s2) {
+                                        const float (&rs)[SLICE_RPT]) {
     const int tid = threadIdx.x, ph = 5 * l;
     const uint32_t tag = (A.seq << 8) | (uint32_t)(l + 1);
     const float* in_norm = P.norms + (size_t)l * 2 * P.Kh;
-    rdetail(P, l, 0, 0);
+    rdetail<TR>(P, l, 0, 0);
     const float wsc = l == 0 ? role_stage_embed(P, c, token, in_norm)
                              : role_stage(P, c, role_dsum(P, c, l - 1), P.dcontrib, P.coarse_down, in_norm);
-    rtrace(P, 0, ph + 1);
-    rdetail_sync(P, l, 0, 1);
+    rtrace<TR>(P, 0, ph + 1);
+    rdetail_sync<TR>(P, l, 0, 1);
     const bool okg = wsc > 0.f && warp_slot_wait(c.mb + 0, (uint32_t)l & 1u, c.st);
-    rdetail_sync(P, l, 0, 2);
-    role_gemv<(RA_ROWS_MAX + 31) / 32>(c.slot0, P.SH, c.ra, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
-    rdetail(P, l, 0, 3);
+    rdetail_sync<TR>(P, l, 0, 2);
+    role_gemv<RA_ROWS_MAX / 16>(c.slot0, P.SH, c.ra, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
+    rdetail<TR>(P, l, 0, 3);
     if (should_abort(c.st)) return false;
     attn_epilogue<KV>(P, A, c, l, tag);
     __syncthreads();  // the QKV slot is consumed
-    rdetail(P, l, 0, 4);
+    rdetail<TR>(P, l, 0, 4);
     if (tid == COPY_T && l + 1 < P.L) {
         fence_proxy_async();
         attn_fill_qkv(P, c, l + 1);
     }
-    rtrace(P, 1, ph + 1);
-    rdetail(P, l, 1, 0);
+    rtrace<TR>(P, 1, ph + 1);
+    rdetail<TR>(P, l, 1, 0);
     if (!attn_gather<KV>(P, A, c, l, tag)) return false;
-    rtrace(P, 0, ph + 2);
-    rdetail(P, l, 1, 1);
+    rtrace<TR>(P, 0, ph + 2);
+    rdetail<TR>(P, l, 1, 1);
     attend_resident<KV, MD>(c.ring, P.chunk_bytes, P.D, c.n_att, c.misc, c.sc, c.part, c.red, c.misc + 384);
-    rdetail(P, l, 1, 2);
+    rdetail<TR>(P, l, 1, 2);
     if (tid == COPY_T && P.bulk_kv && l + 1 < P.L) {
         fence_proxy_async();
         attn_fill_ring(P, A, c, l + 1, (int)sizeof(KV));
     }
-    rtrace(P, 1, ph + 2);
-    rtrace(P, 0, ph + 3);
-    rdetail(P, l, 2, 0);
-    if (!sum_share(P, c, c.misc + 384, c.slot1, P.o_dw, c.or0, c.or1, s0, s1, s2, c.ar.h == 0 ? c.xr : nullptr,
+    rtrace<TR>(P, 1, ph + 2);
+    rtrace<TR>(P, 0, ph + 3);
+    rdetail<TR>(P, l, 2, 0);
+    if (!sum_share(P, c, c.misc + 384, c.slot1, P.o_dw, c.or0, c.or1, rs, c.ar.h == 0 ? c.xr : nullptr,
                    role_osum(P, c, l), (uint32_t)l & 1u))
         return false;
-    rdetail(P, l, 2, 1);
+    rdetail<TR>(P, l, 2, 1);
     if (tid == COPY_T && l + 1 < P.L) {
         fence_proxy_async();
         attn_fill_o(P, c, l + 1);
     }
-    rtrace(P, 1, ph + 3);
+    rtrace<TR>(P, 1, ph + 3);
     return true;
 }
 
-__device__ __forceinline__ bool ffn_layer(const RoleParams& P, const RoleCtx& c, int l, float s0, float s1, float s2) {
+template <bool TR>
+__device__ __forceinline__ bool ffn_layer(const RoleParams& P, const RoleCtx& c, int l, const float (&rs)[SLICE_RPT]) {
     const int tid = threadIdx.x, ph = 5 * l;
     const float* post_norm = P.norms + (size_t)l * 2 * P.Kh + P.Kh;
-    rtrace(P, 0, ph + 4);
-    rdetail(P, l, 3, 0);
+    rtrace<TR>(P, 0, ph + 4);
+    rdetail<TR>(P, l, 3, 0);
     const float wsc = role_stage(P, c, role_osum(P, c, l), P.NH, P.coarse_o, post_norm);
-    rdetail_sync(P, l, 3, 1);
+    rdetail_sync<TR>(P, l, 3, 1);
     const bool okg = wsc > 0.f && warp_slot_wait(c.mb + 0, (uint32_t)l & 1u, c.st);
-    rdetail_sync(P, l, 3, 2);
-    role_gemv<(RG_ROWS_MAX + 31) / 32>(c.slot0, P.SH, 2 * c.gn, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
-    rdetail(P, l, 3, 3);
+    rdetail_sync<TR>(P, l, 3, 2);
+    role_gemv<RG_ROWS_MAX / 16>(c.slot0, P.SH, 2 * c.gn, P.Kh / 16, c.xq, P.xq_plane, c.part, wsc, okg);
+    rdetail<TR>(P, l, 3, 3);
     if (should_abort(c.st)) return false;
     ffn_epilogue(P, c);
     __syncthreads();  // the gate/up slot is consumed; the SiLU*up values are complete
-    rdetail(P, l, 3, 4);
+    rdetail<TR>(P, l, 3, 4);
     if (tid == COPY_T && l + 1 < P.L) {
         fence_proxy_async();
         ffn_fill_gu(P, c, l + 1);
     }
-    rtrace(P, 1, ph + 4);
-    rtrace(P, 0, ph + 5);
-    rdetail(P, l, 4, 0);
+    rtrace<TR>(P, 1, ph + 4);
+    rtrace<TR>(P, 0, ph + 5);
+    rdetail<TR>(P, l, 4, 0);
     // The last FFN block also adds x_b: the down sums are the next layer's x.
-    if (!sum_share(P, c, c.sc, c.slot1, P.dw, 0, P.H, s0, s1, s2, c.f == P.NG - 1 ? c.xr : nullptr,
+    if (!sum_share(P, c, c.sc, c.slot1, P.dw, 0, P.H, rs, c.f == P.NG - 1 ? c.xr : nullptr,
                    role_dsum(P, c, l), (uint32_t)l & 1u))
         return false;
-    rdetail(P, l, 4, 1);
+    rdetail<TR>(P, l, 4, 1);
     if (tid == COPY_T && l + 1 < P.L) {
         fence_proxy_async();
         ffn_fill_down(P, c, l + 1);
     }
-    rtrace(P, 1, ph + 5);
+    rtrace<TR>(P, 1, ph + 5);
     return true;
 }
 
 // ---- final RMSNorm + tied LM head + argmax (src/model.cpp:318-326, src/main.cpp:35-37) ----
 // Rows [ha, ha + hn) of this block; the block's best (value, first index) into P.amax.
+template <bool TR>
 __device__ __forceinline__ bool role_lm_head(const RoleParams& P, const StepArgs& A, const RoleCtx& c) {
     const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ha = part_lo(b, G, P.V), hn = part_lo(b + 1, G, P.V) - ha;
@@ -740,7 +758,7 @@ __device__ __forceinline__ bool role_lm_head(const RoleParams& P, const StepArgs
                     xv[k][0] = xv[k][1] = xv[k][2] = make_int4(0, 0, 0, 0);
                 }
             }
-            rtrace(P, 0, 5 * P.L + 1);
+            rtrace<TR>(P, 0, 5 * P.L + 1);
             const int ngroups = (hn + HEAD_R - 1) / HEAD_R;
             int4 wc[HEAD_R][HEAD_MAXC], wn[HEAD_R][HEAD_MAXC];
             float sc[HEAD_R], sn[HEAD_R];
@@ -824,12 +842,13 @@ __device__ __forceinline__ bool role_lm_head(const RoleParams& P, const StepArgs
     }
     __syncthreads();
     grid_argmax<NT>(s_best, P.amax, P.sync, A.argmax_dev, reinterpret_cast<ArgBest*>(c.misc), &s_last);
-    rtrace(P, 1, 5 * P.L + 1);
+    rtrace<TR>(P, 1, 5 * P.L + 1);
     return true;
 }
 
 // Warm L2 for the next token, clear the other half of the sum words, and on
 // abort wait (bounded) for this block's copies in flight.
+template <bool TR>
 __device__ __forceinline__ void role_finish(const RoleParams& P, const StepArgs& A, const RoleCtx& c, bool ok) {
     const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
     if (ok && tid == 0) {
@@ -852,13 +871,13 @@ __device__ __forceinline__ void role_finish(const RoleParams& P, const StepArgs&
             }
         }
     }
-    rtrace(P, 0, 5 * P.L + 2);
-    rtrace(P, 1, 5 * P.L + 2);
+    rtrace<TR>(P, 0, 5 * P.L + 2);
+    rtrace<TR>(P, 1, 5 * P.L + 2);
 }
 
 // MD: 32-dim groups of the head dimension a lane covers in the attention
 // scores (1: D <= 32, 2: D <= 64, 4: D <= 128).
-template <typename KV, int MD>
+template <typename KV, int MD, bool TR>
 __global__ void __launch_bounds__(NT, 1)
     role_step_kernel(const __grid_constant__ RoleParams P, const __grid_constant__ StepArgs A) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -930,11 +949,11 @@ __global__ void __launch_bounds__(NT, 1)
     }
     if (is_attn) {
         role_rope_table(P, A, s_cos, s_sin);
-        if (tid < 128) c.misc[384 + tid] = 0.f;  // the head output, zero past D (the O share reads o_dw bytes of it)
+        if (tid < 128) c.misc[384 + tid] = 0.f;  // the head output, zero past D
     }
     __syncthreads();
-    rtrace(P, 0, 0);
-    rtrace(P, 1, 0);
+    rtrace<TR>(P, 0, 0);
+    rtrace<TR>(P, 1, 0);
 
     int token = A.token_dev ? __ldcg(A.token_dev) : A.token;
     if ((unsigned)token >= (unsigned)P.V) {
@@ -959,12 +978,11 @@ __global__ void __launch_bounds__(NT, 1)
                         ? __ldg((is_attn ? P.o_scale : P.down_scale) + (size_t)l * H + r)
                         : 0.f;
         }
-        ok = is_attn ? attn_layer<KV, MD>(P, A, c, l, token, rs[0], rs[1], rs[2])
-                     : ffn_layer(P, c, l, rs[0], rs[1], rs[2]);
+        ok = is_attn ? attn_layer<KV, MD, TR>(P, A, c, l, token, rs) : ffn_layer<TR>(P, c, l, rs);
         if (!ok) break;
     }
-    if (ok && A.head) ok = role_lm_head(P, A, c);
-    role_finish(P, A, c, ok);
+    if (ok && A.head) ok = role_lm_head<TR>(P, A, c);
+    role_finish<TR>(P, A, c, ok);
 }
 
 }  // namespace dcb

@@ -82,6 +82,7 @@ struct dcb_engine {
     RoleParams R{};
     bool role_ok = false, role_on = true;
     void* role_kernel = nullptr;
+    void* role_kernel_traced = nullptr;
     int role_smem = 0, role_max_pos = 0;
     // The LM head as its own kernel after a two-role step (head_kernel.cuh),
     // chained by programmatic dependent launch; 2 blocks per SM.
@@ -218,7 +219,7 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
         A.head_follows = sep ? 1 : 0;
         if (sep) A.head = 0;
         void* args[] = {(void*)&e->R, (void*)&A};
-        DCB_CUDA(cudaLaunchCooperativeKernel(e->role_kernel, dim3(e->grid), dim3(NT), args, (size_t)e->role_smem,
+        DCB_CUDA(cudaLaunchCooperativeKernel(e->R.trace ? e->role_kernel_traced : e->role_kernel, dim3(e->grid), dim3(NT), args, (size_t)e->role_smem,
                                              e->stream));
         ++e->launches;
         if (sep) {
@@ -333,7 +334,6 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     if (ra_max > RA_ROWS_MAX || 2 * gmax > RG_ROWS_MAX) return 0;
     R.ra_stride = ra_max;
     R.dw = slice_row_bytes(gmax);
-    if (R.dw > 4 * (ROLE_PLANE / 4) - 16 || R.o_dw > ROLE_PLANE - 16) return 0;
     R.down_slice = (int)round_up((size_t)H * R.dw, 16);
     R.dcontrib = 0;
     for (int f = 0; f < R.NG; ++f) R.dcontrib += plo(f + 1, R.NG, I) > plo(f, R.NG, I);
@@ -345,10 +345,22 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     // Shared memory: vectors both roles use, then either role's region.
     cudaFuncAttributes fattr;
     const bool f16 = e->kv_dtype == DCB_KV_F16;
-    void* k = D <= 32   ? (f16 ? (void*)role_step_kernel<__half, 1> : (void*)role_step_kernel<float, 1>)
-              : D <= 64 ? (f16 ? (void*)role_step_kernel<__half, 2> : (void*)role_step_kernel<float, 2>)
-                        : (f16 ? (void*)role_step_kernel<__half, 4> : (void*)role_step_kernel<float, 4>);
+    // Each (KV type, head size) has a plain and a traced instantiation.
+    void* kt[2];
+    for (int tr = 0; tr < 2; ++tr)
+        kt[tr] = D <= 32 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 1, true> : (void*)role_step_kernel<__half, 1, false>)
+                                : (tr ? (void*)role_step_kernel<float, 1, true> : (void*)role_step_kernel<float, 1, false>))
+                 : D <= 64 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 2, true> : (void*)role_step_kernel<__half, 2, false>)
+                                  : (tr ? (void*)role_step_kernel<float, 2, true> : (void*)role_step_kernel<float, 2, false>))
+                           : (f16 ? (tr ? (void*)role_step_kernel<__half, 4, true> : (void*)role_step_kernel<__half, 4, false>)
+                                  : (tr ? (void*)role_step_kernel<float, 4, true> : (void*)role_step_kernel<float, 4, false>));
+    void* k = kt[0];
     if (cudaFuncGetAttributes(&fattr, k) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
+    {
+        cudaFuncAttributes ft;
+        if (cudaFuncGetAttributes(&ft, kt[1]) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
+        fattr.sharedSizeBytes = std::max(fattr.sharedSizeBytes, ft.sharedSizeBytes);
+    }
     const size_t budget = (size_t)max_optin - fattr.sharedSizeBytes;
     size_t off = 0;
     R.off_xf = (int)off;
@@ -384,15 +396,17 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     R.nbufs = (int)std::min<size_t>(RES_BUFS_MAX, (budget - attn_fixed) / R.chunk_bytes);
     if (R.nbufs < 1) return 0;
     const size_t smem = std::max(attn_fixed + (size_t)R.nbufs * R.chunk_bytes, ffn_end);
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
-        cudaGetLastError();
-        return 0;
-    }
+    for (void* kk : kt)
+        if (cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, NT, smem) != cudaSuccess || per_sm < 1) {
-        cudaGetLastError();
-        return 0;
-    }
+    for (void* kk : kt)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kk, NT, smem) != cudaSuccess || per_sm < 1) {
+            cudaGetLastError();
+            return 0;
+        }
     // Packed QKV rows per (layer, attention block), zero rows past its count.
     std::vector<uint8_t> buf((size_t)e->L * R.NA * ra_max * P.SH, 0);
     for (int l = 0; l < e->L; ++l) {
@@ -434,6 +448,7 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     }
     if (int rc = upload(e, &d8, buf)) return rc;
     R.down_cols = d8;
+
     // The separate LM-head kernel (argmax candidates of its own).
     {
         HeadParams& HP = e->HP;
@@ -466,7 +481,8 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
         e->head_sep = e->head_sep && v && std::atoi(v) != 0;
         cudaGetLastError();
     }
-    e->role_kernel = k;
+    e->role_kernel = kt[0];
+    e->role_kernel_traced = kt[1];
     e->role_smem = (int)smem;
     e->role_max_pos = R.nbufs * ATT_CHUNK;
     e->role_ok = true;

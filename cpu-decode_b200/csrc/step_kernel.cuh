@@ -505,7 +505,9 @@ constexpr long long DACC_BIAS = 1LL << 47;
 constexpr uint64_t DACC_LOW = (1ull << DACC_CNT_SHIFT) - 1;
 
 __device__ __forceinline__ void dacc_add(uint64_t* p, float v) {
-    long long q = __double2ll_rn((double)v * DACC_ONE);
+    // v * 2^26 is exact in FP32 (a power-of-two scaling), so rounding it to
+    // an integer here equals rounding the double product.
+    long long q = __float2ll_rn(v * (float)DACC_ONE);
     q = q > DACC_BIAS - 1 ? DACC_BIAS - 1 : (q < 1 - DACC_BIAS ? 1 - DACC_BIAS : q);
     const uint64_t c = (1ull << DACC_CNT_SHIFT) + (uint64_t)(q + DACC_BIAS);
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(c) : "memory");
@@ -513,7 +515,8 @@ __device__ __forceinline__ void dacc_add(uint64_t* p, float v) {
 __device__ __forceinline__ unsigned dacc_count(uint64_t w) { return (unsigned)(w >> DACC_CNT_SHIFT); }
 __device__ __forceinline__ float dacc_value(uint64_t w) {
     const long long q = (long long)(w & DACC_LOW) - (long long)dacc_count(w) * DACC_BIAS;
-    return (float)((double)q * (1.0 / DACC_ONE));
+    // One rounding of q (|q| < 2^53 here) to FP32, then an exact power-of-two scaling.
+    return (float)q * (float)(1.0 / DACC_ONE);
 }
 
 // Per-warp staging of x = xr + down sums (the residual stream entering a
