@@ -37,7 +37,7 @@ EXPORTS = (
     "dcb_read_bandwidth",
     "dcb_trace_enable", "dcb_trace_read", "dcb_exchange_buffer", "dcb_ipc_handle", "dcb_ipc_open", "dcb_ipc_close",
     "dcb_set_kv_shard", "dcb_batch_create", "dcb_batch_destroy", "dcb_batch_info", "dcb_batch_set_position",
-    "dcb_batch_position", "dcb_batch_kv_write", "dcb_batch_kv_read", "dcb_batch_step", "dcb_batch_step_greedy",
+    "dcb_batch_position", "dcb_batch_kv_write", "dcb_batch_kv_read", "dcb_batch_step", "dcb_batch_step_greedy", "dcb_prefill",
     "dcb_batch_read", "dcb_batch_stream", "dcb_batch_kernels_per_step",
 )
 
@@ -106,6 +106,7 @@ def lib() -> C.CDLL:
     L.dcb_batch_kv_write.argtypes = [vp, i32, i32, sz, sz, vp, vp]
     L.dcb_batch_kv_read.argtypes = [vp, i32, i32, sz, sz, vp, vp]
     L.dcb_batch_step.argtypes = [vp, i32, vp, vp, vp]
+    L.dcb_prefill.argtypes = [vp, vp, i32, vp, vp]
     L.dcb_batch_step_greedy.argtypes = [vp, i32, i32]
     L.dcb_batch_read.argtypes = [vp, i32, vp, vp]
     L.dcb_batch_stream.argtypes = [vp]
@@ -147,6 +148,15 @@ class Engine:
                               self.logits.ctypes.data if want else None,
                               C.addressof(self._argmax) if head else None))
         return (self.logits if want else None), (int(self._argmax.value) if head else None)
+
+    def prefill(self, tokens, logits: bool = True):
+        """All prompt tokens in batched form (dcb_prefill): the engine ends at
+        position + len(tokens) with their K/V rows written. Returns (the last
+        token's logits or None, its argmax)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        _check(lib().dcb_prefill(self._h, t.ctypes.data, int(t.shape[0]),
+                                 self.logits.ctypes.data if logits else None, C.addressof(self._argmax)))
+        return (self.logits if logits else None), int(self._argmax.value)
 
     def rewind(self, position: int) -> None:
         _check(lib().dcb_rewind(self._h, int(position)))

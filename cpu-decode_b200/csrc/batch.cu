@@ -110,21 +110,32 @@ struct dcb_batch {
     bool fuse_stage = false;   // staging of the next input inside the O, gate/up and down projections
     size_t stage_f_elems = 0;
     int* h_io = nullptr;  // pinned: [slots] tokens in, then [slots] argmax + error word out
+    int* h_pos = nullptr;  // pinned: [slots] positions in (prefill)
+    // 1: every slot has its own cache; 0 (prefill): the slots are consecutive
+    // positions of one sequence whose cache (borrowed from a step engine) they share.
+    int kv_seq = 1;
     std::vector<CUtensorMap> map_qkv, map_o, map_gu, map_down;
     CUtensorMap map_head{}, map_ph{}, map_pi{}, map_k{}, map_v{};
     bool attn64 = false;  // head_dim 64, at most 8 query heads per KV head: attention64_tc_kernel
     std::vector<size_t> pos_host;
+    // Instantiated step graphs by (sequences, logits copied, LM head); exec is
+    // the one the last build_graph chose.
+    struct GraphEntry {
+        int n;
+        bool logits, head;
+        cudaGraphExec_t exec;
+    };
+    std::vector<GraphEntry> graphs;
     cudaGraphExec_t exec = nullptr;
-    int graph_n = -1;
-    bool graph_logits = false;
     uint64_t steps = 0;
 
     ~dcb_batch() {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
-        if (exec) cudaGraphExecDestroy(exec);
+        for (const GraphEntry& g : graphs) cudaGraphExecDestroy(g.exec);
         for (void* p : allocations) cudaFree(p);
         if (h_io) cudaFreeHost(h_io);
+        if (h_pos) cudaFreeHost(h_pos);
         if (stream) cudaStreamDestroy(stream);
     }
     template <class T>
@@ -245,8 +256,10 @@ int allow_smem(int slots) {
     return 0;
 }
 
+// One step of n slots; head false: no LM head and no argmax (the slots'
+// positions and tokens are then not advanced on the device).
 template <typename KV>
-int enqueue_step(dcb_batch* b, int n, bool want_logits) {
+int enqueue_step(dcb_batch* b, int n, bool want_logits, bool head) {
     const Params& P = b->M.P;
     const int H = P.H, I = P.I, D = P.D;
     const int st_smem_h = P.Kh * (int)sizeof(float), st_smem_i = P.Ki * (int)sizeof(float);
@@ -274,6 +287,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
     g.rope = b->rope;
     g.kcache = b->kc;
     g.vcache = b->vc;
+    g.kv_seq = b->kv_seq;
     g.amax = b->amax;
     g.err = b->err;
 
@@ -313,6 +327,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
     aa.capacity = (int)b->capacity;
     aa.split_len = b->split_len;
     aa.max_splits = b->max_splits;
+    aa.kv_seq = b->kv_seq;
     const size_t at_smem = attention_smem_bytes(D, (int)sizeof(KV), P.NH / P.NKV);
     CombineArgs ca{};
     ca.part = b->part;
@@ -357,6 +372,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             a6.capacity = (int)b->capacity;
             a6.split_len = b->split_len;
             a6.max_splits = b->max_splits;
+            a6.kv_seq = b->kv_seq;
             a6.err = b->err;
             a6.seq_done = b->seq_done;
             a6.cb = ca;
@@ -472,6 +488,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
             if (int rc = launch(stage_kernel, dim3(n), ST_NT, st_smem_h, b->stream, 1, s)) return rc;
         }
     }
+    if (!head) return 0;
     // Tied LM head + per-tile argmax, then the argmax per sequence.
     {
         GemmArgs a = g;
@@ -493,15 +510,22 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits) {
     return launch(argmax_kernel, dim3(n), ARG_NT, 0, b->stream, 1, ga);
 }
 
-int build_graph(dcb_batch* b, int n, bool want_logits) {
-    if (b->exec && b->graph_n == n && b->graph_logits == want_logits) return 0;
-    if (b->exec) {
-        cudaGraphExecDestroy(b->exec);
-        b->exec = nullptr;
+constexpr size_t MAX_GRAPHS = 6;
+
+int build_graph(dcb_batch* b, int n, bool want_logits, bool head = true) {
+    for (const auto& g : b->graphs)
+        if (g.n == n && g.logits == want_logits && g.head == head) {
+            b->exec = g.exec;
+            return 0;
+        }
+    b->exec = nullptr;
+    if (b->graphs.size() >= MAX_GRAPHS) {
+        cudaGraphExecDestroy(b->graphs.front().exec);
+        b->graphs.erase(b->graphs.begin());
     }
     BT_CUDA(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal));
-    const int rc = b->kv_dtype == DCB_KV_F16 ? enqueue_step<__half>(b, n, want_logits)
-                                             : enqueue_step<float>(b, n, want_logits);
+    const int rc = b->kv_dtype == DCB_KV_F16 ? enqueue_step<__half>(b, n, want_logits, head)
+                                             : enqueue_step<float>(b, n, want_logits, head);
     cudaGraph_t graph = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(b->stream, &graph);
     if (rc) {
@@ -509,11 +533,12 @@ int build_graph(dcb_batch* b, int n, bool want_logits) {
         return rc;
     }
     if (ce != cudaSuccess) return bfail(DCB_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
-    const cudaError_t ie = cudaGraphInstantiate(&b->exec, graph, 0);
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     if (ie != cudaSuccess) return bfail(DCB_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
-    b->graph_n = n;
-    b->graph_logits = want_logits;
+    b->graphs.push_back({n, want_logits, head, exec});
+    b->exec = exec;
     return 0;
 }
 
@@ -536,9 +561,11 @@ int device_status(dcb_batch* b, int err) {
 
 }  // namespace
 
-extern "C" {
-
-int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int kv_dtype, dcb_batch** out) {
+// A batched context over engine `model`'s weights. kc/vc null: every slot
+// gets a cache of `capacity` positions; else the slots share that one cache
+// (the engine's own, for its prefill).
+static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, int kv_dtype, void* shared_kc,
+                        void* shared_vc, dcb_batch** out) {
     if (!model || !out) return bfail(DCB_ERR_ARGUMENT, "null argument");
     *out = nullptr;
     if (max_seqs < 1 || max_seqs > MAX_SLOTS) return bfail(DCB_ERR_ARGUMENT, "max_seqs must be 1..64");
@@ -583,7 +610,11 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
     if (int rc = b->alloc(&b->pos, S)) return bail(rc);
     if (int rc = b->alloc(&b->argmax, S + 1)) return bail(rc);
     b->err = b->argmax + S;  // read with the argmax in one copy
-    {
+    if (shared_kc) {
+        b->kc = shared_kc;
+        b->vc = shared_vc;
+        b->kv_seq = 0;
+    } else {
         unsigned char *kc, *vc;
         const size_t n = (size_t)S * P.L * P.NKV * capacity * P.D * b->kv_elem();
         if (int rc = b->alloc(&kc, n)) return bail(rc);
@@ -591,6 +622,7 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
         b->kc = kc;
         b->vc = vc;
     }
+    const size_t caches = shared_kc ? 1 : (size_t)S;
     b->pos_host.assign(S, 0);
     // Tensor maps: weights in their packed rows (int8 part only), and the planes.
     b->map_qkv.resize(P.L);
@@ -609,7 +641,7 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
     if (int rc = make_map(&b->map_pi, b->pi, P.Ki, 3 * (uint64_t)S, P.Ki, 3 * S)) return bail(rc);
     if (b->attn64) {
         // KV rows of every sequence, layer and head as one 2D array of 64-element rows.
-        const uint64_t rows = (uint64_t)S * P.L * P.NKV * capacity;
+        const uint64_t rows = (uint64_t)caches * P.L * P.NKV * capacity;
         const bool f16 = kv_dtype == DCB_KV_F16;
         const CUtensorMapDataType t = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
         const uint32_t inner = f16 ? 64 : 32;  // 128-byte boxes
@@ -661,12 +693,19 @@ int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int
             BT_CUDA(set((const void*)attention_kernel<float, 0>));
         }
     }
-    if (cudaMallocHost(&b->h_io, (size_t)2 * (S + 1) * sizeof(int)) != cudaSuccess)
+    if (cudaMallocHost(&b->h_io, (size_t)2 * (S + 1) * sizeof(int)) != cudaSuccess ||
+        cudaMallocHost(&b->h_pos, (size_t)S * sizeof(int)) != cudaSuccess)
         return bail(bfail(DCB_ERR_CUDA, "cudaMallocHost failed"));
     BT_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
     BT_CUDA(cudaDeviceSynchronize());
     *out = b;
     return 0;
+}
+
+extern "C" {
+
+int dcb_batch_create(const dcb_engine* model, int max_seqs, size_t capacity, int kv_dtype, dcb_batch** out) {
+    return create_batch(model, max_seqs, capacity, kv_dtype, nullptr, nullptr, out);
 }
 
 void dcb_batch_destroy(dcb_batch* b) { delete b; }
@@ -838,6 +877,63 @@ uint64_t dcb_batch_kernels_per_step(const dcb_batch* b, int n) {
     if (!b) return 0;
     const uint64_t per_layer = 5 + (b->attn64 && b->fuse_combine ? 0 : 1) + (b->fuse_stage ? 0 : 3);
     return 1 + (uint64_t)b->M.P.L * per_layer + 2;
+}
+
+// Prefill of an engine's prompt in batched form. The reference prefills one
+// token at a time (src/main.cpp:134-137: Engine::step with the head only on
+// the last token); here up to 64 consecutive positions form one batched step
+// whose slots share the engine's cache: the QKV projection writes every
+// slot's K/V row at its position, then each slot attends over positions 0 ..
+// its own (causal), so the rows and the last token's logits are those of the
+// token-by-token steps (up to the rounding of the batched staging, which
+// scales each token's activations as a whole vector).
+int dcb_prefill(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out) {
+    if (!e || !tokens) return bfail(DCB_ERR_ARGUMENT, "null argument");
+    if (n < 1) return bfail(DCB_ERR_ARGUMENT, "prefill needs at least one token");
+    EngineKV kv;
+    if (int rc = engine_kv(e, &kv)) return rc;
+    if (!kv.whole_sequence)
+        return bfail(DCB_ERR_UNSUPPORTED, "prefill needs an engine that keeps the whole sequence (no KV split)");
+    if (kv.pos + (size_t)n > kv.capacity) return bfail(DCB_ERR_CAPACITY, "context capacity exceeded");
+    dcb_batch*& b = engine_prefill_batch(e);
+    if (b && b->capacity != kv.capacity) {
+        dcb_batch_destroy(b);
+        b = nullptr;
+    }
+    if (!b)
+        if (int rc = create_batch(e, MAX_SLOTS, kv.capacity, kv.kv_dtype, kv.kcache, kv.vcache, &b)) return rc;
+    const int V = b->M.P.V;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= V) return bfail(DCB_ERR_TOKEN, "token ID outside vocabulary");
+    BT_CUDA(cudaSetDevice(b->device));
+    // The engine's earlier steps have written their rows.
+    BT_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(kv.stream)));
+    int* hout = b->h_io + b->slots + 1;
+    for (int c = 0; c < n; c += b->slots) {
+        const int m = std::min(b->slots, n - c);
+        const bool last = c + m == n;
+        BT_CUDA(cudaStreamSynchronize(b->stream));  // h_io and h_pos are reused
+        for (int i = 0; i < m; ++i) {
+            b->h_io[i] = tokens[c + i];
+            b->h_pos[i] = (int)(kv.pos + (size_t)(c + i));
+        }
+        BT_CUDA(cudaMemcpyAsync(b->tokens, b->h_io, (size_t)m * sizeof(int), cudaMemcpyHostToDevice, b->stream));
+        BT_CUDA(cudaMemcpyAsync(b->pos, b->h_pos, (size_t)m * sizeof(int), cudaMemcpyHostToDevice, b->stream));
+        if (int rc = build_graph(b, m, last && logits != nullptr, last)) return rc;
+        BT_CUDA(cudaGraphLaunch(b->exec, b->stream));
+        if (last) {
+            if (logits)
+                BT_CUDA(cudaMemcpyAsync(logits, b->logits + (size_t)(m - 1) * V, (size_t)V * sizeof(float),
+                                        cudaMemcpyDeviceToHost, b->stream));
+            BT_CUDA(cudaMemcpyAsync(hout, b->argmax, (size_t)(b->slots + 1) * sizeof(int), cudaMemcpyDeviceToHost,
+                                    b->stream));
+            BT_CUDA(cudaStreamSynchronize(b->stream));
+            if (int rc = device_status(b, hout[b->slots])) return rc;
+            if (argmax_out) *argmax_out = hout[m - 1];
+        }
+    }
+    engine_advance(e, (size_t)n);
+    return 0;
 }
 
 }  // extern "C"

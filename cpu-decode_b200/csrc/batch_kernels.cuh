@@ -25,6 +25,7 @@
 #pragma once
 #include "attention.cuh"
 #include "step_kernel.cuh"
+#include "tcgen05.cuh"
 
 #include <cuda.h>
 
@@ -66,11 +67,12 @@ struct GemmArgs {
     int ldo;
     // QKV: rows are RoPE pairs (j, j + D/2) of q heads, then k heads, then v heads
     int NH, NKV, D, L, layer, capacity, cached_rope;
+    int kv_seq;  // 1: slot s owns cache s; 0: every slot is a position of one sequence (cache 0)
     const float* rope_inv;  // [D/2]
     const float* rope_den;  // [D/2]
     const int* pos;         // [slots] position of each sequence's new token
     const float2* rope;     // [slots][D/2] (cos, sin) of each sequence's position
-    void* kcache;           // [slots][L][NKV][capacity][D]
+    void* kcache;           // [slots or 1][L][NKV][capacity][D]
     void* vcache;
     ArgBest* amax;  // HEAD: [tiles][slots] best (value, row) of each tile and sequence
     int* err;       // set to ERR_WAIT when a wait runs out
@@ -98,23 +100,6 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
     return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
            ((uint64_t)2 << 61);
 }
-// Instruction descriptor of kind::i8: signed A and B, S32 accumulators, both
-// K-major, M = GM, N = n.
-__host__ __device__ constexpr uint32_t idesc_i8(int n) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
-}
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
-    const uint32_t z = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
-}
-// Arrive on m once every MMA issued so far by this thread has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* m) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(m))
-                 : "memory");
-}
 __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* m) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
@@ -122,29 +107,6 @@ __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* map, int x, 
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(m))
         : "memory");
 }
-__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-// 32 TMEM lanes (one per thread of the warp) x 16 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
 // Programmatic dependent launch: a kernel may start while its predecessor in
 // the stream still runs; griddep_wait() returns once the predecessor has
 // completed and its writes are visible. Work before it may only touch data
@@ -369,7 +331,7 @@ __global__ void __launch_bounds__(GT, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // MMA issuer: 4 MMAs of K = 32 per stage, accumulating in TMEM.
-            const uint32_t idesc = idesc_i8(N);
+            const uint32_t idesc = idesc_i8(GM, N);
             for (int i = 0; i < nkl; ++i) {
                 const int s = i % GSTAGES;
                 if (!wait_phase(&full[s], (uint32_t)(i / GSTAGES) & 1u, a.err)) break;
@@ -506,7 +468,7 @@ __global__ void __launch_bounds__(GT, 1)
                         out[(size_t)s * a.ldo + q_hd * a.D + idx] = val;
                     } else {
                         KV* cache = static_cast<KV*>(q_kind == 1 ? a.kcache : a.vcache) +
-                                    ((((size_t)s * a.L + a.layer) * a.NKV + q_hd) * a.capacity + p) * a.D;
+                                    ((((size_t)s * a.kv_seq * a.L + a.layer) * a.NKV + q_hd) * a.capacity + p) * a.D;
                         kv_store(cache + idx, val);
                     }
                 }
@@ -652,11 +614,12 @@ __global__ void __launch_bounds__(ST_NT) stage_kernel(const StageArgs a) {
 // ---- attention ---------------------------------------------------------------------
 struct AttnArgs {
     const float* q;  // [slots][NH*D] rotated queries
-    const void* kcache;  // [slots][L][NKV][capacity][D]
+    const void* kcache;  // [slots or 1][L][NKV][capacity][D]
     const void* vcache;
     float* part;  // [slots][NH][max_splits][D+2]: (max, sum, unnormalised output) of each split
     const int* pos;
     int NH, NKV, D, L, layer, capacity, split_len, max_splits;
+    int kv_seq;  // as GemmArgs::kv_seq
 };
 
 // Block (split, kv head g, sequence s): positions [split*split_len, ...) up to
@@ -673,7 +636,7 @@ __global__ void __launch_bounds__(AT_NT) attention_kernel(const AttnArgs a) {
     if (t0 >= length) return;
     const int t1 = min(length, t0 + a.split_len);
     const int gq = a.NH / a.NKV;
-    const size_t head = (((size_t)s * a.L + a.layer) * a.NKV + g) * (size_t)a.capacity * D;
+    const size_t head = (((size_t)s * a.kv_seq * a.L + a.layer) * a.NKV + g) * (size_t)a.capacity * D;
     const KV* kg = static_cast<const KV*>(a.kcache) + head;
     const KV* vg = static_cast<const KV*>(a.vcache) + head;
     float* sq = reinterpret_cast<float*>(at_sm + 2 * 2 * (size_t)AT_T * D * sizeof(KV));
@@ -802,6 +765,7 @@ struct Attn64Args {
     float* part;     // [slots][NH][max_splits][66]
     const int* pos;
     int NH, NKV, L, layer, capacity, split_len, max_splits;
+    int kv_seq;  // as GemmArgs::kv_seq
     int* err;
     // Split merge in the kernel (FUSE): the last block to finish for a
     // sequence (seq_done[s] counts them; it resets it) merges its splits.
@@ -900,7 +864,7 @@ __global__ void __launch_bounds__(A64_NT, 2)
     const int t1 = min(length, t0 + a.split_len);
     const int nch = (t1 - t0 + A64_T - 1) / A64_T;
     const int gq = a.NH / a.NKV;
-    const int row0 = (((s * a.L + a.layer) * a.NKV + g) * a.capacity) + t0;
+    const int row0 = (((s * a.kv_seq * a.L + a.layer) * a.NKV + g) * a.capacity) + t0;
 
     auto issue = [&](int c) {
         const int slot = c % NS;
@@ -924,13 +888,17 @@ __global__ void __launch_bounds__(A64_NT, 2)
         s_abort = 0;
         for (int i = 0; i < NS; ++i) mbar_init(&full[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // Chunks wholly before the new position hold earlier steps' rows and
+        // load under the previous kernel's tail; when the slots are positions
+        // of one sequence (kv_seq 0) the other slots' rows of this step sit
+        // there too, so everything waits.
         for (int c = 0; c < NS && c < nch; ++c)
-            if (t0 + (c + 1) * A64_T <= pos) issue(c);
+            if (a.kv_seq && t0 + (c + 1) * A64_T <= pos) issue(c);
     }
     griddep_wait();
     if (tid == 0)
         for (int c = 0; c < NS && c < nch; ++c)
-            if (t0 + (c + 1) * A64_T > pos) issue(c);
+            if (!a.kv_seq || t0 + (c + 1) * A64_T > pos) issue(c);
 
     // QK roles: positions 16*mt.., dims 32*kh..; B fragments of q (scaled by
     // log2(e)/8), head = fragment column gq8, for this warp's two k-steps.

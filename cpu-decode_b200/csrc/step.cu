@@ -89,9 +89,12 @@ struct dcb_engine {
     HeadParams HP{};
     bool head_sep = false;
     int head_grid = 0;
+    // Batched prefill context over this engine's KV cache (dcb_prefill).
+    dcb_batch* prefill = nullptr;
 
     ~dcb_engine() {
         cudaSetDevice(device);
+        if (prefill) dcb_batch_destroy(prefill);
         if (stream) cudaStreamSynchronize(stream);
         for (void* p : allocations) cudaFree(p);
         if (h_result) cudaFreeHost(h_result);
@@ -1053,6 +1056,20 @@ int dcb_trace_read(dcb_engine* e, uint64_t* ready, uint64_t* done, int* phases) 
 }
 
 }  // extern "C"
+
+int dcb::engine_kv(const dcb_engine* e, EngineKV* out) {
+    if (!e || !out) return fail(DCB_ERR_ARGUMENT, "null engine");
+    out->kcache = e->P.kcache;
+    out->vcache = e->P.vcache;
+    out->capacity = e->capacity;
+    out->pos = e->pos;
+    out->kv_dtype = e->kv_dtype;
+    out->whole_sequence = e->P.world == 1 && e->kv_base == 0 && e->kv_end == SIZE_MAX;
+    out->stream = e->stream;
+    return 0;
+}
+void dcb::engine_advance(dcb_engine* e, size_t n) { e->pos += n; }
+dcb_batch*& dcb::engine_prefill_batch(dcb_engine* e) { return e->prefill; }
 
 int dcb::model_view(const dcb_engine* e, ModelView* out) {
     if (!e || !out) return fail(DCB_ERR_ARGUMENT, "null engine");

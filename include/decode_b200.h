@@ -273,6 +273,19 @@ int dcb_batch_read(dcb_batch* b, int n, int* tokens_out, float* logits);
 void* dcb_batch_stream(const dcb_batch* b);
 uint64_t dcb_batch_kernels_per_step(const dcb_batch* b, int n);
 
+/* Prefill: tokens[0..n) enter the engine at positions pos .. pos+n-1 in
+ * batched form instead of n calls of dcb_step (the reference's prefill loop,
+ * src/main.cpp:134-137: Engine::step per prompt token, the LM head on the last
+ * only). Up to 64 positions form one batched step on the tensor cores whose
+ * slots share the engine's KV cache; each attends causally over positions 0
+ * .. its own. The engine's K/V rows and position afterwards are those of the
+ * token-by-token steps (rows within the FP32 tolerance, not bit-identical);
+ * logits (host, V floats, or NULL) and argmax_out (or NULL) are the last
+ * token's. For an engine that keeps the whole sequence (no KV split); runs
+ * after the engine's queued steps and returns when the rows are written.
+ * Errors: DCB_ERR_CAPACITY (pos + n > capacity), DCB_ERR_TOKEN, as dcb_step. */
+int dcb_prefill(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out);
+
 #ifdef __cplusplus
 }
 #endif
