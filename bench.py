@@ -391,6 +391,8 @@ def main() -> None:
         extra["hbm_read_probe"] = {"GB_per_s_median": round(rates[len(rates) // 2], 1),
                                    "GB_per_s_max": round(rates[-1], 1), "array_bytes": probe["array_bytes"],
                                    "passes": probe["passes"], "kernel": probe["kernel"]}
+    if rank == 0:
+        extra["prefill128"] = prefill_time(dcb, model, local)
     if not args.no_long and rank == 0:
         extra["ctx4096"] = long_context(dcb, model, d, K, W, local, 4096)
         extra["ctx32768"] = long_context(dcb, model, d, min(K, 32), W, local, 32768)
@@ -533,6 +535,48 @@ def _timed_calls(fn, n_calls: int, warmup: int = 3) -> tuple[float, float]:
     graphed = s.elapsed_time(e) / n_calls
     del graph
     return eager, graphed
+
+
+def prefill_time(dcb, model: Path, device: int, repeats: int = 5) -> dict:
+    """The bench's 128-token prompt entering an empty engine: the reference's
+    loop (src/main.cpp:134-137, one step per token, the LM head on the last)
+    against dcb_prefill (up to 64 positions per batched tensor-core step).
+    Wall time of the host call sequence, median of `repeats` after two warm-up
+    rounds; both return once the K/V rows are written and the last logits are
+    on the host. The two paths' last logits are compared."""
+    prompt = prompt_tokens()
+    n = len(prompt)
+    eng = dcb.Engine(model, n + 8, device=device)
+
+    def loop():
+        eng.reset()
+        for i, t in enumerate(prompt):
+            out = eng.step(t, head=(i + 1 == n))
+        return out
+
+    def batched():
+        eng.reset()
+        return eng.prefill(prompt)
+
+    times = {}
+    results = {}
+    for name, fn in (("token_by_token", loop), ("batched", batched)):
+        for _ in range(2):
+            fn()
+        samples = []
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            logits, best = fn()
+            samples.append(time.perf_counter() - t0)
+        times[name] = sorted(samples)[len(samples) // 2]
+        results[name] = (logits.copy(), best)
+    eng.close()
+    diff = float(np.abs(results["batched"][0] - results["token_by_token"][0]).max())
+    return {"prompt_tokens": n, "token_by_token_ms": round(times["token_by_token"] * 1e3, 3),
+            "batched_ms": round(times["batched"] * 1e3, 3),
+            "speedup": round(times["token_by_token"] / times["batched"], 2),
+            "batched_tokens_per_s": round(n / times["batched"], 1),
+            "max_abs_logit_diff": diff, "argmax_equal": results["batched"][1] == results["token_by_token"][1]}
 
 
 def gemv_sweep(dcb) -> dict:
