@@ -558,9 +558,22 @@ def prefill_time(dcb, model: Path, device: int, repeats: int = 5) -> dict:
         eng.reset()
         return eng.prefill(prompt)
 
+    def dump_loop():
+        # the reference's `logits` command: the head on every token (src/main.cpp:93-114)
+        eng.reset()
+        rows = np.zeros((n, eng.vocab), np.float32)
+        for i, t in enumerate(prompt):
+            rows[i] = eng.step(t)[0]
+        return rows, None
+
+    def dump_batched():
+        eng.reset()
+        return eng.prefill_logits(prompt)
+
     times = {}
     results = {}
-    for name, fn in (("token_by_token", loop), ("batched", batched)):
+    for name, fn in (("token_by_token", loop), ("batched", batched), ("logits_dump_loop", dump_loop),
+                     ("logits_dump_batched", dump_batched)):
         for _ in range(2):
             fn()
         samples = []
@@ -572,11 +585,17 @@ def prefill_time(dcb, model: Path, device: int, repeats: int = 5) -> dict:
         results[name] = (logits.copy(), best)
     eng.close()
     diff = float(np.abs(results["batched"][0] - results["token_by_token"][0]).max())
+    dump_diff = float(np.abs(results["logits_dump_batched"][0] - results["logits_dump_loop"][0]).max())
     return {"prompt_tokens": n, "token_by_token_ms": round(times["token_by_token"] * 1e3, 3),
             "batched_ms": round(times["batched"] * 1e3, 3),
             "speedup": round(times["token_by_token"] / times["batched"], 2),
             "batched_tokens_per_s": round(n / times["batched"], 1),
-            "max_abs_logit_diff": diff, "argmax_equal": results["batched"][1] == results["token_by_token"][1]}
+            "max_abs_logit_diff": diff, "argmax_equal": results["batched"][1] == results["token_by_token"][1],
+            "logits_dump": {"what": "every position's logits to host memory (the reference's logits command)",
+                            "token_by_token_ms": round(times["logits_dump_loop"] * 1e3, 3),
+                            "batched_ms": round(times["logits_dump_batched"] * 1e3, 3),
+                            "speedup": round(times["logits_dump_loop"] / times["logits_dump_batched"], 2),
+                            "max_abs_logit_diff": dump_diff}}
 
 
 def gemv_sweep(dcb) -> dict:

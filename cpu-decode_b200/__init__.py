@@ -34,10 +34,10 @@ EXPORTS = (
     "dcb_step_async", "dcb_synchronize", "dcb_rewind", "dcb_reset", "dcb_position", "dcb_set_stream", "dcb_stream",
     "dcb_logits_device", "dcb_kv_write", "dcb_kv_read", "dcb_set_position", "dcb_launch_info", "dcb_launch_count",
     "dcb_gemv_i8", "dcb_attention", "dcb_attention_noalloc", "dcb_rmsnorm", "dcb_rope", "dcb_argmax",
-    "dcb_read_bandwidth",
+    "dcb_read_bandwidth", "dcb_quantize_rows_bf16", "dcb_quantize_model",
     "dcb_trace_enable", "dcb_trace_read", "dcb_exchange_buffer", "dcb_ipc_handle", "dcb_ipc_open", "dcb_ipc_close",
     "dcb_set_kv_shard", "dcb_batch_create", "dcb_batch_destroy", "dcb_batch_info", "dcb_batch_set_position",
-    "dcb_batch_position", "dcb_batch_kv_write", "dcb_batch_kv_read", "dcb_batch_step", "dcb_batch_step_greedy", "dcb_prefill",
+    "dcb_batch_position", "dcb_batch_kv_write", "dcb_batch_kv_read", "dcb_batch_step", "dcb_batch_step_greedy", "dcb_prefill", "dcb_prefill_logits",
     "dcb_batch_read", "dcb_batch_stream", "dcb_batch_kernels_per_step",
 )
 
@@ -90,6 +90,8 @@ def lib() -> C.CDLL:
     L.dcb_rope.argtypes = [vp, i32, i32, i32, C.c_float, i32, vp]
     L.dcb_argmax.argtypes = [vp, i32, vp, vp]
     L.dcb_read_bandwidth.argtypes = [i32, C.c_size_t, i32, i32, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
+    L.dcb_quantize_rows_bf16.argtypes = [vp, C.c_size_t, C.c_size_t, vp, vp, i32]
+    L.dcb_quantize_model.argtypes = [C.c_char_p, C.c_char_p, i32]
     L.dcb_trace_enable.argtypes = [vp, i32]
     L.dcb_trace_read.argtypes = [vp, vp, vp, C.POINTER(i32)]
     L.dcb_exchange_buffer.argtypes = [vp, C.POINTER(vp), C.POINTER(sz)]
@@ -107,6 +109,7 @@ def lib() -> C.CDLL:
     L.dcb_batch_kv_read.argtypes = [vp, i32, i32, sz, sz, vp, vp]
     L.dcb_batch_step.argtypes = [vp, i32, vp, vp, vp]
     L.dcb_prefill.argtypes = [vp, vp, i32, vp, vp]
+    L.dcb_prefill_logits.argtypes = [vp, vp, i32, vp, vp]
     L.dcb_batch_step_greedy.argtypes = [vp, i32, i32]
     L.dcb_batch_read.argtypes = [vp, i32, vp, vp]
     L.dcb_batch_stream.argtypes = [vp]
@@ -157,6 +160,16 @@ class Engine:
         _check(lib().dcb_prefill(self._h, t.ctypes.data, int(t.shape[0]),
                                  self.logits.ctypes.data if logits else None, C.addressof(self._argmax)))
         return (self.logits if logits else None), int(self._argmax.value)
+
+    def prefill_logits(self, tokens):
+        """Prefill with every position's logits (dcb_prefill_logits): returns
+        (logits [n][vocab], argmax [n])."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        n = int(t.shape[0])
+        out = np.zeros((n, self.vocab), np.float32)
+        best = np.zeros(n, np.int32)
+        _check(lib().dcb_prefill_logits(self._h, t.ctypes.data, n, out.ctypes.data, best.ctypes.data))
+        return out, best
 
     def rewind(self, position: int) -> None:
         _check(lib().dcb_rewind(self._h, int(position)))
@@ -413,6 +426,22 @@ def rope(x: int, heads: int, dim: int, pos: int, theta: float, direct: bool, str
 
 def argmax(x: int, n: int, out: int, stream: int | None = None):
     _check(lib().dcb_argmax(x, n, out, stream))
+
+
+def quantize_model(source, output, device: int = 0) -> None:
+    """BF16 checkpoint directory -> per-row int8 checkpoint, the per-row rule
+    on the GPU (dcb_quantize_model): the reference quantiser's file byte for byte."""
+    _check(lib().dcb_quantize_model(str(source).encode(), str(output).encode(), int(device)))
+
+
+def quantize_rows_bf16(weights: np.ndarray, device: int = 0):
+    """One BF16 matrix (uint16 bits, rows x cols) -> (int8 rows, float32 scales) on the GPU."""
+    w = np.ascontiguousarray(weights, np.uint16)
+    rows, cols = w.shape
+    q = np.zeros((rows, cols), np.int8)
+    sc = np.zeros(rows, np.float32)
+    _check(lib().dcb_quantize_rows_bf16(w.ctypes.data, rows, cols, q.ctypes.data, sc.ctypes.data, int(device)))
+    return q, sc
 
 
 def read_bandwidth(mib: int = 1024, passes: int = 8, repeats: int = 5, device: int = 0) -> dict:

@@ -887,8 +887,11 @@ uint64_t dcb_batch_kernels_per_step(const dcb_batch* b, int n) {
 // its own (causal), so the rows and the last token's logits are those of the
 // token-by-token steps (up to the rounding of the batched staging, which
 // scales each token's activations as a whole vector).
-int dcb_prefill(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out) {
+// all_logits: every position's logits ([n][V], host) and argmax ([n], host,
+// or null), the LM head on every chunk; else only the last token's.
+static int prefill_impl(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out, bool all_logits) {
     if (!e || !tokens) return bfail(DCB_ERR_ARGUMENT, "null argument");
+    if (all_logits && !logits) return bfail(DCB_ERR_ARGUMENT, "null logits buffer");
     if (n < 1) return bfail(DCB_ERR_ARGUMENT, "prefill needs at least one token");
     EngineKV kv;
     if (int rc = engine_kv(e, &kv)) return rc;
@@ -911,7 +914,7 @@ int dcb_prefill(dcb_engine* e, const int* tokens, int n, float* logits, int* arg
     int* hout = b->h_io + b->slots + 1;
     for (int c = 0; c < n; c += b->slots) {
         const int m = std::min(b->slots, n - c);
-        const bool last = c + m == n;
+        const bool last = c + m == n, head = all_logits || last;
         BT_CUDA(cudaStreamSynchronize(b->stream));  // h_io and h_pos are reused
         for (int i = 0; i < m; ++i) {
             b->h_io[i] = tokens[c + i];
@@ -919,21 +922,35 @@ int dcb_prefill(dcb_engine* e, const int* tokens, int n, float* logits, int* arg
         }
         BT_CUDA(cudaMemcpyAsync(b->tokens, b->h_io, (size_t)m * sizeof(int), cudaMemcpyHostToDevice, b->stream));
         BT_CUDA(cudaMemcpyAsync(b->pos, b->h_pos, (size_t)m * sizeof(int), cudaMemcpyHostToDevice, b->stream));
-        if (int rc = build_graph(b, m, last && logits != nullptr, last)) return rc;
+        if (int rc = build_graph(b, m, head && logits != nullptr, head)) return rc;
         BT_CUDA(cudaGraphLaunch(b->exec, b->stream));
-        if (last) {
-            if (logits)
-                BT_CUDA(cudaMemcpyAsync(logits, b->logits + (size_t)(m - 1) * V, (size_t)V * sizeof(float),
-                                        cudaMemcpyDeviceToHost, b->stream));
-            BT_CUDA(cudaMemcpyAsync(hout, b->argmax, (size_t)(b->slots + 1) * sizeof(int), cudaMemcpyDeviceToHost,
-                                    b->stream));
-            BT_CUDA(cudaStreamSynchronize(b->stream));
-            if (int rc = device_status(b, hout[b->slots])) return rc;
-            if (argmax_out) *argmax_out = hout[m - 1];
-        }
+        if (!head) continue;
+        if (all_logits)
+            BT_CUDA(cudaMemcpyAsync(logits + (size_t)c * V, b->logits, (size_t)m * V * sizeof(float),
+                                    cudaMemcpyDeviceToHost, b->stream));
+        else if (logits)
+            BT_CUDA(cudaMemcpyAsync(logits, b->logits + (size_t)(m - 1) * V, (size_t)V * sizeof(float),
+                                    cudaMemcpyDeviceToHost, b->stream));
+        BT_CUDA(cudaMemcpyAsync(hout, b->argmax, (size_t)(b->slots + 1) * sizeof(int), cudaMemcpyDeviceToHost,
+                                b->stream));
+        BT_CUDA(cudaStreamSynchronize(b->stream));
+        if (int rc = device_status(b, hout[b->slots])) return rc;
+        if (all_logits && argmax_out) std::memcpy(argmax_out + c, hout, (size_t)m * sizeof(int));
+        if (!all_logits && argmax_out) *argmax_out = hout[m - 1];
     }
     engine_advance(e, (size_t)n);
     return 0;
+}
+
+int dcb_prefill(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out) {
+    return prefill_impl(e, tokens, n, logits, argmax_out, false);
+}
+
+// The reference's `logits` command (src/main.cpp:93-114) steps every prompt
+// token with the head on and writes each position's logits to PREFIX.bin;
+// this is that stream from batched steps.
+int dcb_prefill_logits(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out) {
+    return prefill_impl(e, tokens, n, logits, argmax_out, true);
 }
 
 }  // extern "C"

@@ -471,6 +471,84 @@ int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* 
 
 }  // extern "C"
 
+namespace {
+// One warp per row of BF16 weights: the reference's per-row rule
+// (src/kernels.cpp:121-131) in IEEE FP32: the largest magnitude, scale =
+// max / 127 (1 for an all-zero row), each weight / scale rounded half away
+// from zero (roundf) and clamped to [-127, 127]. A non-finite weight raises
+// *bad (the row's output is then not used).
+constexpr int QZ_ROWS = 8;  // rows (warps) per block
+__global__ void __launch_bounds__(32 * QZ_ROWS) quantize_rows_kernel(const uint16_t* __restrict__ w, size_t rows,
+                                                                      size_t cols, int8_t* __restrict__ q,
+                                                                      float* __restrict__ scales, int* bad) {
+    const size_t r = (size_t)blockIdx.x * QZ_ROWS + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const uint16_t* row = w + r * cols;
+    float peak = 0.f;
+    bool finite = true;
+    for (size_t j = lane; j < cols; j += 32) {
+        const float v = __uint_as_float((uint32_t)row[j] << 16);
+        finite = finite && isfinite(v);
+        peak = fmaxf(peak, fabsf(v));
+    }
+    peak = warp_max(peak);
+    if (!__all_sync(FULL, finite)) {
+        if (lane == 0) atomicExch(bad, 1);
+        return;
+    }
+    const float scale = peak > 0.f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+    int8_t* out = q + r * cols;
+    for (size_t j = lane; j < cols; j += 32) {
+        const float v = __uint_as_float((uint32_t)row[j] << 16);
+        const float x = roundf(__fdiv_rn(v, scale));
+        out[j] = (int8_t)(x > 127.f ? 127.f : (x < -127.f ? -127.f : x));
+    }
+    if (lane == 0) scales[r] = scale;
+}
+}  // namespace
+
+extern "C" int dcb_quantize_rows_bf16(const uint16_t* weights, size_t rows, size_t cols, int8_t* out, float* scales,
+                                      int device) {
+    if (!weights || !out || !scales) return fail(DCB_ERR_ARGUMENT, "null argument");
+    if (!rows) return 0;
+    if (!cols) return fail(DCB_ERR_ARGUMENT, "empty quantization row");
+    int caller_device = 0;
+    cudaError_t e = cudaGetDevice(&caller_device);
+    if (e != cudaSuccess) return cuda_fail(e, "current device");
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "quantiser device");
+    uint16_t* dw = nullptr;
+    int8_t* dq = nullptr;
+    float* ds = nullptr;
+    int* dbad = nullptr;
+    int bad = 0, rc = 0;
+    auto check = [&](cudaError_t err, const char* what) {
+        if (err != cudaSuccess && !rc) rc = cuda_fail(err, what);
+        return rc == 0;
+    };
+    const size_t n = rows * cols;
+    if (check(cudaMalloc(&dw, n * 2), "quantiser input") && check(cudaMalloc(&dq, n), "quantiser output") &&
+        check(cudaMalloc(&ds, rows * 4), "quantiser scales") && check(cudaMalloc(&dbad, 4), "quantiser flag") &&
+        check(cudaMemset(dbad, 0, 4), "quantiser flag") &&
+        check(cudaMemcpy(dw, weights, n * 2, cudaMemcpyHostToDevice), "quantiser upload")) {
+        quantize_rows_kernel<<<(unsigned)((rows + QZ_ROWS - 1) / QZ_ROWS), 32 * QZ_ROWS>>>(dw, rows, cols, dq, ds,
+                                                                                           dbad);
+        if (check(cudaGetLastError(), "quantiser launch") && check(cudaMemcpy(&bad, dbad, 4, cudaMemcpyDeviceToHost),
+                                                                    "quantiser flag") && !bad) {
+            check(cudaMemcpy(out, dq, n, cudaMemcpyDeviceToHost), "quantiser download");
+            check(cudaMemcpy(scales, ds, rows * 4, cudaMemcpyDeviceToHost), "quantiser download");
+        }
+    }
+    if (dw) cudaFree(dw);
+    if (dq) cudaFree(dq);
+    if (ds) cudaFree(ds);
+    if (dbad) cudaFree(dbad);
+    cudaSetDevice(caller_device);
+    if (!rc && bad) rc = fail(DCB_ERR_ARGUMENT, "nonfinite model weight");
+    return rc;
+}
+
 // ---- attention with its scratch in a static device array --------------------------
 // dcb_attention_noalloc is dcb_attention with the cudaMallocAsync scratch
 // replaced by one fixed array per device, for callers that must not allocate

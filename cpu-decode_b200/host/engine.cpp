@@ -17,6 +17,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <functional>
 #include <cmath>
 #include <cstring>
 #include <filesystem>
@@ -546,10 +547,15 @@ void quantize_row(const float* source, size_t n, int8_t* out, float& scale) {
     });
 }
 
+namespace {
+// Quantises one BF16 matrix (rows x cols, a view into the mapped file) into
+// q [rows][cols] and per-row scales.
+using MatrixQuantizer = std::function<void(const TensorView&, size_t rows, size_t cols, int8_t* q, float* scales)>;
+
 // BF16 checkpoint -> per-row int8 checkpoint in the reference's file layout
 // (src/model.cpp:354-417): name-ordered tensors, matrices as I8 followed by
 // "<name>.scales" F32, vectors as F32, header padded to 8 bytes.
-void quantize_model(const std::string& source, const std::string& output) {
+void write_quantized(const std::string& source, const std::string& output, const MatrixQuantizer& quantize_matrix) {
     const fs::path src(source), dst(output);
     if (fs::weakly_canonical(src) == fs::weakly_canonical(dst)) throw std::runtime_error("quantization output must differ from input");
     const ModelConfig config(load_json(src / "config.json"));
@@ -593,13 +599,10 @@ void quantize_model(const std::string& source, const std::string& output) {
             const TensorView& t = item.second;
             if (t.shape.size() == 2) {
                 const size_t rows = t.shape[0], cols = t.shape[1];
-                std::vector<float> row(cols), sc(rows);
-                std::vector<int8_t> q(cols);
-                for (size_t r = 0; r < rows; ++r) {
-                    for (size_t j = 0; j < cols; ++j) row[j] = t.value(r * cols + j);
-                    quantize_row(row.data(), cols, q.data(), sc[r]);
-                    out.write(reinterpret_cast<const char*>(q.data()), cols);
-                }
+                std::vector<float> sc(rows);
+                std::vector<int8_t> q(rows * cols);
+                quantize_matrix(t, rows, cols, q.data(), sc.data());
+                out.write(reinterpret_cast<const char*>(q.data()), (std::streamsize)q.size());
                 out.write(reinterpret_cast<const char*>(sc.data()), rows * 4);
             } else {
                 for (size_t j = 0; j < t.count(); ++j) {
@@ -619,8 +622,36 @@ void quantize_model(const std::string& source, const std::string& output) {
         throw;
     }
 }
+}  // namespace
+
+void quantize_model(const std::string& source, const std::string& output) {
+    write_quantized(source, output, [](const TensorView& t, size_t rows, size_t cols, int8_t* q, float* sc) {
+        std::vector<float> row(cols);
+        for (size_t r = 0; r < rows; ++r) {
+            for (size_t j = 0; j < cols; ++j) row[j] = t.value(r * cols + j);
+            quantize_row(row.data(), cols, q + r * cols, sc[r]);
+        }
+    });
+}
 
 }  // namespace decode
+
+// The same checkpoint with the per-row rule on a GPU (dcb_quantize_rows_bf16):
+// the output file is byte for byte the CPU quantiser's.
+extern "C" int dcb_quantize_model(const char* source, const char* output, int device) {
+    try {
+        if (!source || !output) throw std::runtime_error("null argument");
+        decode::write_quantized(source, output, [device](const decode::TensorView& t, size_t rows, size_t cols, int8_t* q,
+                                                          float* sc) {
+            if (dcb_quantize_rows_bf16(static_cast<const uint16_t*>(t.data), rows, cols, q, sc, device) != DCB_OK)
+                throw std::runtime_error(dcb_last_error());
+        });
+        return DCB_OK;
+    } catch (const std::exception& e) {
+        dcb_set_error(e.what());
+        return DCB_ERR_ARGUMENT;
+    }
+}
 
 // ---------------------------------------------------------------------------
 // C entry over the loader, so callers without C++ (ctypes, cgo) open a model

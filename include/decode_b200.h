@@ -235,6 +235,22 @@ int dcb_argmax(const float* x, int n, int* out, void* stream);
  * it was. Invalid sizes give DCB_ERR_ARGUMENT ("invalid sweep parameters"). */
 int dcb_read_bandwidth(int device, size_t mib, int passes, int repeats, double* gb_per_s, uint64_t* checksum);
 
+/* ---- the quantiser on the GPU ------------------------------------------------
+ * decode::quantize_row (src/kernels.cpp:121-131) for a whole BF16 matrix
+ * (host, row-major rows x cols): per row the largest magnitude, scale =
+ * max/127 (1 for an all-zero row), weight/scale rounded half away from zero
+ * and clamped to [-127, 127], in IEEE FP32 as the reference computes it, so
+ * out [rows][cols] (host) and scales [rows] (host) are bit-identical to the
+ * CPU rule. Non-finite weights: DCB_ERR_ARGUMENT "nonfinite model weight";
+ * cols 0: "empty quantization row". Uses `device`, synchronises, restores the
+ * calling thread's device. */
+int dcb_quantize_rows_bf16(const uint16_t* weights, size_t rows, size_t cols, int8_t* out, float* scales, int device);
+/* decode::quantize_model (src/model.cpp:354-417) with every matrix quantised
+ * by dcb_quantize_rows_bf16: BF16 checkpoint directory `source` -> per-row
+ * int8 checkpoint `output`, the same file byte for byte and the same checks
+ * and messages. */
+int dcb_quantize_model(const char* source, const char* output, int device);
+
 /* ---- batched decode of independent sequences (one GPU) --------------------
  * No counterpart in the reference, which decodes one sequence per Engine
  * (src/model.cpp:258-329); a caller with many sequences would run one Engine
@@ -285,6 +301,12 @@ uint64_t dcb_batch_kernels_per_step(const dcb_batch* b, int n);
  * after the engine's queued steps and returns when the rows are written.
  * Errors: DCB_ERR_CAPACITY (pos + n > capacity), DCB_ERR_TOKEN, as dcb_step. */
 int dcb_prefill(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out);
+/* The same prefill with the LM head on every position: logits [n][vocab]
+ * (host, required) and argmax_out [n] (host, or NULL) of every prompt
+ * position, as the reference's `logits` command writes them
+ * (src/main.cpp:93-114: one step with the head per token, PREFIX.bin rows).
+ * Each chunk of up to 64 positions is copied back as it completes. */
+int dcb_prefill_logits(dcb_engine* e, const int* tokens, int n, float* logits, int* argmax_out);
 
 #ifdef __cplusplus
 }

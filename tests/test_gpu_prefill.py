@@ -85,3 +85,20 @@ def test_prefill_errors(small_int8):
     assert eng.position == 0
     eng.prefill([1, 2, 3])
     assert eng.position == 3
+
+
+@pytest.mark.parametrize("which,n", [("small", 70), ("g64", 33)])
+def test_prefill_logits_every_position(which, n, small_int8, g64_int8):
+    # the reference's `logits` command: one step with the head per prompt
+    # token, every position's logits and argmax (src/main.cpp:93-114)
+    model = {"small": small_int8, "g64": g64_int8}[which]
+    d, _ = synthetic.load_model(model)
+    prompt = synthetic.random_tokens(n, d.vocab, seed=21)
+    eng = dcb.Engine(model, n + 2)
+    logits, best = eng.prefill_logits(prompt)
+    assert logits.shape == (n, d.vocab) and eng.position == n
+    orc = oracle.Oracle(model, n + 2, threads=host_threads())
+    for i, t in enumerate(prompt):
+        exp = orc.step(t, True)
+        np.testing.assert_allclose(logits[i], exp, atol=LOGIT_ATOL)
+        assert best[i] == oracle.argmax(exp)
