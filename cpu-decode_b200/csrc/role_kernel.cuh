@@ -62,6 +62,13 @@ struct RoleParams {
     // complete (the fine poll of every word takes over from there).
     int coarse_down, coarse_o;
     int nbufs;           // resident KV chunk buffers of an attention block
+    // Spread attention (positions beyond the attention blocks' buffers, head
+    // dim 64): FFN block f < NKV * sp_splits is unit (KV group f / sp_splits,
+    // split f % sp_splits), which keeps chunks split, split + sp_splits, ...
+    // (at most sp_bufs) resident at g_ring and publishes (m, l, o) of every
+    // head of its group into ll_part; g_sq holds its queries and scores.
+    int sp_splits, sp_bufs, g_ring, g_sq;
+    uint64_t* ll_part;   // [NH][sp_splits][D+2] tagged split partials
     int chunk_bytes;     // one chunk buffer: [64 K rows | 64 V rows]
     int bulk_kv;         // K/V rows are a multiple of 16 bytes (bulk copies), else plain loads
     const uint8_t* qkv;     // [L][NA][ra_stride][SH] packed rows
@@ -410,6 +417,7 @@ struct RoleCtx {
     AttnRows ar;
     int is_attn, ra, or0, or1;  // attention: QKV rows, W_o rows [or0, or1)
     int f, ga, gn;              // FFN: block index, gate/up pairs [ga, ga + gn)
+    int sp_g, sp_s, sp_n;       // spread unit: KV group, split, resident chunks (0: no unit)
     int n_att, nchunks;         // positions attended, resident chunks
     float qscale;
 };
@@ -643,8 +651,314 @@ __device__ __forceinline__ void ffn_epilogue(const RoleParams& P, const RoleCtx&
     c.sc[t] = hv;
 }
 
+// ---- spread attention (positions beyond the attention blocks' buffers) ----------
+// The 64-position chunks covering positions 0..pos are dealt round robin to
+// the sp_splits units of each KV group: unit (g, s) keeps chunks s, s + sp,
+// s + 2 sp, ... (its buffers 0, 1, 2, ...). Every position sits in exactly
+// one unit, so each cached K/V byte is read from HBM once per layer for all
+// the group's query heads.
+__device__ __forceinline__ int sp_chunks(int nch, int split, int splits) {
+    return split < nch ? (nch - split + splits - 1) / splits : 0;
+}
+// The cached rows (positions below pos) of the unit's chunks of layer l into
+// its buffers (the copy thread only).
+__device__ __forceinline__ void ffn_fill_sp(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+                                           int kv_bytes) {
+    const size_t rb = (size_t)P.D * kv_bytes;
+    const size_t head = (size_t)l * P.NKV + c.sp_g;
+    uint8_t* ring = c.slot0 + (P.g_ring - P.g_gu);
+#pragma unroll 1
+    for (int k = 0; k < c.sp_n; ++k) {
+        const int ch = c.sp_s + k * P.sp_splits;
+        const int t0 = ch * ATT_CHUNK, t1 = min(t0 + ATT_CHUNK, A.pos);
+        if (t1 <= t0) continue;
+        uint8_t* kd = ring + (size_t)k * P.chunk_bytes;
+        const uint32_t bytes = (uint32_t)((t1 - t0) * rb);
+        ++c.fills[MB_RING + k];
+        mbar_expect(c.mb + MB_RING + k, 2 * bytes);
+        bulk_load(kd, static_cast<const uint8_t*>(P.kcache) + (head * P.capacity + t0) * rb, bytes, c.mb + MB_RING + k);
+        bulk_load(kd + (size_t)ATT_CHUNK * rb, static_cast<const uint8_t*>(P.vcache) + (head * P.capacity + t0) * rb,
+                  bytes, c.mb + MB_RING + k);
+    }
+}
+
+// Unit (g, s) of layer l: the group's queries and new K/V row (tagged words of
+// the attention blocks), its resident chunks, then for every query head of
+// the group the reference's attention (src/kernels.cpp:150-179) restricted to
+// the unit's positions: scores q.k (q pre-scaled by log2(e)/sqrt(D)), the
+// unit's maximum m, p = 2^(s - m), their sum l and sum_t p_t V_t, published
+// as (m, l, o) tagged words. Head dim 64: 8 lanes per position, each lane
+// dims 4q..4q+3 and 32+4q..32+4q+3. Returns false when a wait ran out.
+template <typename KV, bool TR>
+__device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+                                          uint32_t tag) {
+    constexpr int D = 64;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hpg = P.NH / P.NKV, g = c.sp_g, SPL = P.sp_splits, np = c.sp_n * ATT_CHUNK;
+    uint8_t* ring = c.slot0 + (P.g_ring - P.g_gu);
+    float* sq = reinterpret_cast<float*>(c.slot0 + (P.g_sq - P.g_gu));  // [GQA_MAX][D] scaled queries
+    float* s_new = sq + GQA_MAX * D;                                      // [2][D] new K, V row
+    float* hml = s_new + 2 * D;                                           // [GQA_MAX][2] max, sum
+    float* wm = hml + 2 * GQA_MAX;                                        // [NW][GQA_MAX] warp maxima
+    float* S = wm + NW * GQA_MAX;                                         // [np][GQA_MAX] scores
+    {
+        const int nq = hpg * D, nwords = nq + 2 * D;
+        for (int i = tid; i < nwords; i += NT) {
+            const uint64_t* src = i < nq ? P.ll_q + (size_t)g * nq + i : P.ll_kv + (size_t)g * 2 * D + (i - nq);
+            uint64_t t0 = 0;
+            unsigned rounds = 0;
+            uint64_t w = ll_load(src);
+            while ((uint32_t)(w >> 32) != tag) {
+                if ((++rounds & 7u) == 0 && wait_expired(c.st, t0)) break;
+                w = ll_load(src);
+            }
+            const float v = __uint_as_float((uint32_t)w);
+            if (i < nq) sq[i] = v * c.qscale;
+            else s_new[i - nq] = v;  // already rounded to KV by its writer
+        }
+    }
+    if (tid == 0) {
+        uint64_t t0 = 0;
+#pragma unroll 1
+        for (int k = 0; k < c.sp_n; ++k) {
+            const int ch = c.sp_s + k * SPL;
+            if (min(ch * ATT_CHUNK + ATT_CHUNK, A.pos) <= ch * ATT_CHUNK) continue;
+            unsigned spins = 0;
+            bool expired = false;
+            while (!mbar_test(c.mb + MB_RING + k, (uint32_t)l & 1u))
+                if ((++spins & 63u) == 0 && wait_expired(c.st, t0)) {
+                    expired = true;
+                    break;
+                }
+            if (expired) break;
+        }
+    }
+    __syncthreads();
+    if (should_abort(c.st)) return false;
+    rdetail<TR>(P, l, 3, 5);
+    // The new row into its chunk buffer, when this unit keeps position pos.
+    const int pch = A.pos / ATT_CHUNK;
+    if (pch % SPL == c.sp_s && tid < 2 * D) {
+        KV* kb = reinterpret_cast<KV*>(ring + (size_t)(pch / SPL) * P.chunk_bytes);
+        kv_store(kb + (tid < D ? 0 : (size_t)ATT_CHUNK * D) + (size_t)(A.pos % ATT_CHUNK) * D + tid % D, s_new[tid]);
+    }
+    __syncthreads();
+    rdetail<TR>(P, l, 2, 3);
+    // Scores: warp w takes local positions 4w + (lane / 8) of each 64-position
+    // pass; lane q of a position's 8 lanes holds dims 4q..4q+3, 32+4q..+3 of
+    // K and forms partial dots for all 8 head slots, then a reduce-scatter
+    // over the 8 lanes (exchanges of 4, 2, 1 values) leaves lane q with the
+    // full score of head q (head slots past hpg are never stored).
+    {
+        const int grp = lane >> 3, pp = lane & 7;
+        float mw = -INFINITY;  // this lane's head pp
+        for (int base = 0; base < np; base += 4 * NW) {
+            const int li = base + warp * 4 + grp;  // local position: buffer li / 64, row li % 64
+            const int t = (c.sp_s + (li >> 6) * SPL) * ATT_CHUNK + (li & 63);
+            const bool valid = li < np && t <= A.pos;
+            float kk[8];
+            if (valid) {
+                const KV* kr = reinterpret_cast<const KV*>(ring + (size_t)(li >> 6) * P.chunk_bytes) + (size_t)(li & 63) * D;
+                float a4[4], b4[4];
+                load4(kr + 4 * pp, a4);
+                load4(kr + 32 + 4 * pp, b4);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    kk[e] = a4[e];
+                    kk[4 + e] = b4[e];
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) kk[e] = 0.f;
+            }
+            float sc[GQA_MAX];
+#pragma unroll
+            for (int h = 0; h < GQA_MAX; ++h) {
+                const float4 qa = *reinterpret_cast<const float4*>(sq + h * D + 4 * pp);
+                const float4 qb = *reinterpret_cast<const float4*>(sq + h * D + 32 + 4 * pp);
+                float x = qa.x * kk[0];
+                x = fmaf(qa.y, kk[1], x);
+                x = fmaf(qa.z, kk[2], x);
+                x = fmaf(qa.w, kk[3], x);
+                x = fmaf(qb.x, kk[4], x);
+                x = fmaf(qb.y, kk[5], x);
+                x = fmaf(qb.z, kk[6], x);
+                sc[h] = fmaf(qb.w, kk[7], x);
+            }
+            // Reduce-scatter over lanes pp ^ 4, ^ 2, ^ 1.
+            const bool u4 = pp & 4, u2 = pp & 2, u1 = pp & 1;
+            float r4[4], r2[2];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float send = u4 ? sc[e] : sc[e + 4];
+                r4[e] = (u4 ? sc[e + 4] : sc[e]) + __shfl_xor_sync(FULL, send, 4);
+            }
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const float send = u2 ? r4[e] : r4[e + 2];
+                r2[e] = (u2 ? r4[e + 2] : r4[e]) + __shfl_xor_sync(FULL, send, 2);
+            }
+            const float total = (u1 ? r2[1] : r2[0]) + __shfl_xor_sync(FULL, u1 ? r2[0] : r2[1], 1);
+            if (valid && pp < hpg) {
+                S[li * GQA_MAX + pp] = total;
+                mw = fmaxf(mw, total);
+            }
+        }
+        mw = fmaxf(mw, __shfl_xor_sync(FULL, mw, 8));
+        mw = fmaxf(mw, __shfl_xor_sync(FULL, mw, 16));
+        if (lane < hpg) wm[warp * GQA_MAX + lane] = mw;
+    }
+    __syncthreads();
+    rdetail<TR>(P, l, 2, 4);
+    // Warp h: the unit's maximum of head h, p = 2^(s - m) in place, their sum.
+    if (warp < hpg) {
+        float m = lane < NW ? wm[lane * GQA_MAX + warp] : -INFINITY;
+        m = warp_max(m);
+        float lsum = 0.f;
+        for (int li = lane; li < np; li += 32) {
+            const int t = (c.sp_s + (li >> 6) * SPL) * ATT_CHUNK + (li & 63);
+            float pv = 0.f;
+            if (t <= A.pos) {
+                pv = ex2_approx(S[li * GQA_MAX + warp] - m);
+                lsum += pv;
+            }
+            S[li * GQA_MAX + warp] = pv;
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) {
+            hml[2 * warp] = m;
+            hml[2 * warp + 1] = lsum;
+        }
+    }
+    __syncthreads();
+    rdetail<TR>(P, l, 2, 5);
+    // P.V: warp w takes local positions w, w + 16, ...; lane the dimension
+    // pair (2 lane, 2 lane + 1) for every head at once (each V pair read once,
+    // the position's probabilities as two broadcast float4). Positions past
+    // pos have p = 0 and rows past pos are skipped.
+    {
+        float2 acc[GQA_MAX];
+#pragma unroll
+        for (int h = 0; h < GQA_MAX; ++h) acc[h] = make_float2(0.f, 0.f);
+#pragma unroll 2
+        for (int li = warp; li < np; li += NW) {
+            const int t = (c.sp_s + (li >> 6) * SPL) * ATT_CHUNK + (li & 63);
+            if (t > A.pos) continue;  // warp-uniform
+            const KV* vr = reinterpret_cast<const KV*>(ring + (size_t)(li >> 6) * P.chunk_bytes) +
+                           (size_t)ATT_CHUNK * D + (size_t)(li & 63) * D;
+            const float2 v = kv_to_float2(vr + 2 * lane);
+            const float4 pa = *reinterpret_cast<const float4*>(S + li * GQA_MAX);
+            const float4 pb = *reinterpret_cast<const float4*>(S + li * GQA_MAX + 4);
+            const float pr[GQA_MAX] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+            for (int h = 0; h < GQA_MAX; ++h) {
+                acc[h].x = fmaf(pr[h], v.x, acc[h].x);
+                acc[h].y = fmaf(pr[h], v.y, acc[h].y);
+            }
+        }
+        __syncthreads();  // every V row is read: buffer 0 takes the warps' shares
+        float* shares = reinterpret_cast<float*>(ring);  // [NW][GQA_MAX][D]
+#pragma unroll
+        for (int h = 0; h < GQA_MAX; ++h)
+            if (h < hpg) *reinterpret_cast<float2*>(shares + ((size_t)warp * GQA_MAX + h) * D + 2 * lane) = acc[h];
+        __syncthreads();
+        if (tid < hpg * D) {
+            const int h = tid >> 6, d = tid & 63;
+            float o = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) o += shares[((size_t)w * GQA_MAX + h) * D + d];
+            uint64_t* pw = P.ll_part + ((size_t)(g * hpg + h) * SPL + c.sp_s) * (D + 2);
+            ll_store(pw + 2 + d, o, tag);
+            if (d == 0) {
+                ll_store(pw, hml[2 * h], tag);
+                ll_store(pw + 1, hml[2 * h + 1], tag);
+            }
+        }
+    }
+    rdetail<TR>(P, l, 2, 6);
+    __syncthreads();  // the chunk buffers are consumed
+    rdetail<TR>(P, l, 2, 7);
+    return true;
+}
+
+// Attention block of head h in spread mode: the (m, l, o) of every unit of
+// its group that holds positions, merged in split order into the head output
+// misc[384 .. 384 + 64): weights 2^(m_s - M), sum_s w_s o_s / sum_s w_s l_s.
+// The partial table and the merge scratch use the (idle) chunk buffers.
+__device__ __forceinline__ bool sp_merge(const RoleParams& P, const StepArgs& A, const RoleCtx& c, uint32_t tag) {
+    constexpr int D = 64, W = D + 2;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int SPL = P.sp_splits, nch = (A.pos + ATT_CHUNK) / ATT_CHUNK, ns = min(nch, SPL);
+    float* table = reinterpret_cast<float*>(c.ring);  // [ns][W]
+    float* wgt = table + SPL * W;                      // [ns]
+    float* share = wgt + SPL;                          // [8][D + 1]
+    const uint64_t* src = P.ll_part + (size_t)c.ar.h * SPL * W;
+    {
+        constexpr int WT = 8;
+        const int nwords = ns * W;
+        for (int base = 0; base < nwords; base += WT * NT) {
+            uint64_t w[WT];
+            unsigned pending = 0;
+#pragma unroll
+            for (int k = 0; k < WT; ++k) {
+                const int i = base + tid + k * NT;
+                if (i < nwords) {
+                    w[k] = ll_load(src + i);
+                    pending |= 1u << k;
+                }
+            }
+            uint64_t t0 = 0;
+            unsigned rounds = 0;
+            while (true) {
+#pragma unroll
+                for (int k = 0; k < WT; ++k)
+                    if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
+                        table[base + tid + k * NT] = __uint_as_float((uint32_t)w[k]);
+                        pending &= ~(1u << k);
+                    }
+                if (!pending) break;
+                if ((++rounds & 7u) == 0 && wait_expired(c.st, t0)) break;
+#pragma unroll
+                for (int k = 0; k < WT; ++k)
+                    if ((pending >> k) & 1u) w[k] = ll_load(src + base + tid + k * NT);
+            }
+        }
+    }
+    __syncthreads();
+    if (should_abort(c.st)) return false;
+    if (warp == 0) {
+        float mx = -INFINITY;
+        for (int i = lane; i < ns; i += 32) mx = fmaxf(mx, table[i * W]);
+        mx = warp_max(mx);
+        for (int i = lane; i < ns; i += 32) wgt[i] = ex2_approx(table[i * W] - mx);
+    }
+    __syncthreads();
+    {
+        const int d = tid & 63, q = tid >> 6;  // q < 8
+        float num = 0.f, den = 0.f;
+        for (int i = q; i < ns; i += 8) {
+            num = fmaf(wgt[i], table[i * W + 2 + d], num);
+            if (d == 0) den = fmaf(wgt[i], table[i * W + 1], den);
+        }
+        share[q * (D + 1) + d] = num;
+        if (d == 0) share[q * (D + 1) + D] = den;
+    }
+    __syncthreads();
+    if (tid < D) {
+        float num = 0.f, den = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            num += share[q * (D + 1) + tid];
+            den += share[q * (D + 1) + D];
+        }
+        c.misc[384 + tid] = num / den;
+    }
+    __syncthreads();
+    return true;
+}
+
 // ---- one layer of each role ----
-template <typename KV, int MD, bool TR>
+template <typename KV, int MD, bool TR, bool SP>
 __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l, int token,
                                         const float (&rs)[SLICE_RPT]) {
     const int tid = threadIdx.x, ph = 5 * l;
@@ -669,14 +983,22 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
     }
     rtrace<TR>(P, 1, ph + 1);
     rdetail<TR>(P, l, 1, 0);
-    if (!attn_gather<KV>(P, A, c, l, tag)) return false;
-    rtrace<TR>(P, 0, ph + 2);
-    rdetail<TR>(P, l, 1, 1);
-    attend_resident<KV, MD>(c.ring, P.chunk_bytes, P.D, c.n_att, c.misc, c.sc, c.part, c.red, c.misc + 384);
-    rdetail<TR>(P, l, 1, 2);
-    if (tid == COPY_T && P.bulk_kv && l + 1 < P.L) {
-        fence_proxy_async();
-        attn_fill_ring(P, A, c, l + 1, (int)sizeof(KV));
+    if (SP) {
+        // The FFN blocks attend; this block merges its head's partials.
+        rtrace<TR>(P, 0, ph + 2);
+        rdetail<TR>(P, l, 1, 1);
+        if (!sp_merge(P, A, c, tag)) return false;
+        rdetail<TR>(P, l, 1, 2);
+    } else {
+        if (!attn_gather<KV>(P, A, c, l, tag)) return false;
+        rtrace<TR>(P, 0, ph + 2);
+        rdetail<TR>(P, l, 1, 1);
+        attend_resident<KV, MD>(c.ring, P.chunk_bytes, P.D, c.n_att, c.misc, c.sc, c.part, c.red, c.misc + 384);
+        rdetail<TR>(P, l, 1, 2);
+        if (tid == COPY_T && P.bulk_kv && l + 1 < P.L) {
+            fence_proxy_async();
+            attn_fill_ring(P, A, c, l + 1, (int)sizeof(KV));
+        }
     }
     rtrace<TR>(P, 1, ph + 2);
     rtrace<TR>(P, 0, ph + 3);
@@ -693,10 +1015,21 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
     return true;
 }
 
-template <bool TR>
-__device__ __forceinline__ bool ffn_layer(const RoleParams& P, const RoleCtx& c, int l, const float (&rs)[SLICE_RPT]) {
+template <typename KV, bool TR, bool SP>
+__device__ __forceinline__ bool ffn_layer(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+                                       const float (&rs)[SLICE_RPT]) {
     const int tid = threadIdx.x, ph = 5 * l;
     const float* post_norm = P.norms + (size_t)l * 2 * P.Kh + P.Kh;
+    if (SP && c.sp_n) {
+        // This block's attention unit first: the attention blocks wait for it.
+        rdetail<TR>(P, l, 3, 6);
+        if (!sp_partial<KV, TR>(P, A, c, l, (A.seq << 8) | (uint32_t)(l + 1))) return false;
+        rdetail<TR>(P, l, 3, 7);
+        if (tid == COPY_T && l + 1 < P.L) {
+            fence_proxy_async();
+            ffn_fill_sp(P, A, c, l + 1, (int)sizeof(KV));
+        }
+    }
     rtrace<TR>(P, 0, ph + 4);
     rdetail<TR>(P, l, 3, 0);
     const float wsc = role_stage(P, c, role_osum(P, c, l), P.NH, P.coarse_o, post_norm);
@@ -877,7 +1210,7 @@ __device__ __forceinline__ void role_finish(const RoleParams& P, const StepArgs&
 
 // MD: 32-dim groups of the head dimension a lane covers in the attention
 // scores (1: D <= 32, 2: D <= 64, 4: D <= 128).
-template <typename KV, int MD, bool TR>
+template <typename KV, int MD, bool TR, bool SP>
 __global__ void __launch_bounds__(NT, 1)
     role_step_kernel(const __grid_constant__ RoleParams P, const __grid_constant__ StepArgs A) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -927,6 +1260,12 @@ __global__ void __launch_bounds__(NT, 1)
             c.gn = part_lo(c.f + 1, P.NG, P.I) - c.ga;
             c.ra = c.or0 = c.or1 = 0;
         }
+        c.sp_g = c.sp_s = c.sp_n = 0;
+        if (SP && !is_attn && c.f < P.NKV * P.sp_splits) {
+            c.sp_g = c.f / P.sp_splits;
+            c.sp_s = c.f % P.sp_splits;
+            c.sp_n = sp_chunks(c.nchunks, c.sp_s, P.sp_splits);
+        }
     }
     if (tid == COPY_T) {
         s_abort = 0;
@@ -941,10 +1280,11 @@ __global__ void __launch_bounds__(NT, 1)
         if (is_attn) {
             attn_fill_qkv(P, c, 0);
             attn_fill_o(P, c, 0);
-            if (P.bulk_kv) attn_fill_ring(P, A, c, 0, (int)sizeof(KV));
+            if (P.bulk_kv && !SP) attn_fill_ring(P, A, c, 0, (int)sizeof(KV));
         } else if (c.gn) {
             ffn_fill_gu(P, c, 0);
             ffn_fill_down(P, c, 0);
+            if (SP && c.sp_n) ffn_fill_sp(P, A, c, 0, (int)sizeof(KV));
         }
     }
     if (is_attn) {
@@ -978,7 +1318,7 @@ __global__ void __launch_bounds__(NT, 1)
                         ? __ldg((is_attn ? P.o_scale : P.down_scale) + (size_t)l * H + r)
                         : 0.f;
         }
-        ok = is_attn ? attn_layer<KV, MD, TR>(P, A, c, l, token, rs) : ffn_layer<TR>(P, c, l, rs);
+        ok = is_attn ? attn_layer<KV, MD, TR, SP>(P, A, c, l, token, rs) : ffn_layer<KV, TR, SP>(P, A, c, l, rs);
         if (!ok) break;
     }
     if (ok && A.head) ok = role_lm_head<TR>(P, A, c);

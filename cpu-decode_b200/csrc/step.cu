@@ -84,6 +84,11 @@ struct dcb_engine {
     void* role_kernel = nullptr;
     void* role_kernel_traced = nullptr;
     int role_smem = 0, role_max_pos = 0;
+    // Its spread mode (the FFN blocks attend) for positions beyond the
+    // attention blocks' buffers, up to role_sp_max_pos (0: not available).
+    void* role_kernel_sp = nullptr;
+    void* role_kernel_sp_traced = nullptr;
+    int role_sp_max_pos = 0;
     // The LM head as its own kernel after a two-role step (head_kernel.cuh),
     // chained by programmatic dependent launch; 2 blocks per SM.
     HeadParams HP{};
@@ -198,10 +203,15 @@ void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len, 
     *nsplit = ceil_div(length, *split_len);
 }
 
-// The two-role kernel takes the step when it is set up, one GPU keeps the
-// whole sequence and every attended position fits in its resident buffers.
-bool use_role(const dcb_engine* e) {
-    return e->role_ok && e->role_on && e->P.world == 1 && e->kv_base == 0 && e->pos + 1 <= (size_t)e->role_max_pos;
+// The two-role kernel takes the step when it is set up and one GPU keeps the
+// whole sequence: 1 when every attended position fits in the attention
+// blocks' resident buffers, 2 (spread mode) when it fits in the FFN blocks'
+// units, else 0.
+int use_role(const dcb_engine* e) {
+    if (!e->role_ok || !e->role_on || e->P.world != 1 || e->kv_base != 0) return 0;
+    if (e->pos + 1 <= (size_t)e->role_max_pos) return 1;
+    if (e->pos + 1 <= (size_t)e->role_sp_max_pos) return 2;
+    return 0;
 }
 
 int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax_dev, float* host_logits = nullptr) {
@@ -217,12 +227,14 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
     A.seq = e->seq;
     A.par = e->par;
     e->par ^= 1;
-    if (use_role(e)) {
+    if (const int mode = use_role(e)) {
         const bool sep = head && e->head_sep;
         A.head_follows = sep ? 1 : 0;
         if (sep) A.head = 0;
         void* args[] = {(void*)&e->R, (void*)&A};
-        DCB_CUDA(cudaLaunchCooperativeKernel(e->R.trace ? e->role_kernel_traced : e->role_kernel, dim3(e->grid), dim3(NT), args, (size_t)e->role_smem,
+        void* k = mode == 2 ? (e->R.trace ? e->role_kernel_sp_traced : e->role_kernel_sp)
+                            : (e->R.trace ? e->role_kernel_traced : e->role_kernel);
+        DCB_CUDA(cudaLaunchCooperativeKernel(k, dim3(e->grid), dim3(NT), args, (size_t)e->role_smem,
                                              e->stream));
         ++e->launches;
         if (sep) {
@@ -351,17 +363,28 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     // Each (KV type, head size) has a plain and a traced instantiation.
     void* kt[2];
     for (int tr = 0; tr < 2; ++tr)
-        kt[tr] = D <= 32 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 1, true> : (void*)role_step_kernel<__half, 1, false>)
-                                : (tr ? (void*)role_step_kernel<float, 1, true> : (void*)role_step_kernel<float, 1, false>))
-                 : D <= 64 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 2, true> : (void*)role_step_kernel<__half, 2, false>)
-                                  : (tr ? (void*)role_step_kernel<float, 2, true> : (void*)role_step_kernel<float, 2, false>))
-                           : (f16 ? (tr ? (void*)role_step_kernel<__half, 4, true> : (void*)role_step_kernel<__half, 4, false>)
-                                  : (tr ? (void*)role_step_kernel<float, 4, true> : (void*)role_step_kernel<float, 4, false>));
+        kt[tr] = D <= 32 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 1, true, false> : (void*)role_step_kernel<__half, 1, false, false>)
+                                : (tr ? (void*)role_step_kernel<float, 1, true, false> : (void*)role_step_kernel<float, 1, false, false>))
+                 : D <= 64 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 2, true, false> : (void*)role_step_kernel<__half, 2, false, false>)
+                                  : (tr ? (void*)role_step_kernel<float, 2, true, false> : (void*)role_step_kernel<float, 2, false, false>))
+                           : (f16 ? (tr ? (void*)role_step_kernel<__half, 4, true, false> : (void*)role_step_kernel<__half, 4, false, false>)
+                                  : (tr ? (void*)role_step_kernel<float, 4, true, false> : (void*)role_step_kernel<float, 4, false, false>));
+    // Spread mode (the FFN blocks attend beyond the resident buffers): head
+    // dim 64, at most GQA_MAX query heads per KV group, every FFN block with
+    // gate/up rows, rows that bulk-copy.
+    const int sp_splits = R.NG / NKV;
+    const bool sp_ok = D == 64 && hpg <= GQA_MAX && sp_splits >= 1 && I >= R.NG && R.bulk_kv;
+    void* ks[2] = {nullptr, nullptr};
+    if (sp_ok) {
+        ks[0] = f16 ? (void*)role_step_kernel<__half, 2, false, true> : (void*)role_step_kernel<float, 2, false, true>;
+        ks[1] = f16 ? (void*)role_step_kernel<__half, 2, true, true> : (void*)role_step_kernel<float, 2, true, true>;
+    }
     void* k = kt[0];
     if (cudaFuncGetAttributes(&fattr, k) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
-    {
+    for (void* kk : {kt[1], ks[0], ks[1]}) {
+        if (!kk) continue;
         cudaFuncAttributes ft;
-        if (cudaFuncGetAttributes(&ft, kt[1]) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
+        if (cudaFuncGetAttributes(&ft, kk) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
         fattr.sharedSizeBytes = std::max(fattr.sharedSizeBytes, ft.sharedSizeBytes);
     }
     const size_t budget = (size_t)max_optin - fattr.sharedSizeBytes;
@@ -398,15 +421,35 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     if (attn_fixed >= budget || ffn_end > budget) return 0;
     R.nbufs = (int)std::min<size_t>(RES_BUFS_MAX, (budget - attn_fixed) / R.chunk_bytes);
     if (R.nbufs < 1) return 0;
-    const size_t smem = std::max(attn_fixed + (size_t)R.nbufs * R.chunk_bytes, ffn_end);
-    for (void* kk : kt)
-        if (cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    // Spread units: their chunk buffers, then queries, new row, maxima, sums
+    // and the score tile ([GQA_MAX][sp_bufs * 64]), as many buffers as fit.
+    R.sp_splits = sp_splits;
+    R.sp_bufs = 0;
+    R.g_ring = (int)ffn_end;
+    size_t ffn_sp_end = ffn_end;
+    if (sp_ok) {
+        for (int nb = RES_BUFS_MAX; nb >= 1; --nb) {
+            const size_t ring_end = ffn_end + (size_t)nb * R.chunk_bytes;
+            const size_t sq = ((size_t)GQA_MAX * D + 2 * D + 2 * GQA_MAX + NW * GQA_MAX + (size_t)GQA_MAX * nb * ATT_CHUNK) * 4;
+            // The buffers also take the P.V shares of every warp ([NW][GQA_MAX][D] floats).
+            if (ring_end + sq <= budget && (size_t)nb * R.chunk_bytes >= (size_t)NW * GQA_MAX * D * 4) {
+                R.sp_bufs = nb;
+                R.g_sq = (int)ring_end;
+                ffn_sp_end = ring_end + sq;
+                break;
+            }
+        }
+    }
+    R.ll_part = P.ll_part;
+    const size_t smem = std::max({attn_fixed + (size_t)R.nbufs * R.chunk_bytes, ffn_end, ffn_sp_end});
+    for (void* kk : {kt[0], kt[1], ks[0], ks[1]})
+        if (kk && cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
             cudaGetLastError();
             return 0;
         }
     int per_sm = 0;
-    for (void* kk : kt)
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kk, NT, smem) != cudaSuccess || per_sm < 1) {
+    for (void* kk : {kt[0], kt[1], ks[0], ks[1]})
+        if (kk && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kk, NT, smem) != cudaSuccess || per_sm < 1)) {
             cudaGetLastError();
             return 0;
         }
@@ -486,6 +529,13 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     }
     e->role_kernel = kt[0];
     e->role_kernel_traced = kt[1];
+    if (sp_ok && R.sp_bufs > 0) {
+        e->role_kernel_sp = ks[0];
+        e->role_kernel_sp_traced = ks[1];
+        e->role_sp_max_pos = R.sp_splits * R.sp_bufs * ATT_CHUNK;
+        if (const char* v = std::getenv("DCB_ROLE_SPREAD"))
+            if (!std::atoi(v)) e->role_sp_max_pos = 0;
+    }
     e->role_smem = (int)smem;
     e->role_max_pos = R.nbufs * ATT_CHUNK;
     e->role_ok = true;
