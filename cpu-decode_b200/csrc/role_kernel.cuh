@@ -63,11 +63,13 @@ struct RoleParams {
     int coarse_down, coarse_o;
     int nbufs;           // resident KV chunk buffers of an attention block
     // Spread attention (positions beyond the attention blocks' buffers, head
-    // dim 64): FFN block f < NKV * sp_splits is unit (KV group f / sp_splits,
-    // split f % sp_splits), which keeps chunks split, split + sp_splits, ...
-    // (at most sp_bufs) resident at g_ring and publishes (m, l, o) of every
-    // head of its group into ll_part; g_sq holds its queries and scores.
-    int sp_splits, sp_bufs, g_ring, g_sq;
+    // dim 64): block b < NKV * sp_splits is unit (KV group b / sp_splits,
+    // split b % sp_splits), which keeps chunks split, split + sp_splits, ...
+    // (at most sp_bufs) resident and publishes (m, l, o) of every head of its
+    // group into ll_part. FFN blocks keep them at g_ring (queries and scores
+    // at g_sq), attention blocks in their chunk buffers (scratch after
+    // sp_bufs of them, at a_ring + a_sq).
+    int sp_splits, sp_bufs, g_ring, g_sq, a_sq;
     uint64_t* ll_part;   // [NH][sp_splits][D+2] tagged split partials
     int chunk_bytes;     // one chunk buffer: [64 K rows | 64 V rows]
     int bulk_kv;         // K/V rows are a multiple of 16 bytes (bulk copies), else plain loads
@@ -418,6 +420,8 @@ struct RoleCtx {
     int is_attn, ra, or0, or1;  // attention: QKV rows, W_o rows [or0, or1)
     int f, ga, gn;              // FFN: block index, gate/up pairs [ga, ga + gn)
     int sp_g, sp_s, sp_n;       // spread unit: KV group, split, resident chunks (0: no unit)
+    uint8_t* sp_ring;           // its chunk buffers
+    float* sp_sq;               // its queries, new row, maxima, sums and score tile
     int n_att, nchunks;         // positions attended, resident chunks
     float qscale;
 };
@@ -662,11 +666,11 @@ __device__ __forceinline__ int sp_chunks(int nch, int split, int splits) {
 }
 // The cached rows (positions below pos) of the unit's chunks of layer l into
 // its buffers (the copy thread only).
-__device__ __forceinline__ void ffn_fill_sp(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
-                                           int kv_bytes) {
+__device__ __forceinline__ void sp_fill(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+                                       int kv_bytes) {
     const size_t rb = (size_t)P.D * kv_bytes;
     const size_t head = (size_t)l * P.NKV + c.sp_g;
-    uint8_t* ring = c.slot0 + (P.g_ring - P.g_gu);
+    uint8_t* ring = c.sp_ring;
 #pragma unroll 1
     for (int k = 0; k < c.sp_n; ++k) {
         const int ch = c.sp_s + k * P.sp_splits;
@@ -695,8 +699,8 @@ __device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& 
     constexpr int D = 64;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hpg = P.NH / P.NKV, g = c.sp_g, SPL = P.sp_splits, np = c.sp_n * ATT_CHUNK;
-    uint8_t* ring = c.slot0 + (P.g_ring - P.g_gu);
-    float* sq = reinterpret_cast<float*>(c.slot0 + (P.g_sq - P.g_gu));  // [GQA_MAX][D] scaled queries
+    uint8_t* ring = c.sp_ring;
+    float* sq = c.sp_sq;                                                  // [GQA_MAX][D] scaled queries
     float* s_new = sq + GQA_MAX * D;                                      // [2][D] new K, V row
     float* hml = s_new + 2 * D;                                           // [GQA_MAX][2] max, sum
     float* wm = hml + 2 * GQA_MAX;                                        // [NW][GQA_MAX] warp maxima
@@ -984,11 +988,18 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
     rtrace<TR>(P, 1, ph + 1);
     rdetail<TR>(P, l, 1, 0);
     if (SP) {
-        // The FFN blocks attend; this block merges its head's partials.
+        // Every block attends as a unit; this block then merges its head's
+        // partials (its buffers are free once its unit is done) and only then
+        // refills them for the next layer.
         rtrace<TR>(P, 0, ph + 2);
+        if (c.sp_n && !sp_partial<KV, TR>(P, A, c, l, tag)) return false;
         rdetail<TR>(P, l, 1, 1);
         if (!sp_merge(P, A, c, tag)) return false;
         rdetail<TR>(P, l, 1, 2);
+        if (tid == COPY_T && c.sp_n && l + 1 < P.L) {
+            fence_proxy_async();
+            sp_fill(P, A, c, l + 1, (int)sizeof(KV));
+        }
     } else {
         if (!attn_gather<KV>(P, A, c, l, tag)) return false;
         rtrace<TR>(P, 0, ph + 2);
@@ -1027,7 +1038,7 @@ __device__ __forceinline__ bool ffn_layer(const RoleParams& P, const StepArgs& A
         rdetail<TR>(P, l, 3, 7);
         if (tid == COPY_T && l + 1 < P.L) {
             fence_proxy_async();
-            ffn_fill_sp(P, A, c, l + 1, (int)sizeof(KV));
+            sp_fill(P, A, c, l + 1, (int)sizeof(KV));
         }
     }
     rtrace<TR>(P, 0, ph + 4);
@@ -1261,9 +1272,11 @@ __global__ void __launch_bounds__(NT, 1)
             c.ra = c.or0 = c.or1 = 0;
         }
         c.sp_g = c.sp_s = c.sp_n = 0;
-        if (SP && !is_attn && c.f < P.NKV * P.sp_splits) {
-            c.sp_g = c.f / P.sp_splits;
-            c.sp_s = c.f % P.sp_splits;
+        c.sp_ring = is_attn ? c.ring : sm + P.g_ring;
+        c.sp_sq = reinterpret_cast<float*>(is_attn ? c.ring + P.a_sq : sm + P.g_sq);
+        if (SP && b < P.NKV * P.sp_splits) {
+            c.sp_g = b / P.sp_splits;
+            c.sp_s = b % P.sp_splits;
             c.sp_n = sp_chunks(c.nchunks, c.sp_s, P.sp_splits);
         }
     }
@@ -1281,10 +1294,11 @@ __global__ void __launch_bounds__(NT, 1)
             attn_fill_qkv(P, c, 0);
             attn_fill_o(P, c, 0);
             if (P.bulk_kv && !SP) attn_fill_ring(P, A, c, 0, (int)sizeof(KV));
+            if (SP && c.sp_n) sp_fill(P, A, c, 0, (int)sizeof(KV));
         } else if (c.gn) {
             ffn_fill_gu(P, c, 0);
             ffn_fill_down(P, c, 0);
-            if (SP && c.sp_n) ffn_fill_sp(P, A, c, 0, (int)sizeof(KV));
+            if (SP && c.sp_n) sp_fill(P, A, c, 0, (int)sizeof(KV));
         }
     }
     if (is_attn) {

@@ -372,7 +372,7 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     // Spread mode (the FFN blocks attend beyond the resident buffers): head
     // dim 64, at most GQA_MAX query heads per KV group, every FFN block with
     // gate/up rows, rows that bulk-copy.
-    const int sp_splits = R.NG / NKV;
+    const int sp_splits = G / NKV;  // every block is a unit
     const bool sp_ok = D == 64 && hpg <= GQA_MAX && sp_splits >= 1 && I >= R.NG && R.bulk_kv;
     void* ks[2] = {nullptr, nullptr};
     if (sp_ok) {
@@ -439,6 +439,13 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
                 break;
             }
         }
+    }
+    // Attention blocks keep a unit's scratch after sp_bufs of their chunk buffers.
+    if (R.sp_bufs > 0) {
+        const size_t sq = ((size_t)GQA_MAX * D + 2 * D + 2 * GQA_MAX + NW * GQA_MAX +
+                           (size_t)GQA_MAX * R.sp_bufs * ATT_CHUNK) * 4;
+        R.a_sq = R.sp_bufs * R.chunk_bytes;
+        if ((size_t)R.a_sq + sq > (size_t)R.nbufs * R.chunk_bytes) R.sp_bufs = 0;
     }
     R.ll_part = P.ll_part;
     const size_t smem = std::max({attn_fixed + (size_t)R.nbufs * R.chunk_bytes, ffn_end, ffn_sp_end});
