@@ -420,8 +420,6 @@ struct RoleCtx {
     int is_attn, ra, or0, or1;  // attention: QKV rows, W_o rows [or0, or1)
     int f, ga, gn;              // FFN: block index, gate/up pairs [ga, ga + gn)
     int sp_g, sp_s, sp_n;       // spread unit: KV group, split, resident chunks (0: no unit)
-    uint8_t* sp_ring;           // its chunk buffers
-    float* sp_sq;               // its queries, new row, maxima, sums and score tile
     int n_att, nchunks;         // positions attended, resident chunks
     float qscale;
 };
@@ -664,43 +662,58 @@ __device__ __forceinline__ void ffn_epilogue(const RoleParams& P, const RoleCtx&
 __device__ __forceinline__ int sp_chunks(int nch, int split, int splits) {
     return split < nch ? (nch - split + splits - 1) / splits : 0;
 }
-// The cached rows (positions below pos) of the unit's chunks of layer l into
-// its buffers (the copy thread only).
-__device__ __forceinline__ void sp_fill(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
-                                       int kv_bytes) {
+// A unit's chunk buffers and scratch (queries, new row, maxima, sums, scores).
+__device__ __forceinline__ uint8_t* sp_ring(const RoleParams& P, const RoleCtx& c) {
+    return c.is_attn ? c.ring : c.slot0 + (P.g_ring - P.g_gu);
+}
+__device__ __forceinline__ float* sp_scratch(const RoleParams& P, const RoleCtx& c) {
+    return reinterpret_cast<float*>(c.is_attn ? c.ring + P.a_sq : c.slot0 + (P.g_sq - P.g_gu));
+}
+// The cached rows (positions below pos) of the unit's k-th chunk of layer l
+// into buffer k % sp_bufs (the copy thread only; a chunk whose rows are all
+// past the cache, i.e. the one starting at pos, needs no copy).
+__device__ __forceinline__ bool sp_chunk_cached(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int k) {
+    const int t0 = (c.sp_s + k * P.sp_splits) * ATT_CHUNK;
+    return min(t0 + ATT_CHUNK, A.pos) > t0;
+}
+__device__ __forceinline__ void sp_fill_chunk(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l, int k,
+                                              int kv_bytes) {
+    if (!sp_chunk_cached(P, A, c, k)) return;
     const size_t rb = (size_t)P.D * kv_bytes;
     const size_t head = (size_t)l * P.NKV + c.sp_g;
-    uint8_t* ring = c.sp_ring;
+    const int b = k % P.sp_bufs;
+    const int t0 = (c.sp_s + k * P.sp_splits) * ATT_CHUNK, t1 = min(t0 + ATT_CHUNK, A.pos);
+    uint8_t* kd = sp_ring(P, c) + (size_t)b * P.chunk_bytes;
+    const uint32_t bytes = (uint32_t)((t1 - t0) * rb);
+    ++c.fills[MB_RING + b];
+    mbar_expect(c.mb + MB_RING + b, 2 * bytes);
+    bulk_load(kd, static_cast<const uint8_t*>(P.kcache) + (head * P.capacity + t0) * rb, bytes, c.mb + MB_RING + b);
+    bulk_load(kd + (size_t)ATT_CHUNK * rb, static_cast<const uint8_t*>(P.vcache) + (head * P.capacity + t0) * rb,
+              bytes, c.mb + MB_RING + b);
+}
+// The first chunks of layer l, one per buffer (the copy thread only).
+__device__ __forceinline__ void sp_fill(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+                                       int kv_bytes) {
 #pragma unroll 1
-    for (int k = 0; k < c.sp_n; ++k) {
-        const int ch = c.sp_s + k * P.sp_splits;
-        const int t0 = ch * ATT_CHUNK, t1 = min(t0 + ATT_CHUNK, A.pos);
-        if (t1 <= t0) continue;
-        uint8_t* kd = ring + (size_t)k * P.chunk_bytes;
-        const uint32_t bytes = (uint32_t)((t1 - t0) * rb);
-        ++c.fills[MB_RING + k];
-        mbar_expect(c.mb + MB_RING + k, 2 * bytes);
-        bulk_load(kd, static_cast<const uint8_t*>(P.kcache) + (head * P.capacity + t0) * rb, bytes, c.mb + MB_RING + k);
-        bulk_load(kd + (size_t)ATT_CHUNK * rb, static_cast<const uint8_t*>(P.vcache) + (head * P.capacity + t0) * rb,
-                  bytes, c.mb + MB_RING + k);
-    }
+    for (int k = 0; k < min(c.sp_n, P.sp_bufs); ++k) sp_fill_chunk(P, A, c, l, k, kv_bytes);
 }
 
-// Unit (g, s) of layer l: the group's queries and new K/V row (tagged words of
-// the attention blocks), its resident chunks, then for every query head of
-// the group the reference's attention (src/kernels.cpp:150-179) restricted to
-// the unit's positions: scores q.k (q pre-scaled by log2(e)/sqrt(D)), the
-// unit's maximum m, p = 2^(s - m), their sum l and sum_t p_t V_t, published
-// as (m, l, o) tagged words. Head dim 64: 8 lanes per position, each lane
-// dims 4q..4q+3 and 32+4q..32+4q+3. Returns false when a wait ran out.
+// Unit (g, s) of layer l when all its chunks are resident (at most sp_bufs):
+// the group's queries and new K/V row (tagged words of the attention blocks),
+// its chunks, then for every query head of the group the reference's
+// attention (src/kernels.cpp:150-179) restricted to the unit's positions in one
+// pass: scores q.k (q pre-scaled by log2(e)/sqrt(D)), the unit's maximum m,
+// p = 2^(s - m), their sum l and sum_t p_t V_t, published as (m, l, o) tagged
+// words. Scores by a reduce-scatter over 8 lanes per position, P.V by warp
+// per position; head dim 64. Returns false when a wait ran out.
 template <typename KV, bool TR>
-__device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+__device__ __forceinline__ bool sp_partial_resident(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
                                           uint32_t tag) {
     constexpr int D = 64;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hpg = P.NH / P.NKV, g = c.sp_g, SPL = P.sp_splits, np = c.sp_n * ATT_CHUNK;
-    uint8_t* ring = c.sp_ring;
-    float* sq = c.sp_sq;                                                  // [GQA_MAX][D] scaled queries
+    uint8_t* ring = sp_ring(P, c);
+    float* sq = sp_scratch(P, c);                                                  // [GQA_MAX][D] scaled queries
     float* s_new = sq + GQA_MAX * D;                                      // [2][D] new K, V row
     float* hml = s_new + 2 * D;                                           // [GQA_MAX][2] max, sum
     float* wm = hml + 2 * GQA_MAX;                                        // [NW][GQA_MAX] warp maxima
@@ -885,6 +898,218 @@ __device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& 
     return true;
 }
 
+// Unit (g, s) of layer l: the group's queries and new K/V row (tagged words of
+// the attention blocks), then its chunks one at a time through its buffers
+// (chunk k in buffer k % sp_bufs; the copy thread refills a buffer with chunk
+// k + sp_bufs once chunk k is consumed), and for every query head of the
+// group the reference's attention (src/kernels.cpp:150-179) restricted to the
+// unit's positions, as an online softmax: scores q.k (q pre-scaled by
+// log2(e)/sqrt(D)), the running maximum m, p = 2^(s - m), the running sum l and
+// sum_t p_t V_t, rescaled by 2^(m_old - m_new) when m grows; published as
+// (m, l, o) tagged words. Head dim 64. c.fills[ROLE_NMB + b]: the fills of
+// buffer b thread 0 has waited for (their phase parity), kept across layers.
+// Returns false when a wait ran out.
+template <typename KV, bool TR>
+__device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+                                          uint32_t tag) {
+    unsigned* waited = c.fills + ROLE_NMB;
+    constexpr int D = 64;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hpg = P.NH / P.NKV, g = c.sp_g, SPL = P.sp_splits;
+    uint8_t* ring = sp_ring(P, c);
+    float* sq = sp_scratch(P, c);                  // [GQA_MAX][D] scaled queries
+    float* s_new = sq + GQA_MAX * D;      // [2][D] new K, V row
+    float* hml = s_new + 2 * D;           // [GQA_MAX][2] running max, sum
+    float* wm = hml + 2 * GQA_MAX;        // [NW][GQA_MAX] warp maxima of a chunk
+    float* S = wm + NW * GQA_MAX;         // [64][GQA_MAX] a chunk's scores, then p
+    float* alpha = S + ATT_CHUNK * GQA_MAX;  // [GQA_MAX] rescale of the running sums
+    {
+        const int nq = hpg * D, nwords = nq + 2 * D;
+        for (int i = tid; i < nwords; i += NT) {
+            const uint64_t* src = i < nq ? P.ll_q + (size_t)g * nq + i : P.ll_kv + (size_t)g * 2 * D + (i - nq);
+            uint64_t t0 = 0;
+            unsigned rounds = 0;
+            uint64_t w = ll_load(src);
+            while ((uint32_t)(w >> 32) != tag) {
+                if ((++rounds & 7u) == 0 && wait_expired(c.st, t0)) break;
+                w = ll_load(src);
+            }
+            const float v = __uint_as_float((uint32_t)w);
+            if (i < nq) sq[i] = v * c.qscale;
+            else s_new[i - nq] = v;  // already rounded to KV by its writer
+        }
+        if (tid < GQA_MAX) {
+            hml[2 * tid] = -INFINITY;
+            hml[2 * tid + 1] = 0.f;
+        }
+    }
+    rdetail<TR>(P, l, 3, 5);
+    const int grp = lane >> 3, pp = lane & 7;
+    float2 acc[GQA_MAX];  // P.V: warp w's positions, lane's dimension pair, every head
+#pragma unroll
+    for (int h = 0; h < GQA_MAX; ++h) acc[h] = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int k = 0; k < c.sp_n; ++k) {
+        const int b = k % P.sp_bufs;
+        const int t0 = (c.sp_s + k * SPL) * ATT_CHUNK, nr = min(ATT_CHUNK, A.pos + 1 - t0);
+        uint8_t* buf = ring + (size_t)b * P.chunk_bytes;
+        if (tid == 0 && sp_chunk_cached(P, A, c, k)) {
+            uint64_t w0 = 0;
+            unsigned spins = 0;
+            while (!mbar_test(c.mb + MB_RING + b, waited[b] & 1u))
+                if ((++spins & 63u) == 0 && wait_expired(c.st, w0)) break;
+            ++waited[b];
+        }
+        __syncthreads();  // the chunk has arrived; the queries are staged
+        if (should_abort(c.st)) return false;
+        if (A.pos - t0 < ATT_CHUNK) {  // block-uniform: this chunk holds position pos
+            // The new row from the tagged words.
+            if (tid < 2 * D) {
+                KV* kb = reinterpret_cast<KV*>(buf);
+                kv_store(kb + (tid < D ? 0 : (size_t)ATT_CHUNK * D) + (size_t)(A.pos - t0) * D + tid % D, s_new[tid]);
+            }
+            __syncthreads();
+        }
+        // Scores: warp w takes rows 4w + (lane / 8); lane q of a row's 8 lanes
+        // holds dims 4q..4q+3, 32+4q..+3 of K and forms partial dots for all 8
+        // head slots, then a reduce-scatter over the 8 lanes (exchanges of 4,
+        // 2, 1 values) leaves lane q with the full score of head q.
+        {
+            float mw = -INFINITY;  // this lane's head pp
+            const int r = warp * 4 + grp;
+            const bool valid = r < nr;
+            float kk[8];
+            if (valid) {
+                const KV* kr = reinterpret_cast<const KV*>(buf) + (size_t)r * D;
+                float a4[4], b4[4];
+                load4(kr + 4 * pp, a4);
+                load4(kr + 32 + 4 * pp, b4);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    kk[e] = a4[e];
+                    kk[4 + e] = b4[e];
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) kk[e] = 0.f;
+            }
+            float sc[GQA_MAX];
+#pragma unroll
+            for (int h = 0; h < GQA_MAX; ++h) {
+                const float4 qa = *reinterpret_cast<const float4*>(sq + h * D + 4 * pp);
+                const float4 qb = *reinterpret_cast<const float4*>(sq + h * D + 32 + 4 * pp);
+                float x = qa.x * kk[0];
+                x = fmaf(qa.y, kk[1], x);
+                x = fmaf(qa.z, kk[2], x);
+                x = fmaf(qa.w, kk[3], x);
+                x = fmaf(qb.x, kk[4], x);
+                x = fmaf(qb.y, kk[5], x);
+                x = fmaf(qb.z, kk[6], x);
+                sc[h] = fmaf(qb.w, kk[7], x);
+            }
+            const bool u4 = pp & 4, u2 = pp & 2, u1 = pp & 1;
+            float r4[4], r2[2];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float send = u4 ? sc[e] : sc[e + 4];
+                r4[e] = (u4 ? sc[e + 4] : sc[e]) + __shfl_xor_sync(FULL, send, 4);
+            }
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const float send = u2 ? r4[e] : r4[e + 2];
+                r2[e] = (u2 ? r4[e + 2] : r4[e]) + __shfl_xor_sync(FULL, send, 2);
+            }
+            const float total = (u1 ? r2[1] : r2[0]) + __shfl_xor_sync(FULL, u1 ? r2[0] : r2[1], 1);
+            if (valid && pp < hpg) {
+                S[r * GQA_MAX + pp] = total;
+                mw = total;
+            }
+            mw = fmaxf(mw, __shfl_xor_sync(FULL, mw, 8));
+            mw = fmaxf(mw, __shfl_xor_sync(FULL, mw, 16));
+            if (lane < hpg) wm[warp * GQA_MAX + lane] = mw;
+        }
+        __syncthreads();
+        // Warp h: the new running maximum of head h, p = 2^(s - m) in place,
+        // the running sum rescaled and increased.
+        if (warp < hpg) {
+            float cm = lane < NW ? wm[lane * GQA_MAX + warp] : -INFINITY;
+            cm = warp_max(cm);
+            const float m_old = hml[2 * warp], m_new = fmaxf(m_old, cm);
+            float lsum = 0.f;
+            for (int r = lane; r < ATT_CHUNK; r += 32) {
+                float pv = 0.f;
+                if (r < nr) {
+                    pv = ex2_approx(S[r * GQA_MAX + warp] - m_new);
+                    lsum += pv;
+                }
+                S[r * GQA_MAX + warp] = pv;
+            }
+            lsum = warp_sum(lsum);
+            if (lane == 0) {
+                const float al = m_old > -INFINITY ? ex2_approx(m_old - m_new) : 0.f;
+                alpha[warp] = al;
+                hml[2 * warp] = m_new;
+                hml[2 * warp + 1] = fmaf(hml[2 * warp + 1], al, lsum);
+            }
+        }
+        __syncthreads();
+        // P.V: warp w takes rows w, w + 16, ...; lane the dimension pair
+        // (2 lane, 2 lane + 1) for every head at once.
+        {
+            const float4 aa = *reinterpret_cast<const float4*>(alpha);
+            const float4 ab = *reinterpret_cast<const float4*>(alpha + 4);
+            const float al[GQA_MAX] = {aa.x, aa.y, aa.z, aa.w, ab.x, ab.y, ab.z, ab.w};
+#pragma unroll
+            for (int h = 0; h < GQA_MAX; ++h) {
+                acc[h].x *= al[h];
+                acc[h].y *= al[h];
+            }
+#pragma unroll 2
+            for (int r = warp; r < nr; r += NW) {
+                const KV* vr = reinterpret_cast<const KV*>(buf) + (size_t)ATT_CHUNK * D + (size_t)r * D;
+                const float2 v = kv_to_float2(vr + 2 * lane);
+                const float4 pa = *reinterpret_cast<const float4*>(S + r * GQA_MAX);
+                const float4 pb = *reinterpret_cast<const float4*>(S + r * GQA_MAX + 4);
+                const float pr[GQA_MAX] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+                for (int h = 0; h < GQA_MAX; ++h) {
+                    acc[h].x = fmaf(pr[h], v.x, acc[h].x);
+                    acc[h].y = fmaf(pr[h], v.y, acc[h].y);
+                }
+            }
+        }
+        __syncthreads();  // the chunk is consumed
+        if (tid == COPY_T && k + P.sp_bufs < c.sp_n) {
+            fence_proxy_async();
+            sp_fill_chunk(P, A, c, l, k + P.sp_bufs, (int)sizeof(KV));
+        }
+    }
+    rdetail<TR>(P, l, 2, 5);
+    // The 16 warps' shares into the chunk buffers (all consumed, no refill
+    // pending), then summed.
+    float* shares = reinterpret_cast<float*>(ring);  // [NW][GQA_MAX][D]
+#pragma unroll
+    for (int h = 0; h < GQA_MAX; ++h)
+        if (h < hpg) *reinterpret_cast<float2*>(shares + ((size_t)warp * GQA_MAX + h) * D + 2 * lane) = acc[h];
+    __syncthreads();
+    if (tid < hpg * D) {
+        const int h = tid >> 6, d = tid & 63;
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) o += shares[((size_t)w * GQA_MAX + h) * D + d];
+        uint64_t* pw = P.ll_part + ((size_t)(g * hpg + h) * SPL + c.sp_s) * (D + 2);
+        ll_store(pw + 2 + d, o, tag);
+        if (d == 0) {
+            ll_store(pw, hml[2 * h], tag);
+            ll_store(pw + 1, hml[2 * h + 1], tag);
+        }
+    }
+    rdetail<TR>(P, l, 2, 6);
+    __syncthreads();
+    rdetail<TR>(P, l, 2, 7);
+    return true;
+}
+
 // Attention block of head h in spread mode: the (m, l, o) of every unit of
 // its group that holds positions, merged in split order into the head output
 // misc[384 .. 384 + 64): weights 2^(m_s - M), sum_s w_s o_s / sum_s w_s l_s.
@@ -962,7 +1187,7 @@ __device__ __forceinline__ bool sp_merge(const RoleParams& P, const StepArgs& A,
 }
 
 // ---- one layer of each role ----
-template <typename KV, int MD, bool TR, bool SP>
+template <typename KV, int MD, bool TR, int SP>
 __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l, int token,
                                         const float (&rs)[SLICE_RPT]) {
     const int tid = threadIdx.x, ph = 5 * l;
@@ -992,7 +1217,8 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
         // partials (its buffers are free once its unit is done) and only then
         // refills them for the next layer.
         rtrace<TR>(P, 0, ph + 2);
-        if (c.sp_n && !sp_partial<KV, TR>(P, A, c, l, tag)) return false;
+        if (c.sp_n && !(SP == 1 ? sp_partial_resident<KV, TR>(P, A, c, l, tag) : sp_partial<KV, TR>(P, A, c, l, tag)))
+            return false;
         rdetail<TR>(P, l, 1, 1);
         if (!sp_merge(P, A, c, tag)) return false;
         rdetail<TR>(P, l, 1, 2);
@@ -1026,7 +1252,7 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
     return true;
 }
 
-template <typename KV, bool TR, bool SP>
+template <typename KV, bool TR, int SP>
 __device__ __forceinline__ bool ffn_layer(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
                                        const float (&rs)[SLICE_RPT]) {
     const int tid = threadIdx.x, ph = 5 * l;
@@ -1034,7 +1260,9 @@ __device__ __forceinline__ bool ffn_layer(const RoleParams& P, const StepArgs& A
     if (SP && c.sp_n) {
         // This block's attention unit first: the attention blocks wait for it.
         rdetail<TR>(P, l, 3, 6);
-        if (!sp_partial<KV, TR>(P, A, c, l, (A.seq << 8) | (uint32_t)(l + 1))) return false;
+        const uint32_t tag = (A.seq << 8) | (uint32_t)(l + 1);
+        if (!(SP == 1 ? sp_partial_resident<KV, TR>(P, A, c, l, tag) : sp_partial<KV, TR>(P, A, c, l, tag)))
+            return false;
         rdetail<TR>(P, l, 3, 7);
         if (tid == COPY_T && l + 1 < P.L) {
             fence_proxy_async();
@@ -1221,7 +1449,9 @@ __device__ __forceinline__ void role_finish(const RoleParams& P, const StepArgs&
 
 // MD: 32-dim groups of the head dimension a lane covers in the attention
 // scores (1: D <= 32, 2: D <= 64, 4: D <= 128).
-template <typename KV, int MD, bool TR, bool SP>
+// SP: 0 resident attention in the attention blocks; 1 spread units whose
+// chunks are all resident; 2 spread units that stream their chunks.
+template <typename KV, int MD, bool TR, int SP>
 __global__ void __launch_bounds__(NT, 1)
     role_step_kernel(const __grid_constant__ RoleParams P, const __grid_constant__ StepArgs A) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -1230,7 +1460,7 @@ __global__ void __launch_bounds__(NT, 1)
     __shared__ __align__(16) float red[2 * NW + 8];
     __shared__ float s_ss[NW];
     __shared__ int s_abort;
-    __shared__ unsigned s_fills[ROLE_NMB];
+    __shared__ unsigned s_fills[ROLE_NMB + RES_BUFS_MAX];  // fills issued, then a unit's fills waited for
     RoleCtx c;
     const int b = blockIdx.x, tid = threadIdx.x, H = P.H;
     const bool is_attn = b < P.NA;
@@ -1272,8 +1502,6 @@ __global__ void __launch_bounds__(NT, 1)
             c.ra = c.or0 = c.or1 = 0;
         }
         c.sp_g = c.sp_s = c.sp_n = 0;
-        c.sp_ring = is_attn ? c.ring : sm + P.g_ring;
-        c.sp_sq = reinterpret_cast<float*>(is_attn ? c.ring + P.a_sq : sm + P.g_sq);
         if (SP && b < P.NKV * P.sp_splits) {
             c.sp_g = b / P.sp_splits;
             c.sp_s = b % P.sp_splits;
@@ -1282,10 +1510,8 @@ __global__ void __launch_bounds__(NT, 1)
     }
     if (tid == COPY_T) {
         s_abort = 0;
-        for (int i = 0; i < ROLE_NMB; ++i) {
-            mbar_init(mb + i, 1);
-            s_fills[i] = 0;
-        }
+        for (int i = 0; i < ROLE_NMB; ++i) mbar_init(mb + i, 1);
+        for (int i = 0; i < ROLE_NMB + RES_BUFS_MAX; ++i) s_fills[i] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();

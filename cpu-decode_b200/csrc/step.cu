@@ -86,9 +86,11 @@ struct dcb_engine {
     int role_smem = 0, role_max_pos = 0;
     // Its spread mode (the FFN blocks attend) for positions beyond the
     // attention blocks' buffers, up to role_sp_max_pos (0: not available).
-    void* role_kernel_sp = nullptr;
+    void* role_kernel_sp = nullptr;  // units with every chunk resident (up to role_sp_resident_pos)
     void* role_kernel_sp_traced = nullptr;
-    int role_sp_max_pos = 0;
+    void* role_kernel_sps = nullptr;  // units streaming their chunks
+    void* role_kernel_sps_traced = nullptr;
+    int role_sp_max_pos = 0, role_sp_resident_pos = 0;
     // The LM head as its own kernel after a two-role step (head_kernel.cuh),
     // chained by programmatic dependent launch; 2 blocks per SM.
     HeadParams HP{};
@@ -232,8 +234,10 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
         A.head_follows = sep ? 1 : 0;
         if (sep) A.head = 0;
         void* args[] = {(void*)&e->R, (void*)&A};
-        void* k = mode == 2 ? (e->R.trace ? e->role_kernel_sp_traced : e->role_kernel_sp)
-                            : (e->R.trace ? e->role_kernel_traced : e->role_kernel);
+        const bool resident_units = e->pos + 1 <= (size_t)e->role_sp_resident_pos;
+        void* k = mode == 1 ? (e->R.trace ? e->role_kernel_traced : e->role_kernel)
+                  : resident_units ? (e->R.trace ? e->role_kernel_sp_traced : e->role_kernel_sp)
+                                   : (e->R.trace ? e->role_kernel_sps_traced : e->role_kernel_sps);
         DCB_CUDA(cudaLaunchCooperativeKernel(k, dim3(e->grid), dim3(NT), args, (size_t)e->role_smem,
                                              e->stream));
         ++e->launches;
@@ -363,25 +367,28 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     // Each (KV type, head size) has a plain and a traced instantiation.
     void* kt[2];
     for (int tr = 0; tr < 2; ++tr)
-        kt[tr] = D <= 32 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 1, true, false> : (void*)role_step_kernel<__half, 1, false, false>)
-                                : (tr ? (void*)role_step_kernel<float, 1, true, false> : (void*)role_step_kernel<float, 1, false, false>))
-                 : D <= 64 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 2, true, false> : (void*)role_step_kernel<__half, 2, false, false>)
-                                  : (tr ? (void*)role_step_kernel<float, 2, true, false> : (void*)role_step_kernel<float, 2, false, false>))
-                           : (f16 ? (tr ? (void*)role_step_kernel<__half, 4, true, false> : (void*)role_step_kernel<__half, 4, false, false>)
-                                  : (tr ? (void*)role_step_kernel<float, 4, true, false> : (void*)role_step_kernel<float, 4, false, false>));
+        kt[tr] = D <= 32 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 1, true, 0> : (void*)role_step_kernel<__half, 1, false, 0>)
+                                : (tr ? (void*)role_step_kernel<float, 1, true, 0> : (void*)role_step_kernel<float, 1, false, 0>))
+                 : D <= 64 ? (f16 ? (tr ? (void*)role_step_kernel<__half, 2, true, 0> : (void*)role_step_kernel<__half, 2, false, 0>)
+                                  : (tr ? (void*)role_step_kernel<float, 2, true, 0> : (void*)role_step_kernel<float, 2, false, 0>))
+                           : (f16 ? (tr ? (void*)role_step_kernel<__half, 4, true, 0> : (void*)role_step_kernel<__half, 4, false, 0>)
+                                  : (tr ? (void*)role_step_kernel<float, 4, true, 0> : (void*)role_step_kernel<float, 4, false, 0>));
     // Spread mode (the FFN blocks attend beyond the resident buffers): head
     // dim 64, at most GQA_MAX query heads per KV group, every FFN block with
     // gate/up rows, rows that bulk-copy.
     const int sp_splits = G / NKV;  // every block is a unit
     const bool sp_ok = D == 64 && hpg <= GQA_MAX && sp_splits >= 1 && I >= R.NG && R.bulk_kv;
-    void* ks[2] = {nullptr, nullptr};
+    // ks: [resident units, streaming units] x [plain, traced].
+    void* ks[4] = {nullptr, nullptr, nullptr, nullptr};
     if (sp_ok) {
-        ks[0] = f16 ? (void*)role_step_kernel<__half, 2, false, true> : (void*)role_step_kernel<float, 2, false, true>;
-        ks[1] = f16 ? (void*)role_step_kernel<__half, 2, true, true> : (void*)role_step_kernel<float, 2, true, true>;
+        ks[0] = f16 ? (void*)role_step_kernel<__half, 2, false, 1> : (void*)role_step_kernel<float, 2, false, 1>;
+        ks[1] = f16 ? (void*)role_step_kernel<__half, 2, true, 1> : (void*)role_step_kernel<float, 2, true, 1>;
+        ks[2] = f16 ? (void*)role_step_kernel<__half, 2, false, 2> : (void*)role_step_kernel<float, 2, false, 2>;
+        ks[3] = f16 ? (void*)role_step_kernel<__half, 2, true, 2> : (void*)role_step_kernel<float, 2, true, 2>;
     }
     void* k = kt[0];
     if (cudaFuncGetAttributes(&fattr, k) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
-    for (void* kk : {kt[1], ks[0], ks[1]}) {
+    for (void* kk : {kt[1], ks[0], ks[1], ks[2], ks[3]}) {
         if (!kk) continue;
         cudaFuncAttributes ft;
         if (cudaFuncGetAttributes(&ft, kk) != cudaSuccess) return fail(DCB_ERR_CUDA, "role kernel attributes");
@@ -430,7 +437,9 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     if (sp_ok) {
         for (int nb = RES_BUFS_MAX; nb >= 1; --nb) {
             const size_t ring_end = ffn_end + (size_t)nb * R.chunk_bytes;
-            const size_t sq = ((size_t)GQA_MAX * D + 2 * D + 2 * GQA_MAX + NW * GQA_MAX + (size_t)GQA_MAX * nb * ATT_CHUNK) * 4;
+            // (scores: every resident position for the one-pass units)
+            const size_t sq = ((size_t)GQA_MAX * D + 2 * D + 2 * GQA_MAX + NW * GQA_MAX +
+                               (size_t)nb * ATT_CHUNK * GQA_MAX + GQA_MAX) * 4;
             // The buffers also take the P.V shares of every warp ([NW][GQA_MAX][D] floats).
             if (ring_end + sq <= budget && (size_t)nb * R.chunk_bytes >= (size_t)NW * GQA_MAX * D * 4) {
                 R.sp_bufs = nb;
@@ -443,19 +452,19 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     // Attention blocks keep a unit's scratch after sp_bufs of their chunk buffers.
     if (R.sp_bufs > 0) {
         const size_t sq = ((size_t)GQA_MAX * D + 2 * D + 2 * GQA_MAX + NW * GQA_MAX +
-                           (size_t)GQA_MAX * R.sp_bufs * ATT_CHUNK) * 4;
+                           (size_t)R.sp_bufs * ATT_CHUNK * GQA_MAX + GQA_MAX) * 4;
         R.a_sq = R.sp_bufs * R.chunk_bytes;
         if ((size_t)R.a_sq + sq > (size_t)R.nbufs * R.chunk_bytes) R.sp_bufs = 0;
     }
     R.ll_part = P.ll_part;
     const size_t smem = std::max({attn_fixed + (size_t)R.nbufs * R.chunk_bytes, ffn_end, ffn_sp_end});
-    for (void* kk : {kt[0], kt[1], ks[0], ks[1]})
+    for (void* kk : {kt[0], kt[1], ks[0], ks[1], ks[2], ks[3]})
         if (kk && cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
             cudaGetLastError();
             return 0;
         }
     int per_sm = 0;
-    for (void* kk : {kt[0], kt[1], ks[0], ks[1]})
+    for (void* kk : {kt[0], kt[1], ks[0], ks[1], ks[2], ks[3]})
         if (kk && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kk, NT, smem) != cudaSuccess || per_sm < 1)) {
             cudaGetLastError();
             return 0;
@@ -539,7 +548,12 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
     if (sp_ok && R.sp_bufs > 0) {
         e->role_kernel_sp = ks[0];
         e->role_kernel_sp_traced = ks[1];
-        e->role_sp_max_pos = R.sp_splits * R.sp_bufs * ATT_CHUNK;
+        e->role_kernel_sps = ks[2];
+        e->role_kernel_sps_traced = ks[3];
+        e->role_sp_resident_pos = R.sp_splits * R.sp_bufs * ATT_CHUNK;
+        // Units stream their chunks through their buffers: every position the
+        // engine's capacity holds.
+        e->role_sp_max_pos = (int)std::min<size_t>(e->capacity, (size_t)INT32_MAX);
         if (const char* v = std::getenv("DCB_ROLE_SPREAD"))
             if (!std::atoi(v)) e->role_sp_max_pos = 0;
     }
