@@ -71,6 +71,13 @@ struct RoleParams {
     // sp_bufs of them, at a_ring + a_sq).
     int sp_splits, sp_bufs, g_ring, g_sq, a_sq;
     uint64_t* ll_part;   // [NH][sp_splits][D+2] tagged split partials
+    // KV sequence split over GPUs (spread mode): this engine keeps positions
+    // [kv_base, kv_end) as local cache rows; rank `rank` of `world` exchanges
+    // each head's (m, l, o) through exch ([2][NH][world][D+2] tagged words,
+    // its own) and peers[q] (rank q's, over NVLink).
+    int kv_base, kv_end, world, rank;
+    uint64_t* const* peers;
+    uint64_t* exch;
     int chunk_bytes;     // one chunk buffer: [64 K rows | 64 V rows]
     int bulk_kv;         // K/V rows are a multiple of 16 bytes (bulk copies), else plain loads
     const uint8_t* qkv;     // [L][NA][ra_stride][SH] packed rows
@@ -420,7 +427,8 @@ struct RoleCtx {
     int is_attn, ra, or0, or1;  // attention: QKV rows, W_o rows [or0, or1)
     int f, ga, gn;              // FFN: block index, gate/up pairs [ga, ga + gn)
     int sp_g, sp_s, sp_n;       // spread unit: KV group, split, resident chunks (0: no unit)
-    int n_att, nchunks;         // positions attended, resident chunks
+    int n_att, nchunks;         // positions attended (local rows), their chunks
+    int lnew;                   // local row of the new token, -1 when another GPU keeps it
     float qscale;
 };
 
@@ -532,10 +540,12 @@ __device__ __forceinline__ void attn_epilogue(const RoleParams& P, const StepArg
         ll_store(P.ll_q + (size_t)ar.h * D + j, y0, tag);
         ll_store(P.ll_q + (size_t)ar.h * D + j + half, y1, tag);
     } else {
-        KV* cache = static_cast<KV*>(kind == 1 ? P.kcache : P.vcache) +
-                    (((size_t)l * P.NKV + ar.g) * P.capacity + A.pos) * D;
-        kv_store(cache + j, y0);
-        kv_store(cache + j + half, y1);
+        if (c.lnew >= 0) {
+            KV* cache = static_cast<KV*>(kind == 1 ? P.kcache : P.vcache) +
+                        (((size_t)l * P.NKV + ar.g) * P.capacity + c.lnew) * D;
+            kv_store(cache + j, y0);
+            kv_store(cache + j + half, y1);
+        }
         uint64_t* nw = P.ll_kv + (size_t)ar.g * 2 * D + (kind == 1 ? 0 : D);
         ll_store(nw + j, round_to(y0, KV()), tag);
         ll_store(nw + j + half, round_to(y1, KV()), tag);
@@ -672,9 +682,11 @@ __device__ __forceinline__ float* sp_scratch(const RoleParams& P, const RoleCtx&
 // The cached rows (positions below pos) of the unit's k-th chunk of layer l
 // into buffer k % sp_bufs (the copy thread only; a chunk whose rows are all
 // past the cache, i.e. the one starting at pos, needs no copy).
+// Local rows already in the cache: all attended ones but the new token's.
+__device__ __forceinline__ int sp_cached(const RoleCtx& c) { return c.lnew >= 0 ? c.lnew : c.n_att; }
 __device__ __forceinline__ bool sp_chunk_cached(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int k) {
     const int t0 = (c.sp_s + k * P.sp_splits) * ATT_CHUNK;
-    return min(t0 + ATT_CHUNK, A.pos) > t0;
+    return min(t0 + ATT_CHUNK, sp_cached(c)) > t0;
 }
 __device__ __forceinline__ void sp_fill_chunk(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l, int k,
                                               int kv_bytes) {
@@ -682,7 +694,7 @@ __device__ __forceinline__ void sp_fill_chunk(const RoleParams& P, const StepArg
     const size_t rb = (size_t)P.D * kv_bytes;
     const size_t head = (size_t)l * P.NKV + c.sp_g;
     const int b = k % P.sp_bufs;
-    const int t0 = (c.sp_s + k * P.sp_splits) * ATT_CHUNK, t1 = min(t0 + ATT_CHUNK, A.pos);
+    const int t0 = (c.sp_s + k * P.sp_splits) * ATT_CHUNK, t1 = min(t0 + ATT_CHUNK, sp_cached(c));
     uint8_t* kd = sp_ring(P, c) + (size_t)b * P.chunk_bytes;
     const uint32_t bytes = (uint32_t)((t1 - t0) * rb);
     ++c.fills[MB_RING + b];
@@ -738,8 +750,7 @@ __device__ __forceinline__ bool sp_partial_resident(const RoleParams& P, const S
         uint64_t t0 = 0;
 #pragma unroll 1
         for (int k = 0; k < c.sp_n; ++k) {
-            const int ch = c.sp_s + k * SPL;
-            if (min(ch * ATT_CHUNK + ATT_CHUNK, A.pos) <= ch * ATT_CHUNK) continue;
+            if (!sp_chunk_cached(P, A, c, k)) continue;
             unsigned spins = 0;
             bool expired = false;
             while (!mbar_test(c.mb + MB_RING + k, (uint32_t)l & 1u))
@@ -754,10 +765,10 @@ __device__ __forceinline__ bool sp_partial_resident(const RoleParams& P, const S
     if (should_abort(c.st)) return false;
     rdetail<TR>(P, l, 3, 5);
     // The new row into its chunk buffer, when this unit keeps position pos.
-    const int pch = A.pos / ATT_CHUNK;
-    if (pch % SPL == c.sp_s && tid < 2 * D) {
+    const int pch = c.lnew / ATT_CHUNK;
+    if (c.lnew >= 0 && pch % SPL == c.sp_s && tid < 2 * D) {
         KV* kb = reinterpret_cast<KV*>(ring + (size_t)(pch / SPL) * P.chunk_bytes);
-        kv_store(kb + (tid < D ? 0 : (size_t)ATT_CHUNK * D) + (size_t)(A.pos % ATT_CHUNK) * D + tid % D, s_new[tid]);
+        kv_store(kb + (tid < D ? 0 : (size_t)ATT_CHUNK * D) + (size_t)(c.lnew % ATT_CHUNK) * D + tid % D, s_new[tid]);
     }
     __syncthreads();
     rdetail<TR>(P, l, 2, 3);
@@ -772,7 +783,7 @@ __device__ __forceinline__ bool sp_partial_resident(const RoleParams& P, const S
         for (int base = 0; base < np; base += 4 * NW) {
             const int li = base + warp * 4 + grp;  // local position: buffer li / 64, row li % 64
             const int t = (c.sp_s + (li >> 6) * SPL) * ATT_CHUNK + (li & 63);
-            const bool valid = li < np && t <= A.pos;
+            const bool valid = li < np && t < c.n_att;
             float kk[8];
             if (valid) {
                 const KV* kr = reinterpret_cast<const KV*>(ring + (size_t)(li >> 6) * P.chunk_bytes) + (size_t)(li & 63) * D;
@@ -835,7 +846,7 @@ __device__ __forceinline__ bool sp_partial_resident(const RoleParams& P, const S
         for (int li = lane; li < np; li += 32) {
             const int t = (c.sp_s + (li >> 6) * SPL) * ATT_CHUNK + (li & 63);
             float pv = 0.f;
-            if (t <= A.pos) {
+            if (t < c.n_att) {
                 pv = ex2_approx(S[li * GQA_MAX + warp] - m);
                 lsum += pv;
             }
@@ -860,7 +871,7 @@ __device__ __forceinline__ bool sp_partial_resident(const RoleParams& P, const S
 #pragma unroll 2
         for (int li = warp; li < np; li += NW) {
             const int t = (c.sp_s + (li >> 6) * SPL) * ATT_CHUNK + (li & 63);
-            if (t > A.pos) continue;  // warp-uniform
+            if (t >= c.n_att) continue;  // warp-uniform
             const KV* vr = reinterpret_cast<const KV*>(ring + (size_t)(li >> 6) * P.chunk_bytes) +
                            (size_t)ATT_CHUNK * D + (size_t)(li & 63) * D;
             const float2 v = kv_to_float2(vr + 2 * lane);
@@ -951,7 +962,7 @@ __device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& 
 #pragma unroll 1
     for (int k = 0; k < c.sp_n; ++k) {
         const int b = k % P.sp_bufs;
-        const int t0 = (c.sp_s + k * SPL) * ATT_CHUNK, nr = min(ATT_CHUNK, A.pos + 1 - t0);
+        const int t0 = (c.sp_s + k * SPL) * ATT_CHUNK, nr = min(ATT_CHUNK, c.n_att - t0);
         uint8_t* buf = ring + (size_t)b * P.chunk_bytes;
         if (tid == 0 && sp_chunk_cached(P, A, c, k)) {
             uint64_t w0 = 0;
@@ -962,11 +973,11 @@ __device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& 
         }
         __syncthreads();  // the chunk has arrived; the queries are staged
         if (should_abort(c.st)) return false;
-        if (A.pos - t0 < ATT_CHUNK) {  // block-uniform: this chunk holds position pos
+        if (c.lnew >= t0 && c.lnew - t0 < ATT_CHUNK) {  // block-uniform: this chunk holds the new token
             // The new row from the tagged words.
             if (tid < 2 * D) {
                 KV* kb = reinterpret_cast<KV*>(buf);
-                kv_store(kb + (tid < D ? 0 : (size_t)ATT_CHUNK * D) + (size_t)(A.pos - t0) * D + tid % D, s_new[tid]);
+                kv_store(kb + (tid < D ? 0 : (size_t)ATT_CHUNK * D) + (size_t)(c.lnew - t0) * D + tid % D, s_new[tid]);
             }
             __syncthreads();
         }
@@ -1114,13 +1125,16 @@ __device__ __forceinline__ bool sp_partial(const RoleParams& P, const StepArgs& 
 // its group that holds positions, merged in split order into the head output
 // misc[384 .. 384 + 64): weights 2^(m_s - M), sum_s w_s o_s / sum_s w_s l_s.
 // The partial table and the merge scratch use the (idle) chunk buffers.
-__device__ __forceinline__ bool sp_merge(const RoleParams& P, const StepArgs& A, const RoleCtx& c, uint32_t tag) {
+__device__ __forceinline__ bool sp_merge(const RoleParams& P, const StepArgs& A, const RoleCtx& c, int l,
+                                        uint32_t tag) {
     constexpr int D = 64, W = D + 2;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int SPL = P.sp_splits, nch = (A.pos + ATT_CHUNK) / ATT_CHUNK, ns = min(nch, SPL);
+    const int SPL = P.sp_splits, ns = min(c.nchunks, SPL);
     float* table = reinterpret_cast<float*>(c.ring);  // [ns][W]
     float* wgt = table + SPL * W;                      // [ns]
     float* share = wgt + SPL;                          // [8][D + 1]
+    float* own = share + 8 * (D + 1);                  // this GPU's (m, l, o) of the head
+    float* tab = own + W;                              // [world][W] every GPU's
     const uint64_t* src = P.ll_part + (size_t)c.ar.h * SPL * W;
     {
         constexpr int WT = 8;
@@ -1160,6 +1174,7 @@ __device__ __forceinline__ bool sp_merge(const RoleParams& P, const StepArgs& A,
         for (int i = lane; i < ns; i += 32) mx = fmaxf(mx, table[i * W]);
         mx = warp_max(mx);
         for (int i = lane; i < ns; i += 32) wgt[i] = ex2_approx(table[i * W] - mx);
+        if (lane == 0) own[0] = mx;  // -inf when this GPU keeps no attended position
     }
     __syncthreads();
     {
@@ -1179,6 +1194,67 @@ __device__ __forceinline__ bool sp_merge(const RoleParams& P, const StepArgs& A,
         for (int q = 0; q < 8; ++q) {
             num += share[q * (D + 1) + tid];
             den += share[q * (D + 1) + D];
+        }
+        if (P.world == 1) {
+            c.misc[384 + tid] = num / den;
+        } else {
+            own[2 + tid] = num;
+            if (tid == 0) own[1] = den;
+        }
+    }
+    __syncthreads();
+    if (P.world == 1) return true;
+    // KV split: this GPU's (m, l, o) into every GPU's exchange buffer (block
+    // s = 0 of the head writes; system-scope tagged words over NVLink), then
+    // every GPU's from the local buffer, merged in rank order so that all GPUs
+    // get the same head output. Slots alternate with the global layer count, so
+    // a GPU one layer ahead writes the other slot.
+    const int slot = (int)((A.seq * (unsigned)P.L + (unsigned)l) & 1u), h = c.ar.h, nw = P.world * W;
+    if (c.ar.s == 0)
+        for (int i = tid; i < nw; i += NT) {
+            const int q = i / W, k = i - q * W;
+            ll_store_sys(P.peers[q] + (((size_t)slot * P.NH + h) * P.world + P.rank) * W + k, own[k], tag);
+        }
+    {
+        const uint64_t* src = P.exch + ((size_t)slot * P.NH + h) * P.world * W;
+        constexpr int WT = 2;  // world * W <= 8 * 66 < 2 * NT
+        uint64_t w[WT];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < WT; ++k) {
+            const int i = tid + k * NT;
+            if (i < nw) {
+                w[k] = ll_load_sys(src + i);
+                pending |= 1u << k;
+            }
+        }
+        uint64_t t0 = 0;
+        unsigned rounds = 0;
+        while (pending) {
+#pragma unroll
+            for (int k = 0; k < WT; ++k)
+                if (((pending >> k) & 1u) && (uint32_t)(w[k] >> 32) == tag) {
+                    tab[tid + k * NT] = __uint_as_float((uint32_t)w[k]);
+                    pending &= ~(1u << k);
+                }
+            if (!pending) break;
+            if ((++rounds & 7u) == 0 && wait_expired(c.st, t0)) break;
+#pragma unroll
+            for (int k = 0; k < WT; ++k)
+                if ((pending >> k) & 1u) w[k] = ll_load_sys(src + tid + k * NT);
+        }
+    }
+    __syncthreads();
+    if (should_abort(c.st)) return false;
+    if (tid < D) {
+        float mx = -INFINITY;
+        for (int q = 0; q < P.world; ++q) mx = fmaxf(mx, tab[q * W]);
+        float num = 0.f, den = 0.f;
+        for (int q = 0; q < P.world; ++q) {
+            const float mq = tab[q * W];
+            const float f = mq > -INFINITY ? ex2_approx(mq - mx) : 0.f;
+            num = fmaf(f, tab[q * W + 2 + tid], num);
+            den = fmaf(f, tab[q * W + 1], den);
         }
         c.misc[384 + tid] = num / den;
     }
@@ -1220,7 +1296,7 @@ __device__ __forceinline__ bool attn_layer(const RoleParams& P, const StepArgs& 
         if (c.sp_n && !(SP == 1 ? sp_partial_resident<KV, TR>(P, A, c, l, tag) : sp_partial<KV, TR>(P, A, c, l, tag)))
             return false;
         rdetail<TR>(P, l, 1, 1);
-        if (!sp_merge(P, A, c, tag)) return false;
+        if (!sp_merge(P, A, c, l, tag)) return false;
         rdetail<TR>(P, l, 1, 2);
         if (tid == COPY_T && c.sp_n && l + 1 < P.L) {
             fence_proxy_async();
@@ -1486,8 +1562,9 @@ __global__ void __launch_bounds__(NT, 1)
         c.dacc = P.dacc + (size_t)A.par * P.L * 2 * P.Hp;
         c.st = BlockState{&s_abort, P.sync};
         c.is_attn = is_attn;
-        c.n_att = A.pos + 1;
-        c.nchunks = (A.pos + ATT_CHUNK) / ATT_CHUNK;
+        c.n_att = A.pos < P.kv_base ? 0 : min(P.kv_end, A.pos + 1) - P.kv_base;
+        c.nchunks = (c.n_att + ATT_CHUNK - 1) / ATT_CHUNK;
+        c.lnew = A.pos >= P.kv_base && A.pos < P.kv_end ? A.pos - P.kv_base : -1;
         c.qscale = LOG2E / sqrtf((float)P.D);
         if (is_attn) {
             c.ar = attn_rows(P, b);

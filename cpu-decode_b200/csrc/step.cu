@@ -210,9 +210,11 @@ void choose_split(const dcb_engine* e, int length, int* nsplit, int* split_len, 
 // blocks' resident buffers, 2 (spread mode) when it fits in the FFN blocks'
 // units, else 0.
 int use_role(const dcb_engine* e) {
-    if (!e->role_ok || !e->role_on || e->P.world != 1 || e->kv_base != 0) return 0;
-    if (e->pos + 1 <= (size_t)e->role_max_pos) return 1;
-    if (e->pos + 1 <= (size_t)e->role_sp_max_pos) return 2;
+    if (!e->role_ok || !e->role_on) return 0;
+    const bool whole = e->P.world == 1 && e->kv_base == 0 && e->kv_end == SIZE_MAX;
+    if (whole && e->pos + 1 <= (size_t)e->role_max_pos) return 1;
+    // Spread mode: one GPU past the resident buffers, or a GPU of a KV split.
+    if (e->role_sp_max_pos > 0 && e->attended(e->pos) <= (size_t)e->role_sp_max_pos) return 2;
     return 0;
 }
 
@@ -234,7 +236,7 @@ int launch(dcb_engine* e, int token, const int* token_dev, int head, int* argmax
         A.head_follows = sep ? 1 : 0;
         if (sep) A.head = 0;
         void* args[] = {(void*)&e->R, (void*)&A};
-        const bool resident_units = e->pos + 1 <= (size_t)e->role_sp_resident_pos;
+        const bool resident_units = e->attended(e->pos) <= (size_t)e->role_sp_resident_pos;
         void* k = mode == 1 ? (e->R.trace ? e->role_kernel_traced : e->role_kernel)
                   : resident_units ? (e->R.trace ? e->role_kernel_sp_traced : e->role_kernel_sp)
                                    : (e->R.trace ? e->role_kernel_sps_traced : e->role_kernel_sps);
@@ -457,6 +459,12 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
         if ((size_t)R.a_sq + sq > (size_t)R.nbufs * R.chunk_bytes) R.sp_bufs = 0;
     }
     R.ll_part = P.ll_part;
+    R.kv_base = P.kv_base;
+    R.kv_end = P.kv_end;
+    R.world = P.world;
+    R.rank = P.rank;
+    R.peers = P.peers;
+    R.exch = P.exch;
     const size_t smem = std::max({attn_fixed + (size_t)R.nbufs * R.chunk_bytes, ffn_end, ffn_sp_end});
     for (void* kk : {kt[0], kt[1], ks[0], ks[1], ks[2], ks[3]})
         if (kk && cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
@@ -1083,6 +1091,10 @@ int dcb_set_kv_shard(dcb_engine* e, int rank, int world, size_t kv_begin, size_t
     e->P.kv_end = kv_end == SIZE_MAX ? 0x7fffffff : (int)kv_end;
     e->P.world = world;
     e->P.rank = rank;
+    e->R.kv_base = e->P.kv_base;
+    e->R.kv_end = e->P.kv_end;
+    e->R.world = world;
+    e->R.rank = rank;
     return 0;
 }
 
