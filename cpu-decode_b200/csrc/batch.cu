@@ -106,6 +106,7 @@ struct dcb_batch {
     float2* rope = nullptr;    // [slots][D/2] (cos, sin) of each sequence's position, per step
     int* seq_done = nullptr;   // [slots] attention blocks finished per sequence (fused split merge)
     int* gbar = nullptr;       // [3][2] grid barriers of the O, gate/up and down projections
+    int* kpart = nullptr;      // [sms][3 * slots][GM] int32 split-K partials of one projection
     bool fuse_combine = false; // split merge inside the attention kernel
     bool fuse_stage = false;   // staging of the next input inside the O, gate/up and down projections
     size_t stage_f_elems = 0;
@@ -215,10 +216,12 @@ int launch_gemm(dcb_batch* b, const CUtensorMap& ma, const CUtensorMap& mb, int 
     a.ksplit = gemm_split(b, EPI, rows, K);
     constexpr int ST = stages_of<EPI>();
     const int smem = gemm_smem_bytes(b->slots, ST);
+    // One [3 * slots][GM] block of split-K partials per CTA.
+    if (a.ksplit > 1 && tiles * a.ksplit > b->sms) return bfail(DCB_ERR_UNSUPPORTED, "split-K grid above the SM count");
     if (a.st_planes)
-        return launch(gemm_i8_kernel<EPI, KV, ST, true>, dim3(tiles * a.ksplit), GT, smem, b->stream, a.ksplit, ma, mb,
+        return launch(gemm_i8_kernel<EPI, KV, ST, true>, dim3(tiles * a.ksplit), gemm_threads<EPI>(), smem, b->stream, a.ksplit, ma, mb,
                       a);
-    return launch(gemm_i8_kernel<EPI, KV, ST>, dim3(tiles * a.ksplit), GT, smem, b->stream, a.ksplit, ma, mb, a);
+    return launch(gemm_i8_kernel<EPI, KV, ST>, dim3(tiles * a.ksplit), gemm_threads<EPI>(), smem, b->stream, a.ksplit, ma, mb, a);
 }
 
 // Can every CTA of this projection's grid be resident at once (needed by its
@@ -230,14 +233,14 @@ bool co_resident(const dcb_batch* b, int rows, int K) {
     const int smem = gemm_smem_bytes(b->slots, ST);
     if (S == 1) {
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_i8_kernel<EPI, KV, ST, true>, GT, smem) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_i8_kernel<EPI, KV, ST, true>, gemm_threads<EPI>(), smem) !=
             cudaSuccess)
             return false;
         return per_sm * b->sms >= grid;
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(GT);
+    cfg.blockDim = dim3(gemm_threads<EPI>());
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -295,6 +298,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits, bool head) {
     g.vcache = b->vc;
     g.kv_seq = b->kv_seq;
     g.amax = b->amax;
+    g.kpart = b->kpart;
     g.err = b->err;
 
     // Layer 0 input: the tokens' embedding rows, RMSNorm-staged.
@@ -605,6 +609,7 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
     if (int rc = b->alloc(&b->rope, (size_t)S * (P.D / 2))) return bail(rc);
     if (int rc = b->alloc(&b->seq_done, S)) return bail(rc);
     if (int rc = b->alloc(&b->gbar, 6)) return bail(rc);
+    if (int rc = b->alloc(&b->kpart, (size_t)b->sms * 3 * S * GM)) return bail(rc);
     if (int rc = b->alloc(&b->xsc, S)) return bail(rc);
     if (int rc = b->alloc(&b->xinv, S)) return bail(rc);
     if (int rc = b->alloc(&b->part, (size_t)S * P.NH * b->max_splits * (P.D + 2))) return bail(rc);

@@ -16,7 +16,8 @@
 //
 // Both operands arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle) into a
 // 4-stage shared-memory ring; one thread issues the MMAs, one the loads, and
-// all four warps read TMEM in the epilogue. Every wait is bounded.
+// every warp reads TMEM in the epilogue (16 warps, four per 32 TMEM lanes, each
+// a share of the sequences). Every wait is bounded.
 //
 // Attention is split-KV over each sequence's own cache (head-major rows, one
 // contiguous block per split), every staged K/V byte serving all query heads
@@ -36,7 +37,8 @@ constexpr int GM = 128;        // weight rows per GEMM tile (UMMA M)
 constexpr int GK = 128;        // reduction bytes per pipeline stage (one 128-byte swizzle row)
 constexpr int GSTAGES = 4;     // pipeline depth of the layer projections (one CTA per SM)
 constexpr int HEAD_STAGES = 2; // LM head: two CTAs per SM, one's loads under the other's prologue and epilogue
-constexpr int GT = 128;        // GEMM threads (four warps: one per 32 TMEM lanes)
+constexpr int GT = 512;        // GEMM threads of a layer projection: 16 warps, four per 32 TMEM lanes
+constexpr int GT_HEAD = 256;   // LM head: 8 warps, two per 32 TMEM lanes (two CTAs per SM)
 constexpr int MAX_SLOTS = 64;  // sequences per batch: N = 3 * slots <= 192
 constexpr uint32_t TMEM_COLS = 256;
 constexpr int A_BYTES = GM * GK;  // 16 KB per stage
@@ -44,6 +46,10 @@ constexpr int ST_NT = 256;        // threads of the staging kernels
 constexpr int ARG_NT = 256;       // threads of the argmax kernel
 
 enum Epi { EPI_PLAIN = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GU = 3, EPI_HEAD = 4 };
+template <int EPI>
+__host__ __device__ constexpr int gemm_threads() {
+    return EPI == EPI_HEAD ? GT_HEAD : GT;
+}
 
 __host__ __device__ constexpr int b_bytes(int slots) { return 3 * slots * GK; }
 // Dynamic shared memory of the GEMM: 1 KB alignment slack, then the A and B rings.
@@ -75,6 +81,7 @@ struct GemmArgs {
     void* kcache;           // [slots or 1][L][NKV][capacity][D]
     void* vcache;
     ArgBest* amax;  // HEAD: [tiles][slots] best (value, row) of each tile and sequence
+    int* kpart;     // split-K: [grid][3 * slots][GM] int32 partials, CTA-major
     int* err;       // set to ERR_WAIT when a wait runs out
     // Staging of the next projection's input once every tile is written (the
     // STAGE instantiation): a grid barrier (all CTAs co-resident), then CTA c
@@ -120,7 +127,7 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* m, uint32_t bytes) {
     asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
 }
-// Thread-block cluster: rank, barrier, and loads from another CTA's shared memory.
+// Thread-block cluster: rank and barrier.
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -128,16 +135,6 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
-    uint32_t out;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
-    return out;
-}
-__device__ __forceinline__ int dsmem_ld(uint32_t addr) {
-    int v;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
-    return v;
 }
 
 // One thread waits for phase `parity` of m, at most WAIT_LIMIT_NS.
@@ -257,8 +254,10 @@ static __device__ void stage_vec(const float* src, int n, int kp, const float* g
 
 // ---- the GEMM ----------------------------------------------------------------------
 template <int EPI, typename KV, int GSTAGES, bool STAGE = false>
-__global__ void __launch_bounds__(GT, 1)
+__global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+    constexpr int NTH = gemm_threads<EPI>();
+    constexpr int NWG = NTH / 128;  // warps per 32 TMEM lanes
     extern __shared__ uint8_t g_sm_raw[];
     uint8_t* g_sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(g_sm_raw) + 1023) & ~uintptr_t(1023));
     const int BB = b_bytes(a.slots), N = 3 * a.slots;
@@ -274,15 +273,25 @@ __global__ void __launch_bounds__(GT, 1)
     __shared__ float s_red[64];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // Epilogue: warp w reads TMEM lanes 32*(w % 4).. (weight rows) and takes
+    // every NWG-th group of 4 sequences from group w / 4 on.
+    const int quad = warp & 3, wg = warp >> 2;
     // Split-K: the S CTAs of a cluster share row tile blockIdx.x / S; rank r
     // takes stages [r*nk/S, (r+1)*nk/S) and, after the exact integer sums
-    // over the cluster, sequences [r*ceil(slots/S), ...) of the epilogue.
+    // over the cluster, sequences [r*per, (r+1)*per) of the epilogue (per a
+    // multiple of 4).
     const int S = a.ksplit;
     const int rank = S > 1 ? (int)cluster_rank() : 0;
     const int m0 = (blockIdx.x / S) * GM;
     const int kb = rank * a.nk / S, nkl = (rank + 1) * a.nk / S - kb;
-    const int per = (a.slots + S - 1) / S;
+    const int per = ((a.slots + S - 1) / S + 3) & ~3;
     const int s_first = rank * per, s_last = min(a.nseq, s_first + per);
+    // This thread's weight row, its scale and bias: weights, which no kernel
+    // of the step writes, so they load before the wait for the previous one.
+    const int r = m0 + 32 * quad + lane;
+    const bool rv = r < a.M;
+    const float wsc = rv ? __ldg(a.wscale + (size_t)r * a.wstride) : 0.f;
+    const float bia = (rv && a.bias) ? __ldg(a.bias + (size_t)r * a.bstride) : 0.f;
 
     if (tid == 0) {
         for (int s = 0; s < GSTAGES; ++s) {
@@ -347,7 +356,7 @@ __global__ void __launch_bounds__(GT, 1)
         __syncwarp();
     }
     griddep_wait();
-    for (int s = tid; s < a.slots; s += GT) {
+    for (int s = tid; s < a.slots; s += NTH) {
         s_xsc[s] = s < a.nseq ? a.xsc[s] : 0.f;
         s_xinv[s] = (a.xinv && s < a.nseq) ? a.xinv[s] : 1.f;
         if (EPI == EPI_QKV) s_pos[s] = s < a.nseq ? a.pos[s] : 0;
@@ -364,29 +373,32 @@ __global__ void __launch_bounds__(GT, 1)
     __syncthreads();
     tc_fence_after();
 
-    // Split-K: this CTA's int32 partials (all N columns) into its own shared
-    // memory as [column][128 rows] (the pipeline buffers are free now), then
-    // visible to the cluster.
-    int* red = reinterpret_cast<int*>(g_sm);
+    const uint32_t trow = tmem + ((uint32_t)(32 * quad) << 16);
+    // Split-K: this CTA's int32 partials (all N columns) to its block of the
+    // L2 scratch, column-major (a warp's 32 rows of one column are 128
+    // contiguous bytes), then visible to the cluster. Warp (quad, wg) moves
+    // the 4-column groups wg, wg + NWG, ... of its 32 rows.
+    const int* kpart_tile = a.kpart + (size_t)(blockIdx.x - rank) * N * GM + 32 * quad + lane;
     if (S > 1) {
-        const uint32_t trow0 = tmem + ((uint32_t)(32 * warp) << 16);
-        for (int c0 = 0; c0 < N; c0 += 16) {
-            uint32_t v[16];
-            tmem_ld16(trow0 + (uint32_t)c0, v);
+        int* mine = a.kpart + (size_t)blockIdx.x * N * GM + 32 * quad + lane;
+        for (int c0 = 4 * wg; c0 < N; c0 += 16 * NWG) {
+            uint32_t v[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (c0 + 4 * NWG * u < N) tmem_ld4(trow + (uint32_t)(c0 + 4 * NWG * u), v[u]);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) red[(c0 + i) * GM + 32 * warp + lane] = (int)v[i];
+            for (int u = 0; u < 4; ++u)
+                if (c0 + 4 * NWG * u < N)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) __stcg(mine + (size_t)(c0 + 4 * NWG * u + k) * GM, (int)v[u][k]);
         }
         cluster_sync();
     }
 
-    // ---- epilogue: thread = weight row m0 + 32*warp + lane. Every global
-    // value the epilogue needs is loaded before the stores of its group, so
-    // the loads of a group are in flight together.
-    const int r = m0 + 32 * warp + lane;
-    const bool rv = r < a.M;
-    const float wsc = rv ? a.wscale[(size_t)r * a.wstride] : 0.f;
-    const float bia = (rv && a.bias) ? a.bias[(size_t)r * a.bstride] : 0.f;
+    // ---- epilogue: thread = weight row r, 4 sequences at a time. Every
+    // global value a group needs is loaded before its stores, so the loads of
+    // a group are in flight together.
     float* __restrict__ out = a.out;
     // QKV: this row's RoPE pair index and frequency (src/model.cpp:222-224,269-274).
     int q_kind = 0, q_hd = 0, q_j = 0;
@@ -398,44 +410,42 @@ __global__ void __launch_bounds__(GT, 1)
         q_hd = pu / half;
         q_j = pu - q_hd * half;
     }
-    const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
-    for (int s0 = s_first; s0 < s_last; s0 += 16) {
-        uint32_t hi[16], md[16], lo[16];
+    for (int s0 = s_first + 4 * wg; s0 < s_last; s0 += 4 * NWG) {
+        uint32_t hi[4], md[4], lo[4];
         if (S == 1) {
-            tmem_ld16(trow + (uint32_t)s0, hi);
-            tmem_ld16(trow + (uint32_t)(a.slots + s0), md);
-            tmem_ld16(trow + (uint32_t)(2 * a.slots + s0), lo);
+            tmem_ld4(trow + (uint32_t)s0, hi);
+            tmem_ld4(trow + (uint32_t)(a.slots + s0), md);
+            tmem_ld4(trow + (uint32_t)(2 * a.slots + s0), lo);
         } else {
-            // Exact sums of the cluster's partials, in rank order.
+            // Exact sums of the cluster's partials (integers: any order).
 #pragma unroll
-            for (int i = 0; i < 16; ++i) hi[i] = md[i] = lo[i] = 0u;
+            for (int i = 0; i < 4; ++i) hi[i] = md[i] = lo[i] = 0u;
+#pragma unroll 2
             for (int q = 0; q < S; ++q) {
-                const uint32_t base = dsmem_addr(red, (uint32_t)q) + 4u * (uint32_t)(32 * warp + lane);
+                const int* pq = kpart_tile + (size_t)q * N * GM;
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    if (s0 + i < s_last) {
-                        hi[i] += (uint32_t)dsmem_ld(base + 4u * (uint32_t)((s0 + i) * GM));
-                        md[i] += (uint32_t)dsmem_ld(base + 4u * (uint32_t)((a.slots + s0 + i) * GM));
-                        lo[i] += (uint32_t)dsmem_ld(base + 4u * (uint32_t)((2 * a.slots + s0 + i) * GM));
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    hi[i] += (uint32_t)__ldcg(pq + (size_t)(s0 + i) * GM);
+                    md[i] += (uint32_t)__ldcg(pq + (size_t)(a.slots + s0 + i) * GM);
+                    lo[i] += (uint32_t)__ldcg(pq + (size_t)(2 * a.slots + s0 + i) * GM);
                 }
             }
         }
-        float xo[16];
-        float2 cs16[16];
+        float xo[4];
+        float2 cs4[4];
         if (EPI == EPI_RESID) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) xo[i] = (rv && s0 + i < s_last) ? out[(size_t)(s0 + i) * a.ldo + r] : 0.f;
+            for (int i = 0; i < 4; ++i) xo[i] = (rv && s0 + i < s_last) ? out[(size_t)(s0 + i) * a.ldo + r] : 0.f;
         }
         if (EPI == EPI_QKV) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-                cs16[i] = (rv && q_kind < 2 && s0 + i < s_last) ? a.rope[(size_t)(s0 + i) * (a.D >> 1) + q_j]
-                                                                : make_float2(1.f, 0.f);
+            for (int i = 0; i < 4; ++i)
+                cs4[i] = (rv && q_kind < 2 && s0 + i < s_last) ? a.rope[(size_t)(s0 + i) * (a.D >> 1) + q_j]
+                                                               : make_float2(1.f, 0.f);
         }
         if (S == 1) tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 4; ++i) {
             const int s = s0 + i;
             const bool sv = s < s_last;
             const int si = sv ? s : 0;
@@ -459,7 +469,7 @@ __global__ void __launch_bounds__(GT, 1)
                     float val = second ? y1 : y0;
                     const int p = s_pos[si];
                     if (q_kind < 2) {
-                        const float cs = cs16[i].x, sn = cs16[i].y;
+                        const float cs = cs4[i].x, sn = cs4[i].y;
                         val = second ? __fadd_rn(__fmul_rn(y1, cs), __fmul_rn(y0, sn))
                                      : __fsub_rn(__fmul_rn(y0, cs), __fmul_rn(y1, sn));
                     }
@@ -485,9 +495,9 @@ __global__ void __launch_bounds__(GT, 1)
                         vi = oi;
                     }
                 }
-                if (lane == 0) {
-                    s_bv[warp][s] = v;
-                    s_bi[warp][s] = vi;
+                if (lane == 0 && sv) {
+                    s_bv[quad][s] = v;
+                    s_bi[quad][s] = vi;
                 }
             }
         }
@@ -505,9 +515,6 @@ __global__ void __launch_bounds__(GT, 1)
             a.amax[(size_t)blockIdx.x * a.slots + tid] = {v, vi};
         }
     }
-    // No CTA leaves (or reuses its shared memory) while a cluster peer may
-    // still read its partials.
-    if (S > 1) cluster_sync();
     if (STAGE && grid_barrier(a.gbar, gridDim.x, a.err, &s_flag)) {
         float* buf = reinterpret_cast<float*>(g_sm);
         for (int s = blockIdx.x; s < a.nseq; s += gridDim.x)
