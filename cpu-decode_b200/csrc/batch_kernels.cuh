@@ -30,6 +30,8 @@
 
 #include <cuda.h>
 
+#include <climits>
+
 namespace dcb {
 namespace batch {
 
@@ -251,6 +253,16 @@ static __device__ void stage_vec(const float* src, int n, int kp, const float* g
     }
     __syncthreads();  // buf and red are reused by the next sequence
 }
+
+// Order-preserving integer key of a logit for a warp max (redux.sync): finite
+// values and infinities in float order, -0 equal to +0, NaN below everything
+// (a NaN is never the better candidate, as in better()).
+__device__ __forceinline__ int argmax_key(float v) {
+    if (v != v) return INT_MIN;
+    const int b = __float_as_int(v + 0.0f);
+    return b >= 0 ? b : b ^ 0x7fffffff;
+}
+__device__ __forceinline__ float argmax_key_value(int k) { return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff); }
 
 // ---- the GEMM ----------------------------------------------------------------------
 template <int EPI, typename KV, int GSTAGES, bool STAGE = false>
@@ -484,20 +496,15 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
                 }
             } else if (EPI == EPI_HEAD) {
                 if (rv && sv && out) out[(size_t)s * a.ldo + r] = y;
-                float v = (rv && sv) ? y : -INFINITY;
-                int vi = r;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(FULL, v, o);
-                    const int oi = __shfl_xor_sync(FULL, vi, o);
-                    if (better(ov, oi, v, vi)) {
-                        v = ov;
-                        vi = oi;
-                    }
-                }
+                // The warp's best row for sequence s: the largest key, then the
+                // lowest lane holding it (rows ascend with the lane: the first
+                // maximum, src/main.cpp:35-37).
+                const int key = argmax_key((rv && sv) ? y : -INFINITY);
+                const int kmax = __reduce_max_sync(FULL, key);
+                const unsigned hit = __ballot_sync(FULL, key == kmax);
                 if (lane == 0 && sv) {
-                    s_bv[quad][s] = v;
-                    s_bi[quad][s] = vi;
+                    s_bv[quad][s] = argmax_key_value(kmax);
+                    s_bi[quad][s] = m0 + 32 * quad + __ffs(hit) - 1;
                 }
             }
         }
