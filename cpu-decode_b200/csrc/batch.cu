@@ -600,7 +600,10 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
     b->capacity = capacity;
     b->kv_dtype = kv_dtype;
     b->attn64 = P.D == 64 && P.NH / P.NKV <= A64_HP;
-    b->split_len = b->attn64 ? 512 : 256;
+    b->split_len = b->attn64 ? 768 : 256;
+    // DCB_BATCH_SPLIT: positions per attention split (a multiple of 64), for tuning.
+    if (const char* sv = std::getenv("DCB_BATCH_SPLIT"))
+        b->split_len = std::max(64, std::min(1 << 16, std::atoi(sv) / 64 * 64));
     b->max_splits = cdiv((int)capacity, b->split_len);
     const int S = b->slots;
     if (int rc = b->alloc(&b->x, (size_t)S * P.Kh)) return bail(rc);
