@@ -12,7 +12,10 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
+#include <memory>
 #include <string>
+#include <thread>
 #include <vector>
 
 namespace dcb {
@@ -134,10 +137,33 @@ void pack_row(uint8_t* dst, const int8_t* w, int K, float scale, float bias) {
     std::memset(dst + K16 + 8, 0, 8);
 }
 
-int upload(dcb_engine* e, uint8_t** out, const std::vector<uint8_t>& host) {
+// Runs f(i) for every i in [0, n) on up to 16 host threads. The load-time
+// packing of the weight layouts uses it: task i writes only its own bytes.
+template <class F>
+void parallel_for(int n, const F& f) {
+    const unsigned hw = std::thread::hardware_concurrency();
+    const int T = std::max(1, std::min({n, 16, (int)(hw ? hw : 1)}));
+    std::atomic<int> next{0};
+    auto work = [&] {
+        for (int i; (i = next.fetch_add(1)) < n;) f(i);
+    };
+    std::vector<std::thread> pool;
+    for (int t = 1; t < T; ++t) pool.emplace_back(work);
+    work();
+    for (auto& t : pool) t.join();
+}
+
+// n bytes of host memory for a packed layout, not initialised: each packing
+// task zeroes or writes every byte of its own region.
+uint8_t* host_bytes(std::unique_ptr<uint8_t[]>& p, size_t n) {
+    p.reset(new uint8_t[std::max<size_t>(n, 1)]);
+    return p.get();
+}
+
+int upload(dcb_engine* e, uint8_t** out, const uint8_t* host, size_t n) {
     uint8_t* d = nullptr;
-    if (int rc = e->alloc(&d, host.size())) return rc;
-    DCB_CUDA(cudaMemcpy(d, host.data(), host.size(), cudaMemcpyHostToDevice));
+    if (int rc = e->alloc(&d, n)) return rc;
+    DCB_CUDA(cudaMemcpy(d, host, n, cudaMemcpyHostToDevice));
     *out = d;
     return 0;
 }
@@ -478,12 +504,16 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
             return 0;
         }
     // Packed QKV rows per (layer, attention block), zero rows past its count.
-    std::vector<uint8_t> buf((size_t)e->L * R.NA * ra_max * P.SH, 0);
-    for (int l = 0; l < e->L; ++l) {
+    std::unique_ptr<uint8_t[]> buf;
+    size_t nb = (size_t)e->L * R.NA * ra_max * P.SH;
+    uint8_t* b = host_bytes(buf, nb);
+    parallel_for(e->L * R.NA, [&](int t) {
+        const int l = t / R.NA, a = t % R.NA;
         const dcb_layer_desc& S = m->layer[l];
-        for (int a = 0; a < R.NA; ++a) {
+        {
             const Share& x = sh[a];
-            uint8_t* dst = &buf[((size_t)l * R.NA + a) * ra_max * P.SH];
+            uint8_t* dst = b + (size_t)t * ra_max * P.SH;
+            std::memset(dst, 0, (size_t)ra_max * P.SH);
             int row = 0;
             auto put = [&](const int8_t* w, const float* sc, const float* bi, int r) {
                 pack_row(dst + (size_t)(row++) * P.SH, w + (size_t)r * H, H, sc[r], bi[r]);
@@ -502,21 +532,22 @@ int setup_role(dcb_engine* e, const dcb_model_desc* m, int max_optin) {
                 }
             }
         }
-    }
+    });
     uint8_t* d8;
-    if (int rc = upload(e, &d8, buf)) return rc;
+    if (int rc = upload(e, &d8, b, nb)) return rc;
     R.qkv = d8;
     // W_down column slices per (layer, FFN block), dw bytes per row.
-    buf.assign((size_t)e->L * R.NG * R.down_slice, 0);
-    for (int l = 0; l < e->L; ++l) {
+    nb = (size_t)e->L * R.NG * R.down_slice;
+    b = host_bytes(buf, nb);
+    parallel_for(e->L * R.NG, [&](int t) {
+        const int l = t / R.NG, f = t % R.NG;
         const dcb_layer_desc& S = m->layer[l];
-        for (int f = 0; f < R.NG; ++f) {
-            const int c0 = plo(f, R.NG, I), c1 = plo(f + 1, R.NG, I);
-            uint8_t* dst = &buf[((size_t)l * R.NG + f) * R.down_slice];
-            for (int r = 0; r < H; ++r) std::memcpy(dst + (size_t)r * R.dw, S.down + (size_t)r * I + c0, (size_t)(c1 - c0));
-        }
-    }
-    if (int rc = upload(e, &d8, buf)) return rc;
+        const int c0 = plo(f, R.NG, I), c1 = plo(f + 1, R.NG, I);
+        uint8_t* dst = b + (size_t)t * R.down_slice;
+        std::memset(dst, 0, R.down_slice);
+        for (int r = 0; r < H; ++r) std::memcpy(dst + (size_t)r * R.dw, S.down + (size_t)r * I + c0, (size_t)(c1 - c0));
+    });
+    if (int rc = upload(e, &d8, b, nb)) return rc;
     R.down_cols = d8;
 
     // The separate LM-head kernel (argmax candidates of its own).
@@ -639,43 +670,63 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     P.world = 1;
     P.rank = 0;
 
-    // ---- weights in packed-row layout
+    // ---- weights in packed-row layout: every layer's four matrices packed on
+    // host threads, then uploaded one by one.
     std::vector<LayerW> lw(e->L);
-    std::vector<uint8_t> buf;
-    for (int l = 0; l < e->L; ++l) {
-        const dcb_layer_desc& S = m->layer[l];
-        LayerW& W = lw[l];
-        buf.assign((size_t)P.qkv_pairs * 2 * P.SH, 0);
-        size_t row = 0;
-        auto add_pairs = [&](const int8_t* w, const float* sc, const float* bi, int heads) {
-            for (int h = 0; h < heads; ++h)
-                for (int j = 0; j < half; ++j)
-                    for (int r : {h * D + j, h * D + j + half})
-                        pack_row(&buf[(row++) * P.SH], w + (size_t)r * H, H, sc[r], bi[r]);
+    {
+        struct LayerPack {
+            std::unique_ptr<uint8_t[]> m[4];  // QKV pairs, O, gate/up, down
+            size_t n[4] = {0, 0, 0, 0};
         };
-        add_pairs(S.q, S.q_scales, S.q_bias, e->NH);
-        add_pairs(S.k, S.k_scales, S.k_bias, e->NKV);
-        add_pairs(S.v, S.v_scales, S.v_bias, e->NKV);
-        uint8_t* d8;
-        if (int rc = upload(e, &d8, buf)) return bail(rc);
-        W.qkv = d8;
-        buf.assign((size_t)H * P.SH, 0);
-        for (int r = 0; r < H; ++r) pack_row(&buf[(size_t)r * P.SH], S.o + (size_t)r * H, H, S.o_scales[r], 0.f);
-        if (int rc = upload(e, &d8, buf)) return bail(rc);
-        W.o = d8;
-        buf.assign((size_t)2 * I * P.SH, 0);
-        for (int j = 0; j < I; ++j) {
-            pack_row(&buf[(size_t)(2 * j) * P.SH], S.gate + (size_t)j * H, H, S.gate_scales[j], 0.f);
-            pack_row(&buf[(size_t)(2 * j + 1) * P.SH], S.up + (size_t)j * H, H, S.up_scales[j], 0.f);
+        std::vector<LayerPack> lp(e->L);
+        parallel_for(4 * e->L, [&](int t) {
+            const int l = t / 4, which = t % 4;
+            const dcb_layer_desc& S = m->layer[l];
+            LayerPack& x = lp[l];
+            if (which == 0) {
+                x.n[0] = (size_t)P.qkv_pairs * 2 * P.SH;
+                uint8_t* b = host_bytes(x.m[0], x.n[0]);
+                size_t row = 0;
+                auto add_pairs = [&](const int8_t* w, const float* sc, const float* bi, int heads) {
+                    for (int h = 0; h < heads; ++h)
+                        for (int j = 0; j < half; ++j)
+                            for (int r : {h * D + j, h * D + j + half})
+                                pack_row(b + (row++) * P.SH, w + (size_t)r * H, H, sc[r], bi[r]);
+                };
+                add_pairs(S.q, S.q_scales, S.q_bias, e->NH);
+                add_pairs(S.k, S.k_scales, S.k_bias, e->NKV);
+                add_pairs(S.v, S.v_scales, S.v_bias, e->NKV);
+            } else if (which == 1) {
+                x.n[1] = (size_t)H * P.SH;
+                uint8_t* b = host_bytes(x.m[1], x.n[1]);
+                for (int r = 0; r < H; ++r) pack_row(b + (size_t)r * P.SH, S.o + (size_t)r * H, H, S.o_scales[r], 0.f);
+            } else if (which == 2) {
+                x.n[2] = (size_t)2 * I * P.SH;
+                uint8_t* b = host_bytes(x.m[2], x.n[2]);
+                for (int j = 0; j < I; ++j) {
+                    pack_row(b + (size_t)(2 * j) * P.SH, S.gate + (size_t)j * H, H, S.gate_scales[j], 0.f);
+                    pack_row(b + (size_t)(2 * j + 1) * P.SH, S.up + (size_t)j * H, H, S.up_scales[j], 0.f);
+                }
+            } else {
+                x.n[3] = (size_t)H * P.SI;
+                uint8_t* b = host_bytes(x.m[3], x.n[3]);
+                for (int r = 0; r < H; ++r)
+                    pack_row(b + (size_t)r * P.SI, S.down + (size_t)r * I, I, S.down_scales[r], 0.f);
+            }
+        });
+        for (int l = 0; l < e->L; ++l) {
+            uint8_t* d8[4];
+            for (int k = 0; k < 4; ++k) {
+                if (int rc = upload(e, &d8[k], lp[l].m[k].get(), lp[l].n[k])) return bail(rc);
+                lp[l].m[k].reset();
+            }
+            lw[l].qkv = d8[0];
+            lw[l].o = d8[1];
+            lw[l].gu = d8[2];
+            lw[l].down = d8[3];
         }
-        if (int rc = upload(e, &d8, buf)) return bail(rc);
-        W.gu = d8;
-        buf.assign((size_t)H * P.SI, 0);
-        for (int r = 0; r < H; ++r)
-            pack_row(&buf[(size_t)r * P.SI], S.down + (size_t)r * I, I, S.down_scales[r], 0.f);
-        if (int rc = upload(e, &d8, buf)) return bail(rc);
-        W.down = d8;
     }
+    std::unique_ptr<uint8_t[]> buf;
     // Down projection for the split-K step: block b's columns [b*I/G, (b+1)*I/G)
     // of every row, DW bytes per row (zero past the block's columns), one
     // down_slice-byte region per (layer, block); per-row scales apart.
@@ -689,20 +740,21 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         if (e->NH > G) return bail(fail(DCB_ERR_UNSUPPORTED, "more query heads than multiprocessors"));
         P.down_dw = DW;
         P.down_slice = (int)round_up((size_t)H * DW, 16);
-        buf.assign((size_t)e->L * G * P.down_slice, 0);
-        std::vector<float> dscale((size_t)e->L * H);
-        for (int l = 0; l < e->L; ++l) {
+        const size_t nb = (size_t)e->L * G * P.down_slice;
+        uint8_t* b = host_bytes(buf, nb);
+        parallel_for(e->L * G, [&](int t) {
+            const int l = t / G, bb = t % G;
             const dcb_layer_desc& S = m->layer[l];
-            for (int bb = 0; bb < G; ++bb) {
-                const int c0 = (int)((long long)bb * I / G), c1 = (int)((long long)(bb + 1) * I / G);
-                uint8_t* dst = &buf[((size_t)l * G + bb) * P.down_slice];
-                for (int r = 0; r < H; ++r)
-                    std::memcpy(dst + (size_t)r * DW, S.down + (size_t)r * I + c0, (size_t)(c1 - c0));
-            }
-            std::copy(S.down_scales, S.down_scales + H, dscale.begin() + (size_t)l * H);
-        }
+            const int c0 = (int)((long long)bb * I / G), c1 = (int)((long long)(bb + 1) * I / G);
+            uint8_t* dst = b + (size_t)t * P.down_slice;
+            std::memset(dst, 0, P.down_slice);
+            for (int r = 0; r < H; ++r) std::memcpy(dst + (size_t)r * DW, S.down + (size_t)r * I + c0, (size_t)(c1 - c0));
+        });
+        std::vector<float> dscale((size_t)e->L * H);
+        for (int l = 0; l < e->L; ++l)
+            std::copy(m->layer[l].down_scales, m->layer[l].down_scales + H, dscale.begin() + (size_t)l * H);
         uint8_t* d8;
-        if (int rc = upload(e, &d8, buf)) return bail(rc);
+        if (int rc = upload(e, &d8, b, nb)) return bail(rc);
         P.down_cols = d8;
         if (int rc = upload_floats(e, &P.down_scale, dscale)) return bail(rc);
     }
@@ -712,18 +764,20 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
     {
         P.o_dw = slice_row_bytes(D);
         P.o_slice = (int)round_up((size_t)H * P.o_dw, 16);
-        buf.assign((size_t)e->L * e->NH * P.o_slice, 0);
-        std::vector<float> oscale((size_t)e->L * H);
-        for (int l = 0; l < e->L; ++l) {
+        const size_t nb = (size_t)e->L * e->NH * P.o_slice;
+        uint8_t* b = host_bytes(buf, nb);
+        parallel_for(e->L * e->NH, [&](int t) {
+            const int l = t / e->NH, h = t % e->NH;
             const dcb_layer_desc& S = m->layer[l];
-            for (int h = 0; h < e->NH; ++h) {
-                uint8_t* dst = &buf[((size_t)l * e->NH + h) * P.o_slice];
-                for (int r = 0; r < H; ++r) std::memcpy(dst + (size_t)r * P.o_dw, S.o + (size_t)r * H + h * D, D);
-            }
-            std::copy(S.o_scales, S.o_scales + H, oscale.begin() + (size_t)l * H);
-        }
+            uint8_t* dst = b + (size_t)t * P.o_slice;
+            std::memset(dst, 0, P.o_slice);
+            for (int r = 0; r < H; ++r) std::memcpy(dst + (size_t)r * P.o_dw, S.o + (size_t)r * H + h * D, D);
+        });
+        std::vector<float> oscale((size_t)e->L * H);
+        for (int l = 0; l < e->L; ++l)
+            std::copy(m->layer[l].o_scales, m->layer[l].o_scales + H, oscale.begin() + (size_t)l * H);
         uint8_t* d8;
-        if (int rc = upload(e, &d8, buf)) return bail(rc);
+        if (int rc = upload(e, &d8, b, nb)) return bail(rc);
         P.o_cols = d8;
         if (int rc = upload_floats(e, &P.o_scale, oscale)) return bail(rc);
     }
@@ -735,13 +789,17 @@ int dcb_create(const dcb_model_desc* m, size_t capacity, int kv_dtype, int cache
         P.layers = d_layers;
     }
     {
-        buf.assign((size_t)e->V * P.SH, 0);
-        for (int r = 0; r < e->V; ++r)
-            pack_row(&buf[(size_t)r * P.SH], m->embed + (size_t)r * H, H, m->embed_scales[r], 0.f);
+        const size_t nb = (size_t)e->V * P.SH;
+        uint8_t* b = host_bytes(buf, nb);
+        constexpr int ROWS = 1024;  // embedding rows per packing task
+        parallel_for(ceil_div(e->V, ROWS), [&](int t) {
+            for (int r = t * ROWS; r < std::min(e->V, (t + 1) * ROWS); ++r)
+                pack_row(b + (size_t)r * P.SH, m->embed + (size_t)r * H, H, m->embed_scales[r], 0.f);
+        });
         uint8_t* d8;
-        if (int rc = upload(e, &d8, buf)) return bail(rc);
+        if (int rc = upload(e, &d8, b, nb)) return bail(rc);
         P.embed = d8;
-        std::vector<uint8_t>().swap(buf);
+        buf.reset();
         // RMSNorm gains, one [input | post-attention] pair per layer, then [final | 0].
         std::vector<float> norms((size_t)(e->L + 1) * 2 * P.Kh, 0.f);
         for (int l = 0; l < e->L; ++l) {
