@@ -810,11 +810,11 @@ __device__ __forceinline__ int a64_off(int r, int d) {
 //   SM: warp h < gq: online softmax of head h over the chunk (base 2) -> P
 //   PV: warp w: dims 16(w%4).., positions 32(w/4)..+31; O^T[dim][head]
 //       accumulates across chunks in the MMA fragments (rescaled per head)
-constexpr int TC_RING_F32 = 3 * 32768;  // three FP32 chunk slots (six F16)
+constexpr int TC_RING_F32 = 2 * 32768;  // two FP32 chunk slots (four F16): three blocks per SM
 constexpr int TC_SS = 9;                 // S row stride (floats): [half][64 positions][9]
 constexpr int TC_PS = 12;                // P row stride (floats): [64 positions][12], conflict-free B loads
 __host__ __device__ constexpr int tc_smem_bytes() {
-    return 1024 + TC_RING_F32 + 2 * A64_T * TC_SS * 4 + A64_T * TC_PS * 4 + 64 + 2 * 64 * A64_HP * 4;
+    return 1024 + TC_RING_F32 + 2 * A64_T * TC_SS * 4 + A64_T * TC_PS * 4 + 64;
 }
 template <typename KV>
 __host__ __device__ constexpr int tc_slots() { return TC_RING_F32 / (2 * a64_tile_bytes<KV>()); }
@@ -853,7 +853,7 @@ __device__ __forceinline__ float tile_one(const uint8_t* tile, int r, int d, __h
 }
 
 template <typename KV, bool FUSE>
-__global__ void __launch_bounds__(A64_NT, 2)
+__global__ void __launch_bounds__(A64_NT, 3)
     attention64_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                           const Attn64Args a) {
     extern __shared__ uint8_t tc_raw[];
@@ -863,7 +863,7 @@ __global__ void __launch_bounds__(A64_NT, 2)
     float* S = reinterpret_cast<float*>(sm + TC_RING_F32);  // [2 halves][64][TC_SS]
     float* P = S + 2 * A64_T * TC_SS;                        // [64][TC_PS]
     float* s_alpha = P + A64_T * TC_PS;                      // [8]
-    float* ow = s_alpha + 16;                                // [2 halves][64 dims][8 heads] at the end
+    float* ow = S;  // [2 halves][64 dims][8 heads] at the end, over the score area
     __shared__ __align__(8) uint64_t full[8];
     __shared__ float s_ml[2 * A64_HP];
     __shared__ int s_abort, s_last;
