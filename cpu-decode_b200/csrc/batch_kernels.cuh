@@ -44,7 +44,7 @@ constexpr int GT_HEAD = 256;   // LM head: 8 warps, two per 32 TMEM lanes (two C
 constexpr int MAX_SLOTS = 64;  // sequences per batch: N = 3 * slots <= 192
 constexpr uint32_t TMEM_COLS = 256;
 constexpr int A_BYTES = GM * GK;  // 16 KB per stage
-constexpr int ST_NT = 256;        // threads of the staging kernels
+constexpr int ST_NT = 512;        // threads of the staging kernels
 constexpr int ARG_NT = 256;       // threads of the argmax kernel
 
 enum Epi { EPI_PLAIN = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GU = 3, EPI_HEAD = 4 };
@@ -591,18 +591,38 @@ __global__ void __launch_bounds__(ST_NT) stage_kernel(const StageArgs a) {
         rsc = *reinterpret_cast<const float*>(row + a.eoff);
     }
     float ss = 0.f, mx = 0.f;
-    for (int j = threadIdx.x; j < a.n; j += ST_NT) {
-        float v;
-        if (row) {
-            v = (float)(int8_t)row[j] * rsc;
-            a.x_out[(size_t)s * a.lds + j] = v;
-        } else {
-            v = a.src[(size_t)s * a.lds + j];
+    if (!row && !(a.n & 3) && !(a.lds & 3)) {
+        // Rows of the previous projection: four values per load.
+        const float4* src4 = reinterpret_cast<const float4*>(a.src + (size_t)s * a.lds);
+        const float4* gain4 = reinterpret_cast<const float4*>(a.gain);
+        for (int q = threadIdx.x; q < a.n / 4; q += ST_NT) {
+            const float4 v = src4[q];
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+            float4 g = v;
+            if (gain4) {
+                const float4 w = gain4[q];
+                g = make_float4(v.x * w.x, v.y * w.y, v.z * w.z, v.w * w.w);
+            }
+            reinterpret_cast<float4*>(st_v)[q] = g;
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(g.x), fabsf(g.y)), fmaxf(fabsf(g.z), fabsf(g.w))));
         }
-        ss = fmaf(v, v, ss);
-        const float g = a.gain ? v * a.gain[j] : v;
-        st_v[j] = g;
-        mx = fmaxf(mx, fabsf(g));
+    } else {
+        for (int j = threadIdx.x; j < a.n; j += ST_NT) {
+            float v;
+            if (row) {
+                v = (float)(int8_t)row[j] * rsc;
+                a.x_out[(size_t)s * a.lds + j] = v;
+            } else {
+                v = a.src[(size_t)s * a.lds + j];
+            }
+            ss = fmaf(v, v, ss);
+            const float g = a.gain ? v * a.gain[j] : v;
+            st_v[j] = g;
+            mx = fmaxf(mx, fabsf(g));
+        }
     }
     block_sum_max(ss, mx, red);
     const float rs = mx > 0.f ? FIX_MAX * __frcp_rn(mx) : 0.f;
@@ -615,8 +635,9 @@ __global__ void __launch_bounds__(ST_NT) stage_kernel(const StageArgs a) {
     int8_t* pl = pm + (size_t)a.slots * a.kp;
     for (int quad = threadIdx.x; quad < a.kp / 4; quad += ST_NT) {
         const int j = 4 * quad;
-        const float4 v4 = make_float4(j < a.n ? st_v[j] : 0.f, j + 1 < a.n ? st_v[j + 1] : 0.f,
-                                      j + 2 < a.n ? st_v[j + 2] : 0.f, j + 3 < a.n ? st_v[j + 3] : 0.f);
+        const float4 v4 = j + 3 < a.n ? reinterpret_cast<const float4*>(st_v)[quad]
+                                      : make_float4(j < a.n ? st_v[j] : 0.f, j + 1 < a.n ? st_v[j + 1] : 0.f,
+                                                    j + 2 < a.n ? st_v[j + 2] : 0.f, j + 3 < a.n ? st_v[j + 3] : 0.f);
         uint32_t h, m, l;
         fix_pack4(v4, rs, h, m, l);
         reinterpret_cast<uint32_t*>(ph)[quad] = h;
