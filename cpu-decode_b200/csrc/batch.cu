@@ -684,6 +684,14 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
     // the kernel instead of in parallel), so they are off by default. The
     // merge needs its scratch to fit the attention kernel's score area; the
     // staging needs every CTA of a projection resident at once.
+    {
+        // The split merge's shared memory: outputs, then a weight per (head, split).
+        const size_t cb = (size_t)(P.NH * P.D + P.NH * b->max_splits) * sizeof(float);
+        if (cb > 227 * 1024) return bail(bfail(DCB_ERR_UNSUPPORTED, "context capacity too large for the split merge"));
+        if (cudaFuncSetAttribute(combine_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cb) !=
+            cudaSuccess)
+            return bail(bfail(DCB_ERR_CUDA, "combine kernel shared memory"));
+    }
     const char* fv = std::getenv("DCB_BATCH_FUSE");
     if (fv && std::atoi(fv)) {
         b->fuse_combine = b->attn64 && (size_t)(P.NH * 64 + P.NH * b->max_splits) * 4 <= (size_t)TC_RING_F32;
