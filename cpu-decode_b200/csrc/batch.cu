@@ -676,14 +676,6 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
     if (int rc = allow_smem<EPI_GU, __half>(S)) return bail(rc);
     if (int rc = allow_smem<EPI_HEAD, float>(S)) return bail(rc);
     if (int rc = allow_smem<EPI_HEAD, __half>(S)) return bail(rc);
-    // Optional fusions (DCB_BATCH_FUSE=1): the split merge by the last
-    // attention block of each sequence, and the staging of the next input by
-    // the O, gate/up and down projections after a grid barrier. Measured on a
-    // B200 with 64 sequences they are slower than the separate kernels (the
-    // merge and the staging of a sequence then run on one block at the end of
-    // the kernel instead of in parallel), so they are off by default. The
-    // merge needs its scratch to fit the attention kernel's score area; the
-    // staging needs every CTA of a projection resident at once.
     {
         // The split merge's shared memory: outputs, then a weight per (head, split).
         const size_t cb = (size_t)(P.NH * P.D + P.NH * b->max_splits) * sizeof(float);
@@ -692,6 +684,14 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
             cudaSuccess)
             return bail(bfail(DCB_ERR_CUDA, "combine kernel shared memory"));
     }
+    // Optional fusions (DCB_BATCH_FUSE=1): the split merge by the last
+    // attention block of each sequence, and the staging of the next input by
+    // the O, gate/up and down projections after a grid barrier. Measured on a
+    // B200 with 64 sequences they are slower than the separate kernels (the
+    // merge and the staging of a sequence then run on one block at the end of
+    // the kernel instead of in parallel), so they are off by default. The
+    // merge needs its scratch to fit the attention kernel's score area; the
+    // staging needs every CTA of a projection resident at once.
     const char* fv = std::getenv("DCB_BATCH_FUSE");
     if (fv && std::atoi(fv)) {
         b->fuse_combine = b->attn64 && (size_t)(P.NH * 64 + P.NH * b->max_splits) * 4 <= (size_t)TC_RING_F32;
