@@ -109,6 +109,7 @@ struct dcb_batch {
     int* kpart = nullptr;      // [sms][3 * slots][GM] int32 split-K partials of one projection
     bool fuse_combine = false; // split merge inside the attention kernel
     bool fuse_stage = false;   // staging of the next input inside the O, gate/up and down projections
+    bool head_persistent = false;  // LM head on head_gemm_kernel (B resident in shared memory)
     size_t stage_f_elems = 0;
     int* h_io = nullptr;  // pinned: [slots] tokens in, then [slots] argmax + error word out
     int* h_pos = nullptr;  // pinned: [slots] positions in (prefill)
@@ -507,7 +508,17 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits, bool head) {
         a.xinv = b->xinv;
         a.out = want_logits ? b->logits : nullptr;
         a.ldo = P.V;
-        if (int rc = launch_gemm<EPI_HEAD, KV>(b, b->map_head, b->map_ph, P.V, P.Kh, a)) return rc;
+        if (b->head_persistent) {
+            a.M = P.V;
+            a.nk = cdiv(P.Kh, GK);
+            a.ksplit = 1;
+            const int grid = std::min(cdiv(P.V, GM), b->sms);
+            if (int rc = launch(head_gemm_kernel, dim3(grid), HB_NT, head_smem_bytes(b->slots), b->stream, 1,
+                                b->map_head, b->map_ph, a))
+                return rc;
+        } else if (int rc = launch_gemm<EPI_HEAD, KV>(b, b->map_head, b->map_ph, P.V, P.Kh, a)) {
+            return rc;
+        }
     }
     ArgmaxArgs ga{};
     ga.amax = b->amax;
@@ -676,6 +687,19 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
     if (int rc = allow_smem<EPI_GU, __half>(S)) return bail(rc);
     if (int rc = allow_smem<EPI_HEAD, float>(S)) return bail(rc);
     if (int rc = allow_smem<EPI_HEAD, __half>(S)) return bail(rc);
+    {
+        // The persistent LM head's 5-stage ring; when it does not fit (or
+        // DCB_BATCH_HEAD=0), the tiled head runs.
+        int optin = 0;
+        BT_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, b->device));
+        const int hs = head_smem_bytes(S);
+        const char* hv = std::getenv("DCB_BATCH_HEAD");
+        if (hs + 4096 <= optin && !(hv && !std::atoi(hv))) {
+            if (cudaFuncSetAttribute(head_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, hs) != cudaSuccess)
+                return bail(bfail(DCB_ERR_CUDA, "LM-head kernel shared memory"));
+            b->head_persistent = true;
+        }
+    }
     {
         // The split merge's shared memory: outputs, then a weight per (head, split).
         const size_t cb = (size_t)(P.NH * P.D + P.NH * b->max_splits) * sizeof(float);

@@ -536,6 +536,202 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     }
 }
 
+// ---- the LM head: persistent -------------------------------------------------------
+// One CTA per SM works through row tiles blockIdx.x, + gridDim.x, ... of the
+// tied head, its loads one stream of (weight tile from HBM, plane tile from
+// L2) stages through a 5-slot ring, so 80 KB of weights are in flight per SM.
+// Two TMEM accumulators (columns 0 and 256) alternate between tiles: the
+// epilogue of one tile (argmax candidates, optional logits) runs under the
+// MMAs of the next. Warps: 0 loads, 1 issues the MMAs, 2 owns TMEM, 4..15 read
+// TMEM (three per 32 lanes, every third group of 4 sequences).
+constexpr int HB_A = 5;     // stages in the ring
+constexpr int HB_NT = 512;  // threads
+constexpr int HB_EW = 12;   // epilogue warps (4..15)
+__host__ __device__ constexpr int head_smem_bytes(int slots) { return 1024 + HB_A * (A_BYTES + b_bytes(slots)); }
+
+__global__ void __launch_bounds__(HB_NT, 1)
+    head_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmArgs a) {
+    extern __shared__ uint8_t hb_raw[];
+    uint8_t* hm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(hb_raw) + 1023) & ~uintptr_t(1023));
+    const int BB = b_bytes(a.slots), N = 3 * a.slots, nk = a.nk;
+    uint8_t* sA = hm;                   // HB_A weight tiles
+    uint8_t* sB = hm + HB_A * A_BYTES;  // HB_A plane tiles (BB is a multiple of 1024)
+    __shared__ __align__(8) uint64_t full[HB_A], empty[HB_A], accf[2], acce[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ float s_xsc[MAX_SLOTS], s_xinv[MAX_SLOTS];
+    __shared__ float s_bv[4][MAX_SLOTS];
+    __shared__ int s_bi[4][MAX_SLOTS];
+    __shared__ int s_abort;  // an epilogue wait ran out: the epilogue warps skip the remaining tiles' work
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ntiles = (a.M + GM - 1) / GM;
+    const int my = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my * nk;
+
+    if (tid == 0) {
+        s_abort = 0;
+        for (int s = 0; s < HB_A; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&accf[s], 1);
+            mbar_init(&acce[s], HB_EW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 2) {
+        tmem_alloc(&s_tmem, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    griddep_launch_dependents();
+
+    int issued = 0;  // thread 0: weight tiles requested
+    if (warp == 0) {
+        if (lane == 0) {
+            // Weight tiles do not depend on the previous kernel: the first
+            // ones are requested before waiting for it.
+            const int npre = min(HB_A, total);
+            for (int g = 0; g < npre; ++g) {
+                const int m0 = ((int)blockIdx.x + (g / nk) * (int)gridDim.x) * GM;
+                mbar_expect_tx(&full[g], A_BYTES);
+                tma2d(sA + g * A_BYTES, &tmA, (g % nk) * GK, m0, &full[g]);
+            }
+            issued = npre;
+            griddep_wait();
+            for (int g = 0; g < npre; ++g) {
+                mbar_expect(&full[g], (uint32_t)BB);
+                tma2d(sB + g * BB, &tmB, (g % nk) * GK, 0, &full[g]);
+            }
+            for (int g = npre; g < total; ++g) {
+                const int slot = g % HB_A;
+                if (!wait_phase(&empty[slot], (uint32_t)((g / HB_A) - 1) & 1u, a.err)) break;
+                const int m0 = ((int)blockIdx.x + (g / nk) * (int)gridDim.x) * GM;
+                mbar_expect(&full[slot], (uint32_t)(A_BYTES + BB));
+                tma2d(sA + slot * A_BYTES, &tmA, (g % nk) * GK, m0, &full[slot]);
+                tma2d(sB + slot * BB, &tmB, (g % nk) * GK, 0, &full[slot]);
+                issued = g + 1;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0 && my > 0) {
+            const uint32_t idesc = idesc_i8(GM, N);
+            bool ok = true;
+            for (int j = 0; ok && j < my; ++j) {
+                const int acc = j & 1;
+                if (j >= 2 && !(ok = wait_phase(&acce[acc], (uint32_t)((j >> 1) - 1) & 1u, a.err))) break;
+                tc_fence_after();
+                const uint32_t td = tmem + (uint32_t)(acc * 256);
+                for (int k = 0; k < nk; ++k) {
+                    const int g = j * nk + k, slot = g % HB_A;
+                    if (!(ok = wait_phase(&full[slot], (uint32_t)(g / HB_A) & 1u, a.err))) break;
+                    tc_fence_after();
+                    const uint64_t da = sw128_desc(sA + slot * A_BYTES), db = sw128_desc(sB + slot * BB);
+#pragma unroll
+                    for (int kk = 0; kk < GK / 32; ++kk)
+                        umma_i8(td, da + 2 * kk, db + 2 * kk, idesc, (k | kk) != 0 ? 1u : 0u);
+                    umma_commit(&empty[slot]);
+                }
+                if (ok) umma_commit(&accf[acc]);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        const int ew = warp - 4, quad = warp & 3, wg = ew >> 2;
+        griddep_wait();
+        for (int s = ew * 32 + lane; s < a.slots; s += HB_EW * 32) {
+            s_xsc[s] = s < a.nseq ? a.xsc[s] : 0.f;
+            s_xinv[s] = (a.xinv && s < a.nseq) ? a.xinv[s] : 1.f;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(HB_EW * 32) : "memory");
+        float* __restrict__ out = a.out;
+        // Row scales one tile ahead (they sit in the weight rows, in HBM).
+        auto row_scale = [&](int j) {
+            const int r = ((int)blockIdx.x + j * (int)gridDim.x) * GM + 32 * quad + lane;
+            return r < a.M ? __ldg(a.wscale + (size_t)r * a.wstride) : 0.f;
+        };
+        float wsc_next = my > 0 ? row_scale(0) : 0.f;
+        for (int j = 0; j < my; ++j) {
+            const int acc = j & 1, tile = (int)blockIdx.x + j * (int)gridDim.x, m0 = tile * GM;
+            const int r = m0 + 32 * quad + lane;
+            const bool rv = r < a.M;
+            const float wsc = wsc_next;
+            if (j + 1 < my) wsc_next = row_scale(j + 1);
+            // Every epilogue warp takes the same barrier steps for every
+            // tile, also after a wait ran out (then without the work).
+            int ok = 1;
+            if (lane == 0) {
+                ok = !*reinterpret_cast<volatile int*>(&s_abort) &&
+                     wait_phase(&accf[acc], (uint32_t)(j >> 1) & 1u, a.err);
+                if (!ok) atomicExch(&s_abort, 1);
+            }
+            ok = __shfl_sync(FULL, ok, 0);
+            tc_fence_after();
+            const uint32_t trow = tmem + (uint32_t)(acc * 256) + ((uint32_t)(32 * quad) << 16);
+            for (int s0 = 4 * wg; ok && s0 < a.nseq; s0 += 4 * (HB_EW / 4)) {
+                uint32_t hi[4], md[4], lo[4];
+                tmem_ld4(trow + (uint32_t)s0, hi);
+                tmem_ld4(trow + (uint32_t)(a.slots + s0), md);
+                tmem_ld4(trow + (uint32_t)(2 * a.slots + s0), lo);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int s = s0 + i;
+                    const bool sv = s < a.nseq;
+                    const int si = sv ? s : 0;
+                    const float y = planes_to_float((int)hi[i], (int)md[i], (int)lo[i]) * s_xsc[si] * s_xinv[si] * wsc + 0.f;
+                    if (rv && sv && out) out[(size_t)s * a.ldo + r] = y;
+                    // The warp's best row for sequence s (first maximum, src/main.cpp:35-37).
+                    const int key = argmax_key((rv && sv) ? y : -INFINITY);
+                    const int kmax = __reduce_max_sync(FULL, key);
+                    const unsigned hit = __ballot_sync(FULL, key == kmax);
+                    if (lane == 0 && sv) {
+                        s_bv[quad][s] = argmax_key_value(kmax);
+                        s_bi[quad][s] = m0 + 32 * quad + __ffs(hit) - 1;
+                    }
+                }
+            }
+            // The accumulator is read: the MMAs of tile j + 2 may reuse it.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[acc]);
+            asm volatile("bar.sync 1, %0;" ::"r"(HB_EW * 32) : "memory");
+            for (int t = ew * 32 + lane; t < a.nseq; t += HB_EW * 32) {
+                float v = s_bv[0][t];
+                int vi = s_bi[0][t];
+                for (int w = 1; w < 4; ++w)
+                    if (better(s_bv[w][t], s_bi[w][t], v, vi)) {
+                        v = s_bv[w][t];
+                        vi = s_bi[w][t];
+                    }
+                a.amax[(size_t)tile * a.slots + t] = {v, vi};
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(HB_EW * 32) : "memory");
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        // Every load issued must land before the block exits (only relevant
+        // after an expired wait; otherwise these phases are complete).
+        for (int s = 0; s < HB_A && s < issued; ++s) {
+            const int last = s + ((issued - 1 - s) / HB_A) * HB_A;
+            wait_phase(&full[s], (uint32_t)(last / HB_A) & 1u, a.err);
+        }
+    }
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 // ---- staging: RMSNorm factor and fixed-point planes of one vector per sequence -----
 struct StageArgs {
     int n;           // vector length
