@@ -89,6 +89,17 @@ def test_batch_fused_path(g64_int8, monkeypatch):
     _run_and_compare(bat, orcs, toks, 2)
 
 
+def test_batch_tiled_head(g64_int8, monkeypatch):
+    """The tiled LM head (one CTA per row tile), which runs when the persistent
+    head's ring does not fit in shared memory."""
+    from conftest import G64
+    monkeypatch.setenv("DCB_BATCH_HEAD", "0")
+    contexts = [0, 64, 600]
+    eng, bat, orcs = _setup(g64_int8, G64, contexts, 2)
+    toks = np.random.default_rng(24).integers(0, G64.vocab, len(contexts))
+    _run_and_compare(bat, orcs, toks, 2)
+
+
 def test_batch_all_64_slots(small_int8):
     contexts = list(np.random.default_rng(3).integers(0, 400, 64))
     eng, bat, orcs = _setup(small_int8, SMALL, contexts, 2)
