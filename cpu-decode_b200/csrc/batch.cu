@@ -351,7 +351,7 @@ int enqueue_step(dcb_batch* b, int n, bool want_logits, bool head) {
     ca.kp = P.Kh;
     ca.planes = b->ph;
     ca.xsc = b->xsc;
-    const int cb_smem = (P.NH * D + P.NH * b->max_splits) * (int)sizeof(float);
+    const int cb_smem = (P.NH * D + 2 * P.NH * b->max_splits) * (int)sizeof(float);
 
     for (int l = 0; l < P.L; ++l) {
         const float* in_norm = P.norms + (size_t)l * 2 * P.Kh;
@@ -701,8 +701,8 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
         }
     }
     {
-        // The split merge's shared memory: outputs, then a weight per (head, split).
-        const size_t cb = (size_t)(P.NH * P.D + P.NH * b->max_splits) * sizeof(float);
+        // The split merge's shared memory: outputs, then a weight and a sum per (head, split).
+        const size_t cb = (size_t)(P.NH * P.D + 2 * P.NH * b->max_splits) * sizeof(float);
         if (cb > 227 * 1024) return bail(bfail(DCB_ERR_UNSUPPORTED, "context capacity too large for the split merge"));
         if (cudaFuncSetAttribute(combine_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cb) !=
             cudaSuccess)
@@ -718,7 +718,7 @@ static int create_batch(const dcb_engine* model, int max_seqs, size_t capacity, 
     // staging needs every CTA of a projection resident at once.
     const char* fv = std::getenv("DCB_BATCH_FUSE");
     if (fv && std::atoi(fv)) {
-        b->fuse_combine = b->attn64 && (size_t)(P.NH * 64 + P.NH * b->max_splits) * 4 <= (size_t)TC_RING_F32;
+        b->fuse_combine = b->attn64 && (size_t)(P.NH * 64 + 2 * P.NH * b->max_splits) * 4 <= (size_t)TC_RING_F32;
         if (kv_dtype == DCB_KV_F16)
             b->fuse_stage = co_resident<EPI_RESID, __half>(b, P.H, P.Kh) &&
                             co_resident<EPI_GU, __half>(b, 2 * P.I, P.Kh) && co_resident<EPI_RESID, __half>(b, P.H, P.Ki);

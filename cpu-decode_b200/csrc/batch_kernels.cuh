@@ -889,7 +889,7 @@ __global__ void __launch_bounds__(AT_NT) attention_kernel(const AttnArgs a) {
 // Merge the splits of every head of sequence s (in split order) and stage the
 // attention output (NH*D values) as planes for the O projection. Run by one
 // whole block; partials are read through L2 (other blocks of the same kernel
-// may have written them). smem: (NH*D + NH*max_splits) floats; red: 64 floats.
+// may have written them). smem: (NH*D + 2*NH*max_splits) floats; red: 64 floats.
 struct CombineArgs {
     const float* part;
     const int* pos;
@@ -897,44 +897,53 @@ struct CombineArgs {
     int8_t* planes;  // [3][slots][kp]
     float* xsc;
 };
+constexpr int CB_SPL = 12;  // splits whose values one warp requests at once
 static __device__ __noinline__ void combine_seq(const CombineArgs& a, int s, float* cb_sm, float* red) {
     const int n = a.NH * a.D, D = a.D, W = D + 2;
     float* outv = cb_sm;
     float* wts = cb_sm + n;
+    float* lsp = wts + a.NH * a.max_splits;  // [NH][max_splits] the splits' sums
     const int ns = (a.pos[s] + a.split_len) / a.split_len;  // splits covering positions 0..pos
     const float* base = a.part + (size_t)s * a.NH * a.max_splits * W;
     const int nt = blockDim.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = nt / 32;
     float mx = 0.f, ss = 0.f;
     // Warp per head: weight of split i = 2^(m_i - M) / sum_i 2^(m_i - M) l_i
     // (lanes over splits), then lanes over dimensions j = lane + 32k with the
-    // loads of eight splits in flight, summed in split order.
+    // loads of CB_SPL splits in flight, summed in split order.
     for (int h = warp; h < a.NH; h += nw) {
         const float* hb = base + (size_t)h * a.max_splits * W;
         float* hw = wts + h * a.max_splits;
+        float* hl = lsp + h * a.max_splits;
         float M = -INFINITY;
-        for (int i = lane; i < ns; i += 32) M = fmaxf(M, __ldcg(hb + (size_t)i * W));
+        for (int i = lane; i < ns; i += 32) {  // (m_i, l_i) requested together, once
+            const float mi = __ldcg(hb + (size_t)i * W), li = __ldcg(hb + (size_t)i * W + 1);
+            hw[i] = mi;
+            hl[i] = li;
+            M = fmaxf(M, mi);
+        }
         M = warp_max(M);
+        __syncwarp();
         float Ls = 0.f;
         for (int i = lane; i < ns; i += 32) {
-            const float mi = __ldcg(hb + (size_t)i * W);
+            const float mi = hw[i];
             const float f = mi > -INFINITY ? at_ex2(mi - M) : 0.f;
             hw[i] = f;
-            Ls = fmaf(f, __ldcg(hb + (size_t)i * W + 1), Ls);
+            Ls = fmaf(f, hl[i], Ls);
         }
         Ls = warp_sum(Ls);
         __syncwarp();
         const float invL = 1.0f / Ls;
         float acc[AT_MAXD] = {0.f, 0.f, 0.f, 0.f};
-        for (int i0 = 0; i0 < ns; i0 += 8) {
-            float v[8][AT_MAXD];
+        for (int i0 = 0; i0 < ns; i0 += CB_SPL) {
+            float v[CB_SPL][AT_MAXD];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < CB_SPL; ++u)
 #pragma unroll
                 for (int k = 0; k < AT_MAXD; ++k)
                     v[u][k] = (i0 + u < ns && lane + 32 * k < D) ? __ldcg(hb + (size_t)(i0 + u) * W + 2 + lane + 32 * k)
                                                                  : 0.f;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < CB_SPL; ++u) {
                 const float f = i0 + u < ns ? hw[i0 + u] : 0.f;
 #pragma unroll
                 for (int k = 0; k < AT_MAXD; ++k) acc[k] = fmaf(f, v[u][k], acc[k]);
