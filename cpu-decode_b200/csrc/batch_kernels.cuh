@@ -542,11 +542,11 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
 // L2) stages through a 5-slot ring, so 80 KB of weights are in flight per SM.
 // Two TMEM accumulators (columns 0 and 256) alternate between tiles: the
 // epilogue of one tile (argmax candidates, optional logits) runs under the
-// MMAs of the next. Warps: 0 loads, 1 issues the MMAs, 2 owns TMEM, 4..15 read
-// TMEM (three per 32 lanes, every third group of 4 sequences).
+// MMAs of the next. Warps: 0 loads, 1 issues the MMAs, 2 owns TMEM, 4..19 read
+// TMEM (four per 32 lanes, every fourth group of 4 sequences).
 constexpr int HB_A = 5;     // stages in the ring
-constexpr int HB_NT = 512;  // threads
-constexpr int HB_EW = 12;   // epilogue warps (4..15)
+constexpr int HB_NT = 640;  // threads
+constexpr int HB_EW = 16;   // epilogue warps (4..19)
 __host__ __device__ constexpr int head_smem_bytes(int slots) { return 1024 + HB_A * (A_BYTES + b_bytes(slots)); }
 
 __global__ void __launch_bounds__(HB_NT, 1)
