@@ -147,8 +147,8 @@ def host_cpu() -> dict:
 
 def reference_bench(model_dir: Path, steps: int, repeats: int, threads: int) -> dict:
     """`cpu-decode bench` of the reference, built from its sources (oracle/_ref),
-    as BASELINE's plan runs it: ctx 128, `steps` greedy steps, `repeats`
-    repeats, the median tokens/s."""
+    as the reference's own measurement tool runs it (tools/measure.py:80-84):
+    ctx 128, `steps` greedy steps, `repeats` repeats, the median tokens/s."""
     exe = ROOT / "oracle" / "_ref" / "cpu-decode"
     kernel = "simd512x4" if "avx512bw" in Path("/proc/cpuinfo").read_text() else "simd256"
     tokens = ",".join(str(t) for t in prompt_tokens())
